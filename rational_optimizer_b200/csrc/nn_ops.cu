@@ -1,0 +1,498 @@
+// Memory-bound transformer ops for sm_100a: RMSNorm (fwd/bwd with a
+// deterministic weight-gradient reduction), fused QKV split + interleaved-pair
+// RoPE (fwd/bwd), and a one-pass softmax cross-entropy that writes the logit
+// gradient in place.  Semantics follow training/train.py:24-45 (RMSNorm,
+// precompute_rope/apply_rope) and the F.cross_entropy mean loss of
+// training/train.py:2868-2870.
+#include "common.cuh"
+
+namespace ro {
+namespace nn {
+
+// ---------------------------------------------------------------------------
+// RMSNorm: y = w * x * rsqrt(mean(x^2) + eps).  One warp per row.  The fast
+// path keeps the row in registers (d = 256 * NCH, lane owns 8 contiguous
+// elements of each 256-wide chunk); the generic path re-reads the row.
+constexpr int kNormWarps = 8;
+
+template <typename T, typename TO, int NCH>
+__global__ void __launch_bounds__(kNormWarps * 32)
+rmsnorm_fwd_fast(const T* __restrict__ x, const float* __restrict__ w, TO* __restrict__ y,
+                 float* __restrict__ rstd_out, int64_t rows, float eps) {
+  constexpr int d = NCH * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[NCH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    load_vec<T, 8>(x + row * d + c * 256 + lane * 8, v[c]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[c][j], v[c][j], ss);
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float wv[8];
+    load_vec<float, 8>(w + c * 256 + lane * 8, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[c][j] = wv[j] * (v[c][j] * r);
+    store_vec<TO, 8>(y + row * d + c * 256 + lane * 8, v[c]);
+  }
+  if (lane == 0) rstd_out[row] = r;
+}
+
+template <typename T, typename TO>
+__global__ void __launch_bounds__(kNormWarps * 32)
+rmsnorm_fwd_generic(const T* __restrict__ x, const float* __restrict__ w, TO* __restrict__ y,
+                    float* __restrict__ rstd_out, int64_t rows, int d, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * d;
+  float ss = 0.f;
+  for (int i = lane; i < d; i += 32) {
+    const float v = to_f<T>(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(d) + eps);
+  for (int i = lane; i < d; i += 32) y[row * d + i] = from_f<TO>(w[i] * (to_f<T>(xr[i]) * r));
+  if (lane == 0) rstd_out[row] = r;
+}
+
+// Backward: dx = r * (w dy - xhat * mean(w dy xhat)), xhat = x r.
+// Weight gradient partial per CTA: partial[blockIdx.x][d] = sum_rows dy*xhat.
+template <typename T, typename TO, int NCH>
+__global__ void __launch_bounds__(kNormWarps * 32)
+rmsnorm_bwd_fast(const TO* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
+                 const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ partial,
+                 int64_t rows, int rows_per_block) {
+  constexpr int d = NCH * 256;
+  __shared__ float red[kNormWarps][256];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float acc[NCH][8];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[c][j] = 0.f;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  int64_t r1 = r0 + rows_per_block;
+  if (r1 > rows) r1 = rows;
+  for (int64_t row = r0 + warp; row < r1; row += kNormWarps) {
+    const float r = rstd[row];
+    float xv[NCH][8], gv[NCH][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      load_vec<T, 8>(x + row * d + c * 256 + lane * 8, xv[c]);
+      load_vec<TO, 8>(dy + row * d + c * 256 + lane * 8, gv[c]);
+      float wv[8];
+      load_vec<float, 8>(w + c * 256 + lane * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = xv[c][j] * r;
+        acc[c][j] = fmaf(gv[c][j], xh, acc[c][j]);
+        const float wg = wv[j] * gv[c][j];
+        dot = fmaf(wg, xh, dot);
+        xv[c][j] = xh;
+        gv[c][j] = wg;
+      }
+    }
+    dot = warp_sum(dot) / static_cast<float>(d);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = r * (gv[c][j] - xv[c][j] * dot);
+      store_vec<T, 8>(dx + row * d + c * 256 + lane * 8, o);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = acc[c][j];
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < kNormWarps; ++wi) s += red[wi][threadIdx.x];
+    partial[static_cast<int64_t>(blockIdx.x) * d + c * 256 + threadIdx.x] = s;
+    __syncthreads();
+  }
+}
+
+template <typename T, typename TO>
+__global__ void __launch_bounds__(kNormWarps * 32)
+rmsnorm_bwd_generic(const TO* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
+                    const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ partial,
+                    int64_t rows, int d, int rows_per_block) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  int64_t r1 = r0 + rows_per_block;
+  if (r1 > rows) r1 = rows;
+  for (int64_t row = r0 + warp; row < r1; row += kNormWarps) {
+    const float r = rstd[row];
+    float dot = 0.f;
+    for (int i = lane; i < d; i += 32)
+      dot = fmaf(w[i] * to_f<TO>(dy[row * d + i]), to_f<T>(x[row * d + i]) * r, dot);
+    dot = warp_sum(dot) / static_cast<float>(d);
+    for (int i = lane; i < d; i += 32) {
+      const float xh = to_f<T>(x[row * d + i]) * r;
+      dx[row * d + i] = from_f<T>(r * (w[i] * to_f<TO>(dy[row * d + i]) - xh * dot));
+    }
+  }
+  // Column partials: thread-per-column loop over the CTA's rows (fixed order).
+  for (int col = threadIdx.x; col < d; col += blockDim.x) {
+    float s = 0.f;
+    for (int64_t row = r0; row < r1; ++row)
+      s = fmaf(to_f<TO>(dy[row * d + col]), to_f<T>(x[row * d + col]) * rstd[row], s);
+    partial[static_cast<int64_t>(blockIdx.x) * d + col] = s;
+  }
+}
+
+__global__ void column_reduce_kernel(const float* __restrict__ partial, int blocks, int d,
+                                     float* __restrict__ out, int accumulate) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= d) return;
+  float s = 0.f;
+  for (int b = 0; b < blocks; ++b) s += partial[static_cast<int64_t>(b) * d + col];
+  out[col] = accumulate ? out[col] + s : s;
+}
+
+// ---------------------------------------------------------------------------
+// QKV split + RoPE.  qkv: [B*S, 3*H*hd] (row = token); outputs q, k, v as
+// [B, H, S, hd] contiguous.  Interleaved pairs (2j, 2j+1) rotate by
+// angle = pos * theta^(-2j/hd) using fp32 cos/sin tables [S, hd/2].
+template <typename T>
+__global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, T* __restrict__ q,
+                                    T* __restrict__ k, T* __restrict__ v, int B, int S, int H,
+                                    int hd) {
+  // One thread per 8 contiguous head-dim elements of one (b, h, s) for one of q/k/v.
+  const int vec = hd / 8;
+  const int64_t per_tensor = static_cast<int64_t>(B) * H * S * vec;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= 3 * per_tensor) return;
+  const int which = static_cast<int>(idx / per_tensor);
+  int64_t rem = idx % per_tensor;
+  const int jv = static_cast<int>(rem % vec);
+  rem /= vec;
+  const int s = static_cast<int>(rem % S);
+  rem /= S;
+  const int h = static_cast<int>(rem % H);
+  const int b = static_cast<int>(rem / H);
+  const int d = H * hd;
+  const int64_t src = ((static_cast<int64_t>(b) * S + s) * 3 + which) * d + h * hd + jv * 8;
+  const int64_t dst = ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8;
+  float val[8];
+  load_vec<T, 8>(qkv + src, val);
+  if (which < 2) {
+    const int half = hd / 2;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int j = jv * 4 + p;
+      const float c = cos_t[s * half + j];
+      const float sn = sin_t[s * half + j];
+      const float e = val[2 * p], o = val[2 * p + 1];
+      val[2 * p] = e * c - o * sn;
+      val[2 * p + 1] = e * sn + o * c;
+    }
+  }
+  T* out = which == 0 ? q : (which == 1 ? k : v);
+  store_vec<T, 8>(out + dst, val);
+}
+
+template <typename T>
+__global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ dk,
+                                    const T* __restrict__ dv, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, T* __restrict__ dqkv, int B,
+                                    int S, int H, int hd) {
+  const int vec = hd / 8;
+  const int64_t per_tensor = static_cast<int64_t>(B) * H * S * vec;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= 3 * per_tensor) return;
+  const int which = static_cast<int>(idx / per_tensor);
+  int64_t rem = idx % per_tensor;
+  const int jv = static_cast<int>(rem % vec);
+  rem /= vec;
+  const int s = static_cast<int>(rem % S);
+  rem /= S;
+  const int h = static_cast<int>(rem % H);
+  const int b = static_cast<int>(rem / H);
+  const int d = H * hd;
+  const int64_t dst = ((static_cast<int64_t>(b) * S + s) * 3 + which) * d + h * hd + jv * 8;
+  const int64_t src = ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8;
+  const T* in = which == 0 ? dq : (which == 1 ? dk : dv);
+  float val[8];
+  load_vec<T, 8>(in + src, val);
+  if (which < 2) {
+    const int half = hd / 2;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int j = jv * 4 + p;
+      const float c = cos_t[s * half + j];
+      const float sn = sin_t[s * half + j];
+      const float ge = val[2 * p], go = val[2 * p + 1];
+      val[2 * p] = ge * c + go * sn;
+      val[2 * p + 1] = -ge * sn + go * c;
+    }
+  }
+  store_vec<T, 8>(dqkv + dst, val);
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy with in-place gradient.  One CTA per row; the row is staged
+// in shared memory (V <= kCeMaxSmemElems) so logits are read from HBM once
+// and the gradient written once.  loss_row[r] = lse - x[target]; logits are
+// overwritten by (softmax - onehot) * grad_scale.  Rows whose target equals
+// ignore_index get loss 0 and gradient 0.
+constexpr int kCeThreads = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads)
+ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
+                  float* __restrict__ loss_row, int64_t rows, int V, float grad_scale,
+                  int64_t ignore_index, int use_smem) {
+  extern __shared__ float srow[];
+  __shared__ float red[kCeThreads / 32];
+  __shared__ float bcast;
+  const int64_t row = blockIdx.x;
+  if (row >= rows) return;
+  T* lr = logits + row * V;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t tgt = target[row];
+  // pass 1: max
+  float m = -INFINITY;
+  const bool vec_ok = (V % 8 == 0) && (reinterpret_cast<uintptr_t>(lr) % 16 == 0);
+  if (vec_ok) {
+    for (int i = tid * 8; i < V; i += kCeThreads * 8) {
+      float v8[8];
+      load_vec<T, 8>(lr + i, v8);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (use_smem) srow[i + j] = v8[j];
+        m = fmaxf(m, v8[j]);
+      }
+    }
+  } else {
+    for (int i = tid; i < V; i += kCeThreads) {
+      const float v = to_f<T>(lr[i]);
+      if (use_smem) srow[i] = v;
+      m = fmaxf(m, v);
+    }
+  }
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < kCeThreads / 32 ? red[lane] : -INFINITY;
+    t = warp_max(t);
+    if (lane == 0) bcast = t;
+  }
+  __syncthreads();
+  m = bcast;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = tid; i < V; i += kCeThreads) {
+    const float v = use_smem ? srow[i] : to_f<T>(lr[i]);
+    s += __expf(v - m);
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < kCeThreads / 32 ? red[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) bcast = t;
+  }
+  __syncthreads();
+  const float lse = m + __logf(bcast);
+  const bool ignored = (tgt == ignore_index) || tgt < 0 || tgt >= V;
+  if (tid == 0) {
+    const float xt = ignored ? 0.f : (use_smem ? srow[tgt] : to_f<T>(lr[tgt]));
+    loss_row[row] = ignored ? 0.f : (lse - xt);
+  }
+  __syncthreads();
+  const float scale = ignored ? 0.f : grad_scale;
+  if (vec_ok) {
+    for (int i = tid * 8; i < V; i += kCeThreads * 8) {
+      float v8[8];
+      if (use_smem) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v8[j] = srow[i + j];
+      } else {
+        load_vec<T, 8>(lr + i, v8);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float p = __expf(v8[j] - lse);
+        if (i + j == tgt) p -= 1.0f;
+        v8[j] = p * scale;
+      }
+      store_vec<T, 8>(lr + i, v8);
+    }
+  } else {
+    for (int i = tid; i < V; i += kCeThreads) {
+      const float v = use_smem ? srow[i] : to_f<T>(lr[i]);
+      float p = __expf(v - lse);
+      if (i == tgt) p -= 1.0f;
+      lr[i] = from_f<T>(p * scale);
+    }
+  }
+}
+
+}  // namespace nn
+
+// ---------------------------------------------------------------------------
+// Host launchers.
+
+int rmsnorm_forward(const void* x, const float* w, void* y, float* rstd, int64_t rows, int d,
+                    float eps, int dtype, int out_dtype, cudaStream_t stream) {
+  using namespace nn;
+  if (rows <= 0) return 0;
+  const int blocks = ceil_div_i(rows, kNormWarps);
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  auto go = [&](auto tv, auto tov) {
+    using T = decltype(tv);
+    using TO = decltype(tov);
+    const T* xp = static_cast<const T*>(x);
+    TO* yp = static_cast<TO*>(y);
+    if (aligned && d % 256 == 0 && d / 256 <= 8) {
+      switch (d / 256) {
+        case 1: rmsnorm_fwd_fast<T, TO, 1><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, eps); return;
+        case 2: rmsnorm_fwd_fast<T, TO, 2><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, eps); return;
+        case 3: rmsnorm_fwd_fast<T, TO, 3><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, eps); return;
+        case 4: rmsnorm_fwd_fast<T, TO, 4><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, eps); return;
+        case 6: rmsnorm_fwd_fast<T, TO, 6><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, eps); return;
+        case 8: rmsnorm_fwd_fast<T, TO, 8><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, eps); return;
+        default: break;
+      }
+    }
+    rmsnorm_fwd_generic<T, TO><<<blocks, kNormWarps * 32, 0, stream>>>(xp, w, yp, rstd, rows, d, eps);
+  };
+  if (dtype == 0 && out_dtype == 0) go(float{}, float{});
+  else if (dtype == 1 && out_dtype == 1) go(__nv_bfloat16{}, __nv_bfloat16{});
+  else if (dtype == 0 && out_dtype == 1) go(float{}, __nv_bfloat16{});
+  else return -2;
+  return static_cast<int>(cudaGetLastError());
+}
+
+void rmsnorm_backward_plan(int64_t rows, int& blocks, int& rows_per_block) {
+  int64_t b = 148 * 4;
+  const int64_t maxb = (rows + nn::kNormWarps - 1) / nn::kNormWarps;
+  if (b > maxb) b = maxb;
+  if (b < 1) b = 1;
+  rows_per_block = static_cast<int>((rows + b - 1) / b);
+  blocks = static_cast<int>((rows + rows_per_block - 1) / rows_per_block);
+}
+
+int rmsnorm_backward_partial_size(int64_t rows, int d) {
+  int blocks, rpb;
+  rmsnorm_backward_plan(rows, blocks, rpb);
+  return blocks * d;
+}
+
+int rmsnorm_backward(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                     float* dw, float* partial, int64_t rows, int d, int dtype, int out_dtype,
+                     int accumulate_dw, cudaStream_t stream) {
+  using namespace nn;
+  int blocks = 0, rpb = 1;
+  if (rows > 0) {
+    rmsnorm_backward_plan(rows, blocks, rpb);
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(dy) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(dx) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+    auto go = [&](auto tv, auto tov) {
+      using T = decltype(tv);
+      using TO = decltype(tov);
+      const TO* dyp = static_cast<const TO*>(dy);
+      const T* xp = static_cast<const T*>(x);
+      T* dxp = static_cast<T*>(dx);
+      if (aligned && d % 256 == 0 && d / 256 <= 4) {
+        switch (d / 256) {
+          case 1: rmsnorm_bwd_fast<T, TO, 1><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, xp, w, rstd, dxp, partial, rows, rpb); return;
+          case 2: rmsnorm_bwd_fast<T, TO, 2><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, xp, w, rstd, dxp, partial, rows, rpb); return;
+          case 3: rmsnorm_bwd_fast<T, TO, 3><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, xp, w, rstd, dxp, partial, rows, rpb); return;
+          case 4: rmsnorm_bwd_fast<T, TO, 4><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, xp, w, rstd, dxp, partial, rows, rpb); return;
+          default: break;
+        }
+      }
+      rmsnorm_bwd_generic<T, TO><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, xp, w, rstd, dxp, partial, rows, d, rpb);
+    };
+    if (dtype == 0 && out_dtype == 0) go(float{}, float{});
+    else if (dtype == 1 && out_dtype == 1) go(__nv_bfloat16{}, __nv_bfloat16{});
+    else if (dtype == 0 && out_dtype == 1) go(float{}, __nv_bfloat16{});
+    else return -2;
+  }
+  column_reduce_kernel<<<ceil_div_i(d, 256), 256, 0, stream>>>(partial, blocks, d, dw, accumulate_dw);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int rope_qkv_forward(const void* qkv, const float* cos_t, const float* sin_t, void* q, void* k,
+                     void* v, int B, int S, int H, int hd, int dtype, cudaStream_t stream) {
+  if (hd % 8) return -1;
+  const int64_t total = 3LL * B * H * S * (hd / 8);
+  if (total == 0) return 0;
+  const int blocks = ceil_div_i(total, 256);
+  if (dtype == 0)
+    nn::rope_qkv_fwd_kernel<float><<<blocks, 256, 0, stream>>>(
+        static_cast<const float*>(qkv), cos_t, sin_t, static_cast<float*>(q), static_cast<float*>(k),
+        static_cast<float*>(v), B, S, H, hd);
+  else if (dtype == 1)
+    nn::rope_qkv_fwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(qkv), cos_t, sin_t, static_cast<__nv_bfloat16*>(q),
+        static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), B, S, H, hd);
+  else return -2;
+  return static_cast<int>(cudaGetLastError());
+}
+
+int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const float* cos_t,
+                      const float* sin_t, void* dqkv, int B, int S, int H, int hd, int dtype,
+                      cudaStream_t stream) {
+  if (hd % 8) return -1;
+  const int64_t total = 3LL * B * H * S * (hd / 8);
+  if (total == 0) return 0;
+  const int blocks = ceil_div_i(total, 256);
+  if (dtype == 0)
+    nn::rope_qkv_bwd_kernel<float><<<blocks, 256, 0, stream>>>(
+        static_cast<const float*>(dq), static_cast<const float*>(dk), static_cast<const float*>(dv),
+        cos_t, sin_t, static_cast<float*>(dqkv), B, S, H, hd);
+  else if (dtype == 1)
+    nn::rope_qkv_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(dq), static_cast<const __nv_bfloat16*>(dk),
+        static_cast<const __nv_bfloat16*>(dv), cos_t, sin_t, static_cast<__nv_bfloat16*>(dqkv), B, S,
+        H, hd);
+  else return -2;
+  return static_cast<int>(cudaGetLastError());
+}
+
+constexpr int kCeMaxSmemElems = 200 * 1024 / 4;
+
+int cross_entropy_fwd_bwd(void* logits, const int64_t* target, float* loss_row, int64_t rows,
+                          int V, float grad_scale, int64_t ignore_index, int dtype,
+                          cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  const int use_smem = V <= kCeMaxSmemElems ? 1 : 0;
+  const size_t smem = use_smem ? static_cast<size_t>(V) * sizeof(float) : 0;
+  auto go = [&](auto tv) {
+    using T = decltype(tv);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(nn::ce_fwd_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+    nn::ce_fwd_bwd_kernel<T><<<static_cast<unsigned>(rows), nn::kCeThreads, smem, stream>>>(
+        static_cast<T*>(logits), target, loss_row, rows, V, grad_scale, ignore_index, use_smem);
+  };
+  if (dtype == 0) go(float{});
+  else if (dtype == 1) go(__nv_bfloat16{});
+  else return -2;
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace ro

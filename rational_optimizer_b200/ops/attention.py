@@ -1,0 +1,102 @@
+"""Causal self-attention core with interleaved-pair RoPE.
+
+``qkv`` is the fused projection output ``[B*S, 3*d]`` (q | k | v, heads
+contiguous), as produced by ``CausalSelfAttention.qkv`` of the reference
+(training/train.py:48-73).  CUDA: one kernel splits q/k/v into [B,H,S,hd],
+applies RoPE to q and k (fp32 tables), and its backward applies the inverse
+rotation and re-packs into ``[B*S, 3d]``.  The attention itself runs the
+sm_100a flash-attention kernel when available for the shape
+(``csrc/attention_sm100.cu``), otherwise SDPA.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from .. import _ext
+
+
+def precompute_rope(seq_len, head_dim, theta=10000.0):
+    """fp32 cos/sin tables [1,1,S,hd/2] (same formula as the reference)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    positions = torch.arange(seq_len, dtype=torch.float32)
+    freqs = torch.outer(positions, inv_freq)
+    return freqs.cos()[None, None, :, :], freqs.sin()[None, None, :, :]
+
+
+def apply_rope(x, cos, sin):
+    x_even = x[..., 0::2]
+    x_odd = x[..., 1::2]
+    rotated = torch.stack((x_even * cos - x_odd * sin, x_even * sin + x_odd * cos), dim=-1)
+    return rotated.flatten(-2)
+
+
+class _RopeQKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cos2d, sin2d, B, S, H, hd):
+        q, k, v = _ext.ext().rope_qkv_forward(qkv.contiguous(), cos2d, sin2d, B, S, H, hd)
+        ctx.save_for_backward(cos2d, sin2d)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        cos2d, sin2d = ctx.saved_tensors
+        dqkv = _ext.ext().rope_qkv_backward(dq.contiguous(), dk.contiguous(), dv.contiguous(),
+                                            cos2d, sin2d)
+        return dqkv, None, None, None, None, None, None
+
+
+def _flash():
+    if not _ext.available():
+        return None
+    C = _ext.ext()
+    return C if hasattr(C, "flash_attn_fwd") else None
+
+
+class _FlashAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, scale):
+        C = _ext.ext()
+        o, lse = C.flash_attn_fwd(q, k, v, float(scale), True)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.scale = float(scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = _ext.ext().flash_attn_bwd(do.contiguous(), q, k, v, o, lse, ctx.scale, True)
+        return dq, dk, dv, None
+
+
+def causal_attention_core(q, k, v):
+    """softmax(q k^T / sqrt(hd) + causal mask) v for [B, H, S, hd] tensors."""
+    scale = 1.0 / math.sqrt(q.shape[-1])
+    C = _flash()
+    if C is not None and q.is_cuda and q.dtype == torch.bfloat16 and C.flash_attn_supported(q):
+        return _FlashAttention.apply(q, k, v, scale)
+    return F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+
+def causal_self_attention(qkv, batch, seq_len, heads, head_dim, rope_cos, rope_sin):
+    """Return the attention output ``[B, S, H*hd]`` before the output projection."""
+    d = heads * head_dim
+    if qkv.is_cuda:
+        cos2d = rope_cos.reshape(rope_cos.shape[-2], rope_cos.shape[-1]).float().contiguous()
+        sin2d = rope_sin.reshape(rope_sin.shape[-2], rope_sin.shape[-1]).float().contiguous()
+        q, k, v = _RopeQKV.apply(qkv.reshape(batch * seq_len, 3 * d), cos2d, sin2d, batch,
+                                 seq_len, heads, head_dim)
+        y = causal_attention_core(q, k, v)
+        return y.transpose(1, 2).reshape(batch, seq_len, d)
+    q, k, v = qkv.reshape(batch, seq_len, 3 * d).chunk(3, dim=-1)
+    q = q.reshape(batch, seq_len, heads, head_dim).transpose(1, 2)
+    k = k.reshape(batch, seq_len, heads, head_dim).transpose(1, 2)
+    v = v.reshape(batch, seq_len, heads, head_dim).transpose(1, 2)
+    cos = rope_cos[:, :, :seq_len, :].to(dtype=q.dtype)
+    sin = rope_sin[:, :, :seq_len, :].to(dtype=q.dtype)
+    q = apply_rope(q, cos, sin)
+    k = apply_rope(k, cos, sin)
+    y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    return y.transpose(1, 2).reshape(batch, seq_len, d)

@@ -1,0 +1,66 @@
+"""GEMM entry points used by the model and the optimizers.
+
+``matmul_nt(a, b)`` = a @ b^T, ``matmul_nn(a, b)`` = a @ b,
+``matmul_tn(a, b)`` = a^T @ b, and the batched ``bmm``/``baddbmm`` forms used
+by Newton-Schulz.  Shapes the tcgen05 kernel (``csrc/gemm_sm100.cu``)
+supports are routed to it; anything else uses cuBLAS through PyTorch.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .. import _ext
+
+_NATIVE = os.environ.get("RO_NATIVE_GEMM", "1") != "0"
+
+
+def _native():
+    if not _NATIVE or not _ext.available():
+        return None
+    C = _ext.ext()
+    return C if hasattr(C, "gemm_bf16") else None
+
+
+def _native_ok(a: torch.Tensor, b: torch.Tensor) -> bool:
+    return (a.is_cuda and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16)
+
+
+def matmul_nt(a: torch.Tensor, b: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """a [M, K] @ b[N, K]^T -> [M, N]."""
+    C = _native()
+    if C is not None and _native_ok(a, b):
+        out = C.gemm_bf16(a, b, False, True, out_dtype is torch.float32)
+        if out is not None:
+            return out
+    if out_dtype is not None and out_dtype != a.dtype and a.is_cuda:
+        return torch.mm(a, b.t(), out_dtype=out_dtype)
+    out = a @ b.t()
+    return out if out_dtype is None else out.to(out_dtype)
+
+
+def matmul_nn(a: torch.Tensor, b: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """a [M, K] @ b [K, N] -> [M, N]."""
+    C = _native()
+    if C is not None and _native_ok(a, b):
+        out = C.gemm_bf16(a, b, False, False, out_dtype is torch.float32)
+        if out is not None:
+            return out
+    if out_dtype is not None and out_dtype != a.dtype and a.is_cuda:
+        return torch.mm(a, b, out_dtype=out_dtype)
+    out = a @ b
+    return out if out_dtype is None else out.to(out_dtype)
+
+
+def matmul_tn(a: torch.Tensor, b: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """a [K, M]^T @ b [K, N] -> [M, N] (weight gradients: dy^T x)."""
+    C = _native()
+    if C is not None and _native_ok(a, b):
+        out = C.gemm_bf16(a, b, True, False, out_dtype is torch.float32)
+        if out is not None:
+            return out
+    if out_dtype is not None and out_dtype != a.dtype and a.is_cuda:
+        return torch.mm(a.t(), b, out_dtype=out_dtype)
+    out = a.t() @ b
+    return out if out_dtype is None else out.to(out_dtype)

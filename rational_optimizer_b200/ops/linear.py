@@ -1,0 +1,87 @@
+"""Bias-free linear layer in the compute dtype with fp32 master weights.
+
+``y = x @ W^T`` runs in bf16 on CUDA (fp32 accumulation); the weight gradient
+is produced directly in fp32 (``dW = dy^T x``) so fp32 master parameters need
+no extra cast pass.  The bf16 copy of each weight is cached and refreshed
+only when the parameter's version counter changes (i.e. after an optimizer
+step), so each weight is cast once per step, not once per micro-batch.
+On CPU the layer computes in fp32 (reference path for tests).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import gemm
+
+
+class _WeightCache:
+    __slots__ = ("version", "tensor", "data_ptr")
+
+    def __init__(self):
+        self.version = -1
+        self.tensor = None
+        self.data_ptr = 0
+
+
+def cached_cast(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -> torch.Tensor:
+    if weight.dtype == dtype:
+        return weight.detach()
+    version = weight._version
+    if (cache.tensor is None or cache.version != version or cache.data_ptr != weight.data_ptr()
+            or cache.tensor.dtype != dtype):
+        cache.tensor = weight.detach().to(dtype)
+        cache.version = version
+        cache.data_ptr = weight.data_ptr()
+    return cache.tensor
+
+
+class _LinearFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, w_compute):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != w_compute.dtype:
+            x2 = x2.to(w_compute.dtype)
+        y = gemm.matmul_nt(x2, w_compute)
+        ctx.save_for_backward(x2, w_compute)
+        ctx.in_shape = x.shape
+        ctx.x_dtype = x.dtype
+        ctx.w_dtype = weight.dtype
+        return y.reshape(*x.shape[:-1], w_compute.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, w = ctx.saved_tensors
+        g2 = gy.reshape(-1, gy.shape[-1])
+        if g2.dtype != w.dtype:
+            g2 = g2.to(w.dtype)
+        gx = gw = None
+        if ctx.needs_input_grad[0]:
+            gx = gemm.matmul_nn(g2, w).reshape(ctx.in_shape)
+            if gx.dtype != ctx.x_dtype:
+                gx = gx.to(ctx.x_dtype)
+        if ctx.needs_input_grad[1]:
+            gw = gemm.matmul_tn(g2, x2, out_dtype=ctx.w_dtype)
+        return gx, gw, None
+
+
+class Linear(torch.nn.Linear):
+    """``nn.Linear`` (no bias) whose CUDA forward runs in ``compute_dtype``.
+
+    The parameter is the usual ``weight`` so state-dict keys match the
+    reference model (training/train.py:48-162).
+    """
+
+    def __init__(self, in_features, out_features, bias=False, device=None, dtype=None):
+        if bias:
+            raise ValueError("the reference architecture uses bias-free linear layers")
+        super().__init__(in_features, out_features, bias=False, device=device, dtype=dtype)
+        self._cache = _WeightCache()
+        self.compute_dtype = torch.bfloat16
+
+    def forward(self, x):
+        if not x.is_cuda or self.compute_dtype == self.weight.dtype:
+            if x.dtype != self.weight.dtype:
+                x = x.to(self.weight.dtype)
+            return torch.nn.functional.linear(x, self.weight)
+        w = cached_cast(self.weight, self.compute_dtype, self._cache)
+        return _LinearFunction.apply(x, self.weight, w)

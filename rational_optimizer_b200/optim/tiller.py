@@ -1,0 +1,847 @@
+"""TILLER: Tangents Informed by a Loss Ledger for Equal-budget Reweighting.
+
+Public API of optimizer_design/tiller.py (``TILLERRouter``,
+``TILLERAttentionOptimizer``, ``configure_microbatch_count``,
+``tiller_scaling_formula``, ``FAMILY_ID``, ``PREFIX``).  The reference builds
+the live algorithm from a 20-class lineage with runtime patching
+(optimizer_design/_tiller/core.py:3362-3392, 4120-4150, 4310-4317,
+4481-4537); here it is written out once:
+
+Router (GRAIN in_proj / out_proj matrices), every step::
+
+    m      = Nesterov(grad)                         (mu = 0.95, per matrix)
+    p      = NS5 per GRAIN group block, rescaled    (rational_group_zero_power)
+    q      = factorized adaptive-tangent chord(p, m, g; participation, congruence)
+    exact  = <g, adj*q>,  momentum = <m, adj*q>,  weight = ||adj*q||^2 per (layer, group)
+    c      = biatlas transaction(ledger rows, exact, momentum, weight)
+    W     <- (1 - lr wd) W - lr adj c q
+
+On refresh steps (transitions 0, 8, 16, ... = optimizer steps 1, 9, 17, ...)
+the probe packets captured by the module hooks give the response sensor
+(participation/congruence, all-reduced), 32 functional loss rows (gathered),
+and the ledger is advanced with them; on the other 7 steps the cached route
+is reused and the ledger advances with the trace-matched gradient surrogate.
+The attention optimizer consumes the router's layer participation and
+congruence and applies the same chord to head-group NS5 directions.
+
+State keys, state placement (everything on ``state[in_weight of layer 0]``
+except the per-matrix ``momentum_buffer``), parameter-group contents and
+parameter order are those of the reference so ``state_dict`` round-trips.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from . import tiller_math as tm
+from .newton_schulz import (attention_head_group_zero_power, match_rms_adamw_adjustment,
+                            rational_group_zero_power)
+
+FAMILY_ID = "tiller_v1"
+PREFIX = "tiller_"
+MATCHED_BETA2 = tm.MATCHED_BETA2
+
+# Number of gradient-accumulation micro-batches whose probe rows are captured
+# per optimizer step (configure_microbatch_count).
+_EXPECTED_MICROBATCHES = 4
+
+# Parameter-group contents written by the reference lineage (they appear in
+# checkpoints, so they are reproduced verbatim).
+_ROUTER_GROUP_KEYS = {
+    "ten_probe_family_id": "loss_weighted_four_role_sign_transport_muon_v1",
+    "muon_momentum": 0.95,
+    "muon_ns_steps": 5,
+    "muon_adjust_lr_fn": "match_rms_adamw",
+    "fixed32_transaction_family_id": "loss_weighted_four_role_sign_transport_muon_v1",
+    "response_fisher_family_id": "loss_weighted_four_role_sign_transport_muon_v1",
+    "residual_fisher_attention_family_id": "loss_weighted_four_role_sign_transport_muon_v1",
+    "loss_weighted_intrinsic_sign_attention_family_id": "loss_weighted_four_role_sign_transport_muon_v1",
+    "loss_weighted_four_role_sign_transport_family_id": "loss_weighted_four_role_response_homotopy_muon_v1",
+    "loss_weighted_four_role_response_homotopy_family_id": "loss_weighted_four_role_response_homotopy_muon_v1",
+    "loss_weighted_four_role_response_homotopy_batched_family_id": "loss_weighted_four_role_response_homotopy_batched_muon_v2",
+    "loss_weighted_four_role_response_homotopy_compact_family_id": "loss_weighted_four_role_response_homotopy_compact_muon_v3",
+    "global_response_transaction_family_id": "global_response_transaction_muon_v1",
+    "lagged_predictive_response_transaction_family_id": "lagged_predictive_response_transaction_muon_v1",
+    "temporal_response_group_polar_family_id": "temporal_response_group_polar_muon_v1",
+    "posterior_rank64_response_group_polar_family_id": "posterior_rank64_response_group_polar_muon_v1",
+    "tiller_family_id": FAMILY_ID,
+    "tiller_refresh_interval": tm.REFRESH_INTERVAL,
+}
+_ATTENTION_GROUP_KEYS = {
+    "residual_fisher_attention_family_id": "residual_fisher_attention_muon_v1",
+    "loss_weighted_intrinsic_sign_attention_family_id": "loss_weighted_intrinsic_sign_attention_muon_v1",
+    "loss_weighted_four_role_sign_transport_family_id": "loss_weighted_four_role_sign_transport_muon_v1",
+    "loss_weighted_four_role_response_homotopy_family_id": "loss_weighted_four_role_response_homotopy_muon_v1",
+    "loss_weighted_four_role_response_homotopy_batched_family_id": "loss_weighted_four_role_response_homotopy_batched_muon_v2",
+    "loss_weighted_four_role_response_homotopy_compact_family_id": "loss_weighted_four_role_response_homotopy_compact_muon_v3",
+    "global_response_transaction_family_id": "global_response_transaction_muon_v1",
+    "lagged_predictive_response_transaction_family_id": "lagged_predictive_response_transaction_muon_v1",
+    "temporal_response_group_polar_family_id": "temporal_response_group_polar_muon_v1",
+    "posterior_rank64_response_group_polar_family_id": "posterior_rank64_response_group_polar_muon_v1",
+    "tiller_family_id": FAMILY_ID,
+}
+_ROUTE_NAMES = ("group_participation", "group_congruence", "intrinsic_participation",
+                "attention_congruence")
+
+
+def configure_microbatch_count(count: int) -> None:
+    """Set the gradient-accumulation micro-batch count before building a router."""
+    global _EXPECTED_MICROBATCHES
+    if isinstance(count, bool) or not isinstance(count, int) or count < 1:
+        raise ValueError("TILLER microbatch count must be a positive integer")
+    _EXPECTED_MICROBATCHES = count
+
+
+def microbatch_count() -> int:
+    return _EXPECTED_MICROBATCHES
+
+
+def tiller_scaling_formula(**kwargs):
+    return tm.tiller_scaling_formula(**kwargs)
+
+
+def _dist_shape(group):
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group=group), dist.get_world_size(group=group)
+    return 0, 1
+
+
+def foreach_nesterov(optimizer, parameters, momentum):
+    """``buf.lerp_(g, 1-mu)``; return stacked fp32 ``g.lerp(buf, mu)``."""
+    grads, bufs = [], []
+    for p in parameters:
+        if p.grad is None:
+            raise RuntimeError("TILLER parameter lacks gradient")
+        grads.append(p.grad)
+        st = optimizer.state[p]
+        buf = st.get("momentum_buffer")
+        if buf is None:
+            buf = torch.zeros_like(p.grad, memory_format=torch.preserve_format)
+            st["momentum_buffer"] = buf
+        bufs.append(buf)
+    torch._foreach_lerp_(bufs, grads, 1.0 - momentum)
+    return torch.stack(torch._foreach_lerp(grads, bufs, momentum)).float()
+
+
+def foreach_apply(parameters, direction, *, decay, alpha):
+    torch._foreach_mul_(parameters, float(decay))
+    torch._foreach_add_(parameters, list(direction.to(parameters[0].dtype).unbind(0)),
+                        alpha=float(alpha))
+
+
+class TILLERRouter(torch.optim.Optimizer):
+    """TILLER on the GRAIN ``in_proj``/``out_proj`` matrices of every layer.
+
+    ``pairs`` is a sequence of dicts with keys ``mlp``, ``module`` (the GRAIN
+    activation), ``in_weight``, ``out_weight``, ``numerator``,
+    ``denominator``, ``groups``, ``hidden_dim`` and ``eps`` (the inventory of
+    ``collect_rlb_optimizer_groups``, training/train.py:1614-1659).
+    """
+
+    family_id = FAMILY_ID
+    telemetry_prefix = PREFIX
+
+    def __init__(self, pairs, *, lr, weight_decay, momentum, ns_steps, beta2, eps,
+                 loss_probe_group=None, strict_validation=None):
+        self.pairs = list(pairs)
+        if not self.pairs:
+            raise ValueError("TILLER requires GRAIN layers")
+        self.momentum = float(momentum)
+        self.ns_steps = int(ns_steps)
+        if self.momentum != 0.95 or self.ns_steps != 5:
+            raise ValueError("TILLER requires matched momentum .95 and NS5")
+        if float(beta2) != MATCHED_BETA2:
+            raise ValueError("TILLER requires locked beta2=.95")
+        if float(eps) != tm.LOCKED_EPS:
+            raise ValueError("TILLER requires eps=1e-8")
+        self.predictive_beta2 = float(beta2)
+        self.loss_probe_group = loss_probe_group
+        rank, world = _dist_shape(loss_probe_group)
+        self.world_size = world
+        self.microbatches = _EXPECTED_MICROBATCHES
+        self.probe_layout = tm.fixed_global_probe_layout(tm.GLOBAL_PROBE_COUNT, rank, world)
+        self.capture_rows = (self.probe_layout.local_probe_count + self.microbatches - 1) // self.microbatches
+        first = self.pairs[0]
+        self.groups = int(first["groups"])
+        self.hidden = int(first["hidden_dim"])
+        self.external = int(first["in_weight"].shape[1])
+        self.grain_eps = float(first["eps"])
+        if self.hidden % self.groups:
+            raise ValueError("TILLER hidden width is not group divisible")
+        self.width = self.hidden // self.groups
+        self.strict = (strict_validation if strict_validation is not None
+                       else not first["in_weight"].is_cuda)
+        params, seen = [], set()
+        for layer, pair in enumerate(self.pairs):
+            inc, out = pair["in_weight"], pair["out_weight"]
+            if (int(pair["groups"]) != self.groups or int(pair["hidden_dim"]) != self.hidden
+                    or float(pair["eps"]) != self.grain_eps
+                    or inc.shape != (self.hidden, self.external)
+                    or out.shape != (self.external, self.hidden)
+                    or pair["numerator"].shape != (self.groups, 6)
+                    or pair["denominator"].shape != (self.groups, 4)):
+                raise ValueError("TILLER GRAIN inventory changed")
+            for p in (inc, out):
+                if id(p) in seen:
+                    raise ValueError("TILLER matrix ownership overlaps")
+                seen.add(id(p))
+                params.append(p)
+        defaults = {"lr": float(lr), "weight_decay": float(weight_decay), "lr_scale": 1.0}
+        defaults.update(_ROUTER_GROUP_KEYS)
+        super().__init__([{"params": params}], defaults)
+        # probe capture buffers
+        self._pending_inputs = [None for _ in self.pairs]
+        self._functional_records = [[] for _ in self.pairs]
+        self._cotangent_records = [[] for _ in self.pairs]
+        self._hook_handles = []
+        for layer, pair in enumerate(self.pairs):
+            self._hook_handles.extend((
+                pair["mlp"].register_forward_pre_hook(self._make_input_hook(layer)),
+                pair["module"].register_forward_hook(self._make_feature_hook(layer)),
+                pair["mlp"].register_forward_hook(self._make_cotangent_hook(layer)),
+            ))
+        anchor = self.state[self.pairs[0]["in_weight"]]
+        anchor.setdefault("four_role_response_frozen_numerators",
+                          torch.stack([p["numerator"].detach().float().clone() for p in self.pairs]))
+        anchor.setdefault("four_role_response_frozen_denominators",
+                          torch.stack([p["denominator"].detach().float().clone() for p in self.pairs]))
+        self._clip_factor = None
+        self._capture_telemetry_next_step = False
+        self._last_telemetry = {}
+        # cadence
+        self._cadence_transition = 0
+        self._capture_response_this_transition = True
+        self._cached_route = None
+        self._cached_selection_scores = None
+        self._cached_selection_decay = None
+        # attention hand-off
+        self._attention_update = 0
+        self._attention_consumed = True
+        self._group_participation = None
+        self._group_response_congruence = None
+        self._intrinsic_participation = None
+        self._attention_response_congruence = None
+        # ledger scratch
+        self._rfd_rows = None
+        self._rfd_decay_derivative = None
+        self._rfd_gradient_scale = None
+        self._rfd_functional_refresh = False
+        self._rfd_selection = None
+        self._last_predictive = None
+
+    # -- properties --------------------------------------------------------
+    @property
+    def anchor(self):
+        return self.state[self.pairs[0]["in_weight"]]
+
+    # -- probe hooks -------------------------------------------------------
+    def _sample_indices(self, rows, device):
+        return tm.evenly_spaced_indices(int(rows), self.capture_rows, device=device)
+
+    def _make_input_hook(self, layer):
+        @torch.no_grad()
+        def capture(module, inputs):
+            if not self._capture_response_this_transition or not module.training:
+                return None
+            if len(inputs) != 1 or not torch.is_tensor(inputs[0]):
+                raise RuntimeError("TILLER MLP input hook changed")
+            if self._pending_inputs[layer] is not None:
+                raise RuntimeError("TILLER probe input remained pending")
+            flat = inputs[0].detach().reshape(-1, self.external)
+            idx = self._sample_indices(flat.shape[0], flat.device)
+            self._pending_inputs[layer] = (int(flat.shape[0]), idx, flat.index_select(0, idx).clone())
+            return None
+        return capture
+
+    def _make_feature_hook(self, layer):
+        @torch.no_grad()
+        def capture(module, inputs, output):
+            if not self._capture_response_this_transition or not module.training:
+                return None
+            pending = self._pending_inputs[layer]
+            if pending is None:
+                raise RuntimeError("TILLER feature lacks aligned input")
+            rows, idx, sampled = pending
+            pre = inputs[0].detach().reshape(-1, self.hidden)
+            feat = output.detach().reshape(-1, self.hidden)
+            if pre.shape[0] != rows or feat.shape[0] != rows:
+                raise RuntimeError("TILLER x/z/h rows differ")
+            self._functional_records[layer].append(
+                (sampled, pre.index_select(0, idx).clone(), feat.index_select(0, idx).clone()))
+            self._pending_inputs[layer] = None
+            return None
+        return capture
+
+    def _make_cotangent_hook(self, layer):
+        def capture(module, _inputs, output):
+            if not self._capture_response_this_transition or not module.training:
+                return None
+            if not torch.is_tensor(output) or not output.requires_grad:
+                raise RuntimeError("TILLER MLP output hook changed")
+            flat = output.reshape(-1, self.external)
+            rows = int(flat.shape[0])
+            idx = self._sample_indices(rows, flat.device)
+
+            def capture_gradient(cotangent):
+                with torch.no_grad():
+                    value = cotangent.detach().reshape(-1, self.external)
+                    if value.shape[0] != rows:
+                        raise RuntimeError("TILLER output/cotangent rows differ")
+                    self._cotangent_records[layer].append((value.index_select(0, idx).clone(), rows))
+                return cotangent
+            output.register_hook(capture_gradient)
+            return None
+        return capture
+
+    def remove_hooks(self):
+        for h in self._hook_handles:
+            h.remove()
+        self._hook_handles = []
+        self._pending_inputs = [None for _ in self.pairs]
+        self._functional_records = [[] for _ in self.pairs]
+        self._cotangent_records = [[] for _ in self.pairs]
+        self._clip_factor = None
+
+    def _consume_probes(self):
+        packets = []
+        mb = self.microbatches
+        for layer in range(len(self.pairs)):
+            if self._pending_inputs[layer] is not None:
+                raise RuntimeError("TILLER probe input remained unmatched")
+            records = self._functional_records[layer]
+            cots = self._cotangent_records[layer]
+            self._functional_records[layer] = []
+            self._cotangent_records[layer] = []
+            if len(records) != mb or len(cots) != mb:
+                raise RuntimeError("TILLER microbatch inventory changed")
+            inputs = torch.cat([r[0] for r in records])
+            pre = torch.cat([r[1] for r in records])
+            feat = torch.cat([r[2] for r in records])
+            scaled = torch.cat([v.float() * float(rows * mb) for v, rows in cots]) * float(self._clip_factor)
+            captured = self.capture_rows * mb
+            if inputs.shape != (captured, self.external) or pre.shape != (captured, self.hidden):
+                raise RuntimeError("TILLER captured packet changed")
+            sel = tm.evenly_spaced_indices(captured, self.probe_layout.local_probe_count,
+                                           device=inputs.device)
+            packets.append((inputs.index_select(0, sel).float(), pre.index_select(0, sel).float(),
+                            feat.index_select(0, sel).float(), scaled.index_select(0, sel).float()))
+        return packets
+
+    # -- trainer contract --------------------------------------------------
+    def record_realized_clipping(self, preclip_norm, max_norm):
+        if self._clip_factor is not None:
+            raise RuntimeError("TILLER observed multiple clipping calls")
+        value = float(preclip_norm)
+        maximum = float(max_norm)
+        if not math.isfinite(value) or value < 0.0 or maximum != 1.0:
+            raise RuntimeError("TILLER received invalid clipping")
+        self._clip_factor = min(1.0, maximum / (value + 1e-6))
+
+    def set_telemetry_capture(self, enabled=True):
+        self._capture_telemetry_next_step = bool(enabled)
+
+    def telemetry(self):
+        return dict(self._last_telemetry)
+
+    def lr_wd_fairness_audit(self):
+        keys = ("global_lr_scale", "rlb_incoming_lr_scale", "rlb_outgoing_lr_scale",
+                "fixed32_loss_measure_lr_scale", "group_intrinsic_participation_lr_scale",
+                "loss_weighted_frozen_response_lr_scale", "postpolar_homotopy_lr_scale",
+                "batched_sensor_lr_scale", "foreach_realization_lr_scale",
+                "moment_exact_compact_lr_scale", "fixed32_global_loss_measure_lr_scale",
+                "signed_global_group_transaction_lr_scale", "row_space_equality_budget_lr_scale",
+                "matched_beta2_predictive_loss_image_lr_scale",
+                "preupdate_history_selection_lr_scale",
+                "rotation_invariant_temporal_response_sketch_lr_scale",
+                "rational_group_polar_lr_scale", "nominal_polar_rank_calibration_lr_scale",
+                "posterior_rank64_subspace_lr_scale", "truncated_svd_response_metric_lr_scale",
+                "elapsed_beta2_cadence8_response_metric_lr_scale",
+                "current_linear_transaction_every_step_lr_scale",
+                "cached_scalar_response_route_lr_scale", "current_window32_response_metric_lr_scale",
+                "no_temporal_covariance_smearing_lr_scale",
+                "matched_beta2_factorized_tangent_lr_scale", "response_energy_chord_lr_scale",
+                "signed_current_gradient_orientation_lr_scale", "exact_native_budget_lr_scale",
+                "compiled_static_fullgraph_execution_lr_scale",
+                "every_step_gradient_score_ledger_lr_scale",
+                "trace_matched_gradient_surrogate_lr_scale", "robust_fd_midpoint_tail_lr_scale",
+                "matrix_free_rfd_krylov_transaction_lr_scale",
+                "unchanged_compiled_factorized_direction_lr_scale",
+                "signed_rfd_coefficients_lr_scale", "weight_decay_scale")
+        return {k: 1.0 for k in keys}
+
+    def consume_response_homotopy(self):
+        if self._attention_consumed:
+            raise RuntimeError("TILLER response route was consumed twice")
+        if self._intrinsic_participation is None or self._attention_response_congruence is None:
+            raise RuntimeError("TILLER attention route is incomplete")
+        self._attention_consumed = True
+        return self._intrinsic_participation, self._attention_response_congruence, int(self._attention_update)
+
+    # -- sensor ------------------------------------------------------------
+    def _response_sensor(self, packets):
+        anchor = self.anchor
+        frozen_num = anchor.get("four_role_response_frozen_numerators")
+        frozen_den = anchor.get("four_role_response_frozen_denominators")
+        L = len(self.pairs)
+        if (frozen_num is None or frozen_num.shape != (L, self.groups, 6) or frozen_den is None
+                or frozen_den.shape != (L, self.groups, 4)):
+            raise RuntimeError("TILLER frozen inventory changed")
+        pre = torch.stack([pk[1] for pk in packets])
+        cot = torch.stack([pk[3] for pk in packets])
+        nums = torch.stack([p["numerator"].detach() for p in self.pairs])
+        dens = torch.stack([p["denominator"].detach() for p in self.pairs])
+        outw = torch.stack([p["out_weight"].detach() for p in self.pairs])
+        factors = tm.stacked_factors(pre, nums, dens, groups=self.groups, width=self.width,
+                                     eps=self.grain_eps)
+        adjoint = tm.response_adjoint(cot, outw, factors, groups=self.groups, width=self.width)
+        part_stats, resp_stats = tm.intrinsic_and_response_statistics(
+            pre, cot, adjoint, factors, frozen_num, frozen_den, eps=self.grain_eps)
+        first = part_stats.numel()
+        packed = torch.cat((part_stats.reshape(-1), resp_stats.reshape(-1)))
+        exact = (torch.all(nums.float() == frozen_num, dim=-1)
+                 & torch.all(dens.float() == frozen_den, dim=-1)).to(torch.int32)
+        if self.world_size > 1:
+            dist.all_reduce(packed, op=dist.ReduceOp.SUM, group=self.loss_probe_group)
+            dist.all_reduce(exact, op=dist.ReduceOp.MIN, group=self.loss_probe_group)
+        part_stats = packed[:first].view_as(part_stats)
+        resp_stats = packed[first:].view_as(resp_stats)
+        participation = tm.group_participation(part_stats)
+        self._group_participation = participation
+        self._group_response_congruence = tm.group_congruence(resp_stats, exact.bool())
+        self._attention_response_congruence = tm.layer_congruence(resp_stats, exact.bool())
+        incoming = participation[..., 0].mean(-1)
+        outgoing = participation[..., 1].mean(-1)
+        self._intrinsic_participation = torch.sqrt((incoming * outgoing).clamp(0.0, 1.0))
+        return participation, factors, adjoint
+
+    # -- direction ----------------------------------------------------------
+    def _chord_state(self, parent, *, groups, width, axis, key_prefix):
+        shape = tm.grouped_shape(parent, groups=groups, width=width, axis=axis)
+        anchor = self.anchor
+        rk, ck = key_prefix + "_row_second_moment", key_prefix + "_column_second_moment"
+        row, col = anchor.get(rk), anchor.get(ck)
+        if row is None:
+            row = torch.zeros(shape[:-1], device=parent.device, dtype=torch.float32)
+            anchor[rk] = row
+        if col is None:
+            col = torch.zeros(shape[:2] + shape[-1:], device=parent.device, dtype=torch.float32)
+            anchor[ck] = col
+        if row.shape != shape[:-1] or col.shape != shape[:2] + shape[-1:]:
+            raise RuntimeError("factorized adaptive tangent checkpoint inventory changed")
+        return row, col
+
+    def _role_directions(self, participation, congruence):
+        """Nesterov -> group NS5 -> chord for both roles; returns per-role records."""
+        L = len(self.pairs)
+        step = int(self.anchor.get("predictive_response_transaction_updates", 0)) + 1
+        records = {}
+        for role, index, axis in (("incoming", 0, "rows"), ("outgoing", 1, "columns")):
+            key = "in_weight" if role == "incoming" else "out_weight"
+            params = [p[key] for p in self.pairs]
+            momenta = foreach_nesterov(self, params, self.momentum)
+            grads = torch.stack([p.grad.detach() for p in params]).float()
+            parent = rational_group_zero_power(momenta, self.ns_steps, groups=self.groups,
+                                               width=self.width).float()
+            row, col = self._chord_state(parent, groups=self.groups, width=self.width, axis=axis,
+                                         key_prefix="factorized_adaptive_tangent_" + axis)
+            pg, restore = tm.group_view(parent, groups=self.groups, width=self.width, axis=axis)
+            mg, _ = tm.group_view(momenta, groups=self.groups, width=self.width, axis=axis)
+            gg, _ = tm.group_view(grads, groups=self.groups, width=self.width, axis=axis)
+            sel_g, meta = tm.adaptive_tangent_chord(pg, mg, gg, row, col, participation[..., index],
+                                                    congruence[..., index], step)
+            selected = restore(sel_g).to(parent.dtype)
+            adjustment = match_rms_adamw_adjustment(params[0].shape)
+            if role == "incoming":
+                sb = selected.view(L, self.groups, self.width, self.external)
+                gb = grads.view_as(sb)
+                mb = momenta.view_as(sb)
+            else:
+                sb = selected.view(L, self.external, self.groups, self.width).permute(0, 2, 3, 1)
+                gb = grads.view(L, self.external, self.groups, self.width).permute(0, 2, 3, 1)
+                mb = momenta.view(L, self.external, self.groups, self.width).permute(0, 2, 3, 1)
+            scaled = sb.float() * adjustment
+            records[role] = {
+                "params": params, "selected": selected, "adjustment": adjustment, "meta": meta,
+                "scaled_blocks": scaled,
+                "exact": (gb * scaled).sum(dim=(-2, -1)),
+                "momentum": (mb.float() * scaled).sum(dim=(-2, -1)),
+            }
+        return records
+
+    # -- ledger + transaction ----------------------------------------------
+    def _previous_ledger(self):
+        a = self.anchor
+        vals = tuple(a.get(k) for k in ("factorized_rfd_persistent_scores",
+                                        "factorized_rfd_persistent_total_diagonal",
+                                        "factorized_rfd_persistent_decay_cross",
+                                        "factorized_rfd_persistent_isotropic_tail"))
+        if all(v is None for v in vals):
+            return (None, None, None, None)
+        if any(not torch.is_tensor(v) for v in vals):
+            raise RuntimeError("TILLER checkpoint inventory changed")
+        return vals
+
+    def _advance_rows(self, scores, decay_action, *, functional):
+        anchor = self.anchor
+        ps, pd, pc, pt = self._previous_ledger()
+        rows = tm.rfd_rows(scores, decay_action, ps, pd, pc, pt, validate=self.strict)
+        anchor["factorized_rfd_persistent_scores"] = rows.persistent_scores.detach().clone()
+        anchor["factorized_rfd_persistent_total_diagonal"] = rows.persistent_total_diagonal.detach().clone()
+        anchor["factorized_rfd_persistent_decay_cross"] = rows.persistent_decay_cross.detach().clone()
+        anchor["factorized_rfd_persistent_isotropic_tail"] = rows.persistent_isotropic_tail.detach().clone()
+        anchor["factorized_rfd_discarded_energy_fraction"] = rows.discarded_energy_fraction.detach().clone()
+        anchor["factorized_rfd_shrinkage"] = rows.fd_shrinkage.detach().clone()
+        anchor["factorized_rfd_step"] = int(anchor.get("factorized_rfd_step", 0)) + 1
+        if functional:
+            anchor["factorized_rfd_reference_row_norm"] = tm.functional_row_norm(
+                scores, validate=False).detach().clone()
+            self._rfd_gradient_scale = scores.new_ones(())
+        self._rfd_rows = rows
+        self._rfd_functional_refresh = bool(functional)
+        return rows
+
+    def _transaction(self, exact_by_role, momentum_by_role, weights, layer_ids, *, eta):
+        if self._rfd_rows is None:
+            reference = self.anchor.get("factorized_rfd_reference_row_norm")
+            decay = self._rfd_decay_derivative
+            if not torch.is_tensor(reference) or not torch.is_tensor(decay):
+                raise RuntimeError("TILLER lacks functional calibration")
+            scores, decay_action, scale = tm.trace_matched_surrogate(exact_by_role, decay, reference)
+            self._rfd_gradient_scale = scale
+            self._advance_rows(scores, decay_action, functional=False)
+        result = tm.biatlas_transaction(self._rfd_rows, exact_by_role, momentum_by_role, weights,
+                                        layer_ids, total_layers=len(self.pairs), eta=float(eta),
+                                        rounds=64, diagnostics=bool(self._capture_telemetry_next_step),
+                                        validate=self.strict)
+        self._rfd_selection = result
+        return result
+
+    def _gather_rows(self, packet):
+        if self.world_size == 1:
+            if packet.shape[0] != tm.GLOBAL_PROBE_COUNT:
+                raise RuntimeError("fixed-probe global row count changed")
+            return packet
+        probes = tm.GLOBAL_PROBE_COUNT
+        counts = [(r + 1) * probes // self.world_size - r * probes // self.world_size
+                  for r in range(self.world_size)]
+        maximum = max(counts)
+        padded = packet.new_zeros((maximum, packet.shape[1]))
+        if packet.shape[0]:
+            padded[: packet.shape[0]].copy_(packet)
+        gathered = [torch.empty_like(padded) for _ in range(self.world_size)]
+        dist.all_gather(gathered, padded, group=self.loss_probe_group)
+        return torch.cat([g[:n] for g, n in zip(gathered, counts)], dim=0)
+
+    # -- step -----------------------------------------------------------------
+    @torch.no_grad()
+    def step(self, closure=None):
+        if self._clip_factor is None:
+            raise RuntimeError("TILLER lacks realized clipping")
+        if not self._attention_consumed:
+            raise RuntimeError("TILLER would overwrite attention state")
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        group = self.param_groups[0]
+        if float(group.get("lr_scale", 1.0)) != 1.0:
+            raise RuntimeError("TILLER refuses nonunit LR scale")
+        lr = float(group["lr"])
+        wd = float(group["weight_decay"])
+        publish = bool(self._capture_telemetry_next_step)
+        self._last_telemetry = {}
+        self._rfd_rows = None
+        self._rfd_functional_refresh = False
+        self._rfd_gradient_scale = None
+        self._rfd_selection = None
+        refresh = bool(self._capture_response_this_transition)
+        for pair in self.pairs:
+            for key in ("in_weight", "out_weight"):
+                if pair[key].grad is None:
+                    raise RuntimeError("TILLER parameter lacks gradient")
+        if not refresh:
+            terms = [(p[k].grad.detach().float() * p[k].detach().float()).sum()
+                     for p in self.pairs for k in ("in_weight", "out_weight")]
+            self._rfd_decay_derivative = torch.stack(terms).sum() * wd
+        L = len(self.pairs)
+        anchor = self.anchor
+        if refresh:
+            packets = self._consume_probes()
+            participation, factors, adjoint = self._response_sensor(packets)
+        else:
+            self._restore_route()
+            participation = self._group_participation
+        congruence = self._group_response_congruence
+        rec = self._role_directions(participation, congruence)
+        inc_b = rec["incoming"]["scaled_blocks"]
+        out_b = rec["outgoing"]["scaled_blocks"]
+        weights = (inc_b.square().sum(dim=(-2, -1)) + out_b.square().sum(dim=(-2, -1))).reshape(-1)
+        exact_by_role = torch.stack([rec[r]["exact"].reshape(-1) for r in ("incoming", "outgoing")])
+        momentum_by_role = torch.stack([rec[r]["momentum"].reshape(-1) for r in ("incoming", "outgoing")])
+        layer_ids = torch.arange(L, device=weights.device, dtype=torch.int64).repeat_interleave(self.groups)
+        if refresh:
+            scores, decay = [], None
+            for layer, (pair, packet) in enumerate(zip(self.pairs, packets)):
+                inputs, _pre, features, cot = packet
+                adj = adjoint[layer]
+                s = tm.group_scores(inputs, features, cot, inc_b[layer].reshape(self.hidden, self.external),
+                                    out_b[layer].reshape(self.hidden, self.external), adj,
+                                    groups=self.groups, width=self.width, validate=self.strict)
+                d = tm.group_scores(inputs, features, cot, pair["in_weight"].float() * wd,
+                                    pair["out_weight"].T.float() * wd, adj, groups=self.groups,
+                                    width=self.width, validate=self.strict).sum(-1)
+                scores.append(s)
+                decay = d if decay is None else decay + d
+            lattice = torch.stack(scores, dim=1).reshape(self.probe_layout.local_probe_count, L * self.groups)
+            packet = torch.cat((lattice, decay[:, None]), dim=1)
+            global_packet = self._gather_rows(packet)
+            g_scores, g_decay = global_packet[:, :-1], global_packet[:, -1]
+            predictive = tm.window32_rows(g_scores, g_decay, anchor.get("predictive_global_score_ema"),
+                                          anchor.get("predictive_global_decay_ema"),
+                                          validate=self.strict)
+            self._advance_rows(g_scores, g_decay, functional=True)
+            selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids, eta=lr)
+            anchor["predictive_global_score_ema"] = predictive.updated_scores.detach().clone()
+            anchor["predictive_global_decay_ema"] = predictive.updated_decay_action.detach().clone()
+            self._last_predictive = predictive
+        else:
+            if self._cached_selection_scores is None or self._cached_selection_decay is None:
+                raise RuntimeError("TILLER selection factor is missing")
+            selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids, eta=lr)
+        coefficients = selection.coefficients.view(L, self.groups)
+        inc_sel = rec["incoming"]["selected"]
+        inc_sel.view(L, self.groups, self.width, self.external).mul_(
+            coefficients[..., None, None].to(inc_sel.dtype))
+        out_sel = rec["outgoing"]["selected"]
+        out_sel.view(L, self.external, self.groups, self.width).permute(0, 2, 3, 1).mul_(
+            coefficients[..., None, None].to(out_sel.dtype))
+        for role in ("incoming", "outgoing"):
+            foreach_apply(rec[role]["params"], rec[role]["selected"], decay=1.0 - lr * wd,
+                          alpha=-lr * rec[role]["adjustment"])
+        updates = int(anchor.get("predictive_response_transaction_updates", 0)) + 1
+        anchor["predictive_response_transaction_updates"] = updates
+        self._attention_update = updates
+        self._attention_consumed = False
+        if refresh:
+            self._cache_refresh_state()
+        if publish:
+            self._publish_telemetry(refresh, coefficients, rec, selection)
+        self._advance_cadence()
+        self._rfd_decay_derivative = None
+        self._capture_telemetry_next_step = False
+        self._clip_factor = None
+        return loss
+
+    def _cache_refresh_state(self):
+        route = {
+            "group_participation": self._group_participation.detach().clone(),
+            "group_congruence": self._group_response_congruence.detach().clone(),
+            "intrinsic_participation": self._intrinsic_participation.detach().clone(),
+            "attention_congruence": self._attention_response_congruence.detach().clone(),
+        }
+        self._cached_route = route
+        anchor = self.anchor
+        for name, value in route.items():
+            anchor["cadence8_" + name] = value
+        anchor["cadence8_relative_score_innovation"] = self._last_predictive.relative_innovation.detach().clone()
+        self._cached_selection_scores = anchor["predictive_global_score_ema"]
+        self._cached_selection_decay = anchor["predictive_global_decay_ema"]
+        anchor["cadence8_transition"] = int(self._cadence_transition)
+
+    def _restore_route(self):
+        route = self._cached_route
+        if route is None or set(route) != set(_ROUTE_NAMES):
+            raise RuntimeError("TILLER cached response route is incomplete")
+        self._group_participation = route["group_participation"]
+        self._group_response_congruence = route["group_congruence"]
+        self._intrinsic_participation = route["intrinsic_participation"]
+        self._attention_response_congruence = route["attention_congruence"]
+
+    def _advance_cadence(self):
+        self._cadence_transition += 1
+        self.anchor["cadence8_transition"] = self._cadence_transition
+        self._capture_response_this_transition = self._cadence_transition % tm.REFRESH_INTERVAL == 0
+
+    def _publish_telemetry(self, refresh, coefficients, rec, selection):
+        flat = coefficients.reshape(-1).float()
+        safe = torch.cat([rec[r]["meta"]["safe"].reshape(-1) for r in ("incoming", "outgoing")])
+        cosine = torch.cat([rec[r]["meta"]["parent_cosine"].reshape(-1) for r in ("incoming", "outgoing")])
+        energy = torch.cat([rec[r]["meta"]["departure_energy"].reshape(-1) for r in ("incoming", "outgoing")])
+        rows = self._rfd_rows
+        scaling = tiller_scaling_formula(total_positions=1, total_layers=len(self.pairs),
+                                         total_groups=self.groups, intermediate_width=self.hidden,
+                                         model_width=self.external)
+        P = PREFIX
+        self._last_telemetry = {
+            P + "family_id": FAMILY_ID,
+            P + "response_refreshed": int(refresh),
+            P + "response_age": 0 if refresh else self._cadence_transition % tm.REFRESH_INTERVAL,
+            P + "functional_score_refresh": int(self._rfd_functional_refresh),
+            P + "trace_matched_gradient_surrogate": int(not self._rfd_functional_refresh),
+            P + "gradient_score_scale": float(self._rfd_gradient_scale.item()),
+            P + "ledger_step": int(self.anchor["factorized_rfd_step"]),
+            P + "selection_factor_rows": int(rows.selection_scores.shape[0]),
+            P + "persistent_factor_rows": int(rows.persistent_scores.shape[0]),
+            P + "persistent_isotropic_tail": float(rows.persistent_isotropic_tail.item()),
+            P + "fd_shrinkage": float(rows.fd_shrinkage.item()),
+            P + "transaction_accepted": int(selection.accepted.item()),
+            P + "rank": int(selection.factor_rank.item()),
+            P + "budget_residual": float(selection.budget_residual.item()),
+            P + "cross_layer_coupling_ratio": float(selection.cross_layer_coupling_ratio.item()),
+            P + "coefficient_min": float(flat.amin().item()),
+            P + "coefficient_median": float(flat.median().item()),
+            P + "coefficient_max": float(flat.amax().item()),
+            P + "adaptive_tangent_safe_fraction": float(safe.float().mean().item()),
+            P + "adaptive_tangent_parent_cosine_median": float(cosine.median().item()),
+            P + "departure_energy_median": float(energy.median().item()),
+            P + "state_coordinate_count": scaling["persistent_state_elements"],
+            P + "ledger_checkpoint_tensor_elements": scaling["ledger_checkpoint_tensor_elements"],
+            P + "realized_clip_factor": float(self._clip_factor),
+        }
+
+    # -- checkpoint ------------------------------------------------------------
+    def load_state_dict(self, state_dict):
+        result = super().load_state_dict(state_dict)
+        anchor = self.anchor
+        step = anchor.get("cadence8_transition")
+        if not isinstance(step, int) or step < 0:
+            raise RuntimeError("cadence8 checkpoint transition changed")
+        self._cadence_transition = step
+        self._capture_response_this_transition = step % tm.REFRESH_INTERVAL == 0
+        route = {name: anchor.get("cadence8_" + name) for name in _ROUTE_NAMES}
+        if any(not torch.is_tensor(v) for v in route.values()):
+            raise RuntimeError("cadence8 checkpoint route changed")
+        self._cached_route = route
+        self._cached_selection_scores = anchor.get("predictive_global_score_ema")
+        self._cached_selection_decay = anchor.get("predictive_global_decay_ema")
+        if not torch.is_tensor(self._cached_selection_scores) or not torch.is_tensor(self._cached_selection_decay):
+            raise RuntimeError("cadence8 checkpoint selection factor changed")
+        innov = anchor.get("cadence8_relative_score_innovation")
+        if innov is not None and (not torch.is_tensor(innov) or innov.numel() != 1):
+            raise RuntimeError("cadence8 checkpoint innovation diagnostic changed")
+        self._previous_ledger()
+        ref = anchor.get("factorized_rfd_reference_row_norm")
+        st = anchor.get("factorized_rfd_step")
+        if not torch.is_tensor(ref) or ref.numel() != 1 or type(st) is not int or st < 1:
+            raise RuntimeError("TILLER reference checkpoint is absent")
+        self._rfd_rows = None
+        self._rfd_gradient_scale = None
+        self._rfd_selection = None
+        self._rfd_decay_derivative = None
+        self._attention_update = 0
+        self._attention_consumed = True
+        return result
+
+
+class TILLERAttentionOptimizer(torch.optim.Optimizer):
+    """TILLER on the attention ``qkv``/``out`` matrices, driven by the router's route."""
+
+    _ROLES = ("qkv", "attn_out")
+
+    def __init__(self, blocks, router: TILLERRouter, *, lr, weight_decay, momentum, ns_steps, beta2,
+                 eps, adjust_lr_fn):
+        if (float(lr) != 0.0003 or float(weight_decay) != 0.1 or float(momentum) != 0.95
+                or int(ns_steps) != 5 or float(beta2) != 0.95 or float(eps) != 1e-08
+                or adjust_lr_fn != "match_rms_adamw"):
+            raise ValueError("TILLER attention requires the locked cell")
+        self.blocks = sorted((dict(b) for b in blocks), key=lambda b: int(b["layer_index"]))
+        if [int(b["layer_index"]) for b in self.blocks] != list(range(len(self.blocks))):
+            raise ValueError("TILLER attention layer inventory changed")
+        self.router = router
+        self.momentum = float(momentum)
+        self.ns_steps = int(ns_steps)
+        self.role_parameters = {"qkv": [b["qkv_weight"] for b in self.blocks],
+                                "attn_out": [b["attn_out_weight"] for b in self.blocks]}
+        params = []
+        seen = {id(pair[r]) for pair in router.pairs for r in ("in_weight", "out_weight")}
+        for role in self._ROLES:
+            for p in self.role_parameters[role]:
+                if p.ndim != 2 or id(p) in seen:
+                    raise ValueError("TILLER attention ownership changed")
+                seen.add(id(p))
+                params.append(p)
+        group = {"params": params, "lr": float(lr), "weight_decay": float(weight_decay), "lr_scale": 1.0}
+        group.update(_ATTENTION_GROUP_KEYS)
+        super().__init__([group], {})
+        self._capture_telemetry_next_step = False
+        self._last_telemetry = {}
+
+    def lr_wd_fairness_audit(self):
+        keys = ("global_lr_scale", "qkv_lr_scale", "attention_output_lr_scale",
+                "residual_coordinate_fisher_lr_scale", "single_ns5_per_attention_role_lr_scale",
+                "moment_exact_compact_lr_scale", "lagged_predictive_response_attention_lr_scale",
+                "attention_head_group_polar_lr_scale",
+                "attention_nominal_polar_rank_calibration_lr_scale",
+                "posterior_rank64_attention_lr_scale", "posterior_rank64_cadence8_attention_lr_scale",
+                "window32_cadence8_attention_lr_scale",
+                "attention_matched_beta2_factorized_tangent_lr_scale",
+                "attention_response_energy_chord_lr_scale",
+                "attention_signed_current_gradient_orientation_lr_scale",
+                "attention_compiled_static_fullgraph_execution_lr_scale",
+                "unchanged_compiled_factorized_attention_lr_scale", "weight_decay_scale")
+        return {k: 1.0 for k in keys}
+
+    def set_telemetry_capture(self, enabled=True):
+        self._capture_telemetry_next_step = bool(enabled)
+
+    def telemetry(self):
+        return dict(self._last_telemetry)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        self._last_telemetry = {}
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        group = self.param_groups[0]
+        if float(group.get("lr_scale", 1.0)) != 1.0:
+            raise RuntimeError("TILLER attention refuses nonunit LR scale")
+        lr = float(group["lr"])
+        wd = float(group["weight_decay"])
+        participation, congruence, router_update = self.router.consume_response_homotopy()
+        anchor = self.state[self.role_parameters["qkv"][0]]
+        previous = int(anchor.get("compact_response_homotopy_router_update", 0))
+        if int(router_update) != previous + 1:
+            raise RuntimeError("TILLER attention missed a router update")
+        anchor["compact_response_homotopy_router_update"] = int(router_update)
+        update = int(anchor.get("factorized_adaptive_tangent_updates", 0)) + 1
+        metas = []
+        for role, key in (("qkv", "qkv"), ("attn_out", "attention_output")):
+            params = self.role_parameters[role]
+            momenta = foreach_nesterov(self, params, self.momentum)
+            grads = torch.stack([p.grad.detach() for p in params]).float()
+            parent = attention_head_group_zero_power(momenta, self.ns_steps).float()
+            shape = tm.grouped_shape(parent, groups=1, width=None, axis="matrix")
+            rk = "factorized_adaptive_tangent_" + key + "_row_second_moment"
+            ck = "factorized_adaptive_tangent_" + key + "_column_second_moment"
+            row, col = anchor.get(rk), anchor.get(ck)
+            if row is None:
+                row = torch.zeros(shape[:-1], device=parent.device, dtype=torch.float32)
+                anchor[rk] = row
+            if col is None:
+                col = torch.zeros(shape[:2] + shape[-1:], device=parent.device, dtype=torch.float32)
+                anchor[ck] = col
+            pg, restore = tm.group_view(parent, groups=1, width=None, axis="matrix")
+            mg, _ = tm.group_view(momenta, groups=1, width=None, axis="matrix")
+            gg, _ = tm.group_view(grads, groups=1, width=None, axis="matrix")
+            sel, meta = tm.adaptive_tangent_chord(pg, mg, gg, row, col, participation[:, None],
+                                                  congruence[:, None], update)
+            metas.append(meta)
+            adjustment = match_rms_adamw_adjustment(params[0].shape)
+            foreach_apply(params, restore(sel).to(parent.dtype), decay=1.0 - lr * wd,
+                          alpha=-lr * adjustment)
+        anchor["factorized_adaptive_tangent_updates"] = update
+        if self._capture_telemetry_next_step:
+            safe = torch.cat([m["safe"].reshape(-1) for m in metas])
+            cosine = torch.cat([m["parent_cosine"].reshape(-1) for m in metas])
+            self._last_telemetry = {
+                PREFIX + "attention_family_id": FAMILY_ID,
+                PREFIX + "attention_router_update": int(router_update),
+                PREFIX + "attention_adaptive_tangent_safe_fraction": float(safe.float().mean()),
+                PREFIX + "attention_adaptive_tangent_parent_cosine_median": float(cosine.median()),
+            }
+        self._capture_telemetry_next_step = False
+        return loss
