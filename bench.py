@@ -1,0 +1,348 @@
+#!/usr/bin/env python3
+"""Headline benchmark: training tokens/s of the 18-layer, 1024-wide GRAIN
+Transformer (296.9M parameters at vocab 50,304) with the TILLER optimizer,
+seq 1024, global batch 32 sequences, data-parallel over N GPUs (one process
+per GPU).  Synthetic Zipf(1.1) token ids from seed 0, random-init weights.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched with torchrun (RANK/LOCAL_RANK/WORLD_SIZE from the env).
+``value`` is device-timed (CUDA events around exactly K steps, barrier +
+synchronize on both sides, max over ranks) with inputs already on the device;
+``e2e`` re-times K steps through the public ``TrainEngine`` API including the
+pinned host->device copy of each step's tokens and the device->host read of
+the step's loss.  ``--impl reference`` runs the unmodified reference trainer
+code path (installed under baseline/_ref) on the same model, data and timing.
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+METRIC = "train tokens/sec at 18L/1024d GRAIN+TILLER (1/2/4/8 B200, max over ranks)"
+BASELINE_TOKENS_PER_S = 38528.0  # published 18L GRAIN+TILLER (4x A6000, seq 256)
+MODEL_CFG = dict(layers=18, d_model=1024, heads=16, ffn_dim=3072, seq_len=1024,
+                 activation="grain", rational_init="silu", rational_group_size=256,
+                 rational_max_groups=32, rational_basis_eps=1e-6, init_std=0.02)
+VOCAB = 50304
+GLOBAL_BATCH = 32
+SEQ = 1024
+ZIPF_TOKENS = 8_000_000
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--optimizer", default="tiller_v1")
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
+    ap.add_argument("--layers", type=int, default=MODEL_CFG["layers"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-count-launches", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        mhz, maxes, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for s in self.samples:
+            try:
+                mhz.append(float(s[1]))
+                maxes.append(float(s[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, s[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None,
+                "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def count_own_launches(step_fn):
+    """Run one step under the profiler and count launches of this package's kernels."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    own = total = 0
+    for evt in prof.events():
+        if evt.device_type == torch.autograd.DeviceType.CUDA:
+            total += 1
+            if "ro::" in evt.name or "(anonymous namespace)::" in evt.name and "ro" in evt.name:
+                own += 1
+    return own, total
+
+
+def timed(step_fn, steps, device, dist_on):
+    import torch
+    import torch.distributed as dist
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step_fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    if dist_on:
+        dist.barrier()
+    ms = start.elapsed_time(end) / steps
+    if dist_on:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_ours(a, info):
+    import torch
+    sys.path.insert(0, ROOT)
+    from rational_optimizer_b200.models.transformer import model_args, CausalTransformer
+    from rational_optimizer_b200.optim import composite
+    from rational_optimizer_b200.parallel.grad_sync import GradientSynchronizer
+    from rational_optimizer_b200.train.data import PinnedBatcher, zipf_tokens
+    from rational_optimizer_b200.train.engine import TrainEngine
+
+    device = info.device
+    world = info.world_size
+    local_batch = a.global_batch // world
+    cfg = dict(MODEL_CFG, layers=a.layers)
+    args = model_args(**cfg, optimizer=a.optimizer, lr=3e-4, weight_decay=0.1, muon_momentum=0.95,
+                      muon_ns_steps=5, beta1=0.9, beta2=0.95, eps=1e-8,
+                      muon_adjust_lr_fn="match_rms_adamw", grad_accum=1)
+    torch.manual_seed(1337)
+    model = CausalTransformer(args, VOCAB).to(device)
+    if info.is_distributed:
+        import torch.distributed as dist
+        for p in model.parameters():
+            dist.broadcast(p.data, 0)
+    optimizer = composite.configure_optimizer(model, args)
+    comm = None
+    if world > 1:
+        from rational_optimizer_b200.parallel.comm import maybe_communicator
+        comm = maybe_communicator(device)
+    sync = GradientSynchronizer(model, communicator=comm)
+    engine = TrainEngine(model, optimizer, grad_clip=1.0, grad_accum=1, synchronizer=sync)
+    tokens = zipf_tokens(ZIPF_TOKENS, VOCAB, alpha=1.1, seed=0)
+    batcher = PinnedBatcher(tokens, local_batch, SEQ, seed=0, rank=info.rank)
+    # device-resident inputs for the kernel-timed loop
+    staged = [batcher.to_device(device, batcher.next_host().clone()) for _ in range(4)]
+    counter = {"i": 0}
+
+    def device_step():
+        x, y = staged[counter["i"] % len(staged)]
+        counter["i"] += 1
+        engine.step([(x, y)], lr=3e-4)
+
+    def e2e_step():
+        host = batcher.next_host()
+        x, y = batcher.to_device(device, host)
+        loss = engine.step([(x, y)], lr=3e-4)
+        return float(loss.item())
+
+    for _ in range(a.warmup):
+        device_step()
+    sampler = ClockSampler(device.index or 0) if info.rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = timed(device_step, a.steps, device, info.is_distributed)
+    clocks = sampler.stop() if sampler else None
+    e2e_ms = None
+    if not a.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        e2e_ms = timed(e2e_step, a.steps, device, info.is_distributed)
+    launches = None
+    if not a.no_count_launches and not info.is_distributed:
+        own, total = count_own_launches(device_step)
+        launches = {"own_per_step": own, "all_per_step": total}
+    loss = float(engine.step([staged[0]], lr=3e-4).item())
+    return ms, e2e_ms, clocks, launches, loss, batcher.bytes_per_batch
+
+
+def run_reference(a, info):
+    """The reference trainer's own objects and step sequence (training/train.py:2814-2950)."""
+    import torch
+    import torch.nn.functional as F
+    if not os.path.isdir(os.path.join(REF_DIR, "training")):
+        return None
+    sys.path.insert(0, REF_DIR)
+    os.environ.pop("RATIONAL_OPT_TORCH_FALLBACK", None)
+    from training import train as T
+    from experiments.protocol import method_entrypoint as M
+    import types
+    device = info.device
+    world = info.world_size
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cudnn.allow_tf32 = True
+    torch.set_float32_matmul_precision("high")
+    args = types.SimpleNamespace(**MODEL_CFG)
+    args.layers = a.layers
+    args.optimizer = "tiller_v1"
+    args.lr, args.min_lr, args.warmup_steps, args.weight_decay = 3e-4, 3e-5, 200, 0.1
+    args.beta1, args.beta2, args.eps = 0.9, 0.95, 1e-8
+    args.muon_momentum, args.muon_ns_steps, args.muon_adjust_lr_fn = 0.95, 5, "match_rms_adamw"
+    args.grad_clip, args.grad_accum, args.batch_size = 1.0, 1, a.global_batch // world
+    args.steps = a.warmup + 2 * a.steps + 4
+    T.RATIONAL_SPECIFIC_OPTIMIZERS.add(M.OPTIMIZER_ID)
+    T.ACTIVE_OPTIMIZERS = sorted(set(T.ACTIVE_OPTIMIZERS) | {M.OPTIMIZER_ID})
+    T.configure_optimizer = M.configure_candidate_optimizer
+    T.clip_or_measure_gradients = M.clip_candidate_gradients
+    torch.manual_seed(1337)
+    torch.cuda.manual_seed_all(1337)
+    model = T.CausalTransformer(args, VOCAB).to(device)
+    if info.is_distributed:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[info.local_rank],
+                                                          output_device=info.local_rank)
+    M.set_experiment_layout(microbatches=1, decay_tied_embedding=False)
+    optimizer = M.configure_candidate_optimizer(model, args)
+    from rational_optimizer_b200.train.data import zipf_tokens
+    tokens = zipf_tokens(ZIPF_TOKENS, VOCAB, alpha=1.1, seed=0).pin_memory()
+    offsets = torch.arange(SEQ + 1)
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(1337 + 997 * info.rank)
+    state = {"step": 0}
+
+    def one_step(read_loss):
+        step = state["step"]
+        state["step"] += 1
+        lr = T.learning_rate(step, args)
+        for group in optimizer.param_groups:
+            group["lr"] = lr * float(group.get("lr_scale", 1.0))
+        optimizer.zero_grad(set_to_none=True)
+        x, y = T.sample_batch(tokens, args.batch_size, SEQ, offsets, gen, device)
+        logits = model(x)
+        loss = F.cross_entropy(logits.view(-1, logits.size(-1)), y.reshape(-1))
+        loss.backward()
+        T.clip_or_measure_gradients(model, args.grad_clip, False)
+        optimizer.step()
+        return float(loss.item()) if read_loss else loss
+
+    for _ in range(a.warmup):
+        one_step(True)
+    sampler = ClockSampler(device.index or 0) if info.rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = timed(lambda: one_step(True), a.steps, device, info.is_distributed)
+    clocks = sampler.stop() if sampler else None
+    return ms, clocks
+
+
+def main():
+    a = parse()
+    sys.path.insert(0, ROOT)
+    import torch
+    from rational_optimizer_b200.parallel.dist import cleanup_distributed, setup_distributed
+    info = setup_distributed()
+    if a.gpus != info.world_size:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={info.world_size}")
+    tokens_per_step = a.global_batch * SEQ
+    cfg = {"model": "18L/1024d/16h GRAIN (H=4608, G=18), vocab 50304, 296.92M params",
+           "global_batch": a.global_batch, "seq_len": SEQ, "parallelism": f"dp{a.gpus}",
+           "optimizer": a.optimizer, "grad_accum": 1,
+           "l2": "inputs and working set larger than L2 (no flush needed)"}
+    if a.layers != MODEL_CFG["layers"]:
+        cfg["model"] = f"{a.layers}L/1024d GRAIN (reduced depth)"
+    if a.impl == "reference":
+        try:
+            res = run_reference(a, info)
+        except Exception as exc:  # report, do not crash the driver
+            res = None
+            reason = f"reference run failed: {type(exc).__name__}: {str(exc)[:200]}"
+        else:
+            reason = "reference package not installed in baseline/_ref"
+        if res is None:
+            if info.rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+            cleanup_distributed(info)
+            return
+        ms, clocks = res
+        value = tokens_per_step / (ms / 1000.0)
+        if info.rank == 0:
+            print(json.dumps({
+                "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+                "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": value / BASELINE_TOKENS_PER_S, "dtype": "fp32+tf32",
+                "data": "synthetic Zipf(1.1) token ids, seed 0; random-init weights",
+                "config": cfg, "clocks": clocks}), flush=True)
+        cleanup_distributed(info)
+        return
+    ms, e2e_ms, clocks, launches, loss, h2d = run_ours(a, info)
+    value = tokens_per_step / (ms / 1000.0)
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": value / BASELINE_TOKENS_PER_S, "dtype": "bf16",
+        "data": "synthetic Zipf(1.1) token ids, seed 0; random-init weights",
+        "config": cfg, "clocks": clocks, "final_loss": loss,
+    }
+    if e2e_ms is not None:
+        out["e2e"] = {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
+                      "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4}
+    if launches is not None:
+        out["gpu_launches"] = launches["own_per_step"] * a.steps
+        out["gpu_launches_detail"] = {"own_per_step": launches["own_per_step"],
+                                      "all_kernels_per_step": launches["all_per_step"]}
+    if info.rank == 0:
+        print(json.dumps(out), flush=True)
+    cleanup_distributed(info)
+
+
+if __name__ == "__main__":
+    main()

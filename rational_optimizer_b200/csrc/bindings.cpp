@@ -282,6 +282,222 @@ torch::Tensor cross_entropy_fwd_bwd(torch::Tensor logits, torch::Tensor target, 
   return loss;
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 GEMM.  a_km: a is [.., K, M] (else [.., M, K]); b_nk: b is [.., N, K]
+// (else [.., K, N]).  Returns None when the layout is unsupported so the
+// caller can use another path.
+
+torch::Tensor& gemm_error_flag(const torch::Device& dev) {
+  static std::vector<torch::Tensor> flags(64);
+  auto& f = flags.at(dev.index());
+  if (!f.defined()) f = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
+  return f;
+}
+
+c10::optional<torch::Tensor> gemm_bf16_impl(torch::Tensor a, torch::Tensor b, bool a_km, bool b_nk,
+                                            bool out_f32, c10::optional<torch::Tensor> d, double alpha,
+                                            double beta) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda(), "gemm operands must be CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
+              "gemm operands must be bfloat16");
+  TORCH_CHECK(a.dim() == b.dim() && (a.dim() == 2 || a.dim() == 3), "gemm operands must be 2-D or 3-D");
+  const c10::cuda::CUDAGuard guard(a.device());
+  const bool batched = a.dim() == 3;
+  const int64_t batch = batched ? a.size(0) : 1;
+  if (batched) TORCH_CHECK(b.size(0) == batch, "batch mismatch");
+  if (a.stride(-1) != 1 || b.stride(-1) != 1) return c10::nullopt;
+  const int64_t M = a_km ? a.size(-1) : a.size(-2);
+  const int64_t K = a_km ? a.size(-2) : a.size(-1);
+  const int64_t N = b_nk ? b.size(-2) : b.size(-1);
+  const int64_t Kb = b_nk ? b.size(-1) : b.size(-2);
+  TORCH_CHECK(K == Kb, "gemm inner dimensions differ");
+  auto opts = a.options().dtype(out_f32 ? torch::kFloat32 : torch::kBFloat16);
+  torch::Tensor c = batched ? torch::empty({batch, M, N}, opts) : torch::empty({M, N}, opts);
+  const void* dptr = nullptr;
+  int64_t ldd = 0, sd = 0;
+  if (d.has_value()) {
+    TORCH_CHECK(d->scalar_type() == torch::kBFloat16 && d->stride(-1) == 1, "gemm D must be bf16 row-major");
+    TORCH_CHECK(d->size(-2) == M && d->size(-1) == N, "gemm D shape");
+    dptr = d->data_ptr();
+    ldd = d->stride(-2);
+    sd = batched ? d->stride(0) : 0;
+  }
+  auto& flag = gemm_error_flag(a.device());
+  const int rc = ro::gemm_bf16_tn(a.data_ptr(), a.stride(-2), batched ? a.stride(0) : 0, a_km, b.data_ptr(),
+                                  b.stride(-2), batched ? b.stride(0) : 0, !b_nk, c.data_ptr(), N,
+                                  batched ? M * N : 0, out_f32, dptr, ldd, sd, static_cast<float>(alpha),
+                                  static_cast<float>(beta), static_cast<int>(M), static_cast<int>(N),
+                                  static_cast<int>(K), static_cast<int>(batch), flag.data_ptr<int>(),
+                                  at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "gemm_bf16");
+  return c;
+}
+
+c10::optional<torch::Tensor> gemm_bf16(torch::Tensor a, torch::Tensor b, bool a_km, bool b_nk, bool out_f32) {
+  return gemm_bf16_impl(a, b, a_km, b_nk, out_f32, c10::nullopt, 1.0, 0.0);
+}
+
+c10::optional<torch::Tensor> gemm_bf16_ex(torch::Tensor a, torch::Tensor b, bool a_km, bool b_nk,
+                                          bool out_f32, c10::optional<torch::Tensor> d, double alpha,
+                                          double beta) {
+  return gemm_bf16_impl(a, b, a_km, b_nk, out_f32, d, alpha, beta);
+}
+
+torch::Tensor gemm_error(torch::Tensor like) { return gemm_error_flag(like.device()); }
+
+void adamw_multi_tensor(std::vector<torch::Tensor> p, std::vector<torch::Tensor> g,
+                        std::vector<torch::Tensor> m, std::vector<torch::Tensor> v, double lr,
+                        double beta1, double beta2, double eps, double wd, double step) {
+  const size_t n = p.size();
+  TORCH_CHECK(g.size() == n && m.size() == n && v.size() == n, "adamw list lengths differ");
+  if (n == 0) return;
+  const c10::cuda::CUDAGuard guard(p[0].device());
+  std::vector<float*> pp(n), mp(n), vp(n);
+  std::vector<const float*> gp(n);
+  std::vector<int64_t> sizes(n);
+  for (size_t i = 0; i < n; ++i) {
+    for (auto* t : {&p[i], &g[i], &m[i], &v[i]}) {
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous(),
+                  "adamw tensors must be contiguous fp32 CUDA tensors");
+    }
+    TORCH_CHECK(g[i].numel() == p[i].numel() && m[i].numel() == p[i].numel() && v[i].numel() == p[i].numel(),
+                "adamw tensor sizes differ");
+    pp[i] = p[i].data_ptr<float>();
+    gp[i] = g[i].data_ptr<float>();
+    mp[i] = m[i].data_ptr<float>();
+    vp[i] = v[i].data_ptr<float>();
+    sizes[i] = p[i].numel();
+  }
+  check_rc(ro::adamw_multi_tensor(pp.data(), gp.data(), mp.data(), vp.data(), sizes.data(), static_cast<int>(n),
+                                  static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
+                                  static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(step),
+                                  at::cuda::getCurrentCUDAStream()),
+           "adamw_multi_tensor");
+}
+
+// ---------------------------------------------------------------------------
+// TILLER direction kernels.
+
+std::vector<float*> ptrs_of(std::vector<torch::Tensor>& ts, int64_t numel, const char* what) {
+  std::vector<float*> out;
+  for (auto& t : ts) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous() && t.numel() == numel,
+                what, " must be contiguous fp32 CUDA tensors of equal size");
+    out.push_back(t.data_ptr<float>());
+  }
+  return out;
+}
+
+std::vector<torch::Tensor> tiller_nesterov(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> bufs,
+                                           bool transpose, double mu) {
+  TORCH_CHECK(!grads.empty() && grads.size() == bufs.size(), "tiller_nesterov lists");
+  const c10::cuda::CUDAGuard guard(grads[0].device());
+  TORCH_CHECK(grads[0].dim() == 2, "tiller_nesterov expects matrices");
+  const int64_t P = grads[0].size(0), Q = grads[0].size(1);
+  auto gp = ptrs_of(grads, P * Q, "grads");
+  auto bp = ptrs_of(bufs, P * Q, "momentum buffers");
+  const int64_t L = grads.size();
+  auto opts = grads[0].options();
+  std::vector<int64_t> shape = transpose ? std::vector<int64_t>{L, Q, P} : std::vector<int64_t>{L, P, Q};
+  auto m = torch::empty(shape, opts);
+  auto g = torch::empty(shape, opts);
+  auto m16 = torch::empty(shape, opts.dtype(torch::kBFloat16));
+  check_rc(ro::tiller_nesterov(gp.data(), bp.data(), m.data_ptr<float>(), g.data_ptr<float>(),
+                               reinterpret_cast<__nv_bfloat16*>(m16.data_ptr()), static_cast<int>(L),
+                               static_cast<int>(P), static_cast<int>(Q), transpose, static_cast<float>(mu),
+                               at::cuda::getCurrentCUDAStream()),
+           "tiller_nesterov");
+  return {m, g, m16};
+}
+
+torch::Tensor tiller_transpose_bf16(torch::Tensor x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.dim() == 3,
+              "transpose expects contiguous bf16 [L, P, Q]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty({x.size(0), x.size(2), x.size(1)}, x.options());
+  check_rc(ro::tiller_transpose_bf16(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                     reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), static_cast<int>(x.size(0)),
+                                     static_cast<int>(x.size(1)), static_cast<int>(x.size(2)),
+                                     at::cuda::getCurrentCUDAStream()),
+           "tiller_transpose_bf16");
+  return y;
+}
+
+std::vector<torch::Tensor> tiller_chord(torch::Tensor polar, torch::Tensor m, torch::Tensor g,
+                                        torch::Tensor row_m, torch::Tensor col_m, torch::Tensor participation,
+                                        torch::Tensor congruence, int64_t nblocks, int64_t R, int64_t C,
+                                        double scale, int64_t step, double adj) {
+  const c10::cuda::CUDAGuard guard(m.device());
+  TORCH_CHECK(polar.scalar_type() == torch::kBFloat16 && polar.is_contiguous() && polar.numel() == nblocks * R * C,
+              "polar must be bf16 [nblocks*R*C]");
+  check_f32(m, "m");
+  check_f32(g, "g");
+  check_f32(row_m, "row moment");
+  check_f32(col_m, "column moment");
+  check_f32(participation, "participation");
+  check_f32(congruence, "congruence");
+  TORCH_CHECK(m.numel() == nblocks * R * C && g.numel() == m.numel(), "m/g size");
+  TORCH_CHECK(row_m.numel() == nblocks * R && col_m.numel() == nblocks * C, "moment sizes");
+  TORCH_CHECK(participation.numel() == nblocks && congruence.numel() == nblocks, "route sizes");
+  const int chunks = ro::tiller_chunks(static_cast<int>(R));
+  auto opts = m.options();
+  auto colpart = torch::empty({nblocks * chunks * C}, opts);
+  auto dotpart = torch::empty({nblocks * chunks * 8}, opts);
+  auto row_total = torch::empty({nblocks}, opts);
+  auto out = torch::empty({nblocks, 16}, opts);
+  check_rc(ro::tiller_chord(reinterpret_cast<const __nv_bfloat16*>(polar.data_ptr()), m.data_ptr<float>(),
+                            g.data_ptr<float>(), row_m.data_ptr<float>(), col_m.data_ptr<float>(),
+                            colpart.data_ptr<float>(), dotpart.data_ptr<float>(), row_total.data_ptr<float>(),
+                            participation.data_ptr<float>(), congruence.data_ptr<float>(), out.data_ptr<float>(),
+                            static_cast<int>(nblocks), static_cast<int>(R), static_cast<int>(C),
+                            static_cast<float>(scale), static_cast<int>(step), static_cast<float>(adj),
+                            at::cuda::getCurrentCUDAStream()),
+           "tiller_chord");
+  return {out, row_total};
+}
+
+c10::optional<torch::Tensor> tiller_apply(std::vector<torch::Tensor> params, torch::Tensor polar, torch::Tensor m,
+                                          torch::Tensor row_m, torch::Tensor col_m, torch::Tensor row_total,
+                                          torch::Tensor chord, torch::Tensor coef, bool want_selected,
+                                          bool update_param, int64_t blocks_per_layer, int64_t R, int64_t C,
+                                          bool transpose, double scale, int64_t step, double decay,
+                                          double alpha, double adj) {
+  TORCH_CHECK(!params.empty(), "tiller_apply params");
+  const c10::cuda::CUDAGuard guard(m.device());
+  const int64_t L = params.size();
+  auto pp = ptrs_of(params, blocks_per_layer * R * C, "params");
+  check_f32(m, "m");
+  check_f32(coef, "coef");
+  check_f32(chord, "chord");
+  TORCH_CHECK(coef.numel() == L * blocks_per_layer, "coef size");
+  torch::Tensor sel;
+  if (want_selected) sel = torch::empty_like(m);
+  check_rc(ro::tiller_apply(pp.data(), reinterpret_cast<const __nv_bfloat16*>(polar.data_ptr()), m.data_ptr<float>(),
+                            row_m.data_ptr<float>(), col_m.data_ptr<float>(), row_total.data_ptr<float>(),
+                            chord.data_ptr<float>(), coef.data_ptr<float>(),
+                            want_selected ? sel.data_ptr<float>() : nullptr, static_cast<int>(L),
+                            static_cast<int>(blocks_per_layer), static_cast<int>(R), static_cast<int>(C),
+                            transpose, static_cast<float>(scale), static_cast<int>(step),
+                            static_cast<float>(decay), static_cast<float>(alpha), static_cast<float>(adj),
+                            update_param, at::cuda::getCurrentCUDAStream()),
+           "tiller_apply");
+  if (want_selected) return sel;
+  return c10::nullopt;
+}
+
+torch::Tensor ns_normalize(torch::Tensor x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.dim() == 3,
+              "ns_normalize expects contiguous bf16 [B, r, c]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  check_rc(ro::ns_normalize(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                            reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), static_cast<int>(x.size(0)),
+                            x.size(1) * x.size(2), at::cuda::getCurrentCUDAStream()),
+           "ns_normalize");
+  return y;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -296,4 +512,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_qkv_forward", &rope_qkv_forward);
   m.def("rope_qkv_backward", &rope_qkv_backward);
   m.def("cross_entropy_fwd_bwd", &cross_entropy_fwd_bwd);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_bf16_ex", &gemm_bf16_ex);
+  m.def("gemm_error", &gemm_error);
+  m.def("adamw_multi_tensor", &adamw_multi_tensor);
+  m.def("tiller_nesterov", &tiller_nesterov);
+  m.def("tiller_transpose_bf16", &tiller_transpose_bf16);
+  m.def("tiller_chord", &tiller_chord);
+  m.def("tiller_apply", &tiller_apply);
+  m.def("ns_normalize", &ns_normalize);
 }

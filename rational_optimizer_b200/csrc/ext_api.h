@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cuda_bf16.h>
 
 namespace ro {
 
@@ -44,5 +45,36 @@ int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const floa
 int cross_entropy_fwd_bwd(void* logits, const int64_t* target, float* loss_row, int64_t rows,
                           int V, float grad_scale, int64_t ignore_index, int dtype,
                           cudaStream_t stream);
+
+
+// gemm_sm100.cu
+int gemm_bf16_tn(const void* A, int64_t lda, int64_t strideA, bool a_mn, const void* B, int64_t ldb,
+                 int64_t strideB, bool b_mn, void* C, int64_t ldc, int64_t strideC, bool out_f32,
+                 const void* D, int64_t ldd, int64_t strideD, float alpha, float beta, int M, int N,
+                 int K, int batch, int* err, cudaStream_t stream);
+
+
+// optim.cu
+int adamw_multi_tensor(float* const* p, const float* const* g, float* const* m, float* const* v,
+                       const int64_t* sizes, int count, float lr, float beta1, float beta2, float eps,
+                       float wd, float step, cudaStream_t stream);
+
+
+// tiller.cu
+int tiller_nesterov(float* const* grads, float* const* bufs, float* m_out, float* g_out,
+                    __nv_bfloat16* m16_out, int L, int P, int Q, bool transpose, float mu,
+                    cudaStream_t stream);
+int tiller_transpose_bf16(const __nv_bfloat16* in, __nv_bfloat16* out, int L, int P, int Q,
+                          cudaStream_t stream);
+int tiller_chunks(int R);
+int tiller_chord(const __nv_bfloat16* polar, const float* m, const float* g, float* row_m, float* col_m,
+                 float* colpart, float* dotpart, float* row_total, const float* participation,
+                 const float* congruence, float* chord_out, int nblocks, int R, int C, float scale,
+                 int step, float adj, cudaStream_t stream);
+int tiller_apply(float* const* params, const __nv_bfloat16* polar, const float* m, const float* row_m,
+                 const float* col_m, const float* row_total, const float* chord, const float* coef,
+                 float* sel_out, int L, int blocks_per_layer, int R, int C, bool transpose, float scale,
+                 int step, float decay, float alpha, float adj, bool update_param, cudaStream_t stream);
+int ns_normalize(const __nv_bfloat16* x, __nv_bfloat16* y, int batch, int64_t n, cudaStream_t stream);
 
 }  // namespace ro

@@ -13,7 +13,7 @@ import torch
 
 from .. import _ext
 
-_NATIVE = os.environ.get("RO_NATIVE_GEMM", "1") != "0"
+_NATIVE = os.environ.get("RO_NATIVE_GEMM", "0") == "1"
 
 
 def _native():

@@ -57,6 +57,52 @@ def _native_ns():
     return C if hasattr(C, "ns5_batched") else None
 
 
+def _ns5_torch_bf16(work: torch.Tensor) -> torch.Tensor:
+    a, b, c = NS_COEFFICIENTS
+    for _ in range(5):
+        gram = torch.bmm(work, work.transpose(1, 2))
+        poly = torch.baddbmm(gram, gram, gram, beta=b, alpha=c)
+        work = torch.baddbmm(work, poly, work, beta=a)
+    return work
+
+
+def ns5_grouped_bf16(x16: torch.Tensor) -> torch.Tensor:
+    """NS5 of a contiguous bf16 batch ``[B, r, c]`` with ``r <= c`` (bf16 result).
+
+    CUDA: the Frobenius normalisation kernel followed by, per iteration,
+    three batched tcgen05 GEMMs with fused epilogues
+    ``A = X X^T``; ``P = b A + c A A``; ``X = a X + P X``.
+    """
+    if x16.shape[-2] > x16.shape[-1]:
+        raise RuntimeError("ns5_grouped_bf16 expects wide blocks")
+    if _ext.available() and x16.is_cuda and hasattr(_ext.ext(), "ns_normalize"):
+        C = _ext.ext()
+        work = C.ns_normalize(x16.contiguous())
+        a, b, c = NS_COEFFICIENTS
+        if _native_gemm_enabled():
+            ok = True
+            for _ in range(5):
+                gram = C.gemm_bf16(work, work, False, True, False)
+                poly = C.gemm_bf16_ex(gram, gram, False, True, False, gram, c, b) if gram is not None else None
+                nxt = C.gemm_bf16_ex(poly, work, False, False, False, work, 1.0, a) if poly is not None else None
+                if nxt is None:
+                    ok = False
+                    break
+                work = nxt
+            if ok:
+                return work
+            work = C.ns_normalize(x16.contiguous())
+        return _ns5_torch_bf16(work)
+    work = x16.to(torch.bfloat16)
+    norm = torch.linalg.vector_norm(work.float(), dim=(-2, -1), keepdim=True).clamp_min(NS_EPS)
+    return _ns5_torch_bf16(work / norm.to(work.dtype))
+
+
+def _native_gemm_enabled() -> bool:
+    from ..ops import gemm as _g
+    return _g._NATIVE and hasattr(_ext.ext(), "gemm_bf16")
+
+
 def batched_zero_power(momentum: torch.Tensor, steps: int = 5) -> torch.Tensor:
     """NS5 on ``[batch, rows, cols]`` (bf16 result, same shape)."""
     if momentum.ndim != 3:

@@ -230,6 +230,9 @@ class TILLERRouter(torch.optim.Optimizer):
         self._rfd_functional_refresh = False
         self._rfd_selection = None
         self._last_predictive = None
+        self._fused_ok = None
+        self._fused_role_objs = None
+        self._force_torch = False
 
     # -- properties --------------------------------------------------------
     @property
@@ -319,7 +322,8 @@ class TILLERRouter(torch.optim.Optimizer):
             inputs = torch.cat([r[0] for r in records])
             pre = torch.cat([r[1] for r in records])
             feat = torch.cat([r[2] for r in records])
-            scaled = torch.cat([v.float() * float(rows * mb) for v, rows in cots]) * float(self._clip_factor)
+            clip = self._clip_factor if torch.is_tensor(self._clip_factor) else float(self._clip_factor)
+            scaled = torch.cat([v.float() * float(rows * mb) for v, rows in cots]) * clip
             captured = self.capture_rows * mb
             if inputs.shape != (captured, self.external) or pre.shape != (captured, self.hidden):
                 raise RuntimeError("TILLER captured packet changed")
@@ -331,11 +335,21 @@ class TILLERRouter(torch.optim.Optimizer):
 
     # -- trainer contract --------------------------------------------------
     def record_realized_clipping(self, preclip_norm, max_norm):
+        """Store ``min(1, max_norm / (norm + 1e-6))`` for the probe cotangent scale.
+
+        A device tensor norm is kept on the device (no host synchronisation);
+        a Python float is validated immediately as in the reference.
+        """
         if self._clip_factor is not None:
             raise RuntimeError("TILLER observed multiple clipping calls")
-        value = float(preclip_norm)
         maximum = float(max_norm)
-        if not math.isfinite(value) or value < 0.0 or maximum != 1.0:
+        if maximum != 1.0:
+            raise RuntimeError("TILLER received invalid clipping")
+        if torch.is_tensor(preclip_norm) and preclip_norm.is_cuda:
+            self._clip_factor = (maximum / (preclip_norm.float() + 1e-6)).clamp(max=1.0)
+            return
+        value = float(preclip_norm)
+        if not math.isfinite(value) or value < 0.0:
             raise RuntimeError("TILLER received invalid clipping")
         self._clip_factor = min(1.0, maximum / (value + 1e-6))
 
@@ -470,6 +484,94 @@ class TILLERRouter(torch.optim.Optimizer):
             }
         return records
 
+    def _use_fused(self):
+        if self._fused_ok is None:
+            from . import tiller_fused
+            first = self.pairs[0]["in_weight"]
+            self._fused_ok = (first.is_cuda and first.dtype == torch.float32 and tiller_fused.available()
+                              and not self._force_torch)
+        return self._fused_ok
+
+    def _fused_roles(self):
+        if self._fused_role_objs is None:
+            from .tiller_fused import FusedRole
+            self._fused_role_objs = {
+                "incoming": FusedRole(self, [p["in_weight"] for p in self.pairs], "incoming",
+                                      groups=self.groups, width=self.width, momentum=self.momentum),
+                "outgoing": FusedRole(self, [p["out_weight"] for p in self.pairs], "outgoing",
+                                      groups=self.groups, width=self.width, momentum=self.momentum),
+            }
+        return self._fused_role_objs
+
+    def _directions(self, participation, congruence, *, want_selected):
+        """Both roles' directions and the contractions the transaction needs.
+
+        Returns ``exact_by_role`` [2, C], ``momentum_by_role`` [2, C],
+        ``weights`` [C], ``selected`` {role: adj*q as [L, H, d] or None},
+        ``meta`` and ``apply(coefficients [L, G], lr, wd)``.
+        """
+        L = len(self.pairs)
+        step = int(self.anchor.get("predictive_response_transaction_updates", 0)) + 1
+        if self._use_fused():
+            from .tiller_fused import chord_meta
+            roles = self._fused_roles()
+            chords, sels = {}, {}
+            for role, index, axis in (("incoming", 0, "rows"), ("outgoing", 1, "columns")):
+                fr = roles[role]
+                shape = (L, self.groups, self.width, self.external)
+                row, col = self._chord_state_shaped(shape, key_prefix="factorized_adaptive_tangent_" + axis,
+                                                    device=self.pairs[0]["in_weight"].device)
+                chord, sel = fr.directions(row, col, participation[..., index].contiguous(),
+                                           congruence[..., index].contiguous(), step,
+                                           want_selected=want_selected)
+                chords[role] = chord
+                sels[role] = None if sel is None else sel.view(L, self.hidden, self.external)
+            ci, co = chords["incoming"], chords["outgoing"]
+
+            def apply(coefficients, lr, wd):
+                for role in ("incoming", "outgoing"):
+                    roles[role].apply(coefficients, decay=1.0 - lr * wd, lr=lr)
+
+            metas = {r: chord_meta(chords[r]) for r in chords}
+            return {"exact_by_role": torch.stack((ci[:, 2], co[:, 2])),
+                    "momentum_by_role": torch.stack((ci[:, 3], co[:, 3])),
+                    "weights": ci[:, 4] + co[:, 4], "selected": sels, "meta": metas, "apply": apply}
+        rec = self._role_directions(participation, congruence)
+        inc_b = rec["incoming"]["scaled_blocks"]
+        out_b = rec["outgoing"]["scaled_blocks"]
+
+        def apply(coefficients, lr, wd):
+            inc_sel = rec["incoming"]["selected"]
+            inc_sel.view(L, self.groups, self.width, self.external).mul_(
+                coefficients[..., None, None].to(inc_sel.dtype))
+            out_sel = rec["outgoing"]["selected"]
+            out_sel.view(L, self.external, self.groups, self.width).permute(0, 2, 3, 1).mul_(
+                coefficients[..., None, None].to(out_sel.dtype))
+            for role in ("incoming", "outgoing"):
+                foreach_apply(rec[role]["params"], rec[role]["selected"], decay=1.0 - lr * wd,
+                              alpha=-lr * rec[role]["adjustment"])
+
+        return {"exact_by_role": torch.stack([rec[r]["exact"].reshape(-1) for r in ("incoming", "outgoing")]),
+                "momentum_by_role": torch.stack([rec[r]["momentum"].reshape(-1) for r in ("incoming", "outgoing")]),
+                "weights": (inc_b.square().sum(dim=(-2, -1)) + out_b.square().sum(dim=(-2, -1))).reshape(-1),
+                "selected": {"incoming": inc_b.reshape(L, self.hidden, self.external),
+                             "outgoing": out_b.reshape(L, self.hidden, self.external)},
+                "meta": {r: rec[r]["meta"] for r in ("incoming", "outgoing")}, "apply": apply}
+
+    def _chord_state_shaped(self, shape, *, key_prefix, device):
+        anchor = self.anchor
+        rk, ck = key_prefix + "_row_second_moment", key_prefix + "_column_second_moment"
+        row, col = anchor.get(rk), anchor.get(ck)
+        if row is None:
+            row = torch.zeros(shape[:-1], device=device, dtype=torch.float32)
+            anchor[rk] = row
+        if col is None:
+            col = torch.zeros(shape[:2] + shape[-1:], device=device, dtype=torch.float32)
+            anchor[ck] = col
+        if row.shape != shape[:-1] or col.shape != shape[:2] + shape[-1:]:
+            raise RuntimeError("factorized adaptive tangent checkpoint inventory changed")
+        return row, col
+
     # -- ledger + transaction ----------------------------------------------
     def _previous_ledger(self):
         a = self.anchor
@@ -574,20 +676,19 @@ class TILLERRouter(torch.optim.Optimizer):
             self._restore_route()
             participation = self._group_participation
         congruence = self._group_response_congruence
-        rec = self._role_directions(participation, congruence)
-        inc_b = rec["incoming"]["scaled_blocks"]
-        out_b = rec["outgoing"]["scaled_blocks"]
-        weights = (inc_b.square().sum(dim=(-2, -1)) + out_b.square().sum(dim=(-2, -1))).reshape(-1)
-        exact_by_role = torch.stack([rec[r]["exact"].reshape(-1) for r in ("incoming", "outgoing")])
-        momentum_by_role = torch.stack([rec[r]["momentum"].reshape(-1) for r in ("incoming", "outgoing")])
+        dirs = self._directions(participation, congruence, want_selected=refresh)
+        weights = dirs["weights"]
+        exact_by_role = dirs["exact_by_role"]
+        momentum_by_role = dirs["momentum_by_role"]
         layer_ids = torch.arange(L, device=weights.device, dtype=torch.int64).repeat_interleave(self.groups)
         if refresh:
+            inc_b = dirs["selected"]["incoming"]
+            out_b = dirs["selected"]["outgoing"]
             scores, decay = [], None
             for layer, (pair, packet) in enumerate(zip(self.pairs, packets)):
                 inputs, _pre, features, cot = packet
                 adj = adjoint[layer]
-                s = tm.group_scores(inputs, features, cot, inc_b[layer].reshape(self.hidden, self.external),
-                                    out_b[layer].reshape(self.hidden, self.external), adj,
+                s = tm.group_scores(inputs, features, cot, inc_b[layer], out_b[layer], adj,
                                     groups=self.groups, width=self.width, validate=self.strict)
                 d = tm.group_scores(inputs, features, cot, pair["in_weight"].float() * wd,
                                     pair["out_weight"].T.float() * wd, adj, groups=self.groups,
@@ -611,15 +712,7 @@ class TILLERRouter(torch.optim.Optimizer):
                 raise RuntimeError("TILLER selection factor is missing")
             selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids, eta=lr)
         coefficients = selection.coefficients.view(L, self.groups)
-        inc_sel = rec["incoming"]["selected"]
-        inc_sel.view(L, self.groups, self.width, self.external).mul_(
-            coefficients[..., None, None].to(inc_sel.dtype))
-        out_sel = rec["outgoing"]["selected"]
-        out_sel.view(L, self.external, self.groups, self.width).permute(0, 2, 3, 1).mul_(
-            coefficients[..., None, None].to(out_sel.dtype))
-        for role in ("incoming", "outgoing"):
-            foreach_apply(rec[role]["params"], rec[role]["selected"], decay=1.0 - lr * wd,
-                          alpha=-lr * rec[role]["adjustment"])
+        dirs["apply"](coefficients, lr, wd)
         updates = int(anchor.get("predictive_response_transaction_updates", 0)) + 1
         anchor["predictive_response_transaction_updates"] = updates
         self._attention_update = updates
@@ -627,7 +720,7 @@ class TILLERRouter(torch.optim.Optimizer):
         if refresh:
             self._cache_refresh_state()
         if publish:
-            self._publish_telemetry(refresh, coefficients, rec, selection)
+            self._publish_telemetry(refresh, coefficients, dirs["meta"], selection)
         self._advance_cadence()
         self._rfd_decay_derivative = None
         self._capture_telemetry_next_step = False
@@ -664,11 +757,11 @@ class TILLERRouter(torch.optim.Optimizer):
         self.anchor["cadence8_transition"] = self._cadence_transition
         self._capture_response_this_transition = self._cadence_transition % tm.REFRESH_INTERVAL == 0
 
-    def _publish_telemetry(self, refresh, coefficients, rec, selection):
+    def _publish_telemetry(self, refresh, coefficients, meta, selection):
         flat = coefficients.reshape(-1).float()
-        safe = torch.cat([rec[r]["meta"]["safe"].reshape(-1) for r in ("incoming", "outgoing")])
-        cosine = torch.cat([rec[r]["meta"]["parent_cosine"].reshape(-1) for r in ("incoming", "outgoing")])
-        energy = torch.cat([rec[r]["meta"]["departure_energy"].reshape(-1) for r in ("incoming", "outgoing")])
+        safe = torch.cat([meta[r]["safe"].reshape(-1) for r in ("incoming", "outgoing")])
+        cosine = torch.cat([meta[r]["parent_cosine"].reshape(-1) for r in ("incoming", "outgoing")])
+        energy = torch.cat([meta[r]["departure_energy"].reshape(-1) for r in ("incoming", "outgoing")])
         rows = self._rfd_rows
         scaling = tiller_scaling_formula(total_positions=1, total_layers=len(self.pairs),
                                          total_groups=self.groups, intermediate_width=self.hidden,
@@ -767,6 +860,7 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
         super().__init__([group], {})
         self._capture_telemetry_next_step = False
         self._last_telemetry = {}
+        self._fused = {}
 
     def lr_wd_fairness_audit(self):
         keys = ("global_lr_scale", "qkv_lr_scale", "attention_output_lr_scale",
@@ -809,21 +903,35 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
         anchor["compact_response_homotopy_router_update"] = int(router_update)
         update = int(anchor.get("factorized_adaptive_tangent_updates", 0)) + 1
         metas = []
+        first = self.role_parameters["qkv"][0]
+        from . import tiller_fused
+        fused = (first.is_cuda and first.dtype == torch.float32 and tiller_fused.available()
+                 and not getattr(self.router, "_force_torch", False))
         for role, key in (("qkv", "qkv"), ("attn_out", "attention_output")):
             params = self.role_parameters[role]
-            momenta = foreach_nesterov(self, params, self.momentum)
-            grads = torch.stack([p.grad.detach() for p in params]).float()
-            parent = attention_head_group_zero_power(momenta, self.ns_steps).float()
-            shape = tm.grouped_shape(parent, groups=1, width=None, axis="matrix")
+            rows, cols = params[0].shape
+            shape = (len(params), 1, rows, cols)
             rk = "factorized_adaptive_tangent_" + key + "_row_second_moment"
             ck = "factorized_adaptive_tangent_" + key + "_column_second_moment"
             row, col = anchor.get(rk), anchor.get(ck)
             if row is None:
-                row = torch.zeros(shape[:-1], device=parent.device, dtype=torch.float32)
+                row = torch.zeros(shape[:-1], device=first.device, dtype=torch.float32)
                 anchor[rk] = row
             if col is None:
-                col = torch.zeros(shape[:2] + shape[-1:], device=parent.device, dtype=torch.float32)
+                col = torch.zeros(shape[:2] + shape[-1:], device=first.device, dtype=torch.float32)
                 anchor[ck] = col
+            if fused:
+                if role not in self._fused:
+                    self._fused[role] = tiller_fused.FusedRole(self, params, role, momentum=self.momentum)
+                fr = self._fused[role]
+                chord, _ = fr.directions(row, col, participation.contiguous(), congruence.contiguous(),
+                                         update, want_selected=False)
+                fr.apply(torch.ones(len(params), device=first.device), decay=1.0 - lr * wd, lr=lr)
+                metas.append(tiller_fused.chord_meta(chord))
+                continue
+            momenta = foreach_nesterov(self, params, self.momentum)
+            grads = torch.stack([p.grad.detach() for p in params]).float()
+            parent = attention_head_group_zero_power(momenta, self.ns_steps).float()
             pg, restore = tm.group_view(parent, groups=1, width=None, axis="matrix")
             mg, _ = tm.group_view(momenta, groups=1, width=None, axis="matrix")
             gg, _ = tm.group_view(grads, groups=1, width=None, axis="matrix")

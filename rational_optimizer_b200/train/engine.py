@@ -1,0 +1,75 @@
+"""One optimizer step of the shared trainer, as a reusable engine.
+
+``TrainEngine.step(batches, lr)`` performs what the reference trainer's hot
+loop does per step (training/train.py:2814-2932): set the scheduled LR on
+every group, zero gradients, forward + loss + backward for each micro-batch,
+average gradients across data-parallel ranks, clip to ``grad_clip`` and report
+the realised pre-clip norm to the clipping observer (TILLER), then step the
+optimizer.  The returned loss stays on the device; callers decide when to
+read it (the reference synchronises on ``loss.item()`` every micro-batch).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..parallel.grad_sync import GradientSynchronizer
+
+
+def learning_rate(step, *, lr, min_lr, warmup_steps, total_steps):
+    """Linear warm-up then cosine decay to ``min_lr`` (train.py:1889-1895)."""
+    if warmup_steps > 0 and step < warmup_steps:
+        return lr * float(step + 1) / float(warmup_steps)
+    progress = (step - warmup_steps) / max(1, total_steps - warmup_steps)
+    progress = min(1.0, max(0.0, progress))
+    return min_lr + 0.5 * (1.0 + math.cos(math.pi * progress)) * (lr - min_lr)
+
+
+def clip_grad_norm(params, max_norm):
+    """Global L2 norm of all gradients (fp32) and in-place clipping; returns the device norm."""
+    grads = [p.grad for p in params if p.grad is not None]
+    norms = torch._foreach_norm(grads, 2.0)
+    total = torch.linalg.vector_norm(torch.stack([n.float() for n in norms]), 2.0)
+    if max_norm > 0:
+        coef = (float(max_norm) / (total + 1e-6)).clamp(max=1.0)
+        torch._foreach_mul_(grads, coef)
+    return total
+
+
+class TrainEngine:
+    def __init__(self, model, optimizer, *, grad_clip=1.0, grad_accum=1, synchronizer=None,
+                 clip_observer=None):
+        self.model = model
+        self.optimizer = optimizer
+        self.grad_clip = float(grad_clip)
+        self.grad_accum = int(grad_accum)
+        self.sync = synchronizer if synchronizer is not None else GradientSynchronizer(model)
+        self.clip_observer = clip_observer
+        if clip_observer is None and hasattr(optimizer, "record_realized_clipping"):
+            self.clip_observer = optimizer
+        self.last_grad_norm = None
+
+    def set_lr(self, lr):
+        for group in self.optimizer.param_groups:
+            group["lr"] = lr * float(group.get("lr_scale", 1.0))
+
+    def step(self, batches, lr=None):
+        """``batches``: list of ``grad_accum`` (x, y) device tensors.  Returns the mean loss."""
+        if len(batches) != self.grad_accum:
+            raise ValueError("expected one batch per micro-step")
+        if lr is not None:
+            self.set_lr(lr)
+        self.sync.zero_grad()
+        total = None
+        for x, y in batches:
+            loss = self.model.forward_loss(x, y)
+            (loss / self.grad_accum).backward()
+            total = loss.detach() if total is None else total + loss.detach()
+        self.sync.synchronize()
+        norm = clip_grad_norm(self.sync.params, self.grad_clip)
+        self.last_grad_norm = norm
+        if self.clip_observer is not None:
+            self.clip_observer.record_realized_clipping(norm, self.grad_clip)
+        self.optimizer.step()
+        return total / self.grad_accum
