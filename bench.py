@@ -172,11 +172,7 @@ def run_ours(a, info):
         for p in model.parameters():
             dist.broadcast(p.data, 0)
     optimizer = composite.configure_optimizer(model, args)
-    comm = None
-    if world > 1:
-        from rational_optimizer_b200.parallel.comm import maybe_communicator
-        comm = maybe_communicator(device)
-    sync = GradientSynchronizer(model, communicator=comm)
+    sync = GradientSynchronizer(model)
     engine = TrainEngine(model, optimizer, grad_clip=1.0, grad_accum=1, synchronizer=sync)
     tokens = zipf_tokens(ZIPF_TOKENS, VOCAB, alpha=1.1, seed=0)
     batcher = PinnedBatcher(tokens, local_batch, SEQ, seed=0, rank=info.rank)
@@ -212,7 +208,9 @@ def run_ours(a, info):
         own, total = count_own_launches(device_step)
         launches = {"own_per_step": own, "all_per_step": total}
     loss = float(engine.step([staged[0]], lr=3e-4).item())
-    return ms, e2e_ms, clocks, launches, loss, batcher.bytes_per_batch
+    if sync.communicator is not None:
+        sync.communicator.check()
+    return ms, e2e_ms, clocks, launches, loss, batcher.bytes_per_batch, sync.transport
 
 
 def run_reference(a, info):
@@ -323,7 +321,7 @@ def main():
                 "config": cfg, "clocks": clocks}), flush=True)
         cleanup_distributed(info)
         return
-    ms, e2e_ms, clocks, launches, loss, h2d = run_ours(a, info)
+    ms, e2e_ms, clocks, launches, loss, h2d, transport = run_ours(a, info)
     value = tokens_per_step / (ms / 1000.0)
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
@@ -332,6 +330,7 @@ def main():
         "data": "synthetic Zipf(1.1) token ids, seed 0; random-init weights",
         "config": cfg, "clocks": clocks, "final_loss": loss,
     }
+    out["config"]["grad_transport"] = transport
     if e2e_ms is not None:
         out["e2e"] = {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                       "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4}

@@ -8,6 +8,8 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <cuda_runtime.h>
+#include <cstring>
+#include <string>
 #include <vector>
 
 #include "ext_api.h"
@@ -222,6 +224,64 @@ std::vector<torch::Tensor> rmsnorm_backward(torch::Tensor dy, torch::Tensor x, t
                                 static_cast<int>(d), dtype_code(x, "x"), dtype_code(dy, "dy"), 0, stream()),
            "rmsnorm_backward");
   return {dx, dw};
+}
+
+// Fused residual add + RMSNorm.  x fp32 [rows, d]; delta bf16 or None.
+// Returns (x_new fp32, y bf16, rstd).  With delta None, x_new is x itself.
+std::vector<torch::Tensor> add_rmsnorm_forward(torch::Tensor x, c10::optional<torch::Tensor> delta,
+                                               torch::Tensor w, double eps) {
+  check_f32(x, "x");
+  check_f32(w, "weight");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t d = x.size(-1);
+  const int64_t rows = x.numel() / d;
+  torch::Tensor x_new = x;
+  const void* dptr = nullptr;
+  if (delta.has_value()) {
+    check_cuda(*delta, "delta");
+    TORCH_CHECK(delta->scalar_type() == torch::kBFloat16 && delta->numel() == x.numel(), "delta must be bf16 like x");
+    dptr = delta->data_ptr();
+    x_new = torch::empty_like(x);
+  }
+  auto y = torch::empty(x.sizes(), x.options().dtype(torch::kBFloat16));
+  auto rstd = torch::empty({rows}, x.options());
+  check_rc(ro::add_rmsnorm_forward(x.data_ptr<float>(), dptr, w.data_ptr<float>(), x_new.data_ptr<float>(),
+                                   y.data_ptr(), rstd.data_ptr<float>(), rows, static_cast<int>(d),
+                                   static_cast<float>(eps), at::cuda::getCurrentCUDAStream()),
+           "add_rmsnorm_forward");
+  return {x_new, y, rstd};
+}
+
+// Returns (dx fp32, ddelta bf16 or undefined, dw).
+std::vector<torch::Tensor> add_rmsnorm_backward(torch::Tensor dy, c10::optional<torch::Tensor> dres,
+                                                torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
+                                                bool want_ddelta) {
+  check_cuda(dy, "dy");
+  check_f32(x, "x");
+  check_f32(w, "weight");
+  check_f32(rstd, "rstd");
+  TORCH_CHECK(dy.scalar_type() == torch::kBFloat16 && dy.numel() == x.numel(), "dy must be bf16 like x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t d = x.size(-1);
+  const int64_t rows = x.numel() / d;
+  const float* rp = nullptr;
+  if (dres.has_value()) {
+    check_f32(*dres, "dres");
+    rp = dres->data_ptr<float>();
+  }
+  auto dx = torch::empty_like(x);
+  torch::Tensor dd;
+  if (want_ddelta) dd = torch::empty(x.sizes(), x.options().dtype(torch::kBFloat16));
+  auto dw = torch::empty_like(w);
+  auto partial = torch::empty({std::max<int64_t>(1, ro::rmsnorm_backward_partial_size(rows, static_cast<int>(d)))},
+                              x.options());
+  check_rc(ro::add_rmsnorm_backward(dy.data_ptr(), rp, x.data_ptr<float>(), w.data_ptr<float>(),
+                                    rstd.data_ptr<float>(), dx.data_ptr<float>(),
+                                    want_ddelta ? dd.data_ptr() : nullptr, dw.data_ptr<float>(),
+                                    partial.data_ptr<float>(), rows, static_cast<int>(d),
+                                    at::cuda::getCurrentCUDAStream()),
+           "add_rmsnorm_backward");
+  return {dx, dd, dw};
 }
 
 std::vector<torch::Tensor> rope_qkv_forward(torch::Tensor qkv, torch::Tensor cos_t,
@@ -498,6 +558,148 @@ torch::Tensor ns_normalize(torch::Tensor x) {
   return y;
 }
 
+// ---------------------------------------------------------------------------
+// NVLink peer-memory collectives.
+
+torch::Tensor comm_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void* ptr = nullptr;
+  const cudaError_t e = cudaMalloc(&ptr, static_cast<size_t>(nbytes));
+  TORCH_CHECK(e == cudaSuccess, "comm_alloc: ", cudaGetErrorString(e));
+  TORCH_CHECK(cudaMemset(ptr, 0, static_cast<size_t>(nbytes)) == cudaSuccess, "comm_alloc memset");
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  return torch::from_blob(ptr, {nbytes}, [device](void* p) {
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+    cudaFree(p);
+  }, opts);
+}
+
+py::bytes comm_handle(torch::Tensor base) {
+  char h[64];
+  check_rc(ro::comm_ipc_handle(base.data_ptr(), h), "cudaIpcGetMemHandle");
+  return py::bytes(h, 64);
+}
+
+int64_t comm_open(py::bytes handle, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  std::string s = handle;
+  TORCH_CHECK(s.size() == 64, "IPC handle must be 64 bytes");
+  void* ptr = nullptr;
+  check_rc(ro::comm_ipc_open(s.data(), &ptr), "cudaIpcOpenMemHandle");
+  return reinterpret_cast<int64_t>(ptr);
+}
+
+void comm_close(int64_t ptr) { ro::comm_ipc_close(reinterpret_cast<void*>(ptr)); }
+
+std::vector<void*> as_ptrs(const std::vector<int64_t>& v) {
+  std::vector<void*> out;
+  for (auto x : v) out.push_back(reinterpret_cast<void*>(x));
+  return out;
+}
+
+std::vector<unsigned int*> as_flag_ptrs(const std::vector<int64_t>& v) {
+  std::vector<unsigned int*> out;
+  for (auto x : v) out.push_back(reinterpret_cast<unsigned int*>(x));
+  return out;
+}
+
+void comm_allreduce_f32(std::vector<int64_t> data, std::vector<int64_t> flags, int64_t rank, int64_t n,
+                        double scale, int64_t epoch, torch::Tensor err, int64_t timeout_ns) {
+  TORCH_CHECK(data.size() == flags.size(), "data/flag lists differ");
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == torch::kInt32, "err must be a CUDA int32 tensor");
+  const c10::cuda::CUDAGuard guard(err.device());
+  auto d = as_ptrs(data);
+  auto f = as_flag_ptrs(flags);
+  check_rc(ro::comm_allreduce_f32(d.data(), f.data(), static_cast<int>(rank), static_cast<int>(data.size()), n,
+                                  static_cast<float>(scale), static_cast<unsigned int>(epoch), err.data_ptr<int>(),
+                                  static_cast<uint64_t>(timeout_ns), at::cuda::getCurrentCUDAStream()),
+           "comm_allreduce_f32");
+}
+
+void comm_allreduce_i8(torch::Tensor src, torch::Tensor out, std::vector<int64_t> data, std::vector<int64_t> flags,
+                       int64_t rank, double scale, int64_t epoch, torch::Tensor err, int64_t timeout_ns) {
+  check_f32(src, "src");
+  check_f32(out, "out");
+  TORCH_CHECK(src.numel() == out.numel(), "src/out sizes");
+  const c10::cuda::CUDAGuard guard(src.device());
+  auto d = as_ptrs(data);
+  auto f = as_flag_ptrs(flags);
+  check_rc(ro::comm_allreduce_i8(src.data_ptr<float>(), out.data_ptr<float>(), d.data(), f.data(),
+                                 static_cast<int>(rank), static_cast<int>(data.size()), src.numel(),
+                                 static_cast<float>(scale), static_cast<unsigned int>(epoch), err.data_ptr<int>(),
+                                 static_cast<uint64_t>(timeout_ns), at::cuda::getCurrentCUDAStream()),
+           "comm_allreduce_i8");
+}
+
+int64_t comm_i8_bytes(int64_t n) { return ro::comm_i8_bytes(n); }
+
+void comm_wait_only(std::vector<int64_t> data, std::vector<int64_t> flags, int64_t rank, int64_t epoch,
+                    torch::Tensor err, int64_t timeout_ns) {
+  const c10::cuda::CUDAGuard guard(err.device());
+  auto d = as_ptrs(data);
+  auto f = as_flag_ptrs(flags);
+  check_rc(ro::comm_wait_only(d.data(), f.data(), static_cast<int>(rank), static_cast<int>(data.size()),
+                              static_cast<unsigned int>(epoch), err.data_ptr<int>(),
+                              static_cast<uint64_t>(timeout_ns), at::cuda::getCurrentCUDAStream()),
+           "comm_wait_only");
+}
+
+// ---------------------------------------------------------------------------
+// TILLER ledger + transaction (single CTA, fp64).
+// state: dict-like tensors; scal: fp32 [8] = [tail, discarded_fraction, shrinkage, ref_row_norm, ...]
+
+std::vector<torch::Tensor> tiller_ledger_transaction(
+    c10::optional<torch::Tensor> cur_scores, c10::optional<torch::Tensor> cur_decay, torch::Tensor exact,
+    torch::Tensor momentum, torch::Tensor weights, torch::Tensor layer_ids,
+    c10::optional<torch::Tensor> decay_derivative, torch::Tensor pers_scores, torch::Tensor pers_total_diag,
+    torch::Tensor pers_decay_cross, torch::Tensor scal, torch::Tensor ws, int64_t prev_rows,
+    int64_t total_layers, double eta) {
+  const c10::cuda::CUDAGuard guard(exact.device());
+  check_f32(exact, "exact");
+  check_f32(momentum, "momentum");
+  check_f32(weights, "weights");
+  check_f32(pers_scores, "persistent scores");
+  check_f32(pers_total_diag, "persistent diagonal");
+  check_f32(pers_decay_cross, "persistent decay cross");
+  check_f32(scal, "ledger scalars");
+  TORCH_CHECK(layer_ids.is_cuda() && layer_ids.scalar_type() == torch::kInt64, "layer ids must be int64 CUDA");
+  const int64_t C = weights.numel();
+  TORCH_CHECK(exact.numel() == 2 * C && momentum.numel() == 2 * C && layer_ids.numel() == C, "transaction sizes");
+  TORCH_CHECK(pers_scores.numel() >= 64 * C && pers_total_diag.numel() == C && pers_decay_cross.numel() == C,
+              "ledger buffer sizes");
+  TORCH_CHECK(scal.numel() >= 8, "ledger scalars");
+  TORCH_CHECK(ws.scalar_type() == torch::kFloat64 && ws.numel() >= ro::ledger_workspace_doubles(static_cast<int>(C)),
+              "workspace too small");
+  const bool functional = cur_scores.has_value();
+  if (functional) {
+    check_f32(*cur_scores, "current scores");
+    check_f32(*cur_decay, "current decay");
+    TORCH_CHECK(cur_scores->numel() == 32 * C && cur_decay->numel() == 32, "current rows");
+  } else {
+    TORCH_CHECK(decay_derivative.has_value(), "surrogate mode needs the decay derivative");
+    check_f32(*decay_derivative, "decay derivative");
+  }
+  auto coef = torch::empty({C}, weights.options());
+  auto cand = torch::empty({C}, weights.options());
+  auto result = torch::zeros({16}, weights.options());
+  float* sp = scal.data_ptr<float>();
+  check_rc(ro::ledger_transaction(functional ? cur_scores->data_ptr<float>() : nullptr,
+                                  functional ? cur_decay->data_ptr<float>() : nullptr, exact.data_ptr<float>(),
+                                  momentum.data_ptr<float>(), weights.data_ptr<float>(),
+                                  layer_ids.data_ptr<int64_t>(),
+                                  functional ? nullptr : decay_derivative->data_ptr<float>(),
+                                  pers_scores.data_ptr<float>(), pers_total_diag.data_ptr<float>(),
+                                  pers_decay_cross.data_ptr<float>(), sp + 0, sp + 1, sp + 2, sp + 3,
+                                  coef.data_ptr<float>(), cand.data_ptr<float>(), result.data_ptr<float>(),
+                                  ws.data_ptr<double>(), static_cast<int>(C), static_cast<int>(prev_rows),
+                                  static_cast<int>(total_layers), functional, eta,
+                                  at::cuda::getCurrentCUDAStream()),
+           "tiller_ledger_transaction");
+  return {coef, cand, result};
+}
+
+int64_t tiller_ledger_workspace(int64_t C) { return ro::ledger_workspace_doubles(static_cast<int>(C)); }
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -509,6 +711,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("legacy_backward", &legacy_backward);
   m.def("rmsnorm_forward", &rmsnorm_forward);
   m.def("rmsnorm_backward", &rmsnorm_backward);
+  m.def("add_rmsnorm_forward", &add_rmsnorm_forward);
+  m.def("add_rmsnorm_backward", &add_rmsnorm_backward);
   m.def("rope_qkv_forward", &rope_qkv_forward);
   m.def("rope_qkv_backward", &rope_qkv_backward);
   m.def("cross_entropy_fwd_bwd", &cross_entropy_fwd_bwd);
@@ -521,4 +725,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tiller_chord", &tiller_chord);
   m.def("tiller_apply", &tiller_apply);
   m.def("ns_normalize", &ns_normalize);
+  m.def("comm_alloc", &comm_alloc);
+  m.def("comm_handle", &comm_handle);
+  m.def("comm_open", &comm_open);
+  m.def("comm_close", &comm_close);
+  m.def("comm_allreduce_f32", &comm_allreduce_f32);
+  m.def("comm_allreduce_i8", &comm_allreduce_i8);
+  m.def("comm_i8_bytes", &comm_i8_bytes);
+  m.def("comm_wait_only", &comm_wait_only);
+  m.def("tiller_ledger_transaction", &tiller_ledger_transaction);
+  m.def("tiller_ledger_workspace", &tiller_ledger_workspace);
 }

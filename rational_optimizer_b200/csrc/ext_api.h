@@ -37,6 +37,11 @@ int rmsnorm_backward_partial_size(int64_t rows, int d);
 int rmsnorm_backward(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                      float* dw, float* partial, int64_t rows, int d, int dtype, int out_dtype,
                      int accumulate_dw, cudaStream_t stream);
+int add_rmsnorm_forward(const float* x, const void* delta, const float* w, float* x_new, void* y,
+                        float* rstd, int64_t rows, int d, float eps, cudaStream_t stream);
+int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, const float* w,
+                         const float* rstd, float* dx, void* ddelta, float* dw, float* partial,
+                         int64_t rows, int d, cudaStream_t stream);
 int rope_qkv_forward(const void* qkv, const float* cos_t, const float* sin_t, void* q, void* k,
                      void* v, int B, int S, int H, int hd, int dtype, cudaStream_t stream);
 int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const float* cos_t,
@@ -76,5 +81,32 @@ int tiller_apply(float* const* params, const __nv_bfloat16* polar, const float* 
                  float* sel_out, int L, int blocks_per_layer, int R, int C, bool transpose, float scale,
                  int step, float decay, float alpha, float adj, bool update_param, cudaStream_t stream);
 int ns_normalize(const __nv_bfloat16* x, __nv_bfloat16* y, int batch, int64_t n, cudaStream_t stream);
+
+
+// comm.cu
+int comm_ipc_handle(const void* base, void* handle_out);
+int comm_ipc_open(const void* handle, void** ptr);
+int comm_ipc_close(void* ptr);
+int comm_allreduce_f32(void* const* data, unsigned int* const* flags, int rank, int world, int64_t n,
+                       float scale, unsigned int epoch, int* err, uint64_t timeout_ns,
+                       cudaStream_t stream);
+int64_t comm_i8_scale_offset(int64_t n);
+int64_t comm_i8_bytes(int64_t n);
+int comm_allreduce_i8(const float* src, float* out, void* const* data, unsigned int* const* flags, int rank,
+                      int world, int64_t n, float scale, unsigned int epoch, int* err,
+                      uint64_t timeout_ns, cudaStream_t stream);
+int comm_wait_only(void* const* data, unsigned int* const* flags, int rank, int world, unsigned int epoch,
+                   int* err, uint64_t timeout_ns, cudaStream_t stream);
+
+
+// ledger.cu
+int64_t ledger_workspace_doubles(int C);
+int ledger_transaction(const float* cur_scores, const float* cur_decay, const float* exact,
+                       const float* momentum, const float* weights, const int64_t* layer_ids,
+                       const float* decay_derivative, float* pers_scores, float* pers_total_diag,
+                       float* pers_decay_cross, float* pers_tail, float* discarded_fraction,
+                       float* shrinkage, float* ref_row_norm, float* coefficients, float* candidate,
+                       float* result, double* ws, int C, int prev_rows, int total_layers,
+                       bool functional, double eta, cudaStream_t stream);
 
 }  // namespace ro

@@ -85,10 +85,10 @@ __device__ __forceinline__ float eval_f(const Coeffs& c, float t) {
   const float t2 = t * t;
   const float p = fmaf(fmaf(fmaf(fmaf(fmaf(c.a[5], t, c.a[4]), t, c.a[3]), t, c.a[2]), t, c.a[1]), t, c.a[0]);
   const float q = 1.0f + c.b[0] * at + c.b[1] * t2 + c.b[2] * at * t2 + c.b[3] * t2 * t2;
-  float f = __fdiv_rn(p, q);
+  float f = __fdividef(p, q);
   for (int k = 0; k < c.nb; ++k) {
     const float u = t - c.center[k];
-    const float inv = __frcp_rn(1.0f + c.beta[k] * u * u);
+    const float inv = __fdividef(1.0f, 1.0f + c.beta[k] * u * u);
     f += c.codd[k] * u * inv + c.cbump[k] * (inv - c.zero_level[k]);
   }
   return f;
@@ -107,7 +107,7 @@ __device__ __forceinline__ void eval_full(const Coeffs& c, float t, float& f, fl
   const float dp = fmaf(fmaf(fmaf(fmaf(5.0f * c.a[5], t, 4.0f * c.a[4]), t, 3.0f * c.a[3]), t, 2.0f * c.a[2]), t, c.a[1]);
   const float q = 1.0f + c.b[0] * at + c.b[1] * t2 + c.b[2] * at3 + c.b[3] * t4;
   const float dq = c.b[0] * sign0(t) + 2.0f * c.b[1] * t + 3.0f * c.b[2] * t * at + 4.0f * c.b[3] * t3;
-  const float iq = __frcp_rn(q);
+  const float iq = __fdividef(1.0f, q);  // q >= 1: fast reciprocal is well conditioned
   const float iq2 = iq * iq;
   f = p * iq;
   df = (dp * q - p * dq) * iq2;
@@ -129,7 +129,7 @@ __device__ __forceinline__ void eval_full(const Coeffs& c, float t, float& f, fl
     if (k < c.nb) {
       const float u = t - c.center[k];
       const float u2 = u * u;
-      const float inv = __frcp_rn(1.0f + c.beta[k] * u2);
+      const float inv = __fdividef(1.0f, 1.0f + c.beta[k] * u2);
       const float inv2 = inv * inv;
       const float odd = u * inv;
       const float odd_dt = (1.0f - c.beta[k] * u2) * inv2;
@@ -198,20 +198,29 @@ forward_kernel(const TI* __restrict__ x, const float* __restrict__ num,
   int64_t r1 = r0 + rows_per_chunk;
   if (r1 > rows) r1 = rows;
   const float inv_w = 1.0f / static_cast<float>(w);
-  for (int64_t r = r0 + warp; r < r1; r += kWarps) {
-    const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
-    float v[E];
-    load_seg<TI, E, CONTIG>(x + off, w, lane, v);
-    float ss = 0.f;
+  constexpr int U = 4;  // rows in flight per warp (memory-level parallelism)
+  for (int64_t rb = r0 + warp; rb < r1; rb += kWarps * U) {
+    float v[U][E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) ss = fmaf(v[j], v[j], ss);
-    ss = warp_sum(ss);
-    const float rho = sqrtf(ss * inv_w + eps);
-    const float irho = 1.0f / rho;
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r < r1) load_seg<TI, E, CONTIG>(x + r * hidden + static_cast<int64_t>(g) * w, w, lane, v[u]);
+    }
 #pragma unroll
-    for (int j = 0; j < E; ++j) v[j] = rho * eval_f(c, v[j] * irho);
-    store_seg<TO, E, CONTIG>(y + off, w, lane, v);
-    if (rho_out != nullptr && lane == 0) rho_out[r * groups + g] = rho;
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r >= r1) break;
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) ss = fmaf(v[u][j], v[u][j], ss);
+      ss = warp_sum(ss);
+      const float rho = sqrtf(ss * inv_w + eps);
+      const float irho = __fdividef(1.0f, rho);
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[u][j] = rho * eval_f(c, v[u][j] * irho);
+      store_seg<TO, E, CONTIG>(y + r * hidden + static_cast<int64_t>(g) * w, w, lane, v[u]);
+      if (rho_out != nullptr && lane == 0) rho_out[r * groups + g] = rho;
+    }
   }
 }
 
@@ -221,7 +230,7 @@ forward_kernel(const TI* __restrict__ x, const float* __restrict__ num,
 // (rational_cuda_kernel.cu:663-673): nonlinear_y = rho f - z alpha - rho beta,
 // grad_x -= gy alpha + (t / w) beta sum(gy).
 template <typename TG, typename TI, typename TO, int E, bool CONTIG, int NGRAD, bool RESTRICT>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 backward_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
                 const float* __restrict__ num, const float* __restrict__ den,
                 const float* __restrict__ logits, const float* __restrict__ centers,
@@ -249,49 +258,102 @@ backward_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
   int64_t r1 = r0 + rows_per_chunk;
   if (r1 > rows) r1 = rows;
   const float inv_w = 1.0f / static_cast<float>(w);
-  for (int64_t r = r0 + warp; r < r1; r += kWarps) {
-    const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
-    float z[E], gy[E];
-    load_seg<TI, E, CONTIG>(x + off, w, lane, z);
-    load_seg<TG, E, CONTIG>(gy_ptr + off, w, lane, gy);
-    float ss = 0.f;
+  constexpr int U = 2;  // rows in flight per warp
+  for (int64_t rb = r0 + warp; rb < r1; rb += kWarps * U) {
+    float z[U][E], gy[U][E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) ss = fmaf(z[j], z[j], ss);
-    ss = warp_sum(ss);
-    const float rho = sqrtf(ss * inv_w + eps);
-    const float irho = 1.0f / rho;
-    float t[E], f[E], df[E];
-    float s = 0.f, sg = 0.f;
-#pragma unroll
-    for (int j = 0; j < E; ++j) {
-      t[j] = z[j] * irho;
-      float part[NGRAD];
-      eval_full<NGRAD>(c, t[j], f[j], df[j], part);
-      if (valid_elem<E, CONTIG>(w, lane, j)) {
-        const float gr = gy[j] * rho;
-#pragma unroll
-        for (int k = 0; k < NGRAD; ++k) acc[k] = fmaf(gr, part[k], acc[k]);
-        s = fmaf(gy[j], f[j] - df[j] * t[j], s);
-        sg += gy[j];
-      } else {
-        gy[j] = 0.f;
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r < r1) {
+        const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
+        load_seg<TI, E, CONTIG>(x + off, w, lane, z[u]);
+        load_seg<TG, E, CONTIG>(gy_ptr + off, w, lane, gy[u]);
       }
     }
-    s = warp_sum(s);
-    if constexpr (RESTRICT) sg = warp_sum(sg);
-    float out[E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) {
-      float gr = gy[j] * df[j] + t[j] * inv_w * s;
-      if constexpr (RESTRICT) {
-        gr -= gy[j] * alpha_g;
-        gr -= t[j] * inv_w * beta_g * sg;
-        f[j] = rho * f[j] - z[j] * alpha_g - rho * beta_g;
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r >= r1) break;
+      const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) ss = fmaf(z[u][j], z[u][j], ss);
+      ss = warp_sum(ss);
+      const float rho = sqrtf(ss * inv_w + eps);
+      const float irho = __fdividef(1.0f, rho);
+      float t[E], df[E];
+      float s = 0.f, sg = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        t[j] = z[u][j] * irho;
+        float f;
+        if constexpr (NGRAD == kBase) {
+          // Base coefficients only: accumulate in factored form,
+          // d/da_k -> t^k / q, d/d|b_j| -> -p/q^2 * {|t|, t^2, |t|^3, t^4}
+          // (the sign of b_j is applied once per CTA at the end).
+          const float tv = t[j];
+          const float at = fabsf(tv);
+          const float t2 = tv * tv;
+          const float p = fmaf(fmaf(fmaf(fmaf(fmaf(c.a[5], tv, c.a[4]), tv, c.a[3]), tv, c.a[2]), tv, c.a[1]), tv, c.a[0]);
+          const float dp = fmaf(fmaf(fmaf(fmaf(5.0f * c.a[5], tv, 4.0f * c.a[4]), tv, 3.0f * c.a[3]), tv, 2.0f * c.a[2]), tv, c.a[1]);
+          const float at3 = at * t2;
+          const float t4 = t2 * t2;
+          const float q = fmaf(c.b[3], t4, fmaf(c.b[2], at3, fmaf(c.b[1], t2, fmaf(c.b[0], at, 1.0f))));
+          const float dq = fmaf(4.0f * c.b[3], t2 * tv, fmaf(3.0f * c.b[2], tv * at, fmaf(2.0f * c.b[1], tv, c.b[0] * sign0(tv))));
+          const float iq = __fdividef(1.0f, q);
+          f = p * iq;
+          df[j] = (dp - f * dq) * iq;
+          if (valid_elem<E, CONTIG>(w, lane, j)) {
+            const float gr = gy[u][j] * rho;
+            float ua = gr * iq;
+            acc[0] += ua;
+            ua *= tv; acc[1] += ua;
+            ua *= tv; acc[2] += ua;
+            ua *= tv; acc[3] += ua;
+            ua *= tv; acc[4] += ua;
+            ua *= tv; acc[5] += ua;
+            const float vb = -gr * f * iq;
+            acc[6] = fmaf(vb, at, acc[6]);
+            acc[7] = fmaf(vb, t2, acc[7]);
+            acc[8] = fmaf(vb, at3, acc[8]);
+            acc[9] = fmaf(vb, t4, acc[9]);
+          }
+        } else {
+          float part[NGRAD];
+          eval_full<NGRAD>(c, t[j], f, df[j], part);
+          if (valid_elem<E, CONTIG>(w, lane, j)) {
+            const float gr = gy[u][j] * rho;
+#pragma unroll
+            for (int k = 0; k < NGRAD; ++k) acc[k] = fmaf(gr, part[k], acc[k]);
+          }
+        }
+        if (valid_elem<E, CONTIG>(w, lane, j)) {
+          s = fmaf(gy[u][j], f - df[j] * t[j], s);
+          sg += gy[u][j];
+        } else {
+          gy[u][j] = 0.f;
+        }
+        if constexpr (RESTRICT) z[u][j] = rho * f - z[u][j] * alpha_g - rho * beta_g;
       }
-      out[j] = gr;
+      s = warp_sum(s);
+      if constexpr (RESTRICT) sg = warp_sum(sg);
+      float out[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        float gr = gy[u][j] * df[j] + t[j] * inv_w * s;
+        if constexpr (RESTRICT) {
+          gr -= gy[u][j] * alpha_g;
+          gr -= t[j] * inv_w * beta_g * sg;
+        }
+        out[j] = gr;
+      }
+      store_seg<TO, E, CONTIG>(gx + off, w, lane, out);
+      if constexpr (RESTRICT) store_seg<float, E, CONTIG>(nonlinear_y + off, w, lane, z[u]);
     }
-    store_seg<TO, E, CONTIG>(gx + off, w, lane, out);
-    if constexpr (RESTRICT) store_seg<float, E, CONTIG>(nonlinear_y + off, w, lane, f);
+  }
+  if constexpr (NGRAD == kBase) {
+#pragma unroll
+    for (int k = 0; k < kDen; ++k) acc[kNum + k] *= c.bs[k];
   }
 #pragma unroll
   for (int k = 0; k < NGRAD; ++k) {

@@ -1,0 +1,630 @@
+// TILLER loss ledger + equal-budget transaction in ONE single-CTA fp64 kernel.
+//
+// Replaces hundreds of tiny launches (and two cuSOLVER eigensolves with host
+// synchronisation) per optimizer step.  Semantics follow
+// optimizer_design/_tiller/core.py:
+//   trace-matched surrogate rows ..... core.py:1142-1159  (ordinary steps)
+//   functional row norm .............. core.py:1161-1169  (refresh steps)
+//   Robust-FD ledger advance ......... core.py:1178-1233
+//   diagonal-completed transaction ... core.py:69-232 (Lanczos-32 with full
+//                                       re-orthogonalisation, 32x32 eigen-
+//                                       solve, 64-round secular bisection,
+//                                       acceptance tests)
+// Symmetric eigenproblems (the <=96x96 row Gram of the ledger and the 32x32
+// Lanczos tridiagonal) use a parallel cyclic Jacobi method (round-robin
+// pairing, n/2 independent rotations per round) in shared memory, followed by
+// an ascending sort, so eigenvalue order matches torch.linalg.eigh.  Row signs
+// and the order of equal eigenvalues may differ from LAPACK; every quantity
+// the algorithm consumes is invariant to them (it depends on S^T S).
+//
+// Launch: one CTA of kThreads threads, dynamic smem = 2*96*96 doubles + 2 KB.
+#include "common.cuh"
+
+namespace ro {
+namespace ledger {
+
+constexpr int kThreads = 1024;
+constexpr int kCurRows = 32;
+constexpr int kPersRows = 64;
+constexpr int kMaxSel = 96;
+constexpr int kKrylov = 32;
+constexpr double kTiny = 2.2250738585072014e-308;
+constexpr double kEps = 2.220446049250313e-16;
+constexpr float kTinyF = 1.17549435e-38f;
+
+struct Args {
+  // inputs
+  const float* cur_scores;     // [32, C] functional rows, or nullptr (surrogate)
+  const float* cur_decay;      // [32]
+  const float* exact;          // [2, C]
+  const float* momentum;       // [2, C]
+  const float* weights;        // [C]
+  const int64_t* layer_ids;    // [C]
+  const float* decay_derivative;  // [1] surrogate mode
+  // persistent ledger state (fp32, read and written)
+  float* pers_scores;          // [64, C] (first prev_rows rows valid)
+  float* pers_total_diag;      // [C]
+  float* pers_decay_cross;     // [C]
+  float* pers_tail;            // [1]
+  float* discarded_fraction;   // [1]
+  float* shrinkage;            // [1]
+  float* ref_row_norm;         // [1]
+  // outputs
+  float* coefficients;         // [C]
+  float* candidate;            // [C]
+  float* result;               // [16]
+  double* ws;                  // workspace (see ws_doubles)
+  int C, prev_rows, total_layers, functional;
+  double eta;
+};
+
+__device__ double block_sum(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (warp == 0) {
+    t = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
+    t = warp_sum_d(t);
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// Parallel cyclic Jacobi on symmetric A (n x n, row-major, smem).  On exit
+// A holds eigenvalues on the diagonal, V the eigenvectors (columns).
+// `players` needs n+1 ints (round-robin tournament), `rp`/`rq` n/2+1 ints,
+// `rc`/`rs` n/2+1 doubles.
+__device__ void jacobi_eigh(double* A, double* V, int n, int* players, int* rp, int* rq, double* rc,
+                            double* rs, double* red) {
+  (void)players;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < n * n; i += blockDim.x) V[i] = (i / n == i % n) ? 1.0 : 0.0;
+  const int m = (n + 1) & ~1;  // even number of players (a dummy if n is odd)
+  const int half = m / 2;
+  __syncthreads();
+  double total = 0.0;
+  for (int i = tid; i < n * n; i += blockDim.x) total += A[i] * A[i];
+  const double scale = sqrt(block_sum(total, red));
+  // Stop once the off-diagonal mass is at rounding level for an n x n fp64 matrix.
+  const double tol = 4.0 * static_cast<double>(n) * kEps * scale;
+  for (int sweep = 0; sweep < 30; ++sweep) {
+    double off = 0.0;
+    for (int i = tid; i < n * n; i += blockDim.x)
+      if (i / n != i % n) off += A[i] * A[i];
+    off = sqrt(block_sum(off, red));
+    if (scale == 0.0 || off <= tol) break;
+    for (int round = 0; round < m - 1; ++round) {
+      // Round-robin schedule in closed form: player m-1 meets `round`; the
+      // others pair as (round+k, round-k) modulo m-1.
+      for (int k = tid; k < half; k += blockDim.x) {
+        int p, q;
+        if (k == 0) {
+          p = round;
+          q = m - 1;
+        } else {
+          p = (round + k) % (m - 1);
+          q = (round - k + (m - 1)) % (m - 1);
+        }
+        if (p > q) { const int t = p; p = q; q = t; }
+        double c = 1.0, s = 0.0;
+        if (q < n) {
+          const double apq = A[p * n + q];
+          const double app = A[p * n + p], aqq = A[q * n + q];
+          if (fabs(apq) > kEps * 1e-3 * sqrt(fabs(app * aqq)) && apq != 0.0) {
+            const double theta = (aqq - app) / (2.0 * apq);
+            const double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
+            c = 1.0 / sqrt(t * t + 1.0);
+            s = t * c;
+          }
+        }
+        rp[k] = p;
+        rq[k] = q;
+        rc[k] = c;
+        rs[k] = s;
+      }
+      __syncthreads();
+      // A <- P^T A P (rows, then columns); disjoint pairs never conflict.
+      for (int idx = tid; idx < half * n; idx += blockDim.x) {
+        const int k = idx / n, j = idx % n;
+        const int p = rp[k], q = rq[k];
+        if (q >= n || rs[k] == 0.0) continue;
+        const double c = rc[k], s = rs[k];
+        const double ap = A[p * n + j], aq = A[q * n + j];
+        A[p * n + j] = c * ap - s * aq;
+        A[q * n + j] = s * ap + c * aq;
+      }
+      __syncthreads();
+      for (int idx = tid; idx < half * n; idx += blockDim.x) {
+        const int k = idx / n, i = idx % n;
+        const int p = rp[k], q = rq[k];
+        if (q >= n || rs[k] == 0.0) continue;
+        const double c = rc[k], s = rs[k];
+        const double ap = A[i * n + p], aq = A[i * n + q];
+        A[i * n + p] = c * ap - s * aq;
+        A[i * n + q] = s * ap + c * aq;
+        const double vp = V[i * n + p], vq = V[i * n + q];
+        V[i * n + p] = c * vp - s * vq;
+        V[i * n + q] = s * vp + c * vq;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Sort eigenpairs ascending: evals[i] from A diag, evecs columns of V -> out (n x n, column i).
+__device__ void sort_eigen(const double* A, const double* V, int n, double* evals, double* evecs,
+                           int* order) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < n; ++i) order[i] = i;
+    for (int i = 1; i < n; ++i) {
+      const int oi = order[i];
+      const double v = A[oi * n + oi];
+      int j = i - 1;
+      while (j >= 0 && A[order[j] * n + order[j]] > v) {
+        order[j + 1] = order[j];
+        --j;
+      }
+      order[j + 1] = oi;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) evals[i] = A[order[i] * n + order[i]];
+  for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
+    const int r = idx / n, col = idx % n;
+    evecs[r * n + col] = V[r * n + order[col]];
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
+  extern __shared__ double sm[];
+  double* A = sm;                       // kMaxSel^2
+  double* V = A + kMaxSel * kMaxSel;    // kMaxSel^2
+  __shared__ double red[40];
+  __shared__ double rc[kMaxSel / 2 + 2], rs[kMaxSel / 2 + 2];
+  __shared__ int rp[kMaxSel / 2 + 2], rq[kMaxSel / 2 + 2];
+  __shared__ int pairs[kMaxSel + 2];
+  __shared__ int order[kMaxSel + 2];
+  __shared__ double evals[kMaxSel];
+  __shared__ double sc[64];             // scalars
+  __shared__ double alphas[kKrylov], betas[kKrylov], proj[kKrylov], lam[kKrylov];
+  const int tid = threadIdx.x;
+  const int C = a.C;
+  // workspace layout (doubles)
+  double* cur = a.ws;                       // [32, C]
+  double* sel = cur + kCurRows * C;         // [96, C] selection rows (fp32-rounded values)
+  double* decay_cross = sel + kMaxSel * C;  // [C]
+  double* Q = decay_cross + C;              // [C, 32] column-major by Krylov index: Q[i*C + c]
+  double* rhs = Q + kKrylov * C;            // [C]
+  double* vec = rhs + C;                    // [C] current
+  double* prv = vec + C;                    // [C]
+  double* act = prv + C;                    // [C]
+  double* res = act + C;                    // [C]
+  double* fb = res + C;                     // [C]
+  double* Lv = fb + C;                      // [96]
+  double* cand = Lv + kMaxSel;              // [C]
+  double* evecT = cand + C;                 // [32*32]
+  double* cdec = evecT + kKrylov * kKrylov; // [32] current decay action
+  double* evecs = cdec + kCurRows;          // [96*96] sorted ledger eigenvectors
+
+  // ---- current rows ------------------------------------------------------
+  if (!a.functional) {
+    double s = 0.0;
+    for (int c = tid; c < C; c += blockDim.x) {
+      const double g = static_cast<double>(a.exact[c]) + static_cast<double>(a.exact[C + c]);
+      s += g * g;
+    }
+    const double norm = sqrt(block_sum(s, red));
+    const double ref = static_cast<double>(a.ref_row_norm[0]);
+    const double scale = norm > kTiny ? ref / fmax(norm, kTiny) : 0.0;
+    for (int c = tid; c < C; c += blockDim.x) {
+      const double g = static_cast<double>(a.exact[c]) + static_cast<double>(a.exact[C + c]);
+      const double v = static_cast<double>(static_cast<float>(g * scale));
+      for (int r = 0; r < kCurRows; ++r) cur[r * C + c] = v;
+    }
+    if (tid < kCurRows)
+      cdec[tid] = static_cast<double>(static_cast<float>(static_cast<double>(a.decay_derivative[0]) * scale));
+    if (tid == 0) a.result[6] = static_cast<float>(scale);
+  } else {
+    for (int i = tid; i < kCurRows * C; i += blockDim.x) cur[i] = static_cast<double>(a.cur_scores[i]);
+    if (tid < kCurRows) cdec[tid] = static_cast<double>(a.cur_decay[tid]);
+    if (tid == 0) a.result[6] = 1.0f;
+  }
+  __syncthreads();
+  if (a.functional) {
+    double s = 0.0;
+    for (int i = tid; i < kCurRows * C; i += blockDim.x) s += cur[i] * cur[i];
+    s = block_sum(s, red);
+    if (tid == 0) a.ref_row_norm[0] = static_cast<float>(sqrt(s / kCurRows));
+  }
+  // ---- ledger --------------------------------------------------------------
+  const double beta2 = 0.95;
+  int nsel;
+  double sel_tail;
+  if (a.prev_rows == 0) {
+    nsel = kCurRows;
+    sel_tail = 0.0;
+    for (int i = tid; i < kCurRows * C; i += blockDim.x) sel[i] = cur[i];
+    for (int c = tid; c < C; c += blockDim.x) {
+      double cross = 0.0, rep = 0.0;
+      for (int r = 0; r < kCurRows; ++r) {
+        cross += cur[r * C + c] * cdec[r];
+        rep += cur[r * C + c] * cur[r * C + c];
+      }
+      decay_cross[c] = static_cast<double>(static_cast<float>(cross / kCurRows));
+      a.pers_decay_cross[c] = static_cast<float>(cross / kCurRows);
+      a.pers_total_diag[c] = static_cast<float>(rep / kCurRows);
+      for (int r = 0; r < kCurRows; ++r) a.pers_scores[r * C + c] = static_cast<float>(cur[r * C + c]);
+    }
+    if (tid == 0) {
+      a.pers_tail[0] = 0.0f;
+      a.discarded_fraction[0] = 0.0f;
+      a.shrinkage[0] = 0.0f;
+      a.result[7] = static_cast<float>(kCurRows);  // persistent rows
+    }
+    __syncthreads();
+  } else {
+    const int prev = a.prev_rows;
+    nsel = prev + kCurRows;
+    const float sb = static_cast<float>(sqrt(beta2)), sc1 = static_cast<float>(sqrt(1.0 - beta2));
+    for (int i = tid; i < prev * C; i += blockDim.x) sel[i] = static_cast<double>(a.pers_scores[i] * sb);
+    for (int i = tid; i < kCurRows * C; i += blockDim.x)
+      sel[prev * C + i] = static_cast<double>(static_cast<float>(cur[i]) * sc1);
+    const double prev_tail = static_cast<double>(a.pers_tail[0]);
+    sel_tail = prev_tail * beta2;
+    for (int c = tid; c < C; c += blockDim.x) {
+      double cross = 0.0;
+      for (int r = 0; r < kCurRows; ++r) cross += cur[r * C + c] * cdec[r];
+      const double dc = static_cast<double>(a.pers_decay_cross[c]) * beta2 + (cross / kCurRows) * (1.0 - beta2);
+      decay_cross[c] = static_cast<double>(static_cast<float>(dc));
+    }
+    __syncthreads();
+    // Gram of the selection rows
+    for (int idx = tid; idx < nsel * nsel; idx += blockDim.x) {
+      const int i = idx / nsel, j = idx % nsel;
+      if (j < i) continue;
+      double s = 0.0;
+      for (int c = 0; c < C; ++c) s += sel[i * C + c] * sel[j * C + c];
+      A[i * nsel + j] = s;
+      A[j * nsel + i] = s;
+    }
+    __syncthreads();
+    jacobi_eigh(A, V, nsel, pairs, rp, rq, rc, rs, red);
+    sort_eigen(A, V, nsel, evals, evecs, order);
+    // stage the sorted eigenvectors in shared memory (A is free once evals are read)
+    for (int i = tid; i < nsel * nsel; i += blockDim.x) A[i] = evecs[i];
+    __syncthreads();
+    for (int i = tid; i < nsel; i += blockDim.x) evals[i] = fmax(evals[i], 0.0);
+    __syncthreads();
+    const int retained = nsel < kPersRows ? nsel : kPersRows;
+    const int discarded = nsel - retained;
+    const double shrink = discarded ? evals[discarded - 1] : 0.0;
+    // persistent = mult * (V_kept^T sel)
+    for (int idx = tid; idx < retained * C; idx += blockDim.x) {
+      const int r = idx / C, c = idx % C;
+      const int col = discarded + r;
+      double s = 0.0;
+      for (int i = 0; i < nsel; ++i) s += A[i * nsel + col] * sel[i * C + c];
+      const double kept = evals[col];
+      const double mult = sqrt(fmax(kept - shrink, 0.0) / fmax(kept, kTiny));
+      a.pers_scores[r * C + c] = static_cast<float>(mult * s);
+    }
+    __syncthreads();
+    const double pers_tail = sel_tail + shrink / (2.0 * kCurRows);
+    for (int c = tid; c < C; c += blockDim.x) {
+      double rep = 0.0;
+      for (int r = 0; r < retained; ++r) {
+        const double v = static_cast<double>(a.pers_scores[r * C + c]);
+        rep += v * v;
+      }
+      a.pers_total_diag[c] = static_cast<float>(rep / kCurRows + pers_tail);
+      a.pers_decay_cross[c] = static_cast<float>(decay_cross[c]);
+    }
+    double tot = 0.0, disc = 0.0;
+    for (int i = tid; i < nsel; i += blockDim.x) {
+      tot += evals[i];
+      if (i < discarded) disc += evals[i];
+    }
+    tot = block_sum(tot, red);
+    disc = block_sum(disc, red);
+    if (tid == 0) {
+      a.pers_tail[0] = static_cast<float>(pers_tail);
+      a.shrinkage[0] = static_cast<float>(shrink);
+      a.discarded_fraction[0] = static_cast<float>(disc / fmax(tot, kTiny));
+      a.result[7] = static_cast<float>(retained);
+    }
+    __syncthreads();
+  }
+  const double diag_res = static_cast<double>(static_cast<float>(sel_tail));
+
+  // ---- transaction -----------------------------------------------------------
+  const double eta = a.eta;
+  // low_rank L[r, c] = sel[r, c] / sqrt(w_c) / sqrt(32): applied on the fly.
+  double bsum = 0.0, rn = 0.0;
+  for (int c = tid; c < C; c += blockDim.x) {
+    const double w = static_cast<double>(a.weights[c]);
+    bsum += w;
+    const double e = static_cast<double>(a.exact[c]) + static_cast<double>(a.exact[C + c]);
+    const double r = (e / eta - decay_cross[c]) / sqrt(w);
+    rhs[c] = r;
+    rn += r * r;
+  }
+  const double budget = block_sum(bsum, red);
+  const double rhs_norm = sqrt(block_sum(rn, red));
+  const int steps = C < kKrylov ? C : kKrylov;
+  const double inv_sqrt_m = 1.0 / sqrt(static_cast<double>(kCurRows));
+  for (int c = tid; c < C; c += blockDim.x) {
+    vec[c] = rhs[c] / fmax(rhs_norm, kTiny);
+    prv[c] = 0.0;
+  }
+  __syncthreads();
+  double prev_beta = 0.0;
+  for (int i = 0; i < steps; ++i) {
+    for (int c = tid; c < C; c += blockDim.x) Q[i * C + c] = vec[c];
+    // Lv[r] = sum_c L[r,c] vec[c]
+    for (int r = tid >> 5; r < nsel; r += blockDim.x >> 5) {
+      double s = 0.0;
+      for (int c = tid & 31; c < C; c += 32)
+        s += sel[r * C + c] / sqrt(static_cast<double>(a.weights[c])) * inv_sqrt_m * vec[c];
+      s = warp_sum_d(s);
+      if ((tid & 31) == 0) Lv[r] = s;
+    }
+    __syncthreads();
+    double adot = 0.0, anorm = 0.0;
+    for (int c = tid; c < C; c += blockDim.x) {
+      const double rw = 1.0 / sqrt(static_cast<double>(a.weights[c]));
+      double s = diag_res / static_cast<double>(a.weights[c]) * vec[c];
+      for (int r = 0; r < nsel; ++r) s += sel[r * C + c] * rw * inv_sqrt_m * Lv[r];
+      act[c] = s;
+      adot += vec[c] * s;
+      anorm += s * s;
+    }
+    const double alpha = block_sum(adot, red);
+    const double action_norm = sqrt(block_sum(anorm, red));
+    for (int c = tid; c < C; c += blockDim.x) res[c] = act[c] - alpha * vec[c] - prev_beta * prv[c];
+    __syncthreads();
+    for (int pass = 0; pass < 2; ++pass) {
+      // coefficients h_j = Q_j . res  (j <= i)
+      for (int j = tid >> 5; j <= i; j += blockDim.x >> 5) {
+        double s = 0.0;
+        for (int c = tid & 31; c < C; c += 32) s += Q[j * C + c] * res[c];
+        s = warp_sum_d(s);
+        if ((tid & 31) == 0) sc[j] = s;
+      }
+      __syncthreads();
+      for (int c = tid; c < C; c += blockDim.x) {
+        double s = res[c];
+        for (int j = 0; j <= i; ++j) s -= Q[j * C + c] * sc[j];
+        res[c] = s;
+      }
+      __syncthreads();
+    }
+    double bn = 0.0;
+    for (int c = tid; c < C; c += blockDim.x) bn += res[c] * res[c];
+    double beta = sqrt(block_sum(bn, red));
+    if (tid == 0) alphas[i] = alpha;
+    if (i + 1 < steps) {
+      const double threshold = 64.0 * kEps * fmax(action_norm, 1.0);
+      for (int c = tid; c < C; c += blockDim.x) fb[c] = cos(static_cast<double>(c + 1) * static_cast<double>(i + 1));
+      __syncthreads();
+      for (int pass = 0; pass < 2; ++pass) {
+        for (int j = tid >> 5; j <= i; j += blockDim.x >> 5) {
+          double s = 0.0;
+          for (int c = tid & 31; c < C; c += 32) s += Q[j * C + c] * fb[c];
+          s = warp_sum_d(s);
+          if ((tid & 31) == 0) sc[j] = s;
+        }
+        __syncthreads();
+        for (int c = tid; c < C; c += blockDim.x) {
+          double s = fb[c];
+          for (int j = 0; j <= i; ++j) s -= Q[j * C + c] * sc[j];
+          fb[c] = s;
+        }
+        __syncthreads();
+      }
+      double fn = 0.0;
+      for (int c = tid; c < C; c += blockDim.x) fn += fb[c] * fb[c];
+      const double fnorm = sqrt(block_sum(fn, red));
+      const bool broke = beta <= threshold;
+      const bool use_fb = (fnorm > threshold) && broke;
+      for (int c = tid; c < C; c += blockDim.x) {
+        const double nxt = use_fb ? fb[c] / fmax(fnorm, kTiny) : res[c] / fmax(beta, kTiny);
+        prv[c] = vec[c];
+        vec[c] = nxt;
+      }
+      if (broke) beta = 0.0;
+      if (tid == 0) betas[i] = beta;
+      prev_beta = beta;
+      __syncthreads();
+    }
+  }
+  // tridiagonal -> A (steps x steps), Jacobi
+  for (int idx = tid; idx < steps * steps; idx += blockDim.x) {
+    const int i = idx / steps, j = idx % steps;
+    double v = 0.0;
+    if (i == j) v = alphas[i];
+    else if (j == i + 1) v = betas[i];
+    else if (i == j + 1) v = betas[j];
+    A[idx] = v;
+  }
+  __syncthreads();
+  jacobi_eigh(A, V, steps, pairs, rp, rq, rc, rs, red);
+  sort_eigen(A, V, steps, lam, evecT, order);
+  for (int i = tid; i < steps; i += blockDim.x) lam[i] = fmax(lam[i], 0.0);
+  __syncthreads();
+  // proj = E^T (Q^T rhs)
+  for (int j = tid >> 5; j < steps; j += blockDim.x >> 5) {
+    double s = 0.0;
+    for (int c = tid & 31; c < C; c += 32) s += Q[j * C + c] * rhs[c];
+    s = warp_sum_d(s);
+    if ((tid & 31) == 0) sc[j] = s;
+  }
+  __syncthreads();
+  if (tid < steps) {
+    double s = 0.0;
+    for (int j = 0; j < steps; ++j) s += evecT[j * steps + tid] * sc[j];
+    proj[tid] = s;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const double lower = kEps * static_cast<double>(C);
+    double lmax = 0.0;
+    for (int j = 0; j < steps; ++j) lmax = fmax(lmax, lam[j]);
+    const double upper = rhs_norm / sqrt(budget) + lmax + lower;
+    double hs = 0.0;
+    for (int j = 0; j < steps; ++j) {
+      const double v = proj[j] / (lam[j] + lower);
+      hs += v * v;
+    }
+    const bool hard = hs < budget;
+    double lo = lower, hi = upper;
+    for (int r = 0; r < 64; ++r) {
+      const double mid = 0.5 * (lo + hi);
+      double s = 0.0;
+      for (int j = 0; j < steps; ++j) {
+        const double v = proj[j] / (lam[j] + mid);
+        s += v * v;
+      }
+      if (s > budget) lo = mid; else hi = mid;
+    }
+    sc[40] = hi;
+    sc[41] = hard ? 1.0 : 0.0;
+    for (int j = 0; j < steps; ++j) sc[j] = proj[j] / (lam[j] + hi);
+  }
+  __syncthreads();
+  // y = E * sc  -> in the Krylov basis; cand = Q y / sqrt(w)
+  if (tid < steps) {
+    double s = 0.0;
+    for (int j = 0; j < steps; ++j) s += evecT[tid * steps + j] * sc[j];
+    proj[tid] = s;  // reuse as y
+  }
+  __syncthreads();
+  double cb = 0.0;
+  for (int c = tid; c < C; c += blockDim.x) {
+    double y = 0.0;
+    for (int j = 0; j < steps; ++j) y += Q[j * C + c] * proj[j];
+    const double w = static_cast<double>(a.weights[c]);
+    const double cc = y / sqrt(w);
+    cand[c] = cc;
+    cb += w * cc * cc;
+  }
+  const double cand_budget = block_sum(cb, red);
+  const double budget_res = fabs(cand_budget - budget) / fmax(budget, 1.0);
+  // scores: actions per selection row
+  double pa2 = 0.0, ca2 = 0.0;
+  for (int r = tid >> 5; r < nsel; r += blockDim.x >> 5) {
+    double sp = 0.0, sc_ = 0.0;
+    for (int c = tid & 31; c < C; c += 32) {
+      sp += sel[r * C + c];
+      sc_ += sel[r * C + c] * cand[c];
+    }
+    sp = warp_sum_d(sp);
+    sc_ = warp_sum_d(sc_);
+    if ((tid & 31) == 0) {
+      pa2 += sp * sp;
+      ca2 += sc_ * sc_;
+    }
+  }
+  pa2 = block_sum(pa2, red);
+  ca2 = block_sum(ca2, red);
+  double pe = 0.0, ce = 0.0, pdiag = 0.0, cdiag = 0.0, pdec = 0.0, cdec2 = 0.0;
+  bool finite = true;
+  for (int c = tid; c < C; c += blockDim.x) {
+    const double e = static_cast<double>(a.exact[c]) + static_cast<double>(a.exact[C + c]);
+    pe += e;
+    ce += e * cand[c];
+    pdiag += diag_res;
+    cdiag += diag_res * cand[c] * cand[c];
+    pdec += decay_cross[c];
+    cdec2 += decay_cross[c] * cand[c];
+    if (!isfinite(cand[c])) finite = false;
+  }
+  pe = block_sum(pe, red);
+  ce = block_sum(ce, red);
+  pdiag = block_sum(pdiag, red);
+  cdiag = block_sum(cdiag, red);
+  pdec = block_sum(pdec, red);
+  cdec2 = block_sum(cdec2, red);
+  const double nonfinite = block_sum(finite ? 0.0 : 1.0, red);
+  const double m = static_cast<double>(kCurRows);
+  const double parent_score = -eta * pe + 0.5 * eta * eta * (pa2 / m + pdiag + 2.0 * pdec);
+  const double cand_score = -eta * ce + 0.5 * eta * eta * (ca2 / m + cdiag + 2.0 * cdec2);
+  // per-layer contractions (both roles): parent exact/momentum and candidate
+  // versions must all be positive.  One warp per layer.
+  __shared__ int layer_ok;
+  if (tid == 0) layer_ok = 1;
+  __syncthreads();
+  for (int l = tid >> 5; l < a.total_layers; l += blockDim.x >> 5) {
+    double v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int c = tid & 31; c < C; c += 32) {
+      if (a.layer_ids[c] != l) continue;
+      for (int role = 0; role < 2; ++role) {
+        const double ex = a.exact[role * C + c], mo = a.momentum[role * C + c];
+        v[role * 4 + 0] += ex;
+        v[role * 4 + 1] += mo;
+        v[role * 4 + 2] += ex * cand[c];
+        v[role * 4 + 3] += mo * cand[c];
+      }
+    }
+    for (int k = 0; k < 8; ++k) {
+      const double t = warp_sum_d(v[k]);
+      if ((tid & 31) == 0 && !(t > 0.0)) atomicExch(&layer_ok, 0);
+    }
+  }
+  __syncthreads();
+  const bool hard = sc[41] != 0.0;
+  const bool accepted = nonfinite == 0.0 && isfinite(cand_score) && isfinite(budget_res) && !hard &&
+                        cand_score < parent_score && budget_res <= 1e-8 && layer_ok;
+  for (int c = tid; c < C; c += blockDim.x) {
+    const float cf = static_cast<float>(cand[c]);
+    a.candidate[c] = cf;
+    a.coefficients[c] = accepted ? cf : 1.0f;
+  }
+  if (tid == 0) {
+    a.result[0] = accepted ? 1.0f : 0.0f;
+    a.result[1] = hard ? 0.0f : static_cast<float>(sc[40]);
+    a.result[2] = hard ? 1.0f : 0.0f;
+    a.result[3] = static_cast<float>(budget_res);
+    a.result[4] = static_cast<float>(parent_score);
+    a.result[5] = static_cast<float>(cand_score);
+    a.result[8] = static_cast<float>(nsel);
+  }
+}
+
+}  // namespace ledger
+
+int64_t ledger_workspace_doubles(int C) {
+  using namespace ledger;
+  return static_cast<int64_t>(kCurRows) * C + static_cast<int64_t>(kMaxSel) * C + C +
+         static_cast<int64_t>(kKrylov) * C + 7LL * C + kMaxSel + C + kKrylov * kKrylov + kCurRows +
+         static_cast<int64_t>(kMaxSel) * kMaxSel;
+}
+
+int ledger_transaction(const float* cur_scores, const float* cur_decay, const float* exact,
+                       const float* momentum, const float* weights, const int64_t* layer_ids,
+                       const float* decay_derivative, float* pers_scores, float* pers_total_diag,
+                       float* pers_decay_cross, float* pers_tail, float* discarded_fraction,
+                       float* shrinkage, float* ref_row_norm, float* coefficients, float* candidate,
+                       float* result, double* ws, int C, int prev_rows, int total_layers,
+                       bool functional, double eta, cudaStream_t stream) {
+  using namespace ledger;
+  if (C < 2 || (prev_rows != 0 && prev_rows != kCurRows && prev_rows != kPersRows)) return -1;
+  Args a{cur_scores, cur_decay, exact, momentum, weights, layer_ids, decay_derivative, pers_scores,
+         pers_total_diag, pers_decay_cross, pers_tail, discarded_fraction, shrinkage, ref_row_norm,
+         coefficients, candidate, result, ws, C, prev_rows, total_layers, functional ? 1 : 0, eta};
+  const size_t smem = 2ull * kMaxSel * kMaxSel * sizeof(double);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(transaction_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    configured = true;
+  }
+  transaction_kernel<<<1, kThreads, smem, stream>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace ro

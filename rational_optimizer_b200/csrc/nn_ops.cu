@@ -163,6 +163,120 @@ __global__ void column_reduce_kernel(const float* __restrict__ partial, int bloc
   out[col] = accumulate ? out[col] + s : s;
 }
 
+
+// Fused residual add + RMSNorm:  x_new = x + delta (fp32), y = w * x_new * rsqrt(mean(x_new^2)+eps).
+// delta may be null (plain norm with x_new written as a copy only if x_new != x).
+template <int NCH>
+__global__ void __launch_bounds__(kNormWarps * 32)
+add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+                       const float* __restrict__ w, float* __restrict__ x_new,
+                       __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int64_t rows,
+                       float eps) {
+  constexpr int d = NCH * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[NCH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t off = row * d + c * 256 + lane * 8;
+    load_vec<float, 8>(x + off, v[c]);
+    if (delta != nullptr) {
+      float dv[8];
+      load_vec<__nv_bfloat16, 8>(delta + off, dv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[c][j] += dv[j];
+      store_vec<float, 8>(x_new + off, v[c]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[c][j], v[c][j], ss);
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float wv[8], o[8];
+    load_vec<float, 8>(w + c * 256 + lane * 8, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = wv[j] * (v[c][j] * r);
+    store_vec<__nv_bfloat16, 8>(y + row * d + c * 256 + lane * 8, o);
+  }
+  if (lane == 0) rstd_out[row] = r;
+}
+
+// Backward of the fused op: dx = dres + r * (w dy - xhat * mean(w dy xhat)) (fp32); optionally
+// also written as bf16 (the gradient of the bf16 delta branch).  dres may be null.
+template <int NCH>
+__global__ void __launch_bounds__(kNormWarps * 32)
+add_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ dres,
+                       const float* __restrict__ x, const float* __restrict__ w,
+                       const float* __restrict__ rstd, float* __restrict__ dx,
+                       __nv_bfloat16* __restrict__ ddelta, float* __restrict__ partial, int64_t rows,
+                       int rows_per_block) {
+  constexpr int d = NCH * 256;
+  __shared__ float red[kNormWarps][256];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float acc[NCH][8];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[c][j] = 0.f;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  int64_t r1 = r0 + rows_per_block;
+  if (r1 > rows) r1 = rows;
+  for (int64_t row = r0 + warp; row < r1; row += kNormWarps) {
+    const float r = rstd[row];
+    float xv[NCH][8], gv[NCH][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t off = row * d + c * 256 + lane * 8;
+      load_vec<float, 8>(x + off, xv[c]);
+      load_vec<__nv_bfloat16, 8>(dy + off, gv[c]);
+      float wv[8];
+      load_vec<float, 8>(w + c * 256 + lane * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = xv[c][j] * r;
+        acc[c][j] = fmaf(gv[c][j], xh, acc[c][j]);
+        const float wg = wv[j] * gv[c][j];
+        dot = fmaf(wg, xh, dot);
+        xv[c][j] = xh;
+        gv[c][j] = wg;
+      }
+    }
+    dot = warp_sum(dot) / static_cast<float>(d);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t off = row * d + c * 256 + lane * 8;
+      float o[8];
+      if (dres != nullptr) {
+        load_vec<float, 8>(dres + off, o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] += r * (gv[c][j] - xv[c][j] * dot);
+      store_vec<float, 8>(dx + off, o);
+      if (ddelta != nullptr) store_vec<__nv_bfloat16, 8>(ddelta + off, o);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = acc[c][j];
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < kNormWarps; ++wi) s += red[wi][threadIdx.x];
+    partial[static_cast<int64_t>(blockIdx.x) * d + c * 256 + threadIdx.x] = s;
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // QKV split + RoPE.  qkv: [B*S, 3*H*hd] (row = token); outputs q, k, v as
 // [B, H, S, hd] contiguous.  Interleaved pairs (2j, 2j+1) rotate by
@@ -432,6 +546,48 @@ int rmsnorm_backward(const void* dy, const void* x, const float* w, const float*
     else return -2;
   }
   column_reduce_kernel<<<ceil_div_i(d, 256), 256, 0, stream>>>(partial, blocks, d, dw, accumulate_dw);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int add_rmsnorm_forward(const float* x, const void* delta, const float* w, float* x_new, void* y,
+                        float* rstd, int64_t rows, int d, float eps, cudaStream_t stream) {
+  using namespace nn;
+  if (rows <= 0) return 0;
+  if (d % 256 || d / 256 > 8) return -1;
+  const int blocks = ceil_div_i(rows, kNormWarps);
+  const auto* dp = static_cast<const __nv_bfloat16*>(delta);
+  auto* yp = static_cast<__nv_bfloat16*>(y);
+  switch (d / 256) {
+    case 1: add_rmsnorm_fwd_kernel<1><<<blocks, kNormWarps * 32, 0, stream>>>(x, dp, w, x_new, yp, rstd, rows, eps); break;
+    case 2: add_rmsnorm_fwd_kernel<2><<<blocks, kNormWarps * 32, 0, stream>>>(x, dp, w, x_new, yp, rstd, rows, eps); break;
+    case 3: add_rmsnorm_fwd_kernel<3><<<blocks, kNormWarps * 32, 0, stream>>>(x, dp, w, x_new, yp, rstd, rows, eps); break;
+    case 4: add_rmsnorm_fwd_kernel<4><<<blocks, kNormWarps * 32, 0, stream>>>(x, dp, w, x_new, yp, rstd, rows, eps); break;
+    case 6: add_rmsnorm_fwd_kernel<6><<<blocks, kNormWarps * 32, 0, stream>>>(x, dp, w, x_new, yp, rstd, rows, eps); break;
+    case 8: add_rmsnorm_fwd_kernel<8><<<blocks, kNormWarps * 32, 0, stream>>>(x, dp, w, x_new, yp, rstd, rows, eps); break;
+    default: return -1;
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, const float* w,
+                         const float* rstd, float* dx, void* ddelta, float* dw, float* partial,
+                         int64_t rows, int d, cudaStream_t stream) {
+  using namespace nn;
+  if (d % 256 || d / 256 > 4) return -1;
+  int blocks = 0, rpb = 1;
+  if (rows > 0) {
+    rmsnorm_backward_plan(rows, blocks, rpb);
+    const auto* dyp = static_cast<const __nv_bfloat16*>(dy);
+    auto* ddp = static_cast<__nv_bfloat16*>(ddelta);
+    switch (d / 256) {
+      case 1: add_rmsnorm_bwd_kernel<1><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
+      case 2: add_rmsnorm_bwd_kernel<2><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
+      case 3: add_rmsnorm_bwd_kernel<3><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
+      case 4: add_rmsnorm_bwd_kernel<4><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
+      default: return -1;
+    }
+  }
+  column_reduce_kernel<<<ceil_div_i(d, 256), 256, 0, stream>>>(partial, blocks, d, dw, 0);
   return static_cast<int>(cudaGetLastError());
 }
 

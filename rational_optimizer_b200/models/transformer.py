@@ -22,7 +22,7 @@ import torch.nn as nn
 from ..ops.attention import causal_self_attention, precompute_rope
 from ..ops.cross_entropy import linear_cross_entropy
 from ..ops.linear import Linear, cached_cast, _WeightCache
-from ..ops.norm import rms_norm
+from ..ops.norm import add_rms_norm, fused_add_norm_supported, rms_norm
 from .grain import GRAIN
 
 GRAIN_ACTIVATION = "grain"
@@ -208,6 +208,7 @@ class CausalTransformer(nn.Module):
         self.lm_head.weight = self.token_embedding.weight
         self.apply(lambda module: init_weights(module, args.init_std))
         self._head_cache = _WeightCache()
+        self.fuse_residual_norm = True
         self.compute_dtype = torch.float32
         self.set_compute_dtype(torch.bfloat16)
 
@@ -225,9 +226,28 @@ class CausalTransformer(nn.Module):
 
     def hidden_states(self, input_ids):
         x = self.token_embedding(input_ids)
+        if (self.fuse_residual_norm and self.compute_dtype == torch.bfloat16
+                and fused_add_norm_supported(x)):
+            return self._hidden_states_fused(x)
         for layer in self.layers:
             x = layer(x)
         return self.norm(x)
+
+    def _hidden_states_fused(self, x):
+        """Same computation with every residual add fused into the following RMSNorm.
+
+        Each block's two branch outputs are carried as a pending bf16 delta and
+        added inside the next norm kernel (whose backward also folds the
+        residual-gradient accumulation), so no standalone add runs.
+        """
+        pending = None
+        for layer in self.layers:
+            x, h = add_rms_norm(x, pending, layer.attn_norm.weight, layer.attn_norm.eps)
+            a = layer.attn(h)
+            x, h = add_rms_norm(x, a, layer.ffn_norm.weight, layer.ffn_norm.eps)
+            pending = layer.mlp(h)
+        _, h = add_rms_norm(x, pending, self.norm.weight, self.norm.eps)
+        return h
 
     def forward(self, input_ids):
         h = self.hidden_states(input_ids)

@@ -31,6 +31,47 @@ class _RMSNormFunction(torch.autograd.Function):
         return dx.reshape(ctx.shape), dw.to(ctx.wdtype), None, None
 
 
+class _AddRMSNormFunction(torch.autograd.Function):
+    """(x_new, y) = (x + delta, rmsnorm(x + delta)); x fp32, delta/y bf16."""
+
+    @staticmethod
+    def forward(ctx, x, delta, weight, eps):
+        d = x.shape[-1]
+        x2 = x.reshape(-1, d).contiguous()
+        dl = delta.reshape(-1, d).contiguous()
+        w = weight.detach().float().contiguous()
+        x_new, y, rstd = ext().add_rmsnorm_forward(x2, dl, w, float(eps))
+        ctx.save_for_backward(x_new, w, rstd)
+        ctx.shape = x.shape
+        ctx.wdtype = weight.dtype
+        return x_new.view(x.shape), y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dx_new, dy):
+        x_new, w, rstd = ctx.saved_tensors
+        d = x_new.shape[-1]
+        if dy is None:
+            dy = torch.zeros(x_new.shape, device=x_new.device, dtype=torch.bfloat16)
+        dres = None if dx_new is None else dx_new.reshape(-1, d).float().contiguous()
+        dx, ddelta, dw = ext().add_rmsnorm_backward(dy.reshape(-1, d).to(torch.bfloat16).contiguous(),
+                                                    dres, x_new, w, rstd, True)
+        return dx.view(ctx.shape), ddelta.view(ctx.shape), dw.to(ctx.wdtype), None
+
+
+def add_rms_norm(x, delta, weight, eps=1e-6):
+    """Fused ``x_new = x + delta`` and ``rmsnorm(x_new)`` (bf16 output) on CUDA."""
+    if delta is None:
+        return x, rms_norm(x, weight, eps, torch.bfloat16 if x.is_cuda else None)
+    if not x.is_cuda:
+        x_new = x + delta
+        return x_new, rms_norm_reference(x_new, weight, eps)
+    return _AddRMSNormFunction.apply(x.float(), delta.to(torch.bfloat16), weight, eps)
+
+
+def fused_add_norm_supported(x) -> bool:
+    return x.is_cuda and x.shape[-1] % 256 == 0 and x.shape[-1] <= 1024
+
+
 def rms_norm_reference(x, weight, eps):
     return weight * x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
 

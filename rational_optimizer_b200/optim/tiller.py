@@ -233,6 +233,7 @@ class TILLERRouter(torch.optim.Optimizer):
         self._fused_ok = None
         self._fused_role_objs = None
         self._force_torch = False
+        self._ledger_bufs = None
 
     # -- properties --------------------------------------------------------
     @property
@@ -620,6 +621,71 @@ class TILLERRouter(torch.optim.Optimizer):
         self._rfd_selection = result
         return result
 
+    def _fast_ledger_ok(self):
+        return (self._use_fused() and not self.strict and not self._capture_telemetry_next_step
+                and hasattr(__import__("rational_optimizer_b200._ext", fromlist=["ext"]).ext(),
+                            "tiller_ledger_transaction"))
+
+    def _ledger_fast(self, *, functional, scores, decay, exact_by_role, momentum_by_role, weights,
+                     layer_ids, eta):
+        """Ledger advance + transaction in one single-CTA fp64 kernel (csrc/ledger.cu)."""
+        from .._ext import ext
+        C = ext()
+        anchor = self.anchor
+        n = int(weights.numel())
+        dev = weights.device
+        if self._ledger_bufs is None or self._ledger_bufs[0].shape[1] != n:
+            self._ledger_bufs = (torch.zeros(tm.PERSISTENT_ROWS, n, device=dev),
+                                 torch.zeros(n, device=dev), torch.zeros(n, device=dev),
+                                 torch.zeros(8, device=dev),
+                                 torch.empty(int(C.tiller_ledger_workspace(n)), device=dev,
+                                             dtype=torch.float64))
+        pers, diag, cross, scal, ws = self._ledger_bufs
+        prev = anchor.get("factorized_rfd_persistent_scores")
+        prev_rows = 0 if prev is None else int(prev.shape[0])
+        if prev is not None and prev.data_ptr() != pers.data_ptr():
+            pers[:prev_rows].copy_(prev)
+            diag.copy_(anchor["factorized_rfd_persistent_total_diagonal"])
+            cross.copy_(anchor["factorized_rfd_persistent_decay_cross"])
+            scal[0].copy_(anchor["factorized_rfd_persistent_isotropic_tail"].reshape(()))
+        if not functional:
+            ref = anchor.get("factorized_rfd_reference_row_norm")
+            if not torch.is_tensor(ref) or not torch.is_tensor(self._rfd_decay_derivative):
+                raise RuntimeError("TILLER lacks functional calibration")
+            if ref.data_ptr() != scal[3].data_ptr():
+                scal[3].copy_(ref.reshape(()))
+        dd = None if functional else self._rfd_decay_derivative.reshape(1).float().contiguous()
+        coef, cand, result = C.tiller_ledger_transaction(
+            scores.float().contiguous() if functional else None,
+            decay.float().contiguous() if functional else None,
+            exact_by_role.float().contiguous(), momentum_by_role.float().contiguous(),
+            weights.float().contiguous(), layer_ids.contiguous(), dd, pers, diag, cross, scal, ws,
+            prev_rows, len(self.pairs), float(eta))
+        new_rows = tm.CURRENT_ROWS if prev_rows == 0 else tm.PERSISTENT_ROWS
+        anchor["factorized_rfd_persistent_scores"] = pers[:new_rows]
+        anchor["factorized_rfd_persistent_total_diagonal"] = diag
+        anchor["factorized_rfd_persistent_decay_cross"] = cross
+        anchor["factorized_rfd_persistent_isotropic_tail"] = scal[0]
+        anchor["factorized_rfd_discarded_energy_fraction"] = scal[1]
+        anchor["factorized_rfd_shrinkage"] = scal[2]
+        anchor["factorized_rfd_reference_row_norm"] = scal[3]
+        anchor["factorized_rfd_step"] = int(anchor.get("factorized_rfd_step", 0)) + 1
+        self._rfd_gradient_scale = result[6]
+        self._rfd_functional_refresh = bool(functional)
+        self._rfd_rows = tm.LedgerRows(
+            selection_scores=pers.new_empty((prev_rows + tm.CURRENT_ROWS if prev_rows else tm.CURRENT_ROWS, 0)),
+            selection_diagonal_residual=None, persistent_scores=pers[:new_rows],
+            persistent_total_diagonal=diag, persistent_diagonal_residual=None,
+            persistent_decay_cross=cross, history_used=prev_rows > 0,
+            discarded_energy_fraction=scal[1], selection_isotropic_tail=None,
+            persistent_isotropic_tail=scal[0], fd_shrinkage=scal[2])
+        zero = result.new_zeros(1)
+        sel = tm.TransactionResult(coef, cand, result[0:1] > 0.5, result[1:2], result[2:3] > 0.5,
+                                   result[3:4], result[4:5], result[5:6],
+                                   torch.zeros(1, dtype=torch.int64, device=dev), zero, zero, zero, zero)
+        self._rfd_selection = sel
+        return sel
+
     def _gather_rows(self, packet):
         if self.world_size == 1:
             if packet.shape[0] != tm.GLOBAL_PROBE_COUNT:
@@ -702,15 +768,29 @@ class TILLERRouter(torch.optim.Optimizer):
             predictive = tm.window32_rows(g_scores, g_decay, anchor.get("predictive_global_score_ema"),
                                           anchor.get("predictive_global_decay_ema"),
                                           validate=self.strict)
-            self._advance_rows(g_scores, g_decay, functional=True)
-            selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids, eta=lr)
+            if self._fast_ledger_ok():
+                selection = self._ledger_fast(functional=True, scores=g_scores, decay=g_decay,
+                                              exact_by_role=exact_by_role,
+                                              momentum_by_role=momentum_by_role, weights=weights,
+                                              layer_ids=layer_ids, eta=lr)
+            else:
+                self._advance_rows(g_scores, g_decay, functional=True)
+                selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids,
+                                              eta=lr)
             anchor["predictive_global_score_ema"] = predictive.updated_scores.detach().clone()
             anchor["predictive_global_decay_ema"] = predictive.updated_decay_action.detach().clone()
             self._last_predictive = predictive
         else:
             if self._cached_selection_scores is None or self._cached_selection_decay is None:
                 raise RuntimeError("TILLER selection factor is missing")
-            selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids, eta=lr)
+            if self._fast_ledger_ok():
+                selection = self._ledger_fast(functional=False, scores=None, decay=None,
+                                              exact_by_role=exact_by_role,
+                                              momentum_by_role=momentum_by_role, weights=weights,
+                                              layer_ids=layer_ids, eta=lr)
+            else:
+                selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids,
+                                              eta=lr)
         coefficients = selection.coefficients.view(L, self.groups)
         dirs["apply"](coefficients, lr, wd)
         updates = int(anchor.get("predictive_response_transaction_updates", 0)) + 1

@@ -10,8 +10,8 @@ from __future__ import annotations
 from .. import _ext
 
 
-def maybe_communicator(device):
-    if not _ext.available() or not hasattr(_ext.ext(), "p2p_allreduce"):
+def maybe_communicator(device, numel, group=None):
+    if not _ext.available() or not hasattr(_ext.ext(), "comm_allreduce_f32"):
         return None
     from .p2p import P2PCommunicator
-    return P2PCommunicator.create(device)
+    return P2PCommunicator.create(device, numel, group=group)

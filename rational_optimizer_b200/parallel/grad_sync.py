@@ -10,13 +10,15 @@ synchroniser only manages the buffer.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
 
 class GradientSynchronizer:
     def __init__(self, model: torch.nn.Module, *, group=None, bucket_bytes: int = 256 << 20,
-                 communicator=None):
+                 communicator=None, transport: str | None = None):
         seen, params = set(), []
         for p in model.parameters():
             if p.requires_grad and id(p) not in seen:
@@ -28,7 +30,18 @@ class GradientSynchronizer:
         dtype = params[0].dtype
         device = params[0].device
         total = sum(p.numel() for p in params)
-        self.flat = torch.zeros(total, dtype=dtype, device=device)
+        if transport is None:
+            transport = os.environ.get("RO_GRAD_TRANSPORT", "p2p")
+        if communicator is None and self.world > 1 and transport == "p2p" and device.type == "cuda":
+            from .comm import maybe_communicator
+            communicator = maybe_communicator(device, total, group=group)
+        self.communicator = communicator
+        self.transport = "p2p" if communicator is not None else ("nccl" if self.world > 1 else "none")
+        if communicator is not None and dtype == torch.float32:
+            self.flat = communicator.float_view(total)
+            self.flat.zero_()
+        else:
+            self.flat = torch.zeros(total, dtype=dtype, device=device)
         self.views = []
         offset = 0
         for p in params:
@@ -38,7 +51,6 @@ class GradientSynchronizer:
             self.views.append(view)
             offset += n
         self.bucket_elems = max(1, bucket_bytes // self.flat.element_size())
-        self.communicator = communicator
 
     def zero_grad(self):
         for p, v in zip(self.params, self.views):

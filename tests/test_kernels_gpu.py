@@ -167,3 +167,44 @@ def test_linear_cross_entropy(V):
     torch.testing.assert_close(loss, lr, rtol=2e-3, atol=2e-3)
     torch.testing.assert_close(h.grad.float(), hr.grad, rtol=5e-2, atol=2e-4)
     torch.testing.assert_close(w.grad, wr.grad, rtol=5e-2, atol=2e-4)
+
+
+def test_add_rms_norm_matches_reference():
+    from rational_optimizer_b200.ops.norm import add_rms_norm
+    x = torch.randn(513, 1024, device=DEV, requires_grad=True)
+    delta = torch.randn(513, 1024, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(1024, device=DEV)).requires_grad_(True)
+    x_new, y = add_rms_norm(x, delta, w, 1e-6)
+    gx_new = torch.randn_like(x_new)
+    gy = torch.randn_like(y)
+    torch.autograd.backward([x_new, y], [gx_new, gy])
+    xr = x.detach().clone().requires_grad_(True)
+    dr = delta.detach().float().clone().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    xn = xr + dr
+    yr = rms_norm_reference(xn, wr, 1e-6)
+    torch.autograd.backward([xn, yr], [gx_new, gy.float()])
+    torch.testing.assert_close(x_new, xn, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(x.grad, xr.grad, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(delta.grad.float(), dr.grad, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=1e-2, atol=5e-2)
+
+
+def test_fused_residual_model_matches_unfused():
+    from rational_optimizer_b200.models.transformer import CausalTransformer, model_args
+    args = model_args(layers=2, d_model=256, heads=4, ffn_dim=512, seq_len=64, activation="grain",
+                      rational_group_size=128)
+    torch.manual_seed(0)
+    m = CausalTransformer(args, 300).cuda()
+    t = torch.randint(0, 300, (3, 65), device=DEV)
+    l1 = m.forward_loss(t[:, :-1], t[:, 1:])
+    l1.backward()
+    g1 = [p.grad.clone() for p in m.parameters()]
+    m.zero_grad()
+    m.fuse_residual_norm = False
+    l2 = m.forward_loss(t[:, :-1], t[:, 1:])
+    l2.backward()
+    assert abs(float(l1) - float(l2)) < 1e-2
+    for a, b in zip(g1, [p.grad for p in m.parameters()]):
+        torch.testing.assert_close(a, b, rtol=5e-2, atol=5e-3)

@@ -1,0 +1,69 @@
+"""Single-CTA fp64 ledger + transaction kernel against the PyTorch restatement."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from rational_optimizer_b200 import _ext
+from rational_optimizer_b200.optim import tiller_math as tm
+
+
+def _torch_step(state, functional, scores, decay, exact, mom, weights, layer_ids, L, eta, dd):
+    ps, pd, pc, pt = state.get("s"), state.get("d"), state.get("c"), state.get("t")
+    if not functional:
+        scores, decay, scale = tm.trace_matched_surrogate(exact, dd, state["ref"])
+    else:
+        scale = scores.new_ones(())
+    rows = tm.rfd_rows(scores, decay, ps, pd, pc, pt, validate=True)
+    if functional:
+        state["ref"] = tm.functional_row_norm(scores)
+    state.update(s=rows.persistent_scores, d=rows.persistent_total_diagonal,
+                 c=rows.persistent_decay_cross, t=rows.persistent_isotropic_tail)
+    res = tm.biatlas_transaction(rows, exact, mom, weights, layer_ids, total_layers=L, eta=eta,
+                                 diagnostics=False)
+    return res, rows, scale
+
+
+@pytest.mark.parametrize("L,G", [(18, 18), (2, 6), (3, 5)])
+def test_ledger_kernel_matches_torch(L, G):
+    C = _ext.ext()
+    n = L * G
+    dev = "cuda"
+    gen = torch.Generator(device=dev).manual_seed(L * 100 + G)
+    layer_ids = torch.arange(L, device=dev).repeat_interleave(G)
+    eta = 3e-4
+    st_t = {}
+    pers = torch.zeros(64, n, device=dev)
+    diag = torch.zeros(n, device=dev)
+    cross = torch.zeros(n, device=dev)
+    scal = torch.zeros(8, device=dev)
+    ws = torch.empty(int(C.tiller_ledger_workspace(n)), device=dev, dtype=torch.float64)
+    prev_rows = 0
+    for step in range(6):
+        functional = step in (0, 3)
+        exact = (torch.rand(2, n, device=dev, generator=gen) + 0.1) * 1e-3
+        mom = (torch.rand(2, n, device=dev, generator=gen) + 0.1) * 1e-3
+        weights = torch.rand(n, device=dev, generator=gen) + 0.5
+        scores = torch.randn(32, n, device=dev, generator=gen) * 1e-3
+        decay = torch.randn(32, device=dev, generator=gen) * 1e-4
+        dd = torch.randn((), device=dev, generator=gen).abs() * 1e-4
+        res, rows, scale = _torch_step(st_t, functional, scores if functional else None,
+                                       decay if functional else None, exact, mom, weights, layer_ids,
+                                       L, eta, dd)
+        coef, cand, result = C.tiller_ledger_transaction(
+            scores if functional else None, decay if functional else None, exact, mom, weights,
+            layer_ids, None if functional else dd.reshape(1), pers, diag, cross, scal, ws, prev_rows,
+            L, eta)
+        prev_rows = 32 if prev_rows == 0 else 64
+        torch.cuda.synchronize()
+        assert bool(result[0] > 0.5) == bool(res.accepted.item()), (step, result, res.accepted)
+        torch.testing.assert_close(cand, res.candidate_coefficients.float(), rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(coef, res.coefficients.float(), rtol=1e-4, atol=1e-5)
+        p_k = pers[:prev_rows].double()
+        p_t = rows.persistent_scores.double()
+        torch.testing.assert_close(p_k.T @ p_k, p_t.T @ p_t, rtol=1e-4, atol=1e-12)
+        torch.testing.assert_close(diag, rows.persistent_total_diagonal, rtol=1e-4, atol=1e-12)
+        torch.testing.assert_close(cross, rows.persistent_decay_cross, rtol=1e-4, atol=1e-12)
+        torch.testing.assert_close(scal[0], rows.persistent_isotropic_tail, rtol=1e-4, atol=1e-14)
+        torch.testing.assert_close(scal[3], st_t["ref"].float(), rtol=1e-5, atol=1e-12)
+        torch.testing.assert_close(result[6], scale.float(), rtol=1e-5, atol=1e-12)
