@@ -653,7 +653,7 @@ std::vector<torch::Tensor> tiller_ledger_transaction(
     torch::Tensor momentum, torch::Tensor weights, torch::Tensor layer_ids,
     c10::optional<torch::Tensor> decay_derivative, torch::Tensor pers_scores, torch::Tensor pers_total_diag,
     torch::Tensor pers_decay_cross, torch::Tensor scal, torch::Tensor ws, int64_t prev_rows,
-    int64_t total_layers, double eta) {
+    int64_t total_layers, double eta, c10::optional<torch::Tensor> timing) {
   const c10::cuda::CUDAGuard guard(exact.device());
   check_f32(exact, "exact");
   check_f32(momentum, "momentum");
@@ -679,6 +679,12 @@ std::vector<torch::Tensor> tiller_ledger_transaction(
     TORCH_CHECK(decay_derivative.has_value(), "surrogate mode needs the decay derivative");
     check_f32(*decay_derivative, "decay derivative");
   }
+  unsigned long long* timing_ptr = nullptr;
+  if (timing.has_value()) {
+    TORCH_CHECK(timing->is_cuda() && timing->scalar_type() == torch::kInt64 && timing->numel() >= 16,
+                "timing buffer must be int64 CUDA with 16 entries");
+    timing_ptr = reinterpret_cast<unsigned long long*>(timing->data_ptr<int64_t>());
+  }
   auto coef = torch::empty({C}, weights.options());
   auto cand = torch::empty({C}, weights.options());
   auto result = torch::zeros({16}, weights.options());
@@ -692,7 +698,7 @@ std::vector<torch::Tensor> tiller_ledger_transaction(
                                   pers_decay_cross.data_ptr<float>(), sp + 0, sp + 1, sp + 2, sp + 3,
                                   coef.data_ptr<float>(), cand.data_ptr<float>(), result.data_ptr<float>(),
                                   ws.data_ptr<double>(), static_cast<int>(C), static_cast<int>(prev_rows),
-                                  static_cast<int>(total_layers), functional, eta,
+                                  static_cast<int>(total_layers), functional, eta, timing_ptr,
                                   at::cuda::getCurrentCUDAStream()),
            "tiller_ledger_transaction");
   return {coef, cand, result};
@@ -733,6 +739,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_allreduce_i8", &comm_allreduce_i8);
   m.def("comm_i8_bytes", &comm_i8_bytes);
   m.def("comm_wait_only", &comm_wait_only);
-  m.def("tiller_ledger_transaction", &tiller_ledger_transaction);
+  m.def("tiller_ledger_transaction", &tiller_ledger_transaction, py::arg("cur_scores"), py::arg("cur_decay"),
+        py::arg("exact"), py::arg("momentum"), py::arg("weights"), py::arg("layer_ids"),
+        py::arg("decay_derivative"), py::arg("pers_scores"), py::arg("pers_total_diag"),
+        py::arg("pers_decay_cross"), py::arg("scal"), py::arg("ws"), py::arg("prev_rows"),
+        py::arg("total_layers"), py::arg("eta"), py::arg("timing") = py::none());
   m.def("tiller_ledger_workspace", &tiller_ledger_workspace);
 }

@@ -107,6 +107,7 @@ int ledger_transaction(const float* cur_scores, const float* cur_decay, const fl
                        float* pers_decay_cross, float* pers_tail, float* discarded_fraction,
                        float* shrinkage, float* ref_row_norm, float* coefficients, float* candidate,
                        float* result, double* ws, int C, int prev_rows, int total_layers,
-                       bool functional, double eta, cudaStream_t stream);
+                       bool functional, double eta, unsigned long long* timing,
+                       cudaStream_t stream);
 
 }  // namespace ro

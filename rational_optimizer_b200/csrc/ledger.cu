@@ -17,7 +17,7 @@
 // and the order of equal eigenvalues may differ from LAPACK; every quantity
 // the algorithm consumes is invariant to them (it depends on S^T S).
 //
-// Launch: one CTA of kThreads threads, dynamic smem = 2*96*96 doubles + 2 KB.
+// Launch: one CTA of kThreads threads, dynamic smem = 2*96*97 doubles (+4 KB static).
 #include "common.cuh"
 
 namespace ro {
@@ -54,9 +54,21 @@ struct Args {
   float* candidate;            // [C]
   float* result;               // [16]
   double* ws;                  // workspace (see ws_doubles)
+  unsigned long long* timing;  // optional [16]: %globaltimer at phase ends, sweep counts
   int C, prev_rows, total_layers, functional;
   double eta;
 };
+
+__device__ __forceinline__ unsigned long long ledger_clock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Phase timestamps for the optional timing buffer (diagnostics only).
+#define STAMP(k)                                                           \
+  do {                                                                     \
+    if (a.timing != nullptr && threadIdx.x == 0) a.timing[k] = ledger_clock(); \
+  } while (0)
 
 __device__ double block_sum(double v, double* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -74,29 +86,39 @@ __device__ double block_sum(double v, double* red) {
   return red[32];
 }
 
-// Parallel cyclic Jacobi on symmetric A (n x n, row-major, smem).  On exit
-// A holds eigenvalues on the diagonal, V the eigenvectors (columns).
-// `players` needs n+1 ints (round-robin tournament), `rp`/`rq` n/2+1 ints,
-// `rc`/`rs` n/2+1 doubles.
-__device__ void jacobi_eigh(double* A, double* V, int n, int* players, int* rp, int* rq, double* rc,
-                            double* rs, double* red) {
-  (void)players;
+// Parallel cyclic Jacobi on symmetric A (n x n, row-major in smem with leading
+// dimension n + 1, so a column walk visits a different bank on every row).  On exit
+// A holds eigenvalues on the diagonal, V the eigenvectors (columns); returns
+// the number of sweeps that rotated anything.  `rp`/`rq` need n/2+1 ints,
+// `rc`/`rs` n/2+1 doubles; `rotated` is a shared flag.
+__device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double* rc, double* rs,
+                           double* red, int* rotated) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < n * n; i += blockDim.x) V[i] = (i / n == i % n) ? 1.0 : 0.0;
+  const int ld = n + 1;
+  for (int i = tid; i < n * n; i += blockDim.x) {
+    const int r = i / n, c = i - r * n;
+    V[r * ld + c] = (r == c) ? 1.0 : 0.0;
+  }
   const int m = (n + 1) & ~1;  // even number of players (a dummy if n is odd)
   const int half = m / 2;
   __syncthreads();
   double total = 0.0;
-  for (int i = tid; i < n * n; i += blockDim.x) total += A[i] * A[i];
+  for (int i = tid; i < n * n; i += blockDim.x) {
+    const int r = i / n, c = i - r * n;
+    total += A[r * ld + c] * A[r * ld + c];
+  }
   const double scale = sqrt(block_sum(total, red));
-  // Stop once the off-diagonal mass is at rounding level for an n x n fp64 matrix.
-  const double tol = 4.0 * static_cast<double>(n) * kEps * scale;
-  for (int sweep = 0; sweep < 30; ++sweep) {
-    double off = 0.0;
-    for (int i = tid; i < n * n; i += blockDim.x)
-      if (i / n != i % n) off += A[i] * A[i];
-    off = sqrt(block_sum(off, red));
-    if (scale == 0.0 || off <= tol) break;
+  // An off-diagonal entry is dropped once it is below 1e-13 of the matrix norm
+  // (absolute floor) or at rounding level of its own diagonal pair (relative
+  // test).  Dropping changes no eigenvalue by more than n * 1e-13 * ||A||_F,
+  // far below the fp32 precision of every output, and it lets sweeps stop:
+  // rotations among rounding-level entries of a degenerate (e.g. rank-one
+  // surrogate) block only reshuffle noise and never reach zero.
+  const double floor_abs = 1e-13 * scale;
+  int sweep = 0;
+  for (; sweep < 30; ++sweep) {
+    if (tid == 0) *rotated = 0;
+    __syncthreads();
     for (int round = 0; round < m - 1; ++round) {
       // Round-robin schedule in closed form: player m-1 meets `round`; the
       // others pair as (round+k, round-k) modulo m-1.
@@ -112,13 +134,19 @@ __device__ void jacobi_eigh(double* A, double* V, int n, int* players, int* rp, 
         if (p > q) { const int t = p; p = q; q = t; }
         double c = 1.0, s = 0.0;
         if (q < n) {
-          const double apq = A[p * n + q];
-          const double app = A[p * n + p], aqq = A[q * n + q];
-          if (fabs(apq) > kEps * 1e-3 * sqrt(fabs(app * aqq)) && apq != 0.0) {
+          const double apq = A[p * ld + q];
+          const double app = A[p * ld + p], aqq = A[q * ld + q];
+          const double aabs = fabs(apq);
+          if (aabs > floor_abs && aabs > 0.5 * kEps * fmax(fabs(app), fabs(aqq))) {
             const double theta = (aqq - app) / (2.0 * apq);
             const double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
             c = 1.0 / sqrt(t * t + 1.0);
             s = t * c;
+            *rotated = 1;
+          } else if (apq != 0.0) {
+            // negligible: drop it so the sweep count reflects real work
+            A[p * ld + q] = 0.0;
+            A[q * ld + p] = 0.0;
           }
         }
         rp[k] = p;
@@ -129,30 +157,34 @@ __device__ void jacobi_eigh(double* A, double* V, int n, int* players, int* rp, 
       __syncthreads();
       // A <- P^T A P (rows, then columns); disjoint pairs never conflict.
       for (int idx = tid; idx < half * n; idx += blockDim.x) {
-        const int k = idx / n, j = idx % n;
+        const int k = idx / n, j = idx - k * n;
         const int p = rp[k], q = rq[k];
         if (q >= n || rs[k] == 0.0) continue;
         const double c = rc[k], s = rs[k];
-        const double ap = A[p * n + j], aq = A[q * n + j];
-        A[p * n + j] = c * ap - s * aq;
-        A[q * n + j] = s * ap + c * aq;
+        const double ap = A[p * ld + j], aq = A[q * ld + j];
+        A[p * ld + j] = c * ap - s * aq;
+        A[q * ld + j] = s * ap + c * aq;
       }
       __syncthreads();
       for (int idx = tid; idx < half * n; idx += blockDim.x) {
-        const int k = idx / n, i = idx % n;
+        const int k = idx / n, i = idx - k * n;
         const int p = rp[k], q = rq[k];
         if (q >= n || rs[k] == 0.0) continue;
         const double c = rc[k], s = rs[k];
-        const double ap = A[i * n + p], aq = A[i * n + q];
-        A[i * n + p] = c * ap - s * aq;
-        A[i * n + q] = s * ap + c * aq;
-        const double vp = V[i * n + p], vq = V[i * n + q];
-        V[i * n + p] = c * vp - s * vq;
-        V[i * n + q] = s * vp + c * vq;
+        const double ap = A[i * ld + p], aq = A[i * ld + q];
+        // the rotated pair's off-diagonal entries are zero by construction
+        A[i * ld + p] = (i == q) ? 0.0 : c * ap - s * aq;
+        A[i * ld + q] = (i == p) ? 0.0 : s * ap + c * aq;
+        const double vp = V[i * ld + p], vq = V[i * ld + q];
+        V[i * ld + p] = c * vp - s * vq;
+        V[i * ld + q] = s * vp + c * vq;
       }
       __syncthreads();
     }
+    if (*rotated == 0) break;
+    __syncthreads();
   }
+  return sweep;
 }
 
 // Sort eigenpairs ascending: evals[i] from A diag, evecs columns of V -> out (n x n, column i).
@@ -162,9 +194,9 @@ __device__ void sort_eigen(const double* A, const double* V, int n, double* eval
     for (int i = 0; i < n; ++i) order[i] = i;
     for (int i = 1; i < n; ++i) {
       const int oi = order[i];
-      const double v = A[oi * n + oi];
+      const double v = A[oi * (n + 1) + oi];
       int j = i - 1;
-      while (j >= 0 && A[order[j] * n + order[j]] > v) {
+      while (j >= 0 && A[order[j] * (n + 1) + order[j]] > v) {
         order[j + 1] = order[j];
         --j;
       }
@@ -172,10 +204,10 @@ __device__ void sort_eigen(const double* A, const double* V, int n, double* eval
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) evals[i] = A[order[i] * n + order[i]];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) evals[i] = A[order[i] * (n + 1) + order[i]];
   for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
     const int r = idx / n, col = idx % n;
-    evecs[r * n + col] = V[r * n + order[col]];
+    evecs[r * n + col] = V[r * (n + 1) + order[col]];
   }
   __syncthreads();
 }
@@ -183,17 +215,18 @@ __device__ void sort_eigen(const double* A, const double* V, int n, double* eval
 __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
   extern __shared__ double sm[];
   double* A = sm;                       // kMaxSel^2
-  double* V = A + kMaxSel * kMaxSel;    // kMaxSel^2
+  double* V = A + kMaxSel * (kMaxSel + 1);  // kMaxSel x (kMaxSel + 1)
   __shared__ double red[40];
   __shared__ double rc[kMaxSel / 2 + 2], rs[kMaxSel / 2 + 2];
   __shared__ int rp[kMaxSel / 2 + 2], rq[kMaxSel / 2 + 2];
-  __shared__ int pairs[kMaxSel + 2];
+  __shared__ int rotated;
   __shared__ int order[kMaxSel + 2];
   __shared__ double evals[kMaxSel];
   __shared__ double sc[64];             // scalars
   __shared__ double alphas[kKrylov], betas[kKrylov], proj[kKrylov], lam[kKrylov];
   const int tid = threadIdx.x;
   const int C = a.C;
+  STAMP(0);
   // workspace layout (doubles)
   double* cur = a.ws;                       // [32, C]
   double* sel = cur + kCurRows * C;         // [96, C] selection rows (fp32-rounded values)
@@ -210,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
   double* evecT = cand + C;                 // [32*32]
   double* cdec = evecT + kKrylov * kKrylov; // [32] current decay action
   double* evecs = cdec + kCurRows;          // [96*96] sorted ledger eigenvectors
+  double* rsw = evecs + kMaxSel * kMaxSel;  // [C] 1/sqrt(w_c)
 
   // ---- current rows ------------------------------------------------------
   if (!a.functional) {
@@ -284,16 +318,23 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     }
     __syncthreads();
     // Gram of the selection rows
-    for (int idx = tid; idx < nsel * nsel; idx += blockDim.x) {
-      const int i = idx / nsel, j = idx % nsel;
+    // one warp per (i, j) pair, lanes stride the coordinates (coalesced rows)
+    for (int idx = tid >> 5; idx < nsel * nsel; idx += blockDim.x >> 5) {
+      const int i = idx / nsel, j = idx - i * nsel;
       if (j < i) continue;
       double s = 0.0;
-      for (int c = 0; c < C; ++c) s += sel[i * C + c] * sel[j * C + c];
-      A[i * nsel + j] = s;
-      A[j * nsel + i] = s;
+      for (int c = tid & 31; c < C; c += 32) s += sel[i * C + c] * sel[j * C + c];
+      s = warp_sum_d(s);
+      if ((tid & 31) == 0) {
+        A[i * (nsel + 1) + j] = s;
+        A[j * (nsel + 1) + i] = s;
+      }
     }
     __syncthreads();
-    jacobi_eigh(A, V, nsel, pairs, rp, rq, rc, rs, red);
+    STAMP(1);
+    const int gram_sweeps = jacobi_eigh(A, V, nsel, rp, rq, rc, rs, red, &rotated);
+    STAMP(2);
+    if (a.timing != nullptr && tid == 0) a.timing[12] = gram_sweeps;
     sort_eigen(A, V, nsel, evals, evecs, order);
     // stage the sorted eigenvectors in shared memory (A is free once evals are read)
     for (int i = tid; i < nsel * nsel; i += blockDim.x) A[i] = evecs[i];
@@ -340,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     __syncthreads();
   }
   const double diag_res = static_cast<double>(static_cast<float>(sel_tail));
+  STAMP(3);
 
   // ---- transaction -----------------------------------------------------------
   const double eta = a.eta;
@@ -353,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     rhs[c] = r;
     rn += r * r;
   }
+  for (int c = tid; c < C; c += blockDim.x) rsw[c] = 1.0 / sqrt(static_cast<double>(a.weights[c]));
   const double budget = block_sum(bsum, red);
   const double rhs_norm = sqrt(block_sum(rn, red));
   const int steps = C < kKrylov ? C : kKrylov;
@@ -363,22 +406,24 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
   }
   __syncthreads();
   double prev_beta = 0.0;
+  STAMP(4);
   for (int i = 0; i < steps; ++i) {
     for (int c = tid; c < C; c += blockDim.x) Q[i * C + c] = vec[c];
     // Lv[r] = sum_c L[r,c] vec[c]
     for (int r = tid >> 5; r < nsel; r += blockDim.x >> 5) {
       double s = 0.0;
-      for (int c = tid & 31; c < C; c += 32)
-        s += sel[r * C + c] / sqrt(static_cast<double>(a.weights[c])) * inv_sqrt_m * vec[c];
+      for (int c = tid & 31; c < C; c += 32) s += sel[r * C + c] * rsw[c] * vec[c];
+      s *= inv_sqrt_m;
       s = warp_sum_d(s);
       if ((tid & 31) == 0) Lv[r] = s;
     }
     __syncthreads();
     double adot = 0.0, anorm = 0.0;
     for (int c = tid; c < C; c += blockDim.x) {
-      const double rw = 1.0 / sqrt(static_cast<double>(a.weights[c]));
-      double s = diag_res / static_cast<double>(a.weights[c]) * vec[c];
-      for (int r = 0; r < nsel; ++r) s += sel[r * C + c] * rw * inv_sqrt_m * Lv[r];
+      const double rw = rsw[c] * inv_sqrt_m;
+      double acc = 0.0;
+      for (int r = 0; r < nsel; ++r) acc += sel[r * C + c] * Lv[r];
+      double s = diag_res / static_cast<double>(a.weights[c]) * vec[c] + acc * rw;
       act[c] = s;
       adot += vec[c] * s;
       anorm += s * s;
@@ -409,6 +454,11 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     if (tid == 0) alphas[i] = alpha;
     if (i + 1 < steps) {
       const double threshold = 64.0 * kEps * fmax(action_norm, 1.0);
+      const bool broke = beta <= threshold;  // uniform: beta is a block reduction
+      double fnorm = 0.0;
+      if (broke) {
+      // Breakdown: continue from a deterministic cosine vector re-orthogonalised
+      // against the basis (used only when it is not itself in the span).
       for (int c = tid; c < C; c += blockDim.x) fb[c] = cos(static_cast<double>(c + 1) * static_cast<double>(i + 1));
       __syncthreads();
       for (int pass = 0; pass < 2; ++pass) {
@@ -428,9 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
       }
       double fn = 0.0;
       for (int c = tid; c < C; c += blockDim.x) fn += fb[c] * fb[c];
-      const double fnorm = sqrt(block_sum(fn, red));
-      const bool broke = beta <= threshold;
-      const bool use_fb = (fnorm > threshold) && broke;
+      fnorm = sqrt(block_sum(fn, red));
+      }
+      const bool use_fb = broke && (fnorm > threshold);
       for (int c = tid; c < C; c += blockDim.x) {
         const double nxt = use_fb ? fb[c] / fmax(fnorm, kTiny) : res[c] / fmax(beta, kTiny);
         prv[c] = vec[c];
@@ -449,10 +499,13 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     if (i == j) v = alphas[i];
     else if (j == i + 1) v = betas[i];
     else if (i == j + 1) v = betas[j];
-    A[idx] = v;
+    A[i * (steps + 1) + j] = v;
   }
   __syncthreads();
-  jacobi_eigh(A, V, steps, pairs, rp, rq, rc, rs, red);
+  STAMP(6);
+  const int tri_sweeps = jacobi_eigh(A, V, steps, rp, rq, rc, rs, red, &rotated);
+  if (a.timing != nullptr && tid == 0) a.timing[13] = tri_sweeps;
+  STAMP(7);
   sort_eigen(A, V, steps, lam, evecT, order);
   for (int i = tid; i < steps; i += blockDim.x) lam[i] = fmax(lam[i], 0.0);
   __syncthreads();
@@ -470,32 +523,33 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     proj[tid] = s;
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 32) {
+    // One warp: lane j owns Krylov term j (steps <= 32), sums by shuffle.
+    const int lane = tid;
+    const bool own = lane < steps;
+    const double pj = own ? proj[lane] : 0.0, lj = own ? lam[lane] : 0.0;
     const double lower = kEps * static_cast<double>(C);
-    double lmax = 0.0;
-    for (int j = 0; j < steps; ++j) lmax = fmax(lmax, lam[j]);
+    double lmax = own ? lj : 0.0;
+    for (int o = 16; o > 0; o >>= 1) lmax = fmax(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
     const double upper = rhs_norm / sqrt(budget) + lmax + lower;
-    double hs = 0.0;
-    for (int j = 0; j < steps; ++j) {
-      const double v = proj[j] / (lam[j] + lower);
-      hs += v * v;
-    }
-    const bool hard = hs < budget;
+    auto secular = [&](double mu) {
+      const double v = own ? pj / (lj + mu) : 0.0;
+      return warp_sum_d(v * v);
+    };
+    const bool hard = secular(lower) < budget;
     double lo = lower, hi = upper;
     for (int r = 0; r < 64; ++r) {
       const double mid = 0.5 * (lo + hi);
-      double s = 0.0;
-      for (int j = 0; j < steps; ++j) {
-        const double v = proj[j] / (lam[j] + mid);
-        s += v * v;
-      }
-      if (s > budget) lo = mid; else hi = mid;
+      if (secular(mid) > budget) lo = mid; else hi = mid;
     }
-    sc[40] = hi;
-    sc[41] = hard ? 1.0 : 0.0;
-    for (int j = 0; j < steps; ++j) sc[j] = proj[j] / (lam[j] + hi);
+    if (own) sc[lane] = pj / (lj + hi);
+    if (lane == 0) {
+      sc[40] = hi;
+      sc[41] = hard ? 1.0 : 0.0;
+    }
   }
   __syncthreads();
+  STAMP(8);
   // y = E * sc  -> in the Krylov basis; cand = Q y / sqrt(w)
   if (tid < steps) {
     double s = 0.0;
@@ -593,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     a.result[5] = static_cast<float>(cand_score);
     a.result[8] = static_cast<float>(nsel);
   }
+  STAMP(9);
 }
 
 }  // namespace ledger
@@ -601,7 +656,7 @@ int64_t ledger_workspace_doubles(int C) {
   using namespace ledger;
   return static_cast<int64_t>(kCurRows) * C + static_cast<int64_t>(kMaxSel) * C + C +
          static_cast<int64_t>(kKrylov) * C + 7LL * C + kMaxSel + C + kKrylov * kKrylov + kCurRows +
-         static_cast<int64_t>(kMaxSel) * kMaxSel;
+         static_cast<int64_t>(kMaxSel) * kMaxSel + C;
 }
 
 int ledger_transaction(const float* cur_scores, const float* cur_decay, const float* exact,
@@ -610,13 +665,15 @@ int ledger_transaction(const float* cur_scores, const float* cur_decay, const fl
                        float* pers_decay_cross, float* pers_tail, float* discarded_fraction,
                        float* shrinkage, float* ref_row_norm, float* coefficients, float* candidate,
                        float* result, double* ws, int C, int prev_rows, int total_layers,
-                       bool functional, double eta, cudaStream_t stream) {
+                       bool functional, double eta, unsigned long long* timing,
+                       cudaStream_t stream) {
   using namespace ledger;
   if (C < 2 || (prev_rows != 0 && prev_rows != kCurRows && prev_rows != kPersRows)) return -1;
   Args a{cur_scores, cur_decay, exact, momentum, weights, layer_ids, decay_derivative, pers_scores,
          pers_total_diag, pers_decay_cross, pers_tail, discarded_fraction, shrinkage, ref_row_norm,
-         coefficients, candidate, result, ws, C, prev_rows, total_layers, functional ? 1 : 0, eta};
-  const size_t smem = 2ull * kMaxSel * kMaxSel * sizeof(double);
+         coefficients, candidate, result, ws, timing, C, prev_rows, total_layers,
+         functional ? 1 : 0, eta};
+  const size_t smem = 2ull * kMaxSel * (kMaxSel + 1) * sizeof(double);
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(transaction_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

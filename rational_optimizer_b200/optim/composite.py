@@ -121,9 +121,15 @@ class CompositeOptimizer:
 
     def __init__(self, optimizers):
         self.optimizers = list(optimizers)
-        self.param_groups = []
-        for opt in self.optimizers:
-            self.param_groups.extend(opt.param_groups)
+
+    @property
+    def param_groups(self):
+        """The children's current groups.  Built on every access because a
+        child's ``load_state_dict`` replaces its group dicts; a list cached at
+        construction would keep receiving scheduled LRs the children no longer
+        read (the reference's composite caches it, so its resumed composite
+        runs step at the checkpointed LR)."""
+        return [g for opt in self.optimizers for g in opt.param_groups]
 
     def zero_grad(self, set_to_none=True):
         for opt in self.optimizers:

@@ -85,7 +85,12 @@ class TillerThenMuonOptimizer:
         self._capture_telemetry_next_step = False
         self._last_telemetry = {}
         self.optimizers = [self.tiller_router, self.tiller_attention, self._adamw]
-        self.param_groups = _groups(self.optimizers)
+
+    @property
+    def param_groups(self):
+        """The active children's current groups (rebuilt per access: loading a
+        child's state replaces its group dicts)."""
+        return _groups(self.optimizers)
 
     @property
     def completed_steps(self):
@@ -162,7 +167,6 @@ class TillerThenMuonOptimizer:
         self._transitioned = True
         self.tiller_router.remove_hooks()
         self.optimizers = [self._ordinary_muon, self._adamw]
-        self.param_groups = _groups(self.optimizers)
 
     @torch.no_grad()
     def step(self):
@@ -225,7 +229,6 @@ class TillerThenMuonOptimizer:
             self._activate_muon_stage()
         else:
             self.optimizers = [self.tiller_router, self.tiller_attention, self._adamw]
-            self.param_groups = _groups(self.optimizers)
         self._last_telemetry = {}
         self._capture_telemetry_next_step = False
 
