@@ -762,3 +762,79 @@ int legacy_rational_backward(const float* gy, const float* x, const float* a, co
 }
 
 }  // namespace ro
+
+// ---------------------------------------------------------------------------
+// Allocation-free backward (declared and documented in grain_noalloc.h; no
+// counterpart in the reference).  Same kernels as grain_backward with fp32
+// tensors; the per-block coefficient partials live in a fixed device array.
+
+#include <mutex>
+
+#include "grain_noalloc.h"
+
+namespace ro {
+namespace grain {
+
+constexpr int64_t kNoAllocScratchFloats = 65536;  // 256 KiB
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+
+static float* noalloc_scratch_for_current_device(int* status) {
+  static std::mutex lock;
+  static float* addr[kNoAllocMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    *status = -3;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> guard(lock);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_partials) != cudaSuccess || p == nullptr) {
+      *status = -3;
+      return nullptr;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  *status = 0;
+  return addr[dev];
+}
+
+}  // namespace grain
+}  // namespace ro
+
+extern "C" int ro_grain_backward_noalloc(const float* gy, const float* x, const float* num,
+                                         const float* den, float* gx, float* grad_num,
+                                         float* grad_den, int64_t rows, int hidden, int groups,
+                                         float eps, cudaStream_t stream) {
+  using namespace ro::grain;
+  if (gy == nullptr || x == nullptr || num == nullptr || den == nullptr || gx == nullptr ||
+      grad_num == nullptr || grad_den == nullptr)
+    return -1;
+  if (groups <= 0 || hidden <= 0 || hidden % groups || rows < 0) return -1;
+  const int w = hidden / groups;
+  if (w > 256) return -1;
+  if (rows == 0) return 0;
+  int chunks, rpc;
+  plan_chunks(rows, groups, chunks, rpc);
+  if (static_cast<int64_t>(chunks) * groups * kBase > kNoAllocScratchFloats) return -2;
+  int status = 0;
+  float* partial = noalloc_scratch_for_current_device(&status);
+  if (partial == nullptr) return status;
+  const bool aligned = (hidden % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(gy) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(gx) % 16 == 0);
+  const dim3 grid(chunks, groups);
+  const bool ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
+    constexpr int E = decltype(e)::value;
+    constexpr bool C = decltype(contig)::value;
+    backward_kernel<float, float, float, E, C, kBase, false><<<grid, kThreads, 0, stream>>>(
+        gy, x, num, den, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, gx, partial, rows,
+        hidden, groups, 0, 0.0f, eps, rpc);
+  });
+  if (!ok) return -1;
+  reduce_coeff_kernel<<<(groups * kBase + 127) / 128, 128, 0, stream>>>(partial, chunks, groups, 0,
+                                                                        grad_num, grad_den, nullptr);
+  return static_cast<int>(cudaGetLastError());
+}
