@@ -178,3 +178,28 @@ def test_lr_trace_digest_matches_reference():
     assert resume.full_lr_trace_digest(args) == er.full_lr_trace_digest(args)
     ref_ns = trainer.reference_namespace(args)
     assert resume.complete_argument_digest(ref_ns) == er.complete_argument_digest(ref_ns)
+
+
+def test_aggregate_matches_reference(tmp_path):
+    refs = require_reference()
+    agg_ref = importlib.import_module("training.aggregate_results")
+    from rational_optimizer_b200.train import aggregate
+    for act, opt in (("silu", "adamw"), ("grain", "adamw"), ("grain", "lion")):
+        assert trainer.main(_tiny_args(tmp_path, "agg", "--activation", act, "--optimizer", opt,
+                                       "--steps", "3")) == 0
+    run_dir = tmp_path / "runs" / "agg"
+    ours = aggregate.build_rows(aggregate.parse_run_dir(run_dir), "silu", "", "adamw")
+    ref = agg_ref.build_rows(agg_ref.parse_run_dir(run_dir), "silu", "", "adamw")
+    import math as _m
+    for a_rows, b_rows in zip(ours, ref):
+        assert len(a_rows) == len(b_rows) > 0
+        for a, b in zip(a_rows, b_rows):
+            assert list(a) == list(b)
+            for k in a:
+                if isinstance(a[k], float) and _m.isnan(a[k]):
+                    assert _m.isnan(b[k])
+                else:
+                    assert a[k] == b[k], k
+    out = tmp_path / "out"
+    aggregate.main(["--run-dir", str(run_dir), "--out-dir", str(out)])
+    assert (out / "per_seed.csv").is_file() and (out / "README.md").is_file()
