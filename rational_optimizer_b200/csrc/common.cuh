@@ -47,11 +47,23 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
   return __float2bfloat16_rn(v);
 }
 
-// Load/store N contiguous elements as float.  N*sizeof(T) must be 4, 8 or 16
-// bytes (or N==1) and the address suitably aligned; callers guarantee it.
+// Load/store N contiguous elements as float.  N*sizeof(T) of 4, 8, 16 or 32
+// bytes uses vector accesses (the address must be aligned to min(16, size));
+// other sizes fall back to element accesses.  Callers guarantee alignment.
 template <typename T, int N>
 __device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&out)[N]) {
-  if constexpr (sizeof(T) * N == 16) {
+  if constexpr (sizeof(T) * N == 32) {
+    // two 16-byte loads (32 bytes, 16-byte aligned)
+    const uint4 raw0 = reinterpret_cast<const uint4*>(p)[0];
+    const uint4 raw1 = reinterpret_cast<const uint4*>(p)[1];
+    const T* e0 = reinterpret_cast<const T*>(&raw0);
+    const T* e1 = reinterpret_cast<const T*>(&raw1);
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      out[i] = to_f<T>(e0[i]);
+      out[N / 2 + i] = to_f<T>(e1[i]);
+    }
+  } else if constexpr (sizeof(T) * N == 16) {
     uint4 raw = *reinterpret_cast<const uint4*>(p);
     const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
@@ -74,7 +86,18 @@ __device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&out)[N
 
 template <typename T, int N>
 __device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&in)[N]) {
-  if constexpr (sizeof(T) * N == 16) {
+  if constexpr (sizeof(T) * N == 32) {
+    uint4 raw0, raw1;
+    T* e0 = reinterpret_cast<T*>(&raw0);
+    T* e1 = reinterpret_cast<T*>(&raw1);
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      e0[i] = from_f<T>(in[i]);
+      e1[i] = from_f<T>(in[N / 2 + i]);
+    }
+    reinterpret_cast<uint4*>(p)[0] = raw0;
+    reinterpret_cast<uint4*>(p)[1] = raw1;
+  } else if constexpr (sizeof(T) * N == 16) {
     uint4 raw;
     T* e = reinterpret_cast<T*>(&raw);
 #pragma unroll

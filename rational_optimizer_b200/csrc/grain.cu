@@ -17,7 +17,10 @@
 // registers, and coefficient gradients are reduced deterministically in two
 // stages (per-CTA partials, then a fixed-order reduction) instead of fp32
 // atomics, so data-parallel replicas stay bitwise identical.
+#include <mutex>
+
 #include "common.cuh"
+#include "packed.cuh"
 
 namespace ro {
 namespace grain {
@@ -369,6 +372,206 @@ backward_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Packed fast path (no local-basis atoms, no affine restriction, lanes own
+// E = w / 32 contiguous elements, E even).  Every elementwise step runs on
+// fp32 pairs with FFMA2/FMUL2, which halves the FP32 issue slots of the
+// scalar kernels above; the denominator is evaluated by Horner's rule in |t|
+// (Q = 1 + |t|(|b0| + |t|(|b1| + |t|(|b2| + |t||b3|)))), the same polynomial.
+
+struct PairCoeffs {
+  float2 a[kNum];   // numerator
+  float2 b[kDen];   // |denominator|
+};
+
+__device__ __forceinline__ void load_pair_coeffs(PairCoeffs& c, int g, const float* __restrict__ num,
+                                                 const float* __restrict__ den) {
+#pragma unroll
+  for (int j = 0; j < kNum; ++j) c.a[j] = splat2(num[g * kNum + j]);
+#pragma unroll
+  for (int j = 0; j < kDen; ++j) c.b[j] = splat2(fabsf(den[g * kDen + j]));
+}
+
+template <typename TI, typename TO, int E>
+__global__ void __launch_bounds__(kThreads, 4)
+forward_packed_kernel(const TI* __restrict__ x, const float* __restrict__ num,
+                      const float* __restrict__ den, TO* __restrict__ y, float* __restrict__ rho_out,
+                      int64_t rows, int hidden, int groups, float eps, int rows_per_chunk) {
+  constexpr int P = E / 2;
+  const int g = blockIdx.y;
+  const int w = hidden / groups;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  PairCoeffs c;
+  load_pair_coeffs(c, g, num, den);
+  const float2 one = splat2(1.0f);
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_chunk;
+  const int64_t r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
+  const float inv_w = 1.0f / static_cast<float>(w);
+  constexpr int U = E == 2 ? 4 : 2;  // rows in flight per warp (register budget)
+  const int64_t col = static_cast<int64_t>(g) * w + lane * E;
+  for (int64_t rb = r0 + warp; rb < r1; rb += kWarps * U) {
+    float2 v[U][P];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r < r1) load_pairs<TI, E>(x + r * hidden + col, v[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r >= r1) break;
+      float2 s2 = splat2(0.0f);
+#pragma unroll
+      for (int i = 0; i < P; ++i) s2 = fma2(v[u][i], v[u][i], s2);
+      const float ss = warp_sum(s2.x + s2.y);
+      const float rho = sqrtf(ss * inv_w + eps);
+      const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const float2 t = mul2(v[u][i], ir);
+        const float2 at = abs2(t);
+        float2 p = fma2(c.a[5], t, c.a[4]);
+        p = fma2(p, t, c.a[3]);
+        p = fma2(p, t, c.a[2]);
+        p = fma2(p, t, c.a[1]);
+        p = fma2(p, t, c.a[0]);
+        float2 q = fma2(c.b[3], at, c.b[2]);
+        q = fma2(q, at, c.b[1]);
+        q = fma2(q, at, c.b[0]);
+        q = fma2(q, at, one);
+        v[u][i] = mul2(mul2(p, rh), rcp2(q));
+      }
+      store_pairs<TO, E>(y + r * hidden + col, v[u]);
+      if (rho_out != nullptr && lane == 0) rho_out[r * groups + g] = rho;
+    }
+  }
+}
+
+// Backward of the packed path.  Coefficient partials are accumulated in the
+// factored form of the scalar kernel: d/da_k -> gy rho t^k / Q and
+// d/d|b_j| -> -gy rho f / Q {|t|, t^2, |t|^3, t^4}; the signs of b_j are
+// applied once per CTA.
+template <typename TG, typename TI, typename TO, int E>
+__global__ void __launch_bounds__(kThreads, 3)
+backward_packed_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
+                       const float* __restrict__ num, const float* __restrict__ den,
+                       TO* __restrict__ gx, float* __restrict__ partial, int64_t rows, int hidden,
+                       int groups, float eps, int rows_per_chunk) {
+  constexpr int P = E / 2;
+  __shared__ float red[kWarps][kBase];
+  const int g = blockIdx.y;
+  const int w = hidden / groups;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  PairCoeffs c;
+  load_pair_coeffs(c, g, num, den);
+  // derivative coefficients: P' = a1 + 2a2 t + 3a3 t^2 + 4a4 t^3 + 5a5 t^4,
+  // dQ/dt = sign0(t)|b0| + t (2|b1| + |t| (3|b2| + 4|b3||t|))
+  const float2 da5 = mul2(splat2(5.0f), c.a[5]), da4 = mul2(splat2(4.0f), c.a[4]);
+  const float2 da3 = mul2(splat2(3.0f), c.a[3]), da2 = mul2(splat2(2.0f), c.a[2]);
+  const float2 db3 = mul2(splat2(4.0f), c.b[3]), db2 = mul2(splat2(3.0f), c.b[2]);
+  const float2 db1 = mul2(splat2(2.0f), c.b[1]);
+  const float2 one = splat2(1.0f);
+  float2 acc[kBase];
+#pragma unroll
+  for (int k = 0; k < kBase; ++k) acc[k] = splat2(0.0f);
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_chunk;
+  const int64_t r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
+  const float inv_w = 1.0f / static_cast<float>(w);
+  const int64_t col = static_cast<int64_t>(g) * w + lane * E;
+  constexpr int U = E == 8 ? 1 : 2;  // rows in flight per warp (register budget)
+  for (int64_t rb = r0 + warp; rb < r1; rb += kWarps * U) {
+    float2 z[U][P], gy[U][P];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r < r1) {
+        load_pairs<TI, E>(x + r * hidden + col, z[u]);
+        load_pairs<TG, E>(gy_ptr + r * hidden + col, gy[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
+      if (r >= r1) break;
+      float2 s2 = splat2(0.0f);
+#pragma unroll
+      for (int i = 0; i < P; ++i) s2 = fma2(z[u][i], z[u][i], s2);
+      const float ss = warp_sum(s2.x + s2.y);
+      const float rho = sqrtf(ss * inv_w + eps);
+      const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
+      float2 sacc = splat2(0.0f);
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const float2 t = mul2(z[u][i], ir);
+        const float2 at = abs2(t);
+        const float2 t2 = mul2(t, t);
+        float2 p = fma2(c.a[5], t, c.a[4]);
+        p = fma2(p, t, c.a[3]);
+        p = fma2(p, t, c.a[2]);
+        p = fma2(p, t, c.a[1]);
+        p = fma2(p, t, c.a[0]);
+        float2 dp = fma2(da5, t, da4);
+        dp = fma2(dp, t, da3);
+        dp = fma2(dp, t, da2);
+        dp = fma2(dp, t, c.a[1]);
+        float2 q = fma2(c.b[3], at, c.b[2]);
+        q = fma2(q, at, c.b[1]);
+        q = fma2(q, at, c.b[0]);
+        q = fma2(q, at, one);
+        float2 h = fma2(db3, at, db2);
+        h = fma2(h, at, db1);
+        const float2 dq = fma2(t, h, mul2(c.b[0], sign02(t)));
+        const float2 iq = rcp2(q);
+        const float2 f = mul2(p, iq);
+        const float2 df = mul2(fma2(neg2(f), dq, dp), iq);
+        const float2 g2 = gy[u][i];
+        // sum over the group of gy (f - t f')
+        sacc = fma2(g2, fma2(neg2(t), df, f), sacc);
+        // coefficient partials
+        const float2 s1 = mul2(mul2(g2, rh), iq);
+        const float2 t3 = mul2(t2, t), t4 = mul2(t2, t2);
+        acc[0] = add2(acc[0], s1);
+        acc[1] = fma2(s1, t, acc[1]);
+        acc[2] = fma2(s1, t2, acc[2]);
+        acc[3] = fma2(s1, t3, acc[3]);
+        acc[4] = fma2(s1, t4, acc[4]);
+        acc[5] = fma2(s1, mul2(t4, t), acc[5]);
+        const float2 vb = mul2(s1, f);
+        acc[6] = fma2(vb, at, acc[6]);
+        acc[7] = fma2(vb, t2, acc[7]);
+        acc[8] = fma2(vb, mul2(at, t2), acc[8]);
+        acc[9] = fma2(vb, t4, acc[9]);
+        // keep t and gy f' for grad_x
+        z[u][i] = t;
+        gy[u][i] = mul2(g2, df);
+      }
+      const float2 sw = splat2(warp_sum(sacc.x + sacc.y) * inv_w);
+#pragma unroll
+      for (int i = 0; i < P; ++i) z[u][i] = fma2(z[u][i], sw, gy[u][i]);
+      store_pairs<TO, E>(gx + r * hidden + col, z[u]);
+    }
+  }
+  float sgn[kDen];
+#pragma unroll
+  for (int k = 0; k < kDen; ++k) sgn[k] = -sign0(den[g * kDen + k]);
+#pragma unroll
+  for (int k = 0; k < kBase; ++k) {
+    float v = acc[k].x + acc[k].y;
+    if (k >= kNum) v *= sgn[k - kNum];
+    v = warp_sum(v);
+    if (lane == 0) red[warp][k] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kBase) {
+    float v = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < kWarps; ++wi) v += red[wi][threadIdx.x];
+    partial[(static_cast<int64_t>(blockIdx.x) * groups + g) * kBase + threadIdx.x] = v;
+  }
+}
+
 // Fixed-order reduction of the per-chunk partials into the three gradient
 // tensors (fp64 accumulation; output fp32).
 __global__ void reduce_coeff_kernel(const float* __restrict__ partial, int chunks, int groups,
@@ -604,9 +807,23 @@ int grain_forward(const void* x, int x_dtype, const float* num, const float* den
   const bool aligned = (hidden % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(y) % 16 == 0);
   bool ok = false;
+  const bool packed = nb == 0 && aligned && (w == 256 || w == 128 || w == 64);
   auto go = [&](auto ti, auto to) {
     using TI = decltype(ti);
     using TO = decltype(to);
+    if (packed) {
+      auto launch = [&](auto e) {
+        constexpr int E = decltype(e)::value;
+        forward_packed_kernel<TI, TO, E><<<grid, kThreads, 0, stream>>>(
+            static_cast<const TI*>(x), num, den, static_cast<TO*>(y), rho_out, rows, hidden, groups,
+            eps, rpc);
+      };
+      if (w == 256) launch(std::integral_constant<int, 8>{});
+      else if (w == 128) launch(std::integral_constant<int, 4>{});
+      else launch(std::integral_constant<int, 2>{});
+      ok = true;
+      return;
+    }
     ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
       constexpr int E = decltype(e)::value;
       constexpr bool C = decltype(contig)::value;
@@ -650,10 +867,24 @@ int grain_backward(const void* gy, int gy_dtype, const void* x, int x_dtype, con
                        (reinterpret_cast<uintptr_t>(gx) % 16 == 0) &&
                        (!restrict_ || reinterpret_cast<uintptr_t>(nonlinear_y) % 16 == 0);
   bool ok = false;
+  const bool packed = nb == 0 && !restrict_ && aligned && (w == 256 || w == 128 || w == 64);
   auto go = [&](auto tg, auto ti, auto to) {
     using TG = decltype(tg);
     using TI = decltype(ti);
     using TO = decltype(to);
+    if (packed) {
+      auto launch = [&](auto e) {
+        constexpr int E = decltype(e)::value;
+        backward_packed_kernel<TG, TI, TO, E><<<grid, kThreads, 0, stream>>>(
+            static_cast<const TG*>(gy), static_cast<const TI*>(x), num, den, static_cast<TO*>(gx),
+            partial, rows, hidden, groups, eps, rpc);
+      };
+      if (w == 256) launch(std::integral_constant<int, 8>{});
+      else if (w == 128) launch(std::integral_constant<int, 4>{});
+      else launch(std::integral_constant<int, 2>{});
+      ok = true;
+      return;
+    }
     ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
       constexpr int E = decltype(e)::value;
       constexpr bool C = decltype(contig)::value;
@@ -768,8 +999,6 @@ int legacy_rational_backward(const float* gy, const float* x, const float* a, co
 // counterpart in the reference).  Same kernels as grain_backward with fp32
 // tensors; the per-block coefficient partials live in a fixed device array.
 
-#include <mutex>
-
 #include "grain_noalloc.h"
 
 namespace ro {
@@ -819,20 +1048,34 @@ extern "C" int ro_grain_backward_noalloc(const float* gy, const float* x, const 
   int chunks, rpc;
   plan_chunks(rows, groups, chunks, rpc);
   if (static_cast<int64_t>(chunks) * groups * kBase > kNoAllocScratchFloats) return -2;
-  int status = 0;
-  float* partial = noalloc_scratch_for_current_device(&status);
-  if (partial == nullptr) return status;
+  int setup = 0;
+  float* partial = noalloc_scratch_for_current_device(&setup);
+  if (partial == nullptr) return setup;
   const bool aligned = (hidden % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(gy) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(gx) % 16 == 0);
   const dim3 grid(chunks, groups);
-  const bool ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
-    constexpr int E = decltype(e)::value;
-    constexpr bool C = decltype(contig)::value;
-    backward_kernel<float, float, float, E, C, kBase, false><<<grid, kThreads, 0, stream>>>(
-        gy, x, num, den, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, gx, partial, rows,
-        hidden, groups, 0, 0.0f, eps, rpc);
-  });
+  bool ok = false;
+  if (aligned && (w == 256 || w == 128 || w == 64)) {
+    // same kernel choice as grain_backward, so both entry points agree bitwise
+    auto launch = [&](auto e) {
+      constexpr int E = decltype(e)::value;
+      backward_packed_kernel<float, float, float, E><<<grid, kThreads, 0, stream>>>(
+          gy, x, num, den, gx, partial, rows, hidden, groups, eps, rpc);
+    };
+    if (w == 256) launch(std::integral_constant<int, 8>{});
+    else if (w == 128) launch(std::integral_constant<int, 4>{});
+    else launch(std::integral_constant<int, 2>{});
+    ok = true;
+  } else {
+    ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
+      constexpr int E = decltype(e)::value;
+      constexpr bool C = decltype(contig)::value;
+      backward_kernel<float, float, float, E, C, kBase, false><<<grid, kThreads, 0, stream>>>(
+          gy, x, num, den, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, gx, partial, rows,
+          hidden, groups, 0, 0.0f, eps, rpc);
+    });
+  }
   if (!ok) return -1;
   reduce_coeff_kernel<<<(groups * kBase + 127) / 128, 128, 0, stream>>>(partial, chunks, groups, 0,
                                                                         grad_num, grad_den, nullptr);

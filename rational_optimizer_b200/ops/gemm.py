@@ -64,3 +64,18 @@ def matmul_tn(a: torch.Tensor, b: torch.Tensor, out_dtype=None) -> torch.Tensor:
         return torch.mm(a.t(), b, out_dtype=out_dtype)
     out = a.t() @ b
     return out if out_dtype is None else out.to(out_dtype)
+
+
+_ADDMM_DTYPE_OUT = True
+
+
+def matmul_tn_accumulate_(out: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``out += a^T @ b`` with bf16 operands and an fp32 ``out`` (weight-gradient
+    accumulation straight into a gradient buffer, beta = 1 in the GEMM)."""
+    global _ADDMM_DTYPE_OUT
+    if _ADDMM_DTYPE_OUT and a.is_cuda and out.dtype == torch.float32 and a.dtype != torch.float32:
+        try:
+            return torch.addmm(out, a.t(), b, out_dtype=torch.float32, out=out)
+        except (RuntimeError, TypeError):
+            _ADDMM_DTYPE_OUT = False
+    return out.add_(matmul_tn(a, b, out_dtype=out.dtype))

@@ -2,7 +2,8 @@
 
 ``y = x @ W^T`` runs in bf16 on CUDA (fp32 accumulation); the weight gradient
 is produced directly in fp32 (``dW = dy^T x``) so fp32 master parameters need
-no extra cast pass.  The bf16 copy of each weight is cached and refreshed
+no extra cast pass.  When the weight's ``.grad`` is a managed fp32 buffer, ``dW`` is accumulated
+into it inside the GEMM.  The bf16 copy of each weight is cached and refreshed
 only when the parameter's version counter changes (i.e. after an optimizer
 step), so each weight is cast once per step, not once per micro-batch.
 On CPU the layer computes in fp32 (reference path for tests).
@@ -12,6 +13,12 @@ from __future__ import annotations
 import torch
 
 from . import gemm
+
+# Parameters carrying this attribute (set by the data-parallel gradient
+# synchroniser, whose ``zero_grad`` zeroes their ``.grad`` buffers every step)
+# receive weight gradients by in-GEMM accumulation into ``.grad`` instead of
+# through autograd.  ``torch.autograd.grad`` therefore sees no gradient for them.
+ACCUMULATE_ATTR = "_ro_accumulate_grad"
 
 
 class _WeightCache:
@@ -38,6 +45,7 @@ def cached_cast(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -
 class _LinearFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, w_compute):
+        ctx.weight = weight
         x2 = x.reshape(-1, x.shape[-1])
         if x2.dtype != w_compute.dtype:
             x2 = x2.to(w_compute.dtype)
@@ -60,7 +68,14 @@ class _LinearFunction(torch.autograd.Function):
             if gx.dtype != ctx.x_dtype:
                 gx = gx.to(ctx.x_dtype)
         if ctx.needs_input_grad[1]:
-            gw = gemm.matmul_tn(g2, x2, out_dtype=ctx.w_dtype)
+            buf = ctx.weight.grad
+            if (getattr(ctx.weight, ACCUMULATE_ATTR, False) and buf is not None and buf.is_cuda
+                    and buf.dtype == torch.float32 and buf.is_contiguous()):
+                # dW accumulates in the GEMM (beta = 1) straight into the
+                # parameter's gradient buffer; autograd then has nothing to add.
+                gemm.matmul_tn_accumulate_(buf, g2, x2)
+            else:
+                gw = gemm.matmul_tn(g2, x2, out_dtype=ctx.w_dtype)
         return gx, gw, None
 
 

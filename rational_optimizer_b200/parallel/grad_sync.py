@@ -15,6 +15,8 @@ import os
 import torch
 import torch.distributed as dist
 
+from ..ops.linear import ACCUMULATE_ATTR
+
 
 class GradientSynchronizer:
     def __init__(self, model: torch.nn.Module, *, group=None, bucket_bytes: int = 256 << 20,
@@ -44,10 +46,14 @@ class GradientSynchronizer:
             self.flat = torch.zeros(total, dtype=dtype, device=device)
         self.views = []
         offset = 0
+        accumulate = self.flat.is_cuda and self.flat.dtype == torch.float32
         for p in params:
             n = p.numel()
             view = self.flat[offset: offset + n].view_as(p)
             p.grad = view
+            if accumulate:
+                # the model's GEMMs may add weight gradients straight into the view
+                setattr(p, ACCUMULATE_ATTR, True)
             self.views.append(view)
             offset += n
         self.bucket_elems = max(1, bucket_bytes // self.flat.element_size())
