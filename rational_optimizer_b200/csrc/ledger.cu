@@ -303,11 +303,18 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     __syncthreads();
   } else {
     const int prev = a.prev_rows;
-    nsel = prev + kCurRows;
+    // Surrogate rows are 32 copies of one row.  Everything downstream depends
+    // on the selection only through sel^T sel, so the copies collapse into a
+    // single row scaled by sqrt(32): the eigenproblem shrinks from 96 to 65
+    // rows (the 31 removed eigenvalues are exactly zero and always discarded).
+    const bool collapse = !a.functional;
+    const int cur_rows = collapse ? 1 : kCurRows;
+    nsel = prev + cur_rows;
     const float sb = static_cast<float>(sqrt(beta2)), sc1 = static_cast<float>(sqrt(1.0 - beta2));
+    const double row_scale = collapse ? sqrt(static_cast<double>(kCurRows)) : 1.0;
     for (int i = tid; i < prev * C; i += blockDim.x) sel[i] = static_cast<double>(a.pers_scores[i] * sb);
-    for (int i = tid; i < kCurRows * C; i += blockDim.x)
-      sel[prev * C + i] = static_cast<double>(static_cast<float>(cur[i]) * sc1);
+    for (int i = tid; i < cur_rows * C; i += blockDim.x)
+      sel[prev * C + i] = static_cast<double>(static_cast<float>(cur[i]) * sc1) * row_scale;
     const double prev_tail = static_cast<double>(a.pers_tail[0]);
     sel_tail = prev_tail * beta2;
     for (int c = tid; c < C; c += blockDim.x) {
@@ -354,6 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
       const double mult = sqrt(fmax(kept - shrink, 0.0) / fmax(kept, kTiny));
       a.pers_scores[r * C + c] = static_cast<float>(mult * s);
     }
+    // rows of the removed zero eigenvalues (collapsed surrogate only)
+    for (int idx = retained * C + tid; idx < kPersRows * C; idx += blockDim.x) a.pers_scores[idx] = 0.0f;
     __syncthreads();
     const double pers_tail = sel_tail + shrink / (2.0 * kCurRows);
     for (int c = tid; c < C; c += blockDim.x) {
@@ -376,7 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
       a.pers_tail[0] = static_cast<float>(pers_tail);
       a.shrinkage[0] = static_cast<float>(shrink);
       a.discarded_fraction[0] = static_cast<float>(disc / fmax(tot, kTiny));
-      a.result[7] = static_cast<float>(retained);
+      const int logical = a.prev_rows + kCurRows;
+      a.result[7] = static_cast<float>(logical < kPersRows ? logical : kPersRows);
     }
     __syncthreads();
   }
@@ -645,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     a.result[3] = static_cast<float>(budget_res);
     a.result[4] = static_cast<float>(parent_score);
     a.result[5] = static_cast<float>(cand_score);
-    a.result[8] = static_cast<float>(nsel);
+    a.result[8] = static_cast<float>(a.prev_rows == 0 || a.functional ? nsel : nsel + kCurRows - 1);
   }
   STAMP(9);
 }

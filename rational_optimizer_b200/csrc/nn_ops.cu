@@ -281,43 +281,50 @@ add_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __rest
 // QKV split + RoPE.  qkv: [B*S, 3*H*hd] (row = token); outputs q, k, v as
 // [B, H, S, hd] contiguous.  Interleaved pairs (2j, 2j+1) rotate by
 // angle = pos * theta^(-2j/hd) using fp32 cos/sin tables [S, hd/2].
+// One CTA per token row (blockIdx.x = b * S + s); thread t owns 8 contiguous
+// head-dim elements of (which, h) = (t / (H * hd/8), (t / (hd/8)) % H).  The
+// qkv row is read contiguously; each (which, h) segment of hd elements is
+// written contiguously.
+__device__ __forceinline__ void rope_rotate(float (&val)[8], const float* __restrict__ cs,
+                                            const float* __restrict__ sn, bool inverse) {
+  const float4 c4 = *reinterpret_cast<const float4*>(cs);
+  const float4 s4 = *reinterpret_cast<const float4*>(sn);
+  const float c[4] = {c4.x, c4.y, c4.z, c4.w}, si[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float e = val[2 * p], o = val[2 * p + 1];
+    if (!inverse) {
+      val[2 * p] = e * c[p] - o * si[p];
+      val[2 * p + 1] = e * si[p] + o * c[p];
+    } else {
+      val[2 * p] = e * c[p] + o * si[p];
+      val[2 * p + 1] = -e * si[p] + o * c[p];
+    }
+  }
+}
+
 template <typename T>
 __global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __restrict__ cos_t,
                                     const float* __restrict__ sin_t, T* __restrict__ q,
                                     T* __restrict__ k, T* __restrict__ v, int B, int S, int H,
                                     int hd) {
-  // One thread per 8 contiguous head-dim elements of one (b, h, s) for one of q/k/v.
   const int vec = hd / 8;
-  const int64_t per_tensor = static_cast<int64_t>(B) * H * S * vec;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= 3 * per_tensor) return;
-  const int which = static_cast<int>(idx / per_tensor);
-  int64_t rem = idx % per_tensor;
-  const int jv = static_cast<int>(rem % vec);
-  rem /= vec;
-  const int s = static_cast<int>(rem % S);
-  rem /= S;
-  const int h = static_cast<int>(rem % H);
-  const int b = static_cast<int>(rem / H);
+  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  if (t >= 3 * H * vec) return;
+  const int token = blockIdx.x;
+  const int b = token / S, s = token - b * S;
+  const int which = t / (H * vec);
+  const int rem = t - which * H * vec;
+  const int h = rem / vec, jv = rem - h * vec;
   const int d = H * hd;
-  const int64_t src = ((static_cast<int64_t>(b) * S + s) * 3 + which) * d + h * hd + jv * 8;
-  const int64_t dst = ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8;
   float val[8];
-  load_vec<T, 8>(qkv + src, val);
+  load_vec<T, 8>(qkv + (static_cast<int64_t>(token) * 3 + which) * d + h * hd + jv * 8, val);
   if (which < 2) {
     const int half = hd / 2;
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int j = jv * 4 + p;
-      const float c = cos_t[s * half + j];
-      const float sn = sin_t[s * half + j];
-      const float e = val[2 * p], o = val[2 * p + 1];
-      val[2 * p] = e * c - o * sn;
-      val[2 * p + 1] = e * sn + o * c;
-    }
+    rope_rotate(val, cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, false);
   }
   T* out = which == 0 ? q : (which == 1 ? k : v);
-  store_vec<T, 8>(out + dst, val);
+  store_vec<T, 8>(out + ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8, val);
 }
 
 template <typename T>
@@ -326,41 +333,27 @@ __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restric
                                     const float* __restrict__ sin_t, T* __restrict__ dqkv, int B,
                                     int S, int H, int hd) {
   const int vec = hd / 8;
-  const int64_t per_tensor = static_cast<int64_t>(B) * H * S * vec;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= 3 * per_tensor) return;
-  const int which = static_cast<int>(idx / per_tensor);
-  int64_t rem = idx % per_tensor;
-  const int jv = static_cast<int>(rem % vec);
-  rem /= vec;
-  const int s = static_cast<int>(rem % S);
-  rem /= S;
-  const int h = static_cast<int>(rem % H);
-  const int b = static_cast<int>(rem / H);
+  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  if (t >= 3 * H * vec) return;
+  const int token = blockIdx.x;
+  const int b = token / S, s = token - b * S;
+  const int which = t / (H * vec);
+  const int rem = t - which * H * vec;
+  const int h = rem / vec, jv = rem - h * vec;
   const int d = H * hd;
-  const int64_t dst = ((static_cast<int64_t>(b) * S + s) * 3 + which) * d + h * hd + jv * 8;
-  const int64_t src = ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8;
   const T* in = which == 0 ? dq : (which == 1 ? dk : dv);
   float val[8];
-  load_vec<T, 8>(in + src, val);
+  load_vec<T, 8>(in + ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8, val);
   if (which < 2) {
     const int half = hd / 2;
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int j = jv * 4 + p;
-      const float c = cos_t[s * half + j];
-      const float sn = sin_t[s * half + j];
-      const float ge = val[2 * p], go = val[2 * p + 1];
-      val[2 * p] = ge * c + go * sn;
-      val[2 * p + 1] = -ge * sn + go * c;
-    }
+    rope_rotate(val, cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, true);
   }
-  store_vec<T, 8>(dqkv + dst, val);
+  store_vec<T, 8>(dqkv + (static_cast<int64_t>(token) * 3 + which) * d + h * hd + jv * 8, val);
 }
 
 // ---------------------------------------------------------------------------
 // Cross-entropy with in-place gradient.  One CTA per row; the row is staged
-// in shared memory (V <= kCeMaxSmemElems) so logits are read from HBM once
+// in shared memory (rows of up to 200 KB) so logits are read from HBM once
 // and the gradient written once.  loss_row[r] = lse - x[target]; logits are
 // overwritten by (softmax - onehot) * grad_scale.  Rows whose target equals
 // ignore_index get loss 0 and gradient 0.
@@ -371,76 +364,88 @@ __global__ void __launch_bounds__(kCeThreads)
 ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
                   float* __restrict__ loss_row, int64_t rows, int V, float grad_scale,
                   int64_t ignore_index, int use_smem) {
-  extern __shared__ float srow[];
-  __shared__ float red[kCeThreads / 32];
+  // The row is staged in shared memory in its own dtype (bf16: 100 KB for a
+  // 50k vocabulary, so two CTAs fit per SM); max and sum of exp are taken in
+  // one online pass, then the gradient is written over the logits.
+  extern __shared__ __align__(16) unsigned char ce_smem[];
+  T* srow = reinterpret_cast<T*>(ce_smem);
+  __shared__ float red_m[kCeThreads / 32], red_s[kCeThreads / 32];
   __shared__ float bcast;
   const int64_t row = blockIdx.x;
   if (row >= rows) return;
   T* lr = logits + row * V;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tgt = target[row];
-  // pass 1: max
-  float m = -INFINITY;
   const bool vec_ok = (V % 8 == 0) && (reinterpret_cast<uintptr_t>(lr) % 16 == 0);
+  float m = -INFINITY, s = 0.f;
+  auto absorb = [&](const float (&v)[8], int count) {
+    float mx = v[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j)
+      if (j < count) mx = fmaxf(mx, v[j]);
+    if (mx > m) {
+      s *= __expf(m - mx);
+      m = mx;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < count) s += __expf(v[j] - m);
+  };
   if (vec_ok) {
     for (int i = tid * 8; i < V; i += kCeThreads * 8) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(lr + i);
+      if (use_smem) *reinterpret_cast<uint4*>(srow + i) = raw;
       float v8[8];
-      load_vec<T, 8>(lr + i, v8);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (use_smem) srow[i + j] = v8[j];
-        m = fmaxf(m, v8[j]);
-      }
+      load_vec<T, 8>(reinterpret_cast<const T*>(&raw), v8);
+      absorb(v8, 8);
     }
   } else {
     for (int i = tid; i < V; i += kCeThreads) {
-      const float v = to_f<T>(lr[i]);
-      if (use_smem) srow[i] = v;
-      m = fmaxf(m, v);
+      const T raw = lr[i];
+      if (use_smem) srow[i] = raw;
+      float v8[8] = {to_f<T>(raw), 0, 0, 0, 0, 0, 0, 0};
+      absorb(v8, 1);
     }
   }
-  m = warp_max(m);
-  if (lane == 0) red[warp] = m;
+  // combine (m, s) pairs: warp, then block
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_s[warp] = s;
+  }
   __syncthreads();
   if (warp == 0) {
-    float t = lane < kCeThreads / 32 ? red[lane] : -INFINITY;
-    t = warp_max(t);
-    if (lane == 0) bcast = t;
+    float wm = lane < kCeThreads / 32 ? red_m[lane] : -INFINITY;
+    float ws = lane < kCeThreads / 32 ? red_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, wm, o);
+      const float os = __shfl_xor_sync(0xffffffffu, ws, o);
+      const float nm = fmaxf(wm, om);
+      ws = (wm == -INFINITY ? 0.f : ws * __expf(wm - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+      wm = nm;
+    }
+    if (lane == 0) bcast = wm + __logf(ws);
   }
   __syncthreads();
-  m = bcast;
-  __syncthreads();
-  float s = 0.f;
-  for (int i = tid; i < V; i += kCeThreads) {
-    const float v = use_smem ? srow[i] : to_f<T>(lr[i]);
-    s += __expf(v - m);
-  }
-  s = warp_sum(s);
-  if (lane == 0) red[warp] = s;
-  __syncthreads();
-  if (warp == 0) {
-    float t = lane < kCeThreads / 32 ? red[lane] : 0.f;
-    t = warp_sum(t);
-    if (lane == 0) bcast = t;
-  }
-  __syncthreads();
-  const float lse = m + __logf(bcast);
+  const float lse = bcast;
   const bool ignored = (tgt == ignore_index) || tgt < 0 || tgt >= V;
   if (tid == 0) {
-    const float xt = ignored ? 0.f : (use_smem ? srow[tgt] : to_f<T>(lr[tgt]));
+    const float xt = ignored ? 0.f : to_f<T>(use_smem ? srow[tgt] : lr[tgt]);
     loss_row[row] = ignored ? 0.f : (lse - xt);
   }
-  __syncthreads();
   const float scale = ignored ? 0.f : grad_scale;
   if (vec_ok) {
     for (int i = tid * 8; i < V; i += kCeThreads * 8) {
       float v8[8];
-      if (use_smem) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v8[j] = srow[i + j];
-      } else {
-        load_vec<T, 8>(lr + i, v8);
-      }
+      load_vec<T, 8>(use_smem ? srow + i : lr + i, v8);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float p = __expf(v8[j] - lse);
@@ -451,7 +456,7 @@ ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
     }
   } else {
     for (int i = tid; i < V; i += kCeThreads) {
-      const float v = use_smem ? srow[i] : to_f<T>(lr[i]);
+      const float v = to_f<T>(use_smem ? srow[i] : lr[i]);
       float p = __expf(v - lse);
       if (i == tgt) p -= 1.0f;
       lr[i] = from_f<T>(p * scale);
@@ -594,15 +599,16 @@ int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, cons
 int rope_qkv_forward(const void* qkv, const float* cos_t, const float* sin_t, void* q, void* k,
                      void* v, int B, int S, int H, int hd, int dtype, cudaStream_t stream) {
   if (hd % 8) return -1;
-  const int64_t total = 3LL * B * H * S * (hd / 8);
-  if (total == 0) return 0;
-  const int blocks = ceil_div_i(total, 256);
+  if (static_cast<int64_t>(B) * S * H == 0) return 0;
+  const int per_token = 3 * H * (hd / 8);
+  const int threads = per_token < 512 ? ((per_token + 31) / 32) * 32 : 512;
+  const dim3 blocks(static_cast<unsigned>(B * S), static_cast<unsigned>((per_token + threads - 1) / threads));
   if (dtype == 0)
-    nn::rope_qkv_fwd_kernel<float><<<blocks, 256, 0, stream>>>(
+    nn::rope_qkv_fwd_kernel<float><<<blocks, threads, 0, stream>>>(
         static_cast<const float*>(qkv), cos_t, sin_t, static_cast<float*>(q), static_cast<float*>(k),
         static_cast<float*>(v), B, S, H, hd);
   else if (dtype == 1)
-    nn::rope_qkv_fwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+    nn::rope_qkv_fwd_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(qkv), cos_t, sin_t, static_cast<__nv_bfloat16*>(q),
         static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), B, S, H, hd);
   else return -2;
@@ -613,15 +619,16 @@ int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const floa
                       const float* sin_t, void* dqkv, int B, int S, int H, int hd, int dtype,
                       cudaStream_t stream) {
   if (hd % 8) return -1;
-  const int64_t total = 3LL * B * H * S * (hd / 8);
-  if (total == 0) return 0;
-  const int blocks = ceil_div_i(total, 256);
+  if (static_cast<int64_t>(B) * S * H == 0) return 0;
+  const int per_token = 3 * H * (hd / 8);
+  const int threads = per_token < 512 ? ((per_token + 31) / 32) * 32 : 512;
+  const dim3 blocks(static_cast<unsigned>(B * S), static_cast<unsigned>((per_token + threads - 1) / threads));
   if (dtype == 0)
-    nn::rope_qkv_bwd_kernel<float><<<blocks, 256, 0, stream>>>(
+    nn::rope_qkv_bwd_kernel<float><<<blocks, threads, 0, stream>>>(
         static_cast<const float*>(dq), static_cast<const float*>(dk), static_cast<const float*>(dv),
         cos_t, sin_t, static_cast<float*>(dqkv), B, S, H, hd);
   else if (dtype == 1)
-    nn::rope_qkv_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+    nn::rope_qkv_bwd_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(dq), static_cast<const __nv_bfloat16*>(dk),
         static_cast<const __nv_bfloat16*>(dv), cos_t, sin_t, static_cast<__nv_bfloat16*>(dqkv), B, S,
         H, hd);
@@ -629,14 +636,15 @@ int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const floa
   return static_cast<int>(cudaGetLastError());
 }
 
-constexpr int kCeMaxSmemElems = 200 * 1024 / 4;
+constexpr size_t kCeMaxSmemBytes = 200 * 1024;
 
 int cross_entropy_fwd_bwd(void* logits, const int64_t* target, float* loss_row, int64_t rows,
                           int V, float grad_scale, int64_t ignore_index, int dtype,
                           cudaStream_t stream) {
   if (rows <= 0) return 0;
-  const int use_smem = V <= kCeMaxSmemElems ? 1 : 0;
-  const size_t smem = use_smem ? static_cast<size_t>(V) * sizeof(float) : 0;
+  const size_t elem = dtype == 1 ? 2 : 4;
+  const int use_smem = static_cast<size_t>(V) * elem <= kCeMaxSmemBytes ? 1 : 0;
+  const size_t smem = use_smem ? (static_cast<size_t>(V) * elem + 15) / 16 * 16 : 0;
   auto go = [&](auto tv) {
     using T = decltype(tv);
     if (smem > 48 * 1024)
