@@ -34,6 +34,7 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
+from ..utils import faults
 from .integrity import Manifest
 
 MAIN_SCHEMA = "transformer_lm_exact_resume_v1"
@@ -135,6 +136,7 @@ def save(path: Path, *, args, rank, world_size, is_distributed, device, model, o
             "run_cuda_max_memory_reserved": int(run_cuda_max_memory_reserved),
             "active_seconds": float(active_seconds),
         }, mtmp)
+    faults.maybe_inject("checkpoint_written", rank, completed_step)
     _barrier(is_distributed)
     rtmp.replace(rpath)
     _barrier(is_distributed)

@@ -42,6 +42,7 @@ from ..optim.composite import (ACTIVE_OPTIMIZERS, RATIONAL_SPECIFIC_OPTIMIZERS,
 from ..optim.baselines import resolve_ademamix_warmup
 from ..parallel.dist import cleanup_distributed, reduce_max, reduce_mean, setup_distributed
 from ..parallel.grad_sync import GradientSynchronizer
+from ..utils import faults
 from . import audit, resume, telemetry
 from .data import sample_batch
 from .engine import clip_grad_norm, learning_rate as _lr
@@ -506,6 +507,7 @@ class Run:
         stop_reason = stop_step = None
         model, opt = self.model, self.optimizer
         for step in range(self.resume_step, args.steps):
+            faults.maybe_inject("train_step", self.rank, step + 1)
             model.train()
             t_step = time.perf_counter()
             will_log = (step + 1) % args.log_interval == 0 or step == 0 or step + 1 == args.steps
