@@ -31,9 +31,11 @@ parameter order are those of the reference so ``state_dict`` round-trips.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.distributed as dist
+from torch.autograd.graph import increment_version
 
 from . import tiller_math as tm
 from .newton_schulz import (attention_head_group_zero_power, match_rms_adamw_adjustment,
@@ -129,6 +131,34 @@ def foreach_apply(parameters, direction, *, decay, alpha):
     torch._foreach_mul_(parameters, float(decay))
     torch._foreach_add_(parameters, list(direction.to(parameters[0].dtype).unbind(0)),
                         alpha=float(alpha))
+
+
+def shard_bounds(layers: int, rank: int, world: int):
+    """Contiguous, balanced block of layers owned by ``rank`` (may be empty)."""
+    return rank * layers // world, (rank + 1) * layers // world
+
+
+def layer_owner(layer: int, layers: int, world: int) -> int:
+    for r in range(world):
+        lo, hi = shard_bounds(layers, r, world)
+        if lo <= layer < hi:
+            return r
+    raise ValueError(layer)
+
+
+def sharding_enabled(world: int) -> bool:
+    """Layer-sharded optimizer steps across data-parallel ranks (RO_TILLER_SHARD=0 disables)."""
+    return world > 1 and os.environ.get("RO_TILLER_SHARD", "1") != "0"
+
+
+def broadcast_owned(tensors_by_layer, layers, world, group=None):
+    """Replicate per-layer tensors from their owners; bumps autograd versions."""
+    for layer, tensors in enumerate(tensors_by_layer):
+        src = layer_owner(layer, layers, world)
+        src_global = dist.get_global_rank(group, src) if group is not None else src
+        for t in tensors:
+            dist.broadcast(t.data if isinstance(t, torch.nn.Parameter) else t, src=src_global, group=group)
+            increment_version(t)
 
 
 class TILLERRouter(torch.optim.Optimizer):
@@ -493,16 +523,58 @@ class TILLERRouter(torch.optim.Optimizer):
                               and not self._force_torch)
         return self._fused_ok
 
+    def _shard(self):
+        """(lo, hi, sharded): the layers whose directions this rank computes.
+
+        With several data-parallel ranks on the GPU path each rank owns a
+        contiguous block of layers: it runs the per-layer pipeline (Nesterov,
+        NS5, chord, apply) for those layers only, the per-coordinate
+        contractions and functional scores are assembled with one all-reduce,
+        the ledger and transaction run replicated on identical inputs, and
+        the updated weights are broadcast from their owners.
+        """
+        L = len(self.pairs)
+        if self._use_fused() and sharding_enabled(self.world_size):
+            rank = dist.get_rank(group=self.loss_probe_group)
+            lo, hi = shard_bounds(L, rank, self.world_size)
+            return lo, hi, True
+        return 0, L, False
+
     def _fused_roles(self):
         if self._fused_role_objs is None:
             from .tiller_fused import FusedRole
-            self._fused_role_objs = {
-                "incoming": FusedRole(self, [p["in_weight"] for p in self.pairs], "incoming",
+            lo, hi, _ = self._shard()
+            owned = self.pairs[lo:hi]
+            self._fused_role_objs = {} if not owned else {
+                "incoming": FusedRole(self, [p["in_weight"] for p in owned], "incoming",
                                       groups=self.groups, width=self.width, momentum=self.momentum),
-                "outgoing": FusedRole(self, [p["out_weight"] for p in self.pairs], "outgoing",
+                "outgoing": FusedRole(self, [p["out_weight"] for p in owned], "outgoing",
                                       groups=self.groups, width=self.width, momentum=self.momentum),
             }
         return self._fused_role_objs
+
+    def _sync_shards(self):
+        """Make every rank's optimizer state complete (checkpoints; collective)."""
+        lo, hi, sharded = self._shard()
+        if not sharded:
+            return
+        L = len(self.pairs)
+        anchor = self.anchor
+        keys = [k for k in ("factorized_adaptive_tangent_rows_row_second_moment",
+                            "factorized_adaptive_tangent_rows_column_second_moment",
+                            "factorized_adaptive_tangent_columns_row_second_moment",
+                            "factorized_adaptive_tangent_columns_column_second_moment") if k in anchor]
+        per_layer = []
+        for layer, pair in enumerate(self.pairs):
+            tensors = [self.state[pair[k]].setdefault("momentum_buffer", torch.zeros_like(pair[k]))
+                       for k in ("in_weight", "out_weight")]
+            tensors += [anchor[k][layer] for k in keys]
+            per_layer.append(tensors)
+        broadcast_owned(per_layer, L, self.world_size, self.loss_probe_group)
+
+    def state_dict(self):
+        self._sync_shards()
+        return super().state_dict()
 
     def _directions(self, participation, congruence, *, want_selected):
         """Both roles' directions and the contractions the transaction needs.
@@ -515,28 +587,41 @@ class TILLERRouter(torch.optim.Optimizer):
         step = int(self.anchor.get("predictive_response_transaction_updates", 0)) + 1
         if self._use_fused():
             from .tiller_fused import chord_meta
+            lo, hi, sharded = self._shard()
+            G = self.groups
             roles = self._fused_roles()
+            device = self.pairs[0]["in_weight"].device
             chords, sels = {}, {}
             for role, index, axis in (("incoming", 0, "rows"), ("outgoing", 1, "columns")):
-                fr = roles[role]
-                shape = (L, self.groups, self.width, self.external)
+                shape = (L, G, self.width, self.external)
                 row, col = self._chord_state_shaped(shape, key_prefix="factorized_adaptive_tangent_" + axis,
-                                                    device=self.pairs[0]["in_weight"].device)
-                chord, sel = fr.directions(row, col, participation[..., index].contiguous(),
-                                           congruence[..., index].contiguous(), step,
-                                           want_selected=want_selected)
+                                                    device=device)
+                if hi == lo:
+                    continue
+                chord, sel = roles[role].directions(row[lo:hi], col[lo:hi],
+                                                    participation[lo:hi, :, index].contiguous(),
+                                                    congruence[lo:hi, :, index].contiguous(), step,
+                                                    want_selected=want_selected)
                 chords[role] = chord
-                sels[role] = None if sel is None else sel.view(L, self.hidden, self.external)
-            ci, co = chords["incoming"], chords["outgoing"]
+                sels[role] = None if sel is None else sel.view(hi - lo, self.hidden, self.external)
+            packed = torch.zeros(5, L * G, device=device, dtype=torch.float32)
+            if hi > lo:
+                ci, co = chords["incoming"], chords["outgoing"]
+                packed[:, lo * G:hi * G] = torch.stack((ci[:, 2], co[:, 2], ci[:, 3], co[:, 3], ci[:, 4] + co[:, 4]))
+            if sharded:
+                # one nonzero contributor per entry: the sum is exact
+                dist.all_reduce(packed, group=self.loss_probe_group)
 
             def apply(coefficients, lr, wd):
-                for role in ("incoming", "outgoing"):
-                    roles[role].apply(coefficients, decay=1.0 - lr * wd, lr=lr)
+                for role in roles:
+                    roles[role].apply(coefficients[lo:hi], decay=1.0 - lr * wd, lr=lr)
+                if sharded:
+                    broadcast_owned([(p["in_weight"], p["out_weight"]) for p in self.pairs], L,
+                                    self.world_size, self.loss_probe_group)
 
             metas = {r: chord_meta(chords[r]) for r in chords}
-            return {"exact_by_role": torch.stack((ci[:, 2], co[:, 2])),
-                    "momentum_by_role": torch.stack((ci[:, 3], co[:, 3])),
-                    "weights": ci[:, 4] + co[:, 4], "selected": sels, "meta": metas, "apply": apply}
+            return {"exact_by_role": packed[0:2], "momentum_by_role": packed[2:4], "weights": packed[4],
+                    "selected": sels, "meta": metas, "apply": apply, "owned": (lo, hi, sharded)}
         rec = self._role_directions(participation, congruence)
         inc_b = rec["incoming"]["scaled_blocks"]
         out_b = rec["outgoing"]["scaled_blocks"]
@@ -557,7 +642,8 @@ class TILLERRouter(torch.optim.Optimizer):
                 "weights": (inc_b.square().sum(dim=(-2, -1)) + out_b.square().sum(dim=(-2, -1))).reshape(-1),
                 "selected": {"incoming": inc_b.reshape(L, self.hidden, self.external),
                              "outgoing": out_b.reshape(L, self.hidden, self.external)},
-                "meta": {r: rec[r]["meta"] for r in ("incoming", "outgoing")}, "apply": apply}
+                "meta": {r: rec[r]["meta"] for r in ("incoming", "outgoing")}, "apply": apply,
+                "owned": (0, L, False)}
 
     def _chord_state_shaped(self, shape, *, key_prefix, device):
         anchor = self.anchor
@@ -686,6 +772,48 @@ class TILLERRouter(torch.optim.Optimizer):
         self._rfd_selection = sel
         return sel
 
+    def _sharded_scores(self, packets, adjoint, selected, lo, hi, wd):
+        """Functional score rows [32, C + 1] when layers are sharded across ranks.
+
+        Every rank's probe data (inputs, features, cotangents, adjoints) is
+        gathered so each owner scores its layers on all 32 global probes; the
+        score columns (one owner each) and the decay column (sum of per-owner
+        partial sums) are then assembled with one all-reduce, in the global
+        probe order of the unsharded path.
+        """
+        L, G = len(self.pairs), self.groups
+        world = self.world_size
+        probes = tm.GLOBAL_PROBE_COUNT
+        counts = [(r + 1) * probes // world - r * probes // world for r in range(world)]
+        width = max(counts)
+        local = torch.stack([torch.cat((pk[0].float(), pk[2].float(), pk[3].float(),
+                                        adjoint[i].reshape(adjoint.shape[1], -1).float()), dim=1)
+                             for i, pk in enumerate(packets)])  # [L, n_local, K]
+        padded = local.new_zeros((L, width, local.shape[-1]))
+        if local.shape[1]:
+            padded[:, : local.shape[1]] = local
+        gathered = [torch.empty_like(padded) for _ in range(world)]
+        dist.all_gather(gathered, padded, group=self.loss_probe_group)
+        rows = torch.cat([g[:, :n] for g, n in zip(gathered, counts)], dim=1)  # [L, 32, K]
+        d_ext, hid = self.external, self.hidden
+        full = rows.new_zeros((probes, L * G + 1))
+        for layer in range(lo, hi):
+            pair = self.pairs[layer]
+            r = rows[layer]
+            inputs, features = r[:, :d_ext], r[:, d_ext:d_ext + hid]
+            cot = r[:, d_ext + hid:2 * d_ext + hid]
+            adj = r[:, 2 * d_ext + hid:].reshape(r.shape[0], G, self.width)
+            s = tm.group_scores(inputs, features, cot, selected["incoming"][layer - lo],
+                                selected["outgoing"][layer - lo], adj, groups=G, width=self.width,
+                                validate=self.strict)
+            d = tm.group_scores(inputs, features, cot, pair["in_weight"].float() * wd,
+                                pair["out_weight"].T.float() * wd, adj, groups=G, width=self.width,
+                                validate=self.strict).sum(-1)
+            full[:, layer * G:(layer + 1) * G] = s
+            full[:, -1] += d
+        dist.all_reduce(full, group=self.loss_probe_group)
+        return full
+
     def _gather_rows(self, packet):
         if self.world_size == 1:
             if packet.shape[0] != tm.GLOBAL_PROBE_COUNT:
@@ -748,22 +876,27 @@ class TILLERRouter(torch.optim.Optimizer):
         momentum_by_role = dirs["momentum_by_role"]
         layer_ids = torch.arange(L, device=weights.device, dtype=torch.int64).repeat_interleave(self.groups)
         if refresh:
-            inc_b = dirs["selected"]["incoming"]
-            out_b = dirs["selected"]["outgoing"]
-            scores, decay = [], None
-            for layer, (pair, packet) in enumerate(zip(self.pairs, packets)):
-                inputs, _pre, features, cot = packet
-                adj = adjoint[layer]
-                s = tm.group_scores(inputs, features, cot, inc_b[layer], out_b[layer], adj,
-                                    groups=self.groups, width=self.width, validate=self.strict)
-                d = tm.group_scores(inputs, features, cot, pair["in_weight"].float() * wd,
-                                    pair["out_weight"].T.float() * wd, adj, groups=self.groups,
-                                    width=self.width, validate=self.strict).sum(-1)
-                scores.append(s)
-                decay = d if decay is None else decay + d
-            lattice = torch.stack(scores, dim=1).reshape(self.probe_layout.local_probe_count, L * self.groups)
-            packet = torch.cat((lattice, decay[:, None]), dim=1)
-            global_packet = self._gather_rows(packet)
+            lo, hi, sharded = dirs["owned"]
+            if sharded:
+                global_packet = self._sharded_scores(packets, adjoint, dirs["selected"], lo, hi, wd)
+            else:
+                inc_b = dirs["selected"]["incoming"]
+                out_b = dirs["selected"]["outgoing"]
+                scores, decay = [], None
+                for layer, (pair, packet) in enumerate(zip(self.pairs, packets)):
+                    inputs, _pre, features, cot = packet
+                    adj = adjoint[layer]
+                    s = tm.group_scores(inputs, features, cot, inc_b[layer], out_b[layer], adj,
+                                        groups=self.groups, width=self.width, validate=self.strict)
+                    d = tm.group_scores(inputs, features, cot, pair["in_weight"].float() * wd,
+                                        pair["out_weight"].T.float() * wd, adj, groups=self.groups,
+                                        width=self.width, validate=self.strict).sum(-1)
+                    scores.append(s)
+                    decay = d if decay is None else decay + d
+                lattice = torch.stack(scores, dim=1).reshape(self.probe_layout.local_probe_count,
+                                                             L * self.groups)
+                packet = torch.cat((lattice, decay[:, None]), dim=1)
+                global_packet = self._gather_rows(packet)
             g_scores, g_decay = global_packet[:, :-1], global_packet[:, -1]
             predictive = tm.window32_rows(g_scores, g_decay, anchor.get("predictive_global_score_ema"),
                                           anchor.get("predictive_global_decay_ema"),
@@ -963,6 +1096,31 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
     def telemetry(self):
         return dict(self._last_telemetry)
 
+    def _sync_shards(self):
+        """Complete every rank's state when layers are sharded (collective)."""
+        if not hasattr(self.router, "_shard"):
+            return
+        _, _, sharded = self.router._shard()
+        if not sharded:
+            return
+        L = len(self.blocks)
+        anchor = self.state[self.role_parameters["qkv"][0]]
+        keys = [k for k in ("factorized_adaptive_tangent_qkv_row_second_moment",
+                            "factorized_adaptive_tangent_qkv_column_second_moment",
+                            "factorized_adaptive_tangent_attention_output_row_second_moment",
+                            "factorized_adaptive_tangent_attention_output_column_second_moment") if k in anchor]
+        per_layer = []
+        for layer in range(L):
+            tensors = [self.state[self.role_parameters[r][layer]].setdefault(
+                "momentum_buffer", torch.zeros_like(self.role_parameters[r][layer])) for r in self._ROLES]
+            tensors += [anchor[k][layer] for k in keys]
+            per_layer.append(tensors)
+        broadcast_owned(per_layer, L, self.router.world_size, self.router.loss_probe_group)
+
+    def state_dict(self):
+        self._sync_shards()
+        return super().state_dict()
+
     @torch.no_grad()
     def step(self, closure=None):
         self._last_telemetry = {}
@@ -1001,13 +1159,19 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
                 col = torch.zeros(shape[:2] + shape[-1:], device=first.device, dtype=torch.float32)
                 anchor[ck] = col
             if fused:
-                if role not in self._fused:
-                    self._fused[role] = tiller_fused.FusedRole(self, params, role, momentum=self.momentum)
-                fr = self._fused[role]
-                chord, _ = fr.directions(row, col, participation.contiguous(), congruence.contiguous(),
-                                         update, want_selected=False)
-                fr.apply(torch.ones(len(params), device=first.device), decay=1.0 - lr * wd, lr=lr)
-                metas.append(tiller_fused.chord_meta(chord))
+                lo, hi, sharded = self.router._shard() if hasattr(self.router, "_shard") else (0, len(params), False)
+                if hi > lo:
+                    if role not in self._fused:
+                        self._fused[role] = tiller_fused.FusedRole(self, params[lo:hi], role,
+                                                                   momentum=self.momentum)
+                    fr = self._fused[role]
+                    chord, _ = fr.directions(row[lo:hi], col[lo:hi], participation[lo:hi].contiguous(),
+                                             congruence[lo:hi].contiguous(), update, want_selected=False)
+                    fr.apply(torch.ones(hi - lo, device=first.device), decay=1.0 - lr * wd, lr=lr)
+                    metas.append(tiller_fused.chord_meta(chord))
+                if sharded:
+                    broadcast_owned([(p,) for p in params], len(params), self.router.world_size,
+                                    self.router.loss_probe_group)
                 continue
             momenta = foreach_nesterov(self, params, self.momentum)
             grads = torch.stack([p.grad.detach() for p in params]).float()

@@ -121,6 +121,8 @@ def save(path: Path, *, args, rank, world_size, is_distributed, device, model, o
                 "torch_rng_state": torch.get_rng_state(), "cuda_rng_state": cuda_state,
                 "probe_state": cpu_probe_state(probe_state) if cpu_probe_state else None}, rtmp)
     mtmp = Path(f"{path}.tmp")
+    # every rank takes part: a layer-sharded optimizer completes its state collectively
+    optimizer_state = optimizer.state_dict()
     if rank == 0:
         if mtmp.exists():
             mtmp.unlink()
@@ -128,7 +130,7 @@ def save(path: Path, *, args, rank, world_size, is_distributed, device, model, o
         torch.save({
             "schema": MAIN_SCHEMA, "contract": resume_contract(args, world_size, strict=strict),
             "completed_step": int(completed_step), "model": raw.state_dict(),
-            "optimizer": optimizer.state_dict(), "best_val_loss": float(best_val_loss),
+            "optimizer": optimizer_state, "best_val_loss": float(best_val_loss),
             "step_times": list(step_times), "optimizer_step_times": list(optimizer_step_times),
             "grad_clip_observed_steps": int(grad_clip_observed_steps),
             "grad_clip_triggered_steps": int(grad_clip_triggered_steps),

@@ -121,7 +121,7 @@ def cases(rows):
     def gemm_in_proj():
         a = torch.randn(rows, d, device=dev, dtype=bf)
         b = torch.randn(H, d, device=dev, dtype=bf)
-        return (lambda: C.gemm_bf16(a, b, False, False, False)), 0, 2.0 * rows * d * H
+        return (lambda: C.gemm_bf16(a, b, False, True, False)), 0, 2.0 * rows * d * H
 
     def gemm_in_proj_cublas():
         a = torch.randn(rows, d, device=dev, dtype=bf)
