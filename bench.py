@@ -126,7 +126,7 @@ def count_own_launches(step_fn):
     return own, total
 
 
-def timed(step_fn, steps, device, dist_on):
+def timed(step_fn, steps, device, dist_on, flush=None):
     import torch
     import torch.distributed as dist
     if dist_on:
@@ -137,6 +137,8 @@ def timed(step_fn, steps, device, dist_on):
     start.record()
     for _ in range(steps):
         step_fn()
+    if flush is not None:
+        flush()  # side-stream work of the last step (deferred weight broadcasts) inside the region
     end.record()
     torch.cuda.synchronize(device)
     if dist_on:
@@ -154,6 +156,7 @@ def run_ours(a, info):
     sys.path.insert(0, ROOT)
     from rational_optimizer_b200.models.transformer import model_args, CausalTransformer
     from rational_optimizer_b200.optim import composite
+    from rational_optimizer_b200.parallel import param_ready
     from rational_optimizer_b200.parallel.grad_sync import GradientSynchronizer
     from rational_optimizer_b200.train.data import PinnedBatcher, zipf_tokens
     from rational_optimizer_b200.train.engine import TrainEngine
@@ -196,13 +199,13 @@ def run_ours(a, info):
     sampler = ClockSampler(device.index or 0) if info.rank == 0 else None
     if sampler:
         sampler.start()
-    ms = timed(device_step, a.steps, device, info.is_distributed)
+    ms = timed(device_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all)
     clocks = sampler.stop() if sampler else None
     e2e_ms = None
     if not a.no_e2e:
         for _ in range(2):
             e2e_step()
-        e2e_ms = timed(e2e_step, a.steps, device, info.is_distributed)
+        e2e_ms = timed(e2e_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all)
     launches = None
     if not a.no_count_launches and not info.is_distributed:
         own, total = count_own_launches(device_step)

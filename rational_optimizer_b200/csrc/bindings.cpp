@@ -295,27 +295,34 @@ std::vector<torch::Tensor> rope_qkv_forward(torch::Tensor qkv, torch::Tensor cos
   TORCH_CHECK(hd % 8 == 0, "head_dim must be a multiple of 8");
   const c10::cuda::CUDAGuard guard(qkv.device());
   auto opts = qkv.options();
-  auto q = torch::empty({B, H, S, hd}, opts);
-  auto k = torch::empty({B, H, S, hd}, opts);
-  auto v = torch::empty({B, H, S, hd}, opts);
+  // [B, S, H, hd] storage (token-major, the layout the attention kernels
+  // read and write without transposes), returned as [B, H, S, hd] views.
+  auto q = torch::empty({B, S, H, hd}, opts);
+  auto k = torch::empty({B, S, H, hd}, opts);
+  auto v = torch::empty({B, S, H, hd}, opts);
   check_rc(ro::rope_qkv_forward(qkv.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
                                 q.data_ptr(), k.data_ptr(), v.data_ptr(), static_cast<int>(B),
                                 static_cast<int>(S), static_cast<int>(H), static_cast<int>(hd),
                                 dtype_code(qkv, "qkv"), stream()),
            "rope_qkv_forward");
-  return {q, k, v};
+  return {q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)};
 }
 
 torch::Tensor rope_qkv_backward(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
                                 torch::Tensor cos_t, torch::Tensor sin_t) {
+  TORCH_CHECK(dq.dim() == 4 && dq.sizes() == dk.sizes() && dq.sizes() == dv.sizes(), "dq/dk/dv shapes");
+  const c10::cuda::CUDAGuard guard(dq.device());
+  const int64_t B = dq.size(0), H = dq.size(1), S = dq.size(2), hd = dq.size(3);
+  // gradients of the [B, H, S, hd] views: token-major storage (a copy only
+  // when the producer chose another layout)
+  dq = dq.transpose(1, 2).contiguous();
+  dk = dk.transpose(1, 2).contiguous();
+  dv = dv.transpose(1, 2).contiguous();
   check_cuda(dq, "dq");
   check_cuda(dk, "dk");
   check_cuda(dv, "dv");
   check_f32(cos_t, "cos");
   check_f32(sin_t, "sin");
-  TORCH_CHECK(dq.dim() == 4 && dq.sizes() == dk.sizes() && dq.sizes() == dv.sizes(), "dq/dk/dv shapes");
-  const c10::cuda::CUDAGuard guard(dq.device());
-  const int64_t B = dq.size(0), H = dq.size(1), S = dq.size(2), hd = dq.size(3);
   auto dqkv = torch::empty({B * S, 3 * H * hd}, dq.options());
   check_rc(ro::rope_qkv_backward(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), cos_t.data_ptr<float>(),
                                  sin_t.data_ptr<float>(), dqkv.data_ptr(), static_cast<int>(B),
@@ -406,6 +413,52 @@ c10::optional<torch::Tensor> gemm_bf16_ex(torch::Tensor a, torch::Tensor b, bool
 
 torch::Tensor gemm_error(torch::Tensor like) { return gemm_error_flag(like.device()); }
 
+// 2-SM tcgen05 GEMM: c[M, N] = a[M, K] . b[N, K]^T (bf16, both K-major).
+// None when the shape or alignment is unsupported (callers fall back).
+c10::optional<torch::Tensor> gemm2_bf16(torch::Tensor a, torch::Tensor b) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.dim() == 2 && b.dim() == 2, "gemm2 expects 2-D CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16, "gemm2 expects bf16");
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm2 inner dimensions differ");
+  if (a.stride(1) != 1 || b.stride(1) != 1) return c10::nullopt;
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto c = torch::empty({a.size(0), b.size(0)}, a.options());
+  const int rc = ro::gemm2_bf16_nt(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), c.data_ptr(), c.stride(0),
+                                   static_cast<int>(a.size(0)), static_cast<int>(b.size(0)),
+                                   static_cast<int>(a.size(1)), gemm_error_flag(a.device()).data_ptr<int>(),
+                                   at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "gemm2_bf16");
+  return c;
+}
+
+// In-projection with the GRAIN activation fused into the GEMM epilogue:
+// returns (h = bf16(x w^T), y = GRAIN(h)) for groups of 256 columns; None
+// when unsupported.
+c10::optional<std::vector<torch::Tensor>> grain_in_proj_forward(torch::Tensor x, torch::Tensor w,
+                                                                torch::Tensor num, torch::Tensor den,
+                                                                double eps) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.dim() == 2 && w.dim() == 2, "expects 2-D CUDA tensors");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16, "expects bf16");
+  TORCH_CHECK(x.size(1) == w.size(1), "inner dimensions differ");
+  check_f32(num, "numerator");
+  check_f32(den, "denominator");
+  const int64_t N = w.size(0);
+  if (x.stride(1) != 1 || w.stride(1) != 1 || N % 256 != 0 || num.numel() != (N / 256) * 6 ||
+      den.numel() != (N / 256) * 4)
+    return c10::nullopt;
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto h = torch::empty({x.size(0), N}, x.options());
+  auto y = torch::empty({x.size(0), N}, x.options());
+  const int rc = ro::gemm2_grain_forward(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), h.data_ptr(),
+                                         y.data_ptr(), static_cast<int>(x.size(0)), static_cast<int>(N),
+                                         static_cast<int>(x.size(1)), num.data_ptr<float>(), den.data_ptr<float>(),
+                                         static_cast<float>(eps), gemm_error_flag(x.device()).data_ptr<int>(),
+                                         at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "grain_in_proj_forward");
+  return std::vector<torch::Tensor>{h, y};
+}
+
 void adamw_multi_tensor(std::vector<torch::Tensor> p, std::vector<torch::Tensor> g,
                         std::vector<torch::Tensor> m, std::vector<torch::Tensor> v, double lr,
                         double beta1, double beta2, double eps, double wd, double step) {
@@ -434,6 +487,42 @@ void adamw_multi_tensor(std::vector<torch::Tensor> p, std::vector<torch::Tensor>
                                   static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(step),
                                   at::cuda::getCurrentCUDAStream()),
            "adamw_multi_tensor");
+}
+
+// Sum over tensors of <a_t, b_t> times scale, as a 0-dim fp32 tensor.
+torch::Tensor multi_tensor_dot(std::vector<torch::Tensor> a, std::vector<torch::Tensor> b, double scale) {
+  const size_t n = a.size();
+  TORCH_CHECK(n > 0 && b.size() == n, "multi_tensor_dot list lengths");
+  const c10::cuda::CUDAGuard guard(a[0].device());
+  std::vector<const float*> ap(n), bp(n);
+  std::vector<int64_t> sizes(n);
+  for (size_t i = 0; i < n; ++i) {
+    for (auto* t : {&a[i], &b[i]}) {
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous(),
+                  "multi_tensor_dot tensors must be contiguous fp32 CUDA tensors");
+    }
+    TORCH_CHECK(a[i].numel() == b[i].numel(), "multi_tensor_dot sizes differ");
+    ap[i] = a[i].data_ptr<float>();
+    bp[i] = b[i].data_ptr<float>();
+    sizes[i] = a[i].numel();
+  }
+  auto opts = a[0].options();
+  auto part = torch::empty({std::max<int64_t>(1, ro::multi_tensor_dot_partials(sizes.data(), static_cast<int>(n)))}, opts);
+  auto out = torch::empty({}, opts);
+  check_rc(ro::multi_tensor_dot(ap.data(), bp.data(), sizes.data(), static_cast<int>(n), static_cast<float>(scale),
+                                part.data_ptr<float>(), out.data_ptr<float>(), at::cuda::getCurrentCUDAStream()),
+           "multi_tensor_dot");
+  return out;
+}
+
+// x *= min(max_norm / (sqrt(sumsq) + 1e-6), 1) with sumsq a 1-element device tensor.
+void clip_scale_(torch::Tensor x, torch::Tensor sumsq, double max_norm) {
+  check_f32(x, "x");
+  check_f32(sumsq, "sumsq");
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(ro::clip_scale(x.data_ptr<float>(), x.numel(), sumsq.data_ptr<float>(), static_cast<float>(max_norm),
+                          at::cuda::getCurrentCUDAStream()),
+           "clip_scale_");
 }
 
 // ---------------------------------------------------------------------------
@@ -551,9 +640,11 @@ torch::Tensor ns_normalize(torch::Tensor x) {
               "ns_normalize expects contiguous bf16 [B, r, c]");
   const c10::cuda::CUDAGuard guard(x.device());
   auto y = torch::empty_like(x);
+  const int64_t n = x.size(1) * x.size(2);
+  auto part = torch::empty({x.size(0) * ro::ns_normalize_chunks(n)}, x.options().dtype(torch::kFloat32));
   check_rc(ro::ns_normalize(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                            reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), static_cast<int>(x.size(0)),
-                            x.size(1) * x.size(2), at::cuda::getCurrentCUDAStream()),
+                            reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), part.data_ptr<float>(),
+                            static_cast<int>(x.size(0)), n, at::cuda::getCurrentCUDAStream()),
            "ns_normalize");
   return y;
 }
@@ -726,6 +817,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_ex", &gemm_bf16_ex);
   m.def("gemm_error", &gemm_error);
   m.def("adamw_multi_tensor", &adamw_multi_tensor);
+  m.def("multi_tensor_dot", &multi_tensor_dot);
+  m.def("clip_scale_", &clip_scale_);
+  m.def("gemm2_bf16", &gemm2_bf16);
+  m.def("grain_in_proj_forward", &grain_in_proj_forward);
   m.def("tiller_nesterov", &tiller_nesterov);
   m.def("tiller_transpose_bf16", &tiller_transpose_bf16);
   m.def("tiller_chord", &tiller_chord);

@@ -53,6 +53,10 @@ int cross_entropy_fwd_bwd(void* logits, const int64_t* target, float* loss_row, 
 
 
 // gemm_sm100.cu
+int gemm2_bf16_nt(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int M, int N,
+                  int K, int* err, cudaStream_t stream);
+int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, void* H, void* Y, int M, int N,
+                        int K, const float* num, const float* den, float eps, int* err, cudaStream_t stream);
 int gemm_bf16_tn(const void* A, int64_t lda, int64_t strideA, bool a_mn, const void* B, int64_t ldb,
                  int64_t strideB, bool b_mn, void* C, int64_t ldc, int64_t strideC, bool out_f32,
                  const void* D, int64_t ldd, int64_t strideD, float alpha, float beta, int M, int N,
@@ -63,6 +67,10 @@ int gemm_bf16_tn(const void* A, int64_t lda, int64_t strideA, bool a_mn, const v
 int adamw_multi_tensor(float* const* p, const float* const* g, float* const* m, float* const* v,
                        const int64_t* sizes, int count, float lr, float beta1, float beta2, float eps,
                        float wd, float step, cudaStream_t stream);
+int64_t multi_tensor_dot_partials(const int64_t* sizes, int count);
+int clip_scale(float* x, int64_t n, const float* sumsq, float max_norm, cudaStream_t stream);
+int multi_tensor_dot(const float* const* a, const float* const* b, const int64_t* sizes, int count,
+                     float scale, float* part, float* out, cudaStream_t stream);
 
 
 // tiller.cu
@@ -80,7 +88,9 @@ int tiller_apply(float* const* params, const __nv_bfloat16* polar, const float* 
                  const float* col_m, const float* row_total, const float* chord, const float* coef,
                  float* sel_out, int L, int blocks_per_layer, int R, int C, bool transpose, float scale,
                  int step, float decay, float alpha, float adj, bool update_param, cudaStream_t stream);
-int ns_normalize(const __nv_bfloat16* x, __nv_bfloat16* y, int batch, int64_t n, cudaStream_t stream);
+int64_t ns_normalize_chunks(int64_t n);
+int ns_normalize(const __nv_bfloat16* x, __nv_bfloat16* y, float* part, int batch, int64_t n,
+                 cudaStream_t stream);
 
 
 // comm.cu

@@ -1,0 +1,585 @@
+// Persistent 2-SM GEMM (tcgen05.mma.cta_group::2) with fused epilogues.
+//
+//   acc (M x N) = A (M x K) . B (N x K)^T          bf16 operands, fp32 accumulator
+//
+// A and B are K-major (an activation [M, K] and an nn.Linear weight [N, K]).
+// A CTA pair (a cluster of 2) owns a 256 x 256 output tile: each CTA stages
+// 128 rows of A and 128 rows of B per 64-wide K block, the leader issues
+// M=256 N=256 K=16 MMAs that read both CTAs' shared memory, and each CTA's
+// tensor memory receives its own 128 rows of the accumulator.
+//
+// Per CTA (320 threads, one CTA per SM, grid = 2 x #clusters, persistent):
+//   warp 0      TMA producer: loads into this CTA's ring; the completion
+//               bytes of both CTAs land on the leader's `full` barrier;
+//   warp 1      TMEM allocation (both CTAs) and, in the leader, the MMA
+//               issuer; each K block is released to both producers with a
+//               multicast tcgen05.commit (no multicast loads are used);
+//   warps 2..9  epilogue: 8 warps, two per TMEM lane quarter, each owning 32
+//               rows x 128 columns of the tile; results go through a
+//               128B-swizzled staging buffer to TMA bulk stores.
+// The accumulator is double-buffered in TMEM (2 x 256 columns = all 512), so
+// the epilogue of tile t overlaps the main loop of tile t+1.
+//
+// Epilogues:
+//   kStore      C = bf16(acc)
+//   kGrainFwd   GRAIN activation fused behind the in-projection (group width
+//               256 = one tile width): H = bf16(acc) is stored, rho per row is
+//               the RMS of H over the group, Y = rho * P(t)/Q(|t|) with
+//               t = H / rho is stored (the arithmetic of
+//               ro::grain::forward_packed_kernel).
+//
+// Every mbarrier wait is bounded by a wall-clock limit; on expiry the waiting
+// role records an error code in `err` and stops.  Every thread of both CTAs
+// reaches the final cluster barrier exactly once, TMEM is released, and the
+// kernel returns, so a broken invariant cannot hang the GPU.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "common.cuh"
+#include "packed.cuh"
+
+namespace ro {
+namespace gemm2 {
+
+constexpr int kBM = 256;         // rows per CTA pair
+constexpr int kBN = 256;         // columns per tile
+constexpr int kBK = 64;          // 64 bf16 = 128 B = one swizzle row
+constexpr int kHalfM = 128;      // rows per CTA
+constexpr int kHalfN = 128;      // B rows staged per CTA
+constexpr int kStages = 5;
+constexpr int kABytes = kHalfM * kBK * 2;          // 16 KB
+constexpr int kBBytes = kHalfN * kBK * 2;          // 16 KB
+constexpr int kStageBytes = kABytes + kBBytes;     // 32 KB per CTA
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + kEpiWarps * 32;      // 320
+constexpr int kStageOut = 32 * 128;                // one 32 x 64 bf16 staging tile
+constexpr int kOutBytes = kEpiWarps * 2 * kStageOut;  // double-buffered per warp: 64 KB
+constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
+constexpr int kTmemCols = 512;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+enum Epilogue : int { kStore = 0, kGrainFwd = 1 };
+
+struct Params {
+  int M, N, K;
+  int* err;
+  // GRAIN forward epilogue
+  const float* num;   // [groups, 6]
+  const float* den;   // [groups, 4]
+  float eps;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Arrive on an mbarrier anywhere in the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D tiled TMA load into this CTA's shared memory; the transaction bytes are
+// counted on `bar`, which may live in the peer CTA (cta_group::2).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrive on the barrier at the same offset in both CTAs once every MMA
+// issued so far by this thread has completed.
+__device__ __forceinline__ void tc_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_mma2(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// 32 lanes x 32 columns of 32-bit accumulator per warp.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor, 128B swizzle, K-major (8-row core groups
+// 1024 B apart).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(16 >> 4) << 16;    // leading byte offset (unused for K-major swizzle)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset
+  d |= 1ull << 46;                              // descriptor version (sm_100)
+  d |= 2ull << 61;                              // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16, bf16 x bf16 -> f32, both K-major, M = 256, N = 256.
+__device__ __forceinline__ constexpr uint32_t instr_desc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+         (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& tm, int& tn) {
+  // 8 M-tiles share each sweep over N (L2 reuse of the weight tiles)
+  constexpr int kGroup = 8;
+  const int span = kGroup * num_n;
+  const int g = tile / span;
+  const int first = g * kGroup;
+  int gm = num_m - first;
+  if (gm > kGroup) gm = kGroup;
+  const int r = tile - g * span;
+  tm = first + r % gm;
+  tn = r / gm;
+}
+
+// Write 32 fp32 values of one row (lane = row) as bf16 into a 32 x 64 staging
+// tile laid out for a 128B-swizzled TMA store; `c0` selects the 32-column half.
+__device__ __forceinline__ void stage_row32(uint8_t* stage, int lane, int c0, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = v[q * 8 + j];
+    const int chunk = (c0 / 8 + q) ^ (lane & 7);
+    store_vec<__nv_bfloat16, 8>(reinterpret_cast<__nv_bfloat16*>(stage + lane * 128 + chunk * 16), w);
+  }
+}
+
+// GRAIN coefficients of one group, splatted to fp32 pairs.
+struct GrainCoeffs {
+  float2 a[6];  // numerator
+  float2 b[4];  // |denominator|
+};
+
+__device__ __forceinline__ void load_grain_coeffs(GrainCoeffs& c, int g, const float* __restrict__ num,
+                                                  const float* __restrict__ den) {
+#pragma unroll
+  for (int j = 0; j < 6; ++j) c.a[j] = splat2(num[g * 6 + j]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) c.b[j] = splat2(fabsf(den[g * 4 + j]));
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmY, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* out_stage = smem + kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + kOutBytes);
+  uint64_t* full = bars;                   // [kStages]  (used in the leader)
+  uint64_t* empty = bars + kStages;        // [kStages]  (both CTAs)
+  uint64_t* acc_full = empty + kStages;    // [2]        (both CTAs)
+  uint64_t* acc_empty = acc_full + 2;      // [2]        (used in the leader)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ float rho_part[kEpiWarps][32];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_rank();
+  const bool leader = crank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + kBN - 1) / kBN;
+  const int num_k = (p.K + kBK - 1) / kBK;
+  const int tiles = num_m * num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cluster_id; tile < tiles && ok; tile += num_clusters) {
+        int tm, tn;
+        tile_coords(tile, num_m, num_n, tm, tn);
+        const int m0 = tm * kBM + static_cast<int>(crank) * kHalfM;
+        const int n0 = tn * kBN + static_cast<int>(crank) * kHalfN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, p.err, 1)) { ok = false; break; }
+          const uint32_t fb_local = smem_u32(&full[stage]);
+          if (leader) mbar_expect_tx(fb_local, 2 * kStageBytes);
+          const uint32_t fb = map_to_rank(fb_local, 0);
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          tma_load_2d(sa, &tmA, fb, kb * kBK, m0);
+          tma_load_2d(sa + kABytes, &tmB, fb, kb * kBK, n0);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = instr_desc();
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = cluster_id; tile < tiles && ok; tile += num_clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1, p.err, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * kBN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, p.err, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            tc_mma2(tmem_d, smem_desc(sa + k * 32), smem_desc(sb + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+          tc_commit_both(smem_u32(&empty[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_both(smem_u32(&acc_full[acc]));
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int e = warp - 2;              // 0..7
+    const int quarter = warp & 3;        // TMEM lanes [32*quarter, +32)
+    const int chalf = e >> 2;            // column half: [128*chalf, +128)
+    uint8_t* stage_buf = out_stage + e * 2 * kStageOut;
+    int buf = 0;
+    const uint32_t empty_leader = map_to_rank(smem_u32(&acc_empty[0]), 0);
+    GrainCoeffs gc;
+    float2 one2 = splat2(1.0f);
+    int local = 0;
+    for (int tile = cluster_id; tile < tiles; tile += num_clusters, ++local) {
+      int tm, tn;
+      tile_coords(tile, num_m, num_n, tm, tn);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(smem_u32(&acc_full[acc]), acc_phase, p.err, 4)) break;
+      tc_fence_after();
+      const int row0 = tm * kBM + static_cast<int>(crank) * kHalfM + quarter * 32;
+      const int col0 = tn * kBN + chalf * 128;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN + chalf * 128;
+      float rho = 1.0f;
+      if constexpr (EPI == kGrainFwd) {
+        // pass 1: sum of squares of bf16(acc) over this warp's 128 columns,
+        // combined with the partner warp's half (same rows) through smem
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float h = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j])));
+            ss = fmaf(h, h, ss);
+          }
+        }
+        rho_part[e][lane] = ss;
+        // named barrier per lane quarter: warps e and e^4
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+        const float tot = rho_part[e][lane] + rho_part[e ^ 4][lane];
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+        rho = sqrtf(tot * (1.0f / 256.0f) + p.eps);
+        load_grain_coeffs(gc, tn, p.num, p.den);
+      }
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 64) {
+        uint8_t* st = stage_buf + buf * kStageOut;
+        // the staging buffer's previous bulk store must have read it
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        float hv[2][32];
+        {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) hv[0][j] = __uint_as_float(r[j]);
+          tmem_ld32(tbase + c + 32, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) hv[1][j] = __uint_as_float(r[j]);
+        }
+        stage_row32(st, lane, 0, hv[0]);
+        stage_row32(st, lane, 32, hv[1]);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, smem_u32(st), col0 + c, row0);
+          bulk_commit();
+        }
+        buf ^= 1;
+        if constexpr (EPI == kGrainFwd) {
+          uint8_t* sy = stage_buf + buf * kStageOut;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float2 t = make_float2(__bfloat162float(__float2bfloat16_rn(hv[hh][j])),
+                                     __bfloat162float(__float2bfloat16_rn(hv[hh][j + 1])));
+              t = mul2(t, ir);
+              const float2 at = abs2(t);
+              float2 pp = fma2(gc.a[5], t, gc.a[4]);
+              pp = fma2(pp, t, gc.a[3]);
+              pp = fma2(pp, t, gc.a[2]);
+              pp = fma2(pp, t, gc.a[1]);
+              pp = fma2(pp, t, gc.a[0]);
+              float2 q = fma2(gc.b[3], at, gc.b[2]);
+              q = fma2(q, at, gc.b[1]);
+              q = fma2(q, at, gc.b[0]);
+              q = fma2(q, at, one2);
+              const float2 y = mul2(mul2(pp, rh), rcp2(q));
+              hv[hh][j] = y.x;
+              hv[hh][j + 1] = y.y;
+            }
+          }
+          stage_row32(sy, lane, 0, hv[0]);
+          stage_row32(sy, lane, 32, hv[1]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmY, smem_u32(sy), col0 + c, row0);
+            bulk_commit();
+          }
+          buf ^= 1;
+        }
+      }
+      // accumulator buffer drained: release it to the leader's MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, cols] matrix with row stride `ld`
+// (elements); box = {64, box_rows}, 128B swizzle.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int EPI>
+int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, void* Y, int64_t ldy,
+           const Params& p, cudaStream_t stream) {
+  CUtensorMap ma, mb, mc, my;
+  if (!make_map(&ma, A, p.M, p.K, lda, kHalfM) || !make_map(&mb, B, p.N, p.K, ldb, kHalfN) ||
+      !make_map(&mc, C, p.M, p.N, ldc, 32))
+    return -3;
+  if (EPI == kGrainFwd) {
+    if (!make_map(&my, Y, p.M, p.N, ldy, 32)) return -3;
+  } else {
+    my = mc;
+  }
+  auto kern = gemm2_kernel<EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    configured = true;
+  }
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kBN - 1) / kBN);
+  int clusters = num_sms() / 2;
+  if (tiles < clusters) clusters = tiles;
+  kern<<<2 * clusters, kThreads, kSmemBytes, stream>>>(ma, mb, mc, my, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace gemm2
+
+// C[M, N] = bf16(A[M, K] . B[N, K]^T), both K-major, on the 2-SM path.
+// Returns 0 on success, negative when the configuration is unsupported (the
+// caller falls back), positive CUDA error codes.
+int gemm2_bf16_nt(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int M, int N,
+                  int K, int* err, cudaStream_t stream) {
+  using namespace gemm2;
+  if (M <= 0 || N <= 0 || K <= 0) return -1;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || (lda % 8) || (ldb % 8) || (ldc % 8) || (K % 8) ||
+      (N % 8))
+    return -2;
+  Params p{M, N, K, err, nullptr, nullptr, 0.f};
+  return launch<kStore>(A, lda, B, ldb, C, ldc, nullptr, 0, p, stream);
+}
+
+// GRAIN forward fused behind the in-projection: H = bf16(X W^T) and
+// Y = GRAIN(H) with groups of 256 columns (N = 256 * groups).  num [groups, 6],
+// den [groups, 4] fp32 (no local-basis atoms, no affine restriction).
+int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, void* H, void* Y, int M, int N,
+                        int K, const float* num, const float* den, float eps, int* err, cudaStream_t stream) {
+  using namespace gemm2;
+  if (M <= 0 || N <= 0 || K <= 0 || N % kBN) return -1;
+  if (!aligned16(X) || !aligned16(W) || !aligned16(H) || !aligned16(Y) || (ldx % 8) || (ldw % 8) || (K % 8))
+    return -2;
+  Params p{M, N, K, err, num, den, eps};
+  return launch<kGrainFwd>(X, ldx, W, ldw, H, N, Y, N, p, stream);
+}
+
+}  // namespace ro

@@ -128,8 +128,10 @@ __device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double
           p = round;
           q = m - 1;
         } else {
-          p = (round + k) % (m - 1);
-          q = (round - k + (m - 1)) % (m - 1);
+          p = round + k;
+          if (p >= m - 1) p -= m - 1;
+          q = round - k;
+          if (q < 0) q += m - 1;
         }
         if (p > q) { const int t = p; p = q; q = t; }
         double c = 1.0, s = 0.0;
@@ -138,9 +140,12 @@ __device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double
           const double app = A[p * ld + p], aqq = A[q * ld + q];
           const double aabs = fabs(apq);
           if (aabs > floor_abs && aabs > 0.5 * kEps * fmax(fabs(app), fabs(aqq))) {
-            const double theta = (aqq - app) / (2.0 * apq);
-            const double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
-            c = 1.0 / sqrt(t * t + 1.0);
+            // t = tan of the rotation angle, the smaller root of
+            // t^2 + 2 theta t - 1 = 0 with theta = (aqq - app) / (2 apq)
+            const double diff = aqq - app;
+            const double r = sqrt(fma(diff, diff, 4.0 * apq * apq));
+            const double t = 2.0 * apq / (diff + copysign(r, diff));
+            c = rsqrt(fma(t, t, 1.0));
             s = t * c;
             *rotated = 1;
           } else if (apq != 0.0) {
@@ -155,29 +160,39 @@ __device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double
         rs[k] = s;
       }
       __syncthreads();
-      // A <- P^T A P (rows, then columns); disjoint pairs never conflict.
-      for (int idx = tid; idx < half * n; idx += blockDim.x) {
-        const int k = idx / n, j = idx - k * n;
-        const int p = rp[k], q = rq[k];
-        if (q >= n || rs[k] == 0.0) continue;
-        const double c = rc[k], s = rs[k];
-        const double ap = A[p * ld + j], aq = A[q * ld + j];
-        A[p * ld + j] = c * ap - s * aq;
-        A[q * ld + j] = s * ap + c * aq;
-      }
-      __syncthreads();
-      for (int idx = tid; idx < half * n; idx += blockDim.x) {
-        const int k = idx / n, i = idx - k * n;
-        const int p = rp[k], q = rq[k];
-        if (q >= n || rs[k] == 0.0) continue;
-        const double c = rc[k], s = rs[k];
-        const double ap = A[i * ld + p], aq = A[i * ld + q];
-        // the rotated pair's off-diagonal entries are zero by construction
-        A[i * ld + p] = (i == q) ? 0.0 : c * ap - s * aq;
-        A[i * ld + q] = (i == p) ? 0.0 : s * ap + c * aq;
-        const double vp = V[i * ld + p], vq = V[i * ld + q];
-        V[i * ld + p] = c * vp - s * vq;
-        V[i * ld + q] = s * vp + c * vq;
+      // A <- R^T A R and V <- V R in one pass.  R is block diagonal over the
+      // round's disjoint pairs, so each 2 x 2 block (pair k rows, pair l
+      // columns) of A and each (row, pair) of V is updated independently.
+      const int nblk = half * half;
+      for (int idx = tid; idx < nblk + n * half; idx += blockDim.x) {
+        if (idx < nblk) {
+          const int k = idx / half, l = idx - k * half;
+          const int p = rp[k], q = rq[k], u = rp[l], w = rq[l];
+          const double c = rc[k], sk = rs[k], c2 = rc[l], s2 = rs[l];
+          if (sk == 0.0 && s2 == 0.0) continue;
+          const bool qk = q < n, wl = w < n;
+          const double apu = A[p * ld + u];
+          const double apw = wl ? A[p * ld + w] : 0.0;
+          const double aqu = qk ? A[q * ld + u] : 0.0;
+          const double aqw = (qk && wl) ? A[q * ld + w] : 0.0;
+          // rows (pair k)
+          const double bpu = c * apu - sk * aqu, bqu = sk * apu + c * aqu;
+          const double bpw = c * apw - sk * aqw, bqw = sk * apw + c * aqw;
+          // columns (pair l); the rotated pair's own off-diagonal is zero
+          A[p * ld + u] = c2 * bpu - s2 * bpw;
+          if (wl) A[p * ld + w] = (k == l) ? 0.0 : s2 * bpu + c2 * bpw;
+          if (qk) A[q * ld + u] = (k == l) ? 0.0 : c2 * bqu - s2 * bqw;
+          if (qk && wl) A[q * ld + w] = s2 * bqu + c2 * bqw;
+        } else {
+          const int j = idx - nblk;
+          const int k = j / n, i = j - k * n;
+          const int p = rp[k], q = rq[k];
+          if (q >= n || rs[k] == 0.0) continue;
+          const double c = rc[k], sk = rs[k];
+          const double vp = V[i * ld + p], vq = V[i * ld + q];
+          V[i * ld + p] = c * vp - sk * vq;
+          V[i * ld + q] = sk * vp + c * vq;
+        }
       }
       __syncthreads();
     }
@@ -188,6 +203,202 @@ __device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double
 }
 
 // Sort eigenpairs ascending: evals[i] from A diag, evecs columns of V -> out (n x n, column i).
+// Scratch for arrowhead_eigh (shared memory, sized for n <= kMaxSel).
+struct ArrowScratch {
+  double d[kMaxSel], z[kMaxSel], tau[kMaxSel], zhat[kMaxSel];
+  double rc[kMaxSel], rs[kMaxSel];
+  int idx[kMaxSel], org[kMaxSel], rorg[kMaxSel], rot_i[kMaxSel], rot_j[kMaxSel];
+  int keep, nrot, ok;
+  double alpha, znorm1;
+};
+
+// Eigen-decomposition of an arrowhead matrix
+//   H = [[D, z], [z^T, alpha]],  D = diag(d_0 .. d_{n-2}),
+// stored as A (n x n, leading dimension n + 1) whose leading (n-1) x (n-1)
+// block is diagonal up to rounding of its inputs.  This is the shape of the
+// ledger's Gram when the persistent rows come from the previous
+// decomposition (mutually orthogonal) and the surrogate adds one row.  The
+// method is that of Gu and Eisenstat (SIAM J. Matrix Anal. Appl. 15(4),
+// 1994): deflate negligible z_i and (Givens) coincident d_i; find each root
+// of the secular equation  alpha - lambda + sum_i z_i^2 / (lambda - d_i) = 0
+// by bisection in coordinates shifted to the nearer pole; recompute z from
+// the computed roots (Loewner's formula) so the eigenvectors
+// [z_i / (lambda - d_i); 1] are orthogonal to working precision.  Returns
+// false, touching nothing, when the leading block is not diagonal to
+// 1e-6 relative (the caller then runs the Jacobi method).  On success the
+// eigenvalues are on A's diagonal and V holds the eigenvectors (columns).
+__device__ bool arrowhead_eigh(double* A, double* V, int n, ArrowScratch& S, double* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int ld = n + 1, m = n - 1;
+  // 1. the leading block must be diagonal
+  double off = 0.0;
+  for (int k = tid; k < m * m; k += blockDim.x) {
+    const int i = k / m, j = k - i * m;
+    if (i == j) continue;
+    const double aij = fabs(A[i * ld + j]);
+    const double scale = sqrt(fabs(A[i * ld + i]) * fabs(A[j * ld + j]));
+    if (aij > 1e-6 * scale + 1e-300) off = 1.0;
+  }
+  if (block_sum(off, red) > 0.0) return false;
+  // 2. inputs and ranks of d (ascending, ties by index)
+  for (int i = tid; i < m; i += blockDim.x) {
+    const double di = A[i * ld + i];
+    int r = 0;
+    for (int j = 0; j < m; ++j) {
+      const double dj = A[j * ld + j];
+      r += (dj < di) || (dj == di && j < i);
+    }
+    S.idx[r] = i;
+  }
+  double zn2 = 0.0, zn1 = 0.0, dn2 = 0.0;
+  for (int i = tid; i < m; i += blockDim.x) {
+    const double zi = A[i * ld + m], di = A[i * ld + i];
+    zn2 += zi * zi;
+    zn1 += fabs(zi);
+    dn2 += di * di;
+  }
+  zn2 = block_sum(zn2, red);
+  zn1 = block_sum(zn1, red);
+  dn2 = block_sum(dn2, red);
+  const double alpha = A[m * ld + m];
+  const double hnorm = sqrt(dn2 + 2.0 * zn2 + alpha * alpha);
+  const double tol = 8.0 * kEps * hnorm;
+  // V = I; the deflated coordinates keep their unit vectors
+  for (int k = tid; k < n * n; k += blockDim.x) {
+    const int r = k / n, c = k - r * n;
+    V[r * ld + c] = (r == c) ? 1.0 : 0.0;
+  }
+  __syncthreads();
+  // 3. deflation (one thread, O(m)): sorted order, negligible z and coincident d
+  if (tid == 0) {
+    int keep = 0, nrot = 0, last = -1;
+    for (int r = 0; r < m; ++r) {
+      const int i = S.idx[r];
+      double zi = A[i * ld + m];
+      const double di = A[i * ld + i];
+      if (fabs(zi) <= tol) continue;  // eigenpair (d_i, e_i)
+      if (last >= 0 && fabs(di - S.d[last]) <= tol) {
+        // rotate (kept j, new i) so that z_i vanishes: e_j' = c e_j + s e_i
+        const int j = S.org[last];
+        const double zj = S.z[last];
+        const double rr = sqrt(zj * zj + zi * zi);
+        S.rot_i[nrot] = i;
+        S.rot_j[nrot] = j;
+        S.rc[nrot] = zj / rr;
+        S.rs[nrot] = zi / rr;
+        ++nrot;
+        S.z[last] = rr;
+        continue;
+      }
+      S.d[keep] = di;
+      S.z[keep] = zi;
+      S.org[keep] = i;
+      last = keep;
+      ++keep;
+    }
+    S.keep = keep;
+    S.nrot = nrot;
+    S.alpha = alpha;
+    S.znorm1 = zn1;
+  }
+  __syncthreads();
+  const int K = S.keep;
+  // 4. roots: K + 1 of them; root j lies below d_0 (j = 0), in (d_{j-1}, d_j),
+  // or above d_{K-1} (j = K).  One warp per root; lanes split the sum.
+  const double lower = fmin(K ? S.d[0] : alpha, alpha) - zn1 - tol;
+  const double upper = fmax(K ? S.d[K - 1] : alpha, alpha) + zn1 + tol;
+  for (int j = warp; j <= K; j += nwarps) {
+    if (K == 0) break;
+    // bracket (lo, hi) and the pole used as origin
+    const double lo_abs = j == 0 ? lower : S.d[j - 1];
+    const double hi_abs = j == K ? upper : S.d[j];
+    auto secular = [&](int o, double t) {
+      const double org = S.d[o];
+      double sum = 0.0;
+      for (int i = lane; i < K; i += 32) sum += S.z[i] * S.z[i] / ((org - S.d[i]) + t);
+      sum = warp_sum_d(sum);
+      return S.alpha - (org + t) + sum;
+    };
+    int o;
+    double tlo, thi;
+    if (j == 0) {
+      o = 0;
+      tlo = lower - S.d[0];
+      thi = 0.0;
+    } else if (j == K) {
+      o = K - 1;
+      tlo = 0.0;
+      thi = upper - S.d[K - 1];
+    } else {
+      // origin at the pole nearer to the root: sign of f at the midpoint
+      const double half = 0.5 * (hi_abs - lo_abs);
+      if (secular(j - 1, half) > 0.0) {  // root in the right half
+        o = j;
+        tlo = -half;
+        thi = 0.0;
+      } else {
+        o = j - 1;
+        tlo = 0.0;
+        thi = half;
+      }
+    }
+    for (int it = 0; it < 200; ++it) {
+      const double mid = 0.5 * (tlo + thi);
+      if (mid == tlo || mid == thi) break;
+      if (thi - tlo <= 2.0 * kEps * fmax(fabs(tlo), fabs(thi))) break;
+      // the open end at the pole (t = 0) is never evaluated: mid != 0 here
+      if (secular(o, mid) > 0.0) tlo = mid; else thi = mid;
+    }
+    if (lane == 0) {
+      S.rorg[j] = o;
+      S.tau[j] = 0.5 * (tlo + thi);
+    }
+  }
+  __syncthreads();
+  // lambda_j - d_i, with the root held as (origin pole, offset)
+  auto gap = [&](int j, int i) { return (S.d[S.rorg[j]] - S.d[i]) + S.tau[j]; };
+  // 5. Loewner: |zhat_i|^2 = prod_j (lambda_j - d_i) / prod_{k != i} (d_k - d_i),
+  // evaluated as bounded ratios; interlacing: lambda_i < d_i < lambda_{i+1}.
+  for (int i = tid; i < K; i += blockDim.x) {
+    double p = -gap(i, i) * gap(i + 1, i);
+    for (int k = 0; k < i; ++k) p *= gap(k, i) / (S.d[k] - S.d[i]);
+    for (int k = i + 1; k < K; ++k) p *= gap(k + 1, i) / (S.d[k] - S.d[i]);
+    S.zhat[i] = copysign(sqrt(fmax(p, 0.0)), S.z[i]);
+  }
+  __syncthreads();
+  // 6. eigenvectors of the kept block into the columns of the kept
+  // coordinates plus the arrow column: column c(j) = org[j] for j < K, m for j = K
+  for (int j = warp; j <= K && K > 0; j += nwarps) {
+    const int col = j < K ? S.org[j] : m;
+    double nrm = 0.0;
+    for (int i = lane; i < K; i += 32) {
+      const double u = S.zhat[i] / gap(j, i);
+      nrm += u * u;
+    }
+    nrm = warp_sum_d(nrm) + 1.0;  // the arrow component is 1
+    const double inv = 1.0 / sqrt(nrm);
+    for (int r = lane; r < n; r += 32) V[r * ld + col] = 0.0;
+    __syncwarp();
+    for (int i = lane; i < K; i += 32) V[S.org[i] * ld + col] = S.zhat[i] / gap(j, i) * inv;
+    if (lane == 0) V[m * ld + col] = inv;
+    if (lane == 0) A[col * ld + col] = S.d[S.rorg[j]] + S.tau[j];
+  }
+  __syncthreads();
+  if (K == 0 && tid == 0) A[m * ld + m] = alpha;  // every z negligible
+  // 7. undo the coincident-d rotations (in reverse order) on the rows of V
+  for (int q = S.nrot - 1; q >= 0; --q) {
+    const int i = S.rot_i[q], j = S.rot_j[q];
+    const double c = S.rc[q], sn = S.rs[q];
+    for (int col = tid; col < n; col += blockDim.x) {
+      const double vj = V[j * ld + col], vi = V[i * ld + col];
+      V[j * ld + col] = c * vj - sn * vi;
+      V[i * ld + col] = sn * vj + c * vi;
+    }
+    __syncthreads();
+  }
+  return true;
+}
+
 __device__ void sort_eigen(const double* A, const double* V, int n, double* evals, double* evecs,
                            int* order) {
   if (threadIdx.x == 0) {
@@ -224,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
   __shared__ double evals[kMaxSel];
   __shared__ double sc[64];             // scalars
   __shared__ double alphas[kKrylov], betas[kKrylov], proj[kKrylov], lam[kKrylov];
+  __shared__ ArrowScratch arrow_scratch;
   const int tid = threadIdx.x;
   const int C = a.C;
   STAMP(0);
@@ -339,7 +551,10 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     }
     __syncthreads();
     STAMP(1);
-    const int gram_sweeps = jacobi_eigh(A, V, nsel, rp, rq, rc, rs, red, &rotated);
+    // surrogate rows over persistent rows from a previous decomposition: the
+    // Gram is an arrowhead matrix (orthogonal rows, one new row)
+    const bool arrow = collapse && arrowhead_eigh(A, V, nsel, arrow_scratch, red);
+    const int gram_sweeps = arrow ? -1 : jacobi_eigh(A, V, nsel, rp, rq, rc, rs, red, &rotated);
     STAMP(2);
     if (a.timing != nullptr && tid == 0) a.timing[12] = gram_sweeps;
     sort_eigen(A, V, nsel, evals, evecs, order);

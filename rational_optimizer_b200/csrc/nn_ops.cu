@@ -324,7 +324,7 @@ __global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __re
     rope_rotate(val, cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, false);
   }
   T* out = which == 0 ? q : (which == 1 ? k : v);
-  store_vec<T, 8>(out + ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8, val);
+  store_vec<T, 8>(out + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
 }
 
 template <typename T>
@@ -343,7 +343,7 @@ __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restric
   const int d = H * hd;
   const T* in = which == 0 ? dq : (which == 1 ? dk : dv);
   float val[8];
-  load_vec<T, 8>(in + ((static_cast<int64_t>(b) * H + h) * S + s) * hd + jv * 8, val);
+  load_vec<T, 8>(in + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
   if (which < 2) {
     const int half = hd / 2;
     rope_rotate(val, cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, true);

@@ -86,6 +86,8 @@ def train_step(model, optimizer, sync, data, completed, cfg, device, rank, world
             raise RuntimeError("the packing protocol requires every target to be loss-bearing")
         count += int(mask.sum())
         value = model.forward_loss(torch.from_numpy(x).to(device), torch.from_numpy(y).to(device))
+        if micro == cfg["accumulation"] - 1:
+            sync.begin_backward()
         (value / cfg["accumulation"]).backward()
         summed += value.detach().float() / cfg["accumulation"]
     sync.synchronize()

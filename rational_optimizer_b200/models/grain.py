@@ -64,10 +64,15 @@ class GRAIN(nn.Module):
         self._rlb_optimizer_stat_version = version
         self._rlb_optimizer_stats["stat_version"] = version
 
-    def forward(self, x):
+    def forward(self, x, precomputed=None):
+        """GRAIN(x).  ``precomputed``: the activation already evaluated by a fused
+        producer (the in-projection GEMM epilogue); the module then only records
+        its statistics and hands it on, so its hooks still see (x, GRAIN(x))."""
         if x.size(-1) != self.hidden_dim:
             raise ValueError(f"expected last dimension {self.hidden_dim}, got {x.size(-1)}")
         self._update_optimizer_stats(x)
+        if precomputed is not None:
+            return precomputed
         return rational_local_basis(x, self.numerator, self.denominator, self._empty_coeff,
                                     self._empty_centers, self._empty_beta, 0.0, self.eps,
                                     self.hidden_dim, self.groups)

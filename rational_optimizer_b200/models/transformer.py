@@ -21,7 +21,9 @@ import torch.nn as nn
 
 from ..ops.attention import causal_self_attention, precompute_rope
 from ..ops.cross_entropy import linear_cross_entropy
+from ..ops.grain import in_proj_grain, in_proj_grain_supported
 from ..ops.linear import Linear, cached_cast, _WeightCache
+from ..parallel import param_ready as _ready
 from ..ops.norm import add_rms_norm, fused_add_norm_supported, rms_norm
 from .grain import GRAIN
 
@@ -127,7 +129,17 @@ class GRAINMLP(nn.Module):
         self.out_proj = Linear(self.hidden_dim, dim, bias=False)
 
     def forward(self, x):
-        return self.out_proj(self.rlb_activation(self.in_proj(x)))
+        act = self.rlb_activation
+        if (self.in_proj.compute_dtype == torch.bfloat16 and self.in_proj.weight.dtype == torch.float32
+                and in_proj_grain_supported(x, act.hidden_dim, act.groups)):
+            # GRAIN evaluated in the in-projection's GEMM epilogue (one pass over h)
+            if _ready.pending():
+                _ready.wait(self.in_proj.weight)
+            w = cached_cast(self.in_proj.weight, torch.bfloat16, self.in_proj._cache)
+            y, h = in_proj_grain(x, self.in_proj.weight, w, act.numerator, act.denominator, act.eps,
+                                 act.groups)
+            return self.out_proj(act(h, precomputed=y))
+        return self.out_proj(act(self.in_proj(x)))
 
 
 def apply_rlb_positive_gauge(model: nn.Module, log_scale: float, seed: int) -> int:

@@ -2,11 +2,12 @@
 
 ``qkv`` is the fused projection output ``[B*S, 3*d]`` (q | k | v, heads
 contiguous), as produced by ``CausalSelfAttention.qkv`` of the reference
-(training/train.py:48-73).  CUDA: one kernel splits q/k/v into [B,H,S,hd],
-applies RoPE to q and k (fp32 tables), and its backward applies the inverse
-rotation and re-packs into ``[B*S, 3d]``.  The attention itself runs the
-sm_100a flash-attention kernel when available for the shape
-(``csrc/attention_sm100.cu``), otherwise SDPA.
+(training/train.py:48-73).  CUDA: one kernel splits q/k/v into token-major
+``[B, S, H, hd]`` storage returned as ``[B, H, S, hd]`` views, applying RoPE
+to q and k (fp32 tables); its backward applies the inverse rotation and
+re-packs into ``[B*S, 3d]``.  The attention runs PyTorch's SDPA (cuDNN on
+sm_100), which allocates its output and gradients in the layout of q, so
+the ``[B, S, H*hd]`` output needed by the projection is a view, not a copy.
 """
 from __future__ import annotations
 
@@ -43,8 +44,7 @@ class _RopeQKV(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dq, dk, dv):
         cos2d, sin2d = ctx.saved_tensors
-        dqkv = _ext.ext().rope_qkv_backward(dq.contiguous(), dk.contiguous(), dv.contiguous(),
-                                            cos2d, sin2d)
+        dqkv = _ext.ext().rope_qkv_backward(dq, dk, dv, cos2d, sin2d)
         return dqkv, None, None, None, None, None, None
 
 

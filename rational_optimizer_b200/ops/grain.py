@@ -111,6 +111,89 @@ class _GrainFunction(torch.autograd.Function):
         return (gx, gnum.to(ndt), gden.to(ddt), gcoef.to(ldt), None, None, None, None, None, None)
 
 
+class _InProjGrainFunction(torch.autograd.Function):
+    """``y = GRAIN(x W^T)`` with the activation computed in the GEMM epilogue.
+
+    Forward runs ``grain_in_proj_forward`` (csrc/gemm2_sm100.cu): one 2-SM
+    tcgen05 GEMM whose epilogue stores the pre-activation ``h`` (kept for the
+    backward) and the activation ``y``, so ``h`` is never re-read from HBM in
+    the forward.  ``h`` is also returned (non-differentiable) for the
+    activation module's forward hooks.  Backward: the GRAIN backward kernel,
+    then the in-projection's input and weight gradients (the weight gradient
+    accumulates in the GEMM when the weight's ``.grad`` is a managed buffer,
+    as in ``ops.linear``).
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, w_compute, numerator, denominator, eps, groups):
+        C = ext()
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != w_compute.dtype:
+            x2 = x2.to(w_compute.dtype)
+        x2 = x2.contiguous()
+        num = numerator.detach().float().contiguous()
+        den = denominator.detach().float().contiguous()
+        out = C.grain_in_proj_forward(x2, w_compute, num, den, float(eps))
+        if out is None:
+            raise RuntimeError("fused GRAIN in-projection rejected a supported shape")
+        h, y = out
+        ctx.save_for_backward(x2, w_compute, h, num, den)
+        ctx.weight = weight
+        ctx.meta = (float(eps), int(groups), x.shape, x.dtype, numerator.dtype, denominator.dtype)
+        ctx.mark_non_differentiable(h)
+        shape = tuple(x.shape[:-1]) + (h.shape[-1],)
+        return y.view(shape), h.view(shape)
+
+    @staticmethod
+    def backward(ctx, gy, _gh):
+        from . import gemm
+        from .linear import ACCUMULATE_ATTR, READY_ATTR
+        C = ext()
+        x2, w, h, num, den = ctx.saved_tensors
+        eps, groups, in_shape, x_dtype, ndt, ddt = ctx.meta
+        hidden = h.shape[-1]
+        g2 = gy.reshape(-1, hidden)
+        if g2.dtype != h.dtype:
+            g2 = g2.to(h.dtype)
+        g2 = g2.contiguous()
+        e = num.new_empty(groups, 0)
+        gh, gnum, gden, _ = C.grain_backward(g2, h, num, den, num.new_empty(groups, 0, 2), e, e, 0.0, eps,
+                                             hidden, groups, None, None)
+        gx = gw = None
+        if ctx.needs_input_grad[0]:
+            gx = gemm.matmul_nn(gh, w).reshape(in_shape)
+            if gx.dtype != x_dtype:
+                gx = gx.to(x_dtype)
+        if ctx.needs_input_grad[1]:
+            weight = ctx.weight
+            buf = weight.grad
+            if (getattr(weight, ACCUMULATE_ATTR, False) and buf is not None and buf.is_cuda
+                    and buf.dtype == torch.float32 and buf.is_contiguous()):
+                gemm.matmul_tn_accumulate_(buf, gh, x2)
+                ready = getattr(weight, READY_ATTR, None)
+                if ready is not None:
+                    ready(weight)
+            else:
+                gw = gemm.matmul_tn(gh, x2, out_dtype=weight.dtype)
+        return gx, gw, None, gnum.to(ndt), gden.to(ddt), None, None
+
+
+def in_proj_grain_supported(x, hidden_dim, groups) -> bool:
+    """Whether the fused in-projection + GRAIN path applies (CUDA bf16, groups of 256)."""
+    if not (x.is_cuda and x.dtype == torch.bfloat16) or torch_fallback_requested():
+        return False
+    if int(hidden_dim) != 256 * int(groups):
+        return False
+    if os.environ.get("RO_FUSED_GRAIN", "1") == "0":
+        return False
+    return hasattr(ext(), "grain_in_proj_forward")
+
+
+def in_proj_grain(x, weight, w_compute, numerator, denominator, eps, groups):
+    """``(y, h)``: GRAIN of the in-projection and the pre-activation (no gradient)."""
+    return _InProjGrainFunction.apply(x, weight, w_compute, numerator, denominator, eps, groups)
+
+
 def _validate(x, hidden_dim, groups, centers):
     hidden_dim = int(hidden_dim)
     groups = int(groups)

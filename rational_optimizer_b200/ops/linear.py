@@ -13,12 +13,16 @@ from __future__ import annotations
 import torch
 
 from . import gemm
+from ..parallel import param_ready as _ready
 
 # Parameters carrying this attribute (set by the data-parallel gradient
 # synchroniser, whose ``zero_grad`` zeroes their ``.grad`` buffers every step)
 # receive weight gradients by in-GEMM accumulation into ``.grad`` instead of
 # through autograd.  ``torch.autograd.grad`` therefore sees no gradient for them.
 ACCUMULATE_ATTR = "_ro_accumulate_grad"
+# Optional callable on such parameters, invoked once the in-GEMM accumulation
+# for the current backward pass has been issued (gradient bucketing).
+READY_ATTR = "_ro_grad_ready"
 
 
 class _WeightCache:
@@ -74,6 +78,9 @@ class _LinearFunction(torch.autograd.Function):
                 # dW accumulates in the GEMM (beta = 1) straight into the
                 # parameter's gradient buffer; autograd then has nothing to add.
                 gemm.matmul_tn_accumulate_(buf, g2, x2)
+                ready = getattr(ctx.weight, READY_ATTR, None)
+                if ready is not None:
+                    ready(ctx.weight)
             else:
                 gw = gemm.matmul_tn(g2, x2, out_dtype=ctx.w_dtype)
         return gx, gw, None
@@ -94,6 +101,8 @@ class Linear(torch.nn.Linear):
         self.compute_dtype = torch.bfloat16
 
     def forward(self, x):
+        if _ready.pending():
+            _ready.wait(self.weight)
         if not x.is_cuda or self.compute_dtype == self.weight.dtype:
             if x.dtype != self.weight.dtype:
                 x = x.to(self.weight.dtype)

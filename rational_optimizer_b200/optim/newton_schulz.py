@@ -16,6 +16,7 @@ On CUDA the batched GEMMs go through :mod:`rational_optimizer_b200.ops.gemm`
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -66,36 +67,51 @@ def _ns5_torch_bf16(work: torch.Tensor) -> torch.Tensor:
     return work
 
 
-def ns5_grouped_bf16(x16: torch.Tensor) -> torch.Tensor:
+def ns5_grouped_bf16(x16: torch.Tensor, *, native: bool | None = None) -> torch.Tensor:
     """NS5 of a contiguous bf16 batch ``[B, r, c]`` with ``r <= c`` (bf16 result).
 
     CUDA: the Frobenius normalisation kernel followed by, per iteration,
-    three batched tcgen05 GEMMs with fused epilogues
-    ``A = X X^T``; ``P = b A + c A A``; ``X = a X + P X``.
+    ``A = X X^T``; ``P = b A + c A A``; ``X = a X + P X``.  ``native`` selects
+    the package's batched tcgen05 GEMMs, whose epilogue reads the addend
+    directly (``RO_NATIVE_NS=1`` by default; cuBLAS batched GEMMs otherwise,
+    which first copy the addend into the output).
     """
     if x16.shape[-2] > x16.shape[-1]:
         raise RuntimeError("ns5_grouped_bf16 expects wide blocks")
     if _ext.available() and x16.is_cuda and hasattr(_ext.ext(), "ns_normalize"):
         C = _ext.ext()
         work = C.ns_normalize(x16.contiguous())
-        a, b, c = NS_COEFFICIENTS
-        if _native_gemm_enabled():
-            ok = True
-            for _ in range(5):
-                gram = C.gemm_bf16(work, work, False, True, False)
-                poly = C.gemm_bf16_ex(gram, gram, False, True, False, gram, c, b) if gram is not None else None
-                nxt = C.gemm_bf16_ex(poly, work, False, False, False, work, 1.0, a) if poly is not None else None
-                if nxt is None:
-                    ok = False
-                    break
-                work = nxt
-            if ok:
-                return work
-            work = C.ns_normalize(x16.contiguous())
+        if native is None:
+            native = _native_ns_enabled()
+        if native and hasattr(C, "gemm_bf16_ex"):
+            out = _ns5_native_bf16(C, work)
+            if out is not None:
+                return out
         return _ns5_torch_bf16(work)
     work = x16.to(torch.bfloat16)
     norm = torch.linalg.vector_norm(work.float(), dim=(-2, -1), keepdim=True).clamp_min(NS_EPS)
     return _ns5_torch_bf16(work / norm.to(work.dtype))
+
+
+def _ns5_native_bf16(C, work):
+    a, b, c = NS_COEFFICIENTS
+    for _ in range(5):
+        gram = C.gemm_bf16(work, work, False, True, False)
+        poly = C.gemm_bf16_ex(gram, gram, False, True, False, gram, c, b) if gram is not None else None
+        nxt = C.gemm_bf16_ex(poly, work, False, False, False, work, 1.0, a) if poly is not None else None
+        if nxt is None:
+            return None
+        work = nxt
+    return work
+
+
+def _native_ns_enabled() -> bool:
+    return os.environ.get("RO_NATIVE_NS", _native_default()) == "1"
+
+
+def _native_default() -> str:
+    from ..ops import gemm as _g
+    return "1" if _g._NATIVE else "0"
 
 
 def _native_gemm_enabled() -> bool:

@@ -37,6 +37,8 @@ import torch
 import torch.distributed as dist
 from torch.autograd.graph import increment_version
 
+from ..parallel import param_ready
+
 from . import tiller_math as tm
 from .newton_schulz import (attention_head_group_zero_power, match_rms_adamw_adjustment,
                             rational_group_zero_power)
@@ -151,13 +153,35 @@ def sharding_enabled(world: int) -> bool:
     return world > 1 and os.environ.get("RO_TILLER_SHARD", "1") != "0"
 
 
-def broadcast_owned(tensors_by_layer, layers, world, group=None):
-    """Replicate per-layer tensors from their owners; bumps autograd versions."""
+def broadcast_owned(tensors_by_layer, layers, world, group=None, *, deferred=False):
+    """Replicate per-layer tensors from their owners; bumps autograd versions.
+
+    ``deferred``: enqueue the broadcasts on a side stream after the work
+    issued so far and return at once; each layer's tensors are marked pending
+    until their broadcast completes (``parallel.param_ready``), so the next
+    forward overlaps the transfer of later layers.
+    """
+    flat = [t for tensors in tensors_by_layer for t in tensors]
+    deferred = deferred and bool(flat) and flat[0].is_cuda
+    if deferred:
+        side = param_ready.side_stream(flat[0].device)
+        side.wait_stream(torch.cuda.current_stream(flat[0].device))
     for layer, tensors in enumerate(tensors_by_layer):
         src = layer_owner(layer, layers, world)
         src_global = dist.get_global_rank(group, src) if group is not None else src
+        if deferred:
+            with torch.cuda.stream(side):
+                for t in tensors:
+                    dist.broadcast(t.data if isinstance(t, torch.nn.Parameter) else t, src=src_global,
+                                   group=group)
+                event = torch.cuda.Event()
+                event.record(side)
+            param_ready.defer(tensors, event)
+        else:
+            for t in tensors:
+                dist.broadcast(t.data if isinstance(t, torch.nn.Parameter) else t, src=src_global,
+                               group=group)
         for t in tensors:
-            dist.broadcast(t.data if isinstance(t, torch.nn.Parameter) else t, src=src_global, group=group)
             increment_version(t)
 
 
@@ -573,6 +597,7 @@ class TILLERRouter(torch.optim.Optimizer):
         broadcast_owned(per_layer, L, self.world_size, self.loss_probe_group)
 
     def state_dict(self):
+        param_ready.wait_all()
         self._sync_shards()
         return super().state_dict()
 
@@ -617,7 +642,7 @@ class TILLERRouter(torch.optim.Optimizer):
                     roles[role].apply(coefficients[lo:hi], decay=1.0 - lr * wd, lr=lr)
                 if sharded:
                     broadcast_owned([(p["in_weight"], p["out_weight"]) for p in self.pairs], L,
-                                    self.world_size, self.loss_probe_group)
+                                    self.world_size, self.loss_probe_group, deferred=True)
 
             metas = {r: chord_meta(chords[r]) for r in chords}
             return {"exact_by_role": packed[0:2], "momentum_by_role": packed[2:4], "weights": packed[4],
@@ -858,9 +883,7 @@ class TILLERRouter(torch.optim.Optimizer):
                 if pair[key].grad is None:
                     raise RuntimeError("TILLER parameter lacks gradient")
         if not refresh:
-            terms = [(p[k].grad.detach().float() * p[k].detach().float()).sum()
-                     for p in self.pairs for k in ("in_weight", "out_weight")]
-            self._rfd_decay_derivative = torch.stack(terms).sum() * wd
+            self._rfd_decay_derivative = self._decay_derivative(wd)
         L = len(self.pairs)
         anchor = self.anchor
         if refresh:
@@ -939,6 +962,16 @@ class TILLERRouter(torch.optim.Optimizer):
         self._capture_telemetry_next_step = False
         self._clip_factor = None
         return loss
+
+    def _decay_derivative(self, wd):
+        """wd * sum over routed matrices of <grad, weight> (optimizer_design/_tiller/core.py:4511-4519)."""
+        tensors = [(p[k].grad.detach(), p[k].detach()) for p in self.pairs for k in ("in_weight", "out_weight")]
+        if self._use_fused() and all(g.dtype == torch.float32 and g.is_contiguous() and w.is_contiguous()
+                                     for g, w in tensors):
+            from .._ext import ext
+            return ext().multi_tensor_dot([g for g, _ in tensors], [w for _, w in tensors], float(wd))
+        terms = [(g.float() * w.float()).sum() for g, w in tensors]
+        return torch.stack(terms).sum() * wd
 
     def _cache_refresh_state(self):
         route = {
@@ -1118,6 +1151,7 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
         broadcast_owned(per_layer, L, self.router.world_size, self.router.loss_probe_group)
 
     def state_dict(self):
+        param_ready.wait_all()
         self._sync_shards()
         return super().state_dict()
 
@@ -1171,7 +1205,7 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
                     metas.append(tiller_fused.chord_meta(chord))
                 if sharded:
                     broadcast_owned([(p,) for p in params], len(params), self.router.world_size,
-                                    self.router.loss_probe_group)
+                                    self.router.loss_probe_group, deferred=True)
                 continue
             momenta = foreach_nesterov(self, params, self.momentum)
             grads = torch.stack([p.grad.detach() for p in params]).float()

@@ -2,11 +2,23 @@
 
 Every trainable parameter's ``.grad`` is a view into a single fp32 buffer
 (the reference's DDP runs with per-parameter grads in 25 MB buckets,
-training/train.py:2366-2371).  After backward the whole buffer is averaged
-across ranks in fixed-size buckets, by the in-kernel NVLink all-reduce of
-``csrc/comm.cu`` when the communicator is available (one process per GPU,
-peer memory mapped through CUDA IPC), otherwise by NCCL.  With one rank the
-synchroniser only manages the buffer.
+training/train.py:2366-2371).  Two ways to average it across ranks:
+
+* overlapped (default with NCCL): one bucket per transformer layer.  A
+  layer's bucket is all-reduced (NCCL, ``ReduceOp.AVG``) as soon as the
+  backward pass has produced every gradient in it, so the collectives of
+  layers L-1 .. 1 run under the backward of the layers below; only the
+  embedding/final-norm bucket is reduced after backward.  Readiness is
+  tracked per parameter: weights whose gradient the GEMM accumulates in
+  place report through ``READY_ATTR`` (``ops.linear``), all others through
+  post-accumulate-grad hooks.  Buckets are launched strictly in descending
+  layer order, so every rank issues the same collectives in the same order.
+* whole buffer after backward: the in-kernel NVLink all-reduce of
+  ``csrc/comm.cu`` when the P2P communicator is available (one process per
+  GPU, peer memory mapped through CUDA IPC), otherwise NCCL in fixed-size
+  buckets.
+
+With one rank the synchroniser only manages the buffer.
 """
 from __future__ import annotations
 
@@ -15,12 +27,12 @@ import os
 import torch
 import torch.distributed as dist
 
-from ..ops.linear import ACCUMULATE_ATTR
+from ..ops.linear import ACCUMULATE_ATTR, READY_ATTR
 
 
 class GradientSynchronizer:
     def __init__(self, model: torch.nn.Module, *, group=None, bucket_bytes: int = 256 << 20,
-                 communicator=None, transport: str | None = None):
+                 communicator=None, transport: str | None = None, overlap: bool | None = None):
         seen, params = set(), []
         for p in model.parameters():
             if p.requires_grad and id(p) not in seen:
@@ -33,18 +45,27 @@ class GradientSynchronizer:
         device = params[0].device
         total = sum(p.numel() for p in params)
         if transport is None:
-            transport = os.environ.get("RO_GRAD_TRANSPORT", "p2p")
-        if communicator is None and self.world > 1 and transport == "p2p" and device.type == "cuda":
+            transport = os.environ.get("RO_GRAD_TRANSPORT", "nccl")
+        if overlap is None:
+            overlap = os.environ.get("RO_GRAD_OVERLAP", "1") == "1"
+        self.overlap = bool(overlap and self.world > 1 and device.type == "cuda" and transport == "nccl")
+        if (communicator is None and self.world > 1 and transport == "p2p" and device.type == "cuda"):
             from .comm import maybe_communicator
             communicator = maybe_communicator(device, total, group=group)
         self.communicator = communicator
-        self.transport = "p2p" if communicator is not None else ("nccl" if self.world > 1 else "none")
+        if communicator is not None:
+            self.transport = "p2p"
+        elif self.world > 1:
+            self.transport = "nccl-overlap" if self.overlap else "nccl"
+        else:
+            self.transport = "none"
         if communicator is not None and dtype == torch.float32:
             self.flat = communicator.float_view(total)
             self.flat.zero_()
         else:
             self.flat = torch.zeros(total, dtype=dtype, device=device)
         self.views = []
+        self.offsets = []
         offset = 0
         accumulate = self.flat.is_cuda and self.flat.dtype == torch.float32
         for p in params:
@@ -55,8 +76,82 @@ class GradientSynchronizer:
                 # the model's GEMMs may add weight gradients straight into the view
                 setattr(p, ACCUMULATE_ATTR, True)
             self.views.append(view)
+            self.offsets.append(offset)
             offset += n
         self.bucket_elems = max(1, bucket_bytes // self.flat.element_size())
+        self._armed = False
+        self._works = []
+        if self.overlap:
+            self._setup_buckets(model)
+
+    # -- overlapped buckets ----------------------------------------------------
+    def _setup_buckets(self, model):
+        """One bucket per ``layers.<i>.`` prefix (contiguous in the flat buffer)."""
+        names = {}
+        for n, p in model.named_parameters():
+            names.setdefault(id(p), n)
+        layer_of = []
+        for p in self.params:
+            parts = names.get(id(p), "").split(".")
+            layer_of.append(int(parts[1]) if len(parts) > 2 and parts[0] == "layers" and parts[1].isdigit()
+                            else None)
+        self.bucket_ranges = []      # (lo, hi) element ranges, index = layer
+        self.bucket_params = []      # parameter count per bucket
+        self._bucket_of = {}
+        layers = sorted({l for l in layer_of if l is not None})
+        for layer in layers:
+            idx = [i for i, l in enumerate(layer_of) if l == layer]
+            lo = self.offsets[idx[0]]
+            hi = self.offsets[idx[-1]] + self.params[idx[-1]].numel()
+            if any(layer_of[i] != layer for i in range(idx[0], idx[-1] + 1)):
+                raise RuntimeError("layer parameters are not contiguous in the gradient buffer")
+            b = len(self.bucket_ranges)
+            self.bucket_ranges.append((lo, hi))
+            self.bucket_params.append(len(idx))
+            for i in idx:
+                self._bucket_of[id(self.params[i])] = b
+        covered = set(self._bucket_of)
+        self.rest = [(self.offsets[i], self.offsets[i] + p.numel()) for i, p in enumerate(self.params)
+                     if id(p) not in covered]
+        for p in self.params:
+            if id(p) in covered:
+                setattr(p, READY_ATTR, self._param_ready)
+                p.register_post_accumulate_grad_hook(self._param_ready)
+        self._pending = list(self.bucket_params)
+        self._next = len(self.bucket_ranges) - 1
+
+    def begin_backward(self):
+        """Arm readiness tracking for the backward pass whose gradients are final."""
+        if not self.overlap:
+            return
+        self._armed = True
+        self._pending = list(self.bucket_params)
+        self._next = len(self.bucket_ranges) - 1
+        self._works = []
+
+    def _param_ready(self, p):
+        if not self._armed:
+            return
+        b = self._bucket_of.get(id(p))
+        if b is None:
+            return
+        self._pending[b] -= 1
+        while self._next >= 0 and self._pending[self._next] <= 0:
+            self._launch(self._next)
+            self._next -= 1
+
+    def _launch(self, b):
+        lo, hi = self.bucket_ranges[b]
+        self._works.append(dist.all_reduce(self.flat[lo:hi], op=dist.ReduceOp.AVG, group=self.group,
+                                           async_op=True))
+
+    # -- common ----------------------------------------------------------------
+    def flat_covering(self):
+        """The flat buffer when every managed gradient is still a view of it, else None."""
+        for p, v in zip(self.params, self.views):
+            if p.grad is None or p.grad.data_ptr() != v.data_ptr():
+                return None
+        return self.flat
 
     def zero_grad(self):
         for p, v in zip(self.params, self.views):
@@ -68,6 +163,22 @@ class GradientSynchronizer:
         """Average gradients across ranks (no-op for one rank)."""
         if self.world == 1:
             return
+        if self.overlap:
+            # buckets whose readiness was not reported (e.g. unused parameters)
+            # are launched now, still in descending order
+            while self._next >= 0:
+                self._launch(self._next)
+                self._next -= 1
+            for lo, hi in _merge(self.rest):
+                self._works.append(dist.all_reduce(self.flat[lo:hi], op=dist.ReduceOp.AVG,
+                                                   group=self.group, async_op=True))
+            for w in self._works:
+                w.wait()
+            self._works = []
+            self._armed = False
+            self._pending = list(self.bucket_params)
+            self._next = len(self.bucket_ranges) - 1
+            return
         if self.communicator is not None:
             self.communicator.all_reduce_mean_(self.flat)
             return
@@ -75,3 +186,13 @@ class GradientSynchronizer:
             chunk = self.flat[start: start + self.bucket_elems]
             dist.all_reduce(chunk, op=dist.ReduceOp.SUM, group=self.group)
         self.flat.div_(self.world)
+
+
+def _merge(ranges):
+    out = []
+    for lo, hi in sorted(ranges):
+        if out and out[-1][1] == lo:
+            out[-1] = (out[-1][0], hi)
+        else:
+            out.append((lo, hi))
+    return out

@@ -1,0 +1,52 @@
+"""Deferred parameter replication: CUDA events the next use of a parameter waits on.
+
+With layer-sharded optimizers each rank updates the weights of the layers it
+owns and the updated weights are broadcast from their owners on a side
+stream, so the transfer overlaps whatever the default stream does next (the
+next step's forward).  ``defer(params, event)`` marks parameters as pending
+until ``event``; ``wait(param)`` (called by every ``ops.linear.Linear``
+forward) makes the current stream wait for it first, so a layer's forward
+starts as soon as its own weights have arrived.  ``wait_all()`` is for code
+that reads every parameter (checkpoints, evaluation, state dicts).
+"""
+from __future__ import annotations
+
+import torch
+
+_PENDING: dict[int, torch.cuda.Event] = {}
+_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def side_stream(device: torch.device) -> torch.cuda.Stream:
+    index = torch.device(device).index
+    if index is None:
+        index = torch.cuda.current_device()
+    s = _STREAMS.get(index)
+    if s is None:
+        s = torch.cuda.Stream(device=index)
+        _STREAMS[index] = s
+    return s
+
+
+def defer(params, event: torch.cuda.Event) -> None:
+    for p in params:
+        _PENDING[id(p)] = event
+
+
+def pending() -> bool:
+    return bool(_PENDING)
+
+
+def wait(param) -> None:
+    if _PENDING:
+        ev = _PENDING.pop(id(param), None)
+        if ev is not None:
+            torch.cuda.current_stream(param.device).wait_event(ev)
+
+
+def wait_all() -> None:
+    if not _PENDING:
+        return
+    for ev in set(_PENDING.values()):
+        torch.cuda.current_stream().wait_event(ev)
+    _PENDING.clear()

@@ -26,8 +26,22 @@ def learning_rate(step, *, lr, min_lr, warmup_steps, total_steps):
     return min_lr + 0.5 * (1.0 + math.cos(math.pi * progress)) * (lr - min_lr)
 
 
-def clip_grad_norm(params, max_norm):
-    """Global L2 norm of all gradients (fp32) and in-place clipping; returns the device norm."""
+def clip_grad_norm(params, max_norm, flat=None):
+    """Global L2 norm of all gradients (fp32) and in-place clipping; returns the device norm.
+
+    ``flat``: the single fp32 buffer every gradient is a view of (the data-
+    parallel synchroniser's); on CUDA the norm is then one fixed-order
+    reduction kernel over the buffer and the clip one scaling pass, instead of
+    per-tensor norms (torch.nn.utils.clip_grad_norm_, used by the reference
+    trainer, training/train.py:957).
+    """
+    if flat is not None and flat.is_cuda and flat.dtype == torch.float32 and _has_dot():
+        from .. import _ext
+        C = _ext.ext()
+        sumsq = C.multi_tensor_dot([flat], [flat], 1.0)
+        if max_norm > 0:
+            C.clip_scale_(flat, sumsq.reshape(1), float(max_norm))
+        return sumsq.sqrt()
     grads = [p.grad for p in params if p.grad is not None]
     norms = torch._foreach_norm(grads, 2.0)
     total = torch.linalg.vector_norm(torch.stack([n.float() for n in norms]), 2.0)
@@ -35,6 +49,11 @@ def clip_grad_norm(params, max_norm):
         coef = (float(max_norm) / (total + 1e-6)).clamp(max=1.0)
         torch._foreach_mul_(grads, coef)
     return total
+
+
+def _has_dot():
+    from .. import _ext
+    return _ext.available() and hasattr(_ext.ext(), "multi_tensor_dot")
 
 
 class TrainEngine:
@@ -62,12 +81,14 @@ class TrainEngine:
             self.set_lr(lr)
         self.sync.zero_grad()
         total = None
-        for x, y in batches:
+        for i, (x, y) in enumerate(batches):
             loss = self.model.forward_loss(x, y)
+            if i == len(batches) - 1:
+                self.sync.begin_backward()
             (loss / self.grad_accum).backward()
             total = loss.detach() if total is None else total + loss.detach()
         self.sync.synchronize()
-        norm = clip_grad_norm(self.sync.params, self.grad_clip)
+        norm = clip_grad_norm(self.sync.params, self.grad_clip, self.sync.flat_covering())
         self.last_grad_norm = norm
         if self.clip_observer is not None:
             self.clip_observer.record_realized_clipping(norm, self.grad_clip)

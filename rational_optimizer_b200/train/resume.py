@@ -34,6 +34,7 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
+from ..parallel import param_ready
 from ..utils import faults
 from .integrity import Manifest
 
@@ -109,6 +110,7 @@ def save(path: Path, *, args, rank, world_size, is_distributed, device, model, o
          optimizer_step_times, grad_clip_observed_steps, grad_clip_triggered_steps,
          run_cuda_max_memory_allocated, run_cuda_max_memory_reserved, active_seconds,
          strict=False, cpu_probe_state=None):
+    param_ready.wait_all()
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
     rpath = rank_path(path, rank)
@@ -151,6 +153,7 @@ def save(path: Path, *, args, rank, world_size, is_distributed, device, model, o
 def load(path: Path, *, args, rank, world_size, is_distributed, device, model, optimizer,
          train_generator, probe_state, strict=False):
     """Restore everything :func:`save` wrote; None when no checkpoint exists yet."""
+    param_ready.wait_all()
     path = Path(path).resolve()
     if strict:
         if int(rank) == 0:

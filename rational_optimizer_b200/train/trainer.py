@@ -35,6 +35,7 @@ from pathlib import Path
 
 import torch
 
+from ..parallel import param_ready
 from ..models.transformer import (ACCEPTED_ACTIVATIONS, GRAIN_ACTIVATION_IDS, CausalTransformer,
                                   apply_rlb_positive_gauge, grain_settings)
 from ..optim.composite import (ACTIVE_OPTIMIZERS, RATIONAL_SPECIFIC_OPTIMIZERS,
@@ -226,6 +227,7 @@ def validate_optimizer_protocol(args):
 
 @torch.no_grad()
 def evaluate(model, tokens, args, offsets, rank, device, is_distributed):
+    param_ready.wait_all()
     model.eval()
     gen = torch.Generator(device="cpu")
     gen.manual_seed(args.seed + 1_000_003 + rank)
@@ -526,10 +528,12 @@ class Run:
             audit.assert_optimizer_realized_lr(opt, lr, args)
             self.sync.zero_grad()
             loss_sum = None
-            for _ in range(args.grad_accum):
+            for micro in range(args.grad_accum):
                 x, y = sample_batch(self.train_tokens, args.batch_size, args.seq_len, self.offsets,
                                     self.train_gen, device)
                 loss = model.forward_loss(x, y)
+                if micro == args.grad_accum - 1:
+                    self.sync.begin_backward()
                 (loss / args.grad_accum).backward()
                 loss_sum = loss.detach().float() if loss_sum is None else loss_sum + loss.detach().float()
             self.sync.synchronize()
@@ -537,7 +541,8 @@ class Run:
                 torch.cuda.synchronize(device)
             fb_seconds = time.perf_counter() - t_fb
             # with clipping off the norm is only measured, on log steps
-            norm = clip_grad_norm(self.sync.params, args.grad_clip) if (args.grad_clip > 0 or capture) else None
+            norm = (clip_grad_norm(self.sync.params, args.grad_clip, self.sync.flat_covering())
+                    if (args.grad_clip > 0 or capture) else None)
             if self.clip_observer is not None:
                 self.clip_observer.record_realized_clipping(norm if args.grad_clip > 0 or capture else None,
                                                             args.grad_clip)

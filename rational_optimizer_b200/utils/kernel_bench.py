@@ -104,8 +104,10 @@ def cases(rows):
         return (lambda: C.rope_qkv_forward(qkv, cos, sin, B, S, heads, hd)), 2 * qkv.numel() * 2, 0
 
     def rope_bwd():
-        q = torch.randn(B, heads, S, hd, device=dev, dtype=bf)
-        k, v = torch.randn_like(q), torch.randn_like(q)
+        # gradients in the token-major storage the attention produces
+        q = torch.randn(B, S, heads, hd, device=dev, dtype=bf).transpose(1, 2)
+        k = torch.randn(B, S, heads, hd, device=dev, dtype=bf).transpose(1, 2)
+        v = torch.randn(B, S, heads, hd, device=dev, dtype=bf).transpose(1, 2)
         pos = torch.arange(S, device=dev, dtype=f32)
         inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev, dtype=f32) / hd))
         fr = torch.outer(pos, inv)
@@ -123,10 +125,48 @@ def cases(rows):
         b = torch.randn(H, d, device=dev, dtype=bf)
         return (lambda: C.gemm_bf16(a, b, False, True, False)), 0, 2.0 * rows * d * H
 
+    def gemm2_in_proj():
+        a = torch.randn(rows, d, device=dev, dtype=bf)
+        b = torch.randn(H, d, device=dev, dtype=bf)
+        return (lambda: C.gemm2_bf16(a, b)), 0, 2.0 * rows * d * H
+
+    def grain_in_proj_fused():
+        a = torch.randn(rows, d, device=dev, dtype=bf)
+        b = (torch.randn(H, d, device=dev) * 0.03).to(bf)
+        num = torch.tensor(GRAIN_NUMERATOR, device=dev).repeat(G, 1)
+        den = torch.tensor(GRAIN_DENOMINATOR, device=dev).repeat(G, 1)
+        return (lambda: C.grain_in_proj_forward(a, b, num, den, 1e-6)), 0, 2.0 * rows * d * H
+
+    def grain_in_proj_unfused():
+        a = torch.randn(rows, d, device=dev, dtype=bf)
+        b = (torch.randn(H, d, device=dev) * 0.03).to(bf)
+        num = torch.tensor(GRAIN_NUMERATOR, device=dev).repeat(G, 1)
+        den = torch.tensor(GRAIN_DENOMINATOR, device=dev).repeat(G, 1)
+        e = torch.empty(G, 0, device=dev)
+        e3 = torch.empty(G, 0, 2, device=dev)
+
+        def run():
+            h = a @ b.t()
+            return C.grain_forward(h, num, den, e3, e, e, 0.0, 1e-6, H, G, -1, False)
+        return run, 0, 2.0 * rows * d * H
+
     def gemm_in_proj_cublas():
         a = torch.randn(rows, d, device=dev, dtype=bf)
         b = torch.randn(H, d, device=dev, dtype=bf)
         return (lambda: a @ b.t()), 0, 2.0 * rows * d * H
+
+    def _ns5(native):
+        from ..optim.newton_schulz import ns5_grouped_bf16
+        B, r, c = 18 * G, 256, d  # router incoming blocks of one step
+        x = torch.randn(B, r, c, device=dev, dtype=bf)
+        flops = 5 * B * (2.0 * r * r * c + 2.0 * r * r * r + 2.0 * r * r * c)
+        return (lambda: ns5_grouped_bf16(x, native=native)), 0, flops
+
+    def ns5_router_cublas():
+        return _ns5(False)
+
+    def ns5_router_native():
+        return _ns5(True)
 
     def ledger():
         L = 18
@@ -156,7 +196,10 @@ def cases(rows):
     for name, fn in [("grain_fwd", grain_fwd), ("grain_bwd", grain_bwd), ("add_rmsnorm_fwd", add_norm_fwd),
                      ("add_rmsnorm_bwd", add_norm_bwd), ("rope_fwd", rope_fwd), ("rope_bwd", rope_bwd),
                      ("cross_entropy", cross_entropy), ("gemm_in_proj", gemm_in_proj),
-                     ("gemm_in_proj_cublas", gemm_in_proj_cublas), ("ledger", ledger)]:
+                     ("gemm_in_proj_cublas", gemm_in_proj_cublas),
+                     ("gemm2_in_proj", gemm2_in_proj), ("grain_in_proj_fused", grain_in_proj_fused),
+                     ("grain_in_proj_unfused", grain_in_proj_unfused), ("ns5_router_cublas", ns5_router_cublas),
+                     ("ns5_router_native", ns5_router_native), ("ledger", ledger)]:
         out[name] = fn
     return out
 

@@ -22,3 +22,16 @@ def test_p2p_allreduce_matches_nccl():
     res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert f"COMM_OK {n}" in res.stdout
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs at least two GPUs")
+def test_overlapped_sharded_training_matches_replicated():
+    n = min(torch.cuda.device_count(), 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29518",
+           os.path.join(ROOT, "tests", "train_worker.py")]
+    res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert f"TRAIN_OK {n}" in res.stdout

@@ -68,3 +68,67 @@ def test_gemm_large_linear_shapes():
     _check(dw, gy.float().t() @ x.float(), True)
     torch.cuda.synchronize()
     assert int(C.gemm_error(x).item()) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (1000, 520, 200), (4096, 4608, 1024), (300, 2304, 1024)])
+def test_gemm2_matches_fp32(M, N, K):
+    """2-SM tcgen05 GEMM (csrc/gemm2_sm100.cu): edges in M, N and K included."""
+    C = _ext.ext()
+    torch.manual_seed(1)
+    a = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    b = torch.randn(N, K, device=DEV).to(torch.bfloat16)
+    out = C.gemm2_bf16(a, b)
+    torch.cuda.synchronize()
+    assert int(C.gemm_error(a).item()) == 0
+    _check(out, a.float() @ b.float().t(), False)
+
+
+@pytest.mark.parametrize("M,groups", [(512, 2), (1000, 3), (4096, 18)])
+def test_grain_in_proj_fused_matches_unfused(M, groups):
+    """GRAIN behind the in-projection GEMM equals the GEMM followed by the GRAIN kernel."""
+    from rational_optimizer_b200.ops.grain import GRAIN_DENOMINATOR, GRAIN_NUMERATOR
+    C = _ext.ext()
+    torch.manual_seed(2)
+    K, N = 1024, 256 * groups
+    x = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) * 0.03).to(torch.bfloat16)
+    num = torch.tensor(GRAIN_NUMERATOR, device=DEV).repeat(groups, 1)
+    den = torch.tensor(GRAIN_DENOMINATOR, device=DEV).repeat(groups, 1)
+    num = num + 0.01 * torch.randn_like(num)
+    den = den + 0.01 * torch.randn_like(den)
+    h, y = C.grain_in_proj_forward(x, w, num, den, 1e-6)
+    torch.cuda.synchronize()
+    assert int(C.gemm_error(x).item()) == 0
+    _check(h, x.float() @ w.float().t(), False)
+    e = torch.empty(groups, 0, device=DEV)
+    (y_ref,) = C.grain_forward(h, num, den, torch.empty(groups, 0, 2, device=DEV), e, e, 0.0, 1e-6, N,
+                               groups, -1, False)
+    err = (y.float() - y_ref.float()).abs()
+    tol = 1e-2 * y_ref.float().abs() + 1e-3
+    assert bool((err <= tol).all()), float(err.max())
+
+
+def test_grain_mlp_fused_path_matches_unfused(monkeypatch):
+    """GRAINMLP forward/backward with GRAIN in the GEMM epilogue vs the separate kernels."""
+    import copy
+    from rational_optimizer_b200.models.transformer import GRAINMLP
+    torch.manual_seed(3)
+    base = GRAINMLP(1024, 3072, 256, 32).cuda()
+    with torch.no_grad():
+        base.rlb_activation.numerator.add_(0.01 * torch.randn_like(base.rlb_activation.numerator))
+    outs = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("RO_FUSED_GRAIN", fused)
+        m = copy.deepcopy(base)
+        x = torch.randn(2, 512, 1024, device=DEV, generator=torch.Generator(DEV).manual_seed(4)).to(
+            torch.bfloat16).requires_grad_(True)
+        seen = []
+        m.rlb_activation.register_forward_hook(lambda mod, inp, out: seen.append((inp[0].shape, out.shape)))
+        y = m(x)
+        (y.float() * torch.linspace(-1, 1, y.shape[-1], device=DEV)).sum().backward()
+        assert seen == [((2, 512, 4608), (2, 512, 4608))]
+        outs.append((y.float(), x.grad.float(), m.in_proj.weight.grad.float(),
+                     m.rlb_activation.numerator.grad.float(), m.rlb_activation.denominator.grad.float()))
+    for a, b in zip(*outs):
+        scale = b.abs().amax().item() + 1e-6
+        assert (a - b).abs().amax().item() <= 2e-2 * scale

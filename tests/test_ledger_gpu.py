@@ -40,6 +40,7 @@ def test_ledger_kernel_matches_torch(L, G):
     ws = torch.empty(int(C.tiller_ledger_workspace(n)), device=dev, dtype=torch.float64)
     prev_rows = 0
     timing = torch.zeros(16, dtype=torch.int64, device=dev)
+    arrow_steps = 0
     for step in range(12):
         functional = step in (0, 3, 8)
         exact = (torch.rand(2, n, device=dev, generator=gen) + 0.1) * 1e-3
@@ -59,8 +60,10 @@ def test_ledger_kernel_matches_torch(L, G):
         prev_rows = 32 if prev_rows == 0 else 64
         torch.cuda.synchronize()
         # both Jacobi eigensolves converge well inside their sweep limit
+        # (-1: the Gram was an arrowhead matrix and took the secular-equation path)
         sweeps = timing[12:14].tolist()
         assert sweeps[1] < 20 and (not with_gram or sweeps[0] < 20), sweeps
+        arrow_steps += int(with_gram and sweeps[0] == -1)
         assert bool(result[0] > 0.5) == bool(res.accepted.item()), (step, result, res.accepted)
         torch.testing.assert_close(cand, res.candidate_coefficients.float(), rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(coef, res.coefficients.float(), rtol=1e-4, atol=1e-5)
@@ -73,3 +76,5 @@ def test_ledger_kernel_matches_torch(L, G):
         torch.testing.assert_close(scal[0], rows.persistent_isotropic_tail, rtol=1e-4, atol=1e-14)
         torch.testing.assert_close(scal[3], st_t["ref"].float(), rtol=1e-5, atol=1e-12)
         torch.testing.assert_close(result[6], scale.float(), rtol=1e-5, atol=1e-12)
+    # surrogate steps over rows of a previous decomposition use the arrowhead solver
+    assert arrow_steps >= 5, arrow_steps

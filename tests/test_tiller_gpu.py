@@ -43,3 +43,48 @@ def test_fused_tiller_matches_torch_path():
     for key in ("factorized_adaptive_tangent_rows_row_second_moment",
                 "factorized_adaptive_tangent_columns_column_second_moment"):
         torch.testing.assert_close(fa[key], ra[key], rtol=1e-3, atol=1e-9)
+
+
+def _ext():
+    from rational_optimizer_b200._ext import ext
+    return ext()
+
+
+@pytest.mark.parametrize("P,Q,transpose", [(64, 200, False), (40, 36, False), (128, 192, True),
+                                           (72, 40, True), (40, 36, True)])
+def test_nesterov_kernel_matches_torch(P, Q, transpose):
+    torch.manual_seed(P + Q)
+    mu = 0.95
+    grads = [torch.randn(P, Q, device="cuda") for _ in range(3)]
+    bufs = [torch.randn(P, Q, device="cuda") for _ in range(3)]
+    expect_buf = [torch.lerp(b, g, 1 - mu) for b, g in zip(bufs, grads)]
+    expect_m = torch.stack([torch.lerp(g, b, mu) for g, b in zip(grads, expect_buf)])
+    expect_g = torch.stack(grads)
+    if transpose:
+        expect_m, expect_g = expect_m.transpose(1, 2), expect_g.transpose(1, 2)
+    m, g, m16 = _ext().tiller_nesterov(grads, bufs, transpose, mu)
+    for b, e in zip(bufs, expect_buf):
+        torch.testing.assert_close(b, e, rtol=1e-6, atol=1e-7)
+    torch.testing.assert_close(m, expect_m, rtol=1e-6, atol=1e-7)
+    torch.testing.assert_close(g, expect_g, rtol=0, atol=0)
+    torch.testing.assert_close(m16, m.to(torch.bfloat16), rtol=0, atol=0)
+    torch.testing.assert_close(m16.float(), expect_m, rtol=8e-3, atol=1e-7)
+
+
+@pytest.mark.parametrize("shape", [(5, 256, 1024), (3, 40, 36), (2, 7, 9)])
+def test_ns_normalize_matches_torch(shape):
+    torch.manual_seed(1)
+    x = (torch.randn(shape, device="cuda") * 3).to(torch.bfloat16)
+    norm = torch.linalg.vector_norm(x.float(), dim=(-2, -1), keepdim=True).clamp_min(1e-7)
+    expect = (x.float() / norm.to(torch.bfloat16).float()).to(torch.bfloat16)
+    got = _ext().ns_normalize(x)
+    torch.testing.assert_close(got.float(), expect.float(), rtol=8e-3, atol=0)
+
+
+def test_multi_tensor_dot_matches_torch():
+    torch.manual_seed(2)
+    a = [torch.randn(s, device="cuda") for s in ((1024, 4608), (37,), (3, 5, 7), (4096,))]
+    b = [torch.randn_like(t) for t in a]
+    got = _ext().multi_tensor_dot(a, b, 0.1)
+    expect = sum((x.double() * y.double()).sum() for x, y in zip(a, b)) * 0.1
+    assert abs(float(got) - float(expect)) <= 1e-4 * max(1.0, abs(float(expect)))

@@ -1,0 +1,71 @@
+"""torchrun worker: data-parallel training paths agree across ranks and with each other.
+
+Runs a 4-layer GRAIN+TILLER model for 10 steps per configuration:
+(a) per-layer gradient buckets all-reduced during backward + layer-sharded
+TILLER with deferred weight broadcasts, (b) whole-buffer all-reduce after
+backward + replicated TILLER, (c) = (a) with two micro-batches per step.
+Every configuration must leave bitwise-identical replicas on all ranks; (a)
+and (b) must follow the same loss curve.
+"""
+import os
+import sys
+from types import SimpleNamespace
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from rational_optimizer_b200.models.transformer import CausalTransformer, preset  # noqa: E402
+from rational_optimizer_b200.optim.composite import configure_optimizer  # noqa: E402
+from rational_optimizer_b200.parallel import param_ready  # noqa: E402
+from rational_optimizer_b200.parallel.dist import setup_distributed  # noqa: E402
+from rational_optimizer_b200.parallel.grad_sync import GradientSynchronizer  # noqa: E402
+from rational_optimizer_b200.train.engine import TrainEngine  # noqa: E402
+from rational_optimizer_b200.train.integrity import model_state_sha256  # noqa: E402
+
+
+def run(info, *, overlap, shard, accum):
+    os.environ["RO_TILLER_SHARD"] = "1" if shard else "0"
+    torch.manual_seed(0)
+    args = preset("18l_1024d", layers=4, seq_len=256, activation="grain")
+    model = CausalTransformer(args, 50304).cuda()
+    ns = SimpleNamespace(optimizer="tiller_v1", lr=3e-4, weight_decay=0.1, beta1=0.9, beta2=0.95, eps=1e-8,
+                         muon_momentum=0.95, muon_ns_steps=5, muon_adjust_lr_fn="match_rms_adamw",
+                         grad_accum=accum, layers=4, steps=100)
+    opt = configure_optimizer(model, ns)
+    sync = GradientSynchronizer(model, transport="nccl", overlap=overlap)
+    assert sync.transport == ("nccl-overlap" if overlap else "nccl")
+    eng = TrainEngine(model, opt, grad_clip=1.0, grad_accum=accum, synchronizer=sync)
+    gen = torch.Generator().manual_seed(100 + info.rank)
+    losses = []
+    for _ in range(10):
+        batches = []
+        for _ in range(accum):
+            x = torch.randint(0, 50304, (4 // accum, 257), generator=gen).cuda()
+            batches.append((x[:, :-1], x[:, 1:]))
+        losses.append(eng.step(batches, lr=3e-4))
+    param_ready.wait_all()
+    torch.cuda.synchronize()
+    return [float(v) for v in losses], model_state_sha256(model)
+
+
+def main():
+    info = setup_distributed(timeout_s=120)
+    a = run(info, overlap=True, shard=True, accum=1)
+    b = run(info, overlap=False, shard=False, accum=1)
+    c = run(info, overlap=True, shard=True, accum=2)
+    digests = [None] * info.world_size
+    dist.all_gather_object(digests, (a[1], b[1], c[1]))
+    if info.rank == 0:
+        for k in range(3):
+            assert len({d[k] for d in digests}) == 1, f"replicas differ in configuration {k}"
+        rel = max(abs(x - y) / abs(y) for x, y in zip(a[0], b[0]))
+        assert rel < 1e-2, (a[0], b[0])
+        print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
