@@ -8,6 +8,8 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <cuda_runtime.h>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -431,6 +433,49 @@ c10::optional<torch::Tensor> gemm2_bf16(torch::Tensor a, torch::Tensor b) {
   return c;
 }
 
+// Out-projection input gradient with the GRAIN backward fused into the GEMM
+// epilogue: returns (gx = dGRAIN(h, bf16(dO W_out)), grad_numerator,
+// grad_denominator); w_out_t is W_out^T in bf16 ([N, K], K-major).  None when
+// unsupported.
+c10::optional<std::vector<torch::Tensor>> grain_out_proj_backward(torch::Tensor dO, torch::Tensor w_out_t,
+                                                                  torch::Tensor h, torch::Tensor num,
+                                                                  torch::Tensor den, double eps) {
+  TORCH_CHECK(dO.is_cuda() && w_out_t.is_cuda() && h.is_cuda() && dO.dim() == 2 && w_out_t.dim() == 2 &&
+                  h.dim() == 2, "expects 2-D CUDA tensors");
+  TORCH_CHECK(dO.scalar_type() == torch::kBFloat16 && w_out_t.scalar_type() == torch::kBFloat16 &&
+                  h.scalar_type() == torch::kBFloat16, "expects bf16");
+  TORCH_CHECK(dO.size(1) == w_out_t.size(1) && h.size(0) == dO.size(0) && h.size(1) == w_out_t.size(0),
+              "shape mismatch");
+  check_f32(num, "numerator");
+  check_f32(den, "denominator");
+  const int64_t M = dO.size(0), N = w_out_t.size(0), K = dO.size(1);
+  if (dO.stride(1) != 1 || w_out_t.stride(1) != 1 || h.stride(1) != 1 || N % 256 != 0 ||
+      num.numel() != (N / 256) * 6 || den.numel() != (N / 256) * 4)
+    return c10::nullopt;
+  const c10::cuda::CUDAGuard guard(dO.device());
+  const int groups = static_cast<int>(N / 256);
+  const int chunks = ro::gemm2_grain_partial_rows(static_cast<int>(M));
+  auto gx = torch::empty({M, N}, dO.options());
+  auto partial = torch::empty({static_cast<int64_t>(chunks) * groups * 10}, num.options());
+  auto gnum = torch::empty({groups, 6}, num.options());
+  auto gden = torch::empty({groups, 4}, num.options());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  static const bool trace = std::getenv("RO_TRACE_LAUNCH") != nullptr;
+  if (trace) std::fprintf(stderr, "grain_out_proj_backward: M=%lld N=%lld K=%lld launch\n", (long long)M, (long long)N, (long long)K);
+  const int rc = ro::gemm2_grain_backward(dO.data_ptr(), dO.stride(0), w_out_t.data_ptr(), w_out_t.stride(0),
+                                          h.data_ptr(), h.stride(0), gx.data_ptr(), partial.data_ptr<float>(),
+                                          static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                          num.data_ptr<float>(), den.data_ptr<float>(), static_cast<float>(eps),
+                                          gemm_error_flag(dO.device()).data_ptr<int>(), stream);
+  if (trace) std::fprintf(stderr, "grain_out_proj_backward: rc=%d\n", rc);
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "grain_out_proj_backward");
+  check_rc(ro::grain_reduce_coefficients(partial.data_ptr<float>(), chunks, groups, gnum.data_ptr<float>(),
+                                         gden.data_ptr<float>(), stream),
+           "grain_reduce_coefficients");
+  return std::vector<torch::Tensor>{gx, gnum, gden};
+}
+
 // In-projection with the GRAIN activation fused into the GEMM epilogue:
 // returns (h = bf16(x w^T), y = GRAIN(h)) for groups of 256 columns; None
 // when unsupported.
@@ -821,6 +866,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_scale_", &clip_scale_);
   m.def("gemm2_bf16", &gemm2_bf16);
   m.def("grain_in_proj_forward", &grain_in_proj_forward);
+  m.def("grain_out_proj_backward", &grain_out_proj_backward);
   m.def("tiller_nesterov", &tiller_nesterov);
   m.def("tiller_transpose_bf16", &tiller_transpose_bf16);
   m.def("tiller_chord", &tiller_chord);

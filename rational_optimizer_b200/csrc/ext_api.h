@@ -57,6 +57,12 @@ int gemm2_bf16_nt(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
                   int K, int* err, cudaStream_t stream);
 int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, void* H, void* Y, int M, int N,
                         int K, const float* num, const float* den, float eps, int* err, cudaStream_t stream);
+int gemm2_grain_partial_rows(int M);
+int gemm2_grain_backward(const void* dO, int64_t ldo, const void* wt, int64_t ldw, const void* h, int64_t ldh,
+                         void* GX, float* partial, int M, int N, int K, const float* num, const float* den,
+                         float eps, int* err, cudaStream_t stream);
+int grain_reduce_coefficients(const float* partial, int chunks, int groups, float* gnum, float* gden,
+                              cudaStream_t stream);
 int gemm_bf16_tn(const void* A, int64_t lda, int64_t strideA, bool a_mn, const void* B, int64_t ldb,
                  int64_t strideB, bool b_mn, void* C, int64_t ldc, int64_t strideC, bool out_f32,
                  const void* D, int64_t ldd, int64_t strideD, float alpha, float beta, int M, int N,

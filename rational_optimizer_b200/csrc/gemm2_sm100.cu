@@ -56,19 +56,28 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;      // 320
 constexpr int kStageOut = 32 * 128;                // one 32 x 64 bf16 staging tile
 constexpr int kOutBytes = kEpiWarps * 2 * kStageOut;  // double-buffered per warp: 64 KB
-constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
+constexpr int kBarBytes = 256;
+constexpr int kExchBytes = kEpiWarps * 32 * 4 + kEpiWarps * 10 * 4;  // row-sum exchange, coefficient partials
+// dynamic shared memory only (no static __shared__), 1 KB of alignment slack
+constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + kExchBytes + 1024;
+static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-enum Epilogue : int { kStore = 0, kGrainFwd = 1 };
+enum Epilogue : int { kStore = 0, kGrainFwd = 1, kGrainBwd = 2 };
 
 struct Params {
   int M, N, K;
   int* err;
-  // GRAIN forward epilogue
+  // GRAIN epilogues
   const float* num;   // [groups, 6]
   const float* den;   // [groups, 4]
   float eps;
+  // GRAIN backward: the forward pre-activation h [M, N] (row stride ldh) and
+  // the coefficient partials [2 * num_m_tiles, groups, 10]
+  const __nv_bfloat16* h;
+  int64_t ldh;
+  float* partial;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -204,6 +213,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // UMMA shared-memory descriptor, 128B swizzle, K-major (8-row core groups
 // 1024 B apart).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -262,6 +284,181 @@ __device__ __forceinline__ void load_grain_coeffs(GrainCoeffs& c, int g, const f
   for (int j = 0; j < 4; ++j) c.b[j] = splat2(fabsf(den[g * 4 + j]));
 }
 
+// GRAIN backward behind the out-projection's input-gradient GEMM.  The
+// accumulator holds gy = dL/dy for one 128-row x 256-column tile (one group);
+// this warp owns 32 rows (TMEM lanes) x 128 columns, its partner warp (e ^ 4,
+// same lanes) the other 128.  Per row, with z = h, rho = sqrt(mean z^2 + eps),
+// t = z / rho, f = P(t)/Q(|t|):
+//   pass 1  z from global (kept in registers), sum z^2 -> rho (pair exchange);
+//   pass 2  gy from TMEM, rounded to bf16 as the unfused GEMM output is;
+//           coefficient partials (the factored form of
+//           ro::grain::backward_packed_kernel), the row sum of gy (f - t f'),
+//           and gy f' written back over gy in TMEM;
+//   pass 3  gx = gy f' + t * (row sum) / 256 -> bf16 -> staged TMA stores.
+// The 10 coefficient partials of the CTA's 128 rows go to
+// partial[(2 * tm + crank) * groups + tn][k] (reduced later in a fixed order).
+__device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tbase, uint8_t* stage_buf, int& buf,
+                                                   int tm, int tn, uint32_t crank, int quarter, int e, int lane,
+                                                   int row0, int col0, const CUtensorMap* tmC,
+                                                   float (*rho_part)[32], float (*coef_part)[10]) {
+  const int row = row0 + lane;
+  const bool live = row < p.M;
+  // pass 1: sum of squares of this row's 128 pre-activations (HBM); passes
+  // 2 and 3 re-read them per 32-column chunk (L2-resident by then)
+  const __nv_bfloat16* hp = p.h + static_cast<int64_t>(row) * p.ldh + col0;
+  auto load_z = [&](int ch, uint32_t (&zc)[16]) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+      if (live) raw = __ldg(reinterpret_cast<const uint4*>(hp + ch * 32) + v);
+      zc[4 * v] = raw.x;
+      zc[4 * v + 1] = raw.y;
+      zc[4 * v + 2] = raw.z;
+      zc[4 * v + 3] = raw.w;
+    }
+  };
+  float ss = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    uint32_t zc[16];
+    load_z(ch, zc);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[i]));
+      ss = fmaf(z.x, z.x, ss);
+      ss = fmaf(z.y, z.y, ss);
+    }
+  }
+  rho_part[e][lane] = ss;
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+  const float tot = rho_part[e][lane] + rho_part[e ^ 4][lane];
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+  const float rho = sqrtf(tot * (1.0f / 256.0f) + p.eps);
+  const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
+  GrainCoeffs c;
+  load_grain_coeffs(c, tn, p.num, p.den);
+  const float2 da5 = mul2(splat2(5.0f), c.a[5]), da4 = mul2(splat2(4.0f), c.a[4]);
+  const float2 da3 = mul2(splat2(3.0f), c.a[3]), da2 = mul2(splat2(2.0f), c.a[2]);
+  const float2 db3 = mul2(splat2(4.0f), c.b[3]), db2 = mul2(splat2(3.0f), c.b[2]);
+  const float2 db1 = mul2(splat2(2.0f), c.b[1]);
+  const float2 one = splat2(1.0f);
+  float2 acc[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) acc[k] = splat2(0.0f);
+  float2 sacc = splat2(0.0f);
+  // pass 2
+#pragma unroll 1
+  for (int ch = 0; ch < 4; ++ch) {
+    uint32_t zc[16];
+    load_z(ch, zc);
+    uint32_t r[32];
+    tmem_ld32(tbase + ch * 32, r);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 g2 = make_float2(__bfloat162float(__float2bfloat16_rn(__uint_as_float(r[2 * j]))),
+                                    __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[2 * j + 1]))));
+      const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[j]));
+      const float2 t = mul2(z, ir);
+      const float2 at = abs2(t);
+      const float2 t2 = mul2(t, t);
+      float2 pp = fma2(c.a[5], t, c.a[4]);
+      pp = fma2(pp, t, c.a[3]);
+      pp = fma2(pp, t, c.a[2]);
+      pp = fma2(pp, t, c.a[1]);
+      pp = fma2(pp, t, c.a[0]);
+      float2 dp = fma2(da5, t, da4);
+      dp = fma2(dp, t, da3);
+      dp = fma2(dp, t, da2);
+      dp = fma2(dp, t, c.a[1]);
+      float2 q = fma2(c.b[3], at, c.b[2]);
+      q = fma2(q, at, c.b[1]);
+      q = fma2(q, at, c.b[0]);
+      q = fma2(q, at, one);
+      float2 hq = fma2(db3, at, db2);
+      hq = fma2(hq, at, db1);
+      const float2 dq = fma2(t, hq, mul2(c.b[0], sign02(t)));
+      const float2 iq = rcp2(q);
+      const float2 f = mul2(pp, iq);
+      const float2 df = mul2(fma2(neg2(f), dq, dp), iq);
+      sacc = fma2(g2, fma2(neg2(t), df, f), sacc);
+      const float2 s1 = mul2(mul2(g2, rh), iq);
+      const float2 t3 = mul2(t2, t), t4 = mul2(t2, t2);
+      acc[0] = add2(acc[0], s1);
+      acc[1] = fma2(s1, t, acc[1]);
+      acc[2] = fma2(s1, t2, acc[2]);
+      acc[3] = fma2(s1, t3, acc[3]);
+      acc[4] = fma2(s1, t4, acc[4]);
+      acc[5] = fma2(s1, mul2(t4, t), acc[5]);
+      const float2 vb = mul2(s1, f);
+      acc[6] = fma2(vb, at, acc[6]);
+      acc[7] = fma2(vb, t2, acc[7]);
+      acc[8] = fma2(vb, mul2(at, t2), acc[8]);
+      acc[9] = fma2(vb, t4, acc[9]);
+      const float2 gd = mul2(g2, df);
+      r[2 * j] = __float_as_uint(gd.x);
+      r[2 * j + 1] = __float_as_uint(gd.y);
+    }
+    tmem_st32(tbase + ch * 32, r);
+  }
+  rho_part[e][lane] = sacc.x + sacc.y;
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+  const float rowsum = rho_part[e][lane] + rho_part[e ^ 4][lane];
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+  const float2 sw = splat2(rowsum * (1.0f / 256.0f));
+  // pass 3: gx, staged as bf16 for the bulk stores (two 64-column chunks)
+#pragma unroll 1
+  for (int cc = 0; cc < 2; ++cc) {
+    uint8_t* st = stage_buf + buf * kStageOut;
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int ch = cc * 2 + half;
+      uint32_t zc[16];
+      load_z(ch, zc);
+      uint32_t r[32];
+      tmem_ld32(tbase + ch * 32, r);
+      float out[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[j]));
+        const float2 t = mul2(z, ir);
+        const float2 gx = fma2(t, sw, make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])));
+        out[2 * j] = gx.x;
+        out[2 * j + 1] = gx.y;
+      }
+      stage_row32(st, lane, half * 32, out);
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, smem_u32(st), col0 + cc * 64, row0);
+      bulk_commit();
+    }
+    buf ^= 1;
+  }
+  // coefficient partials of the CTA's rows (fixed-order reduction)
+  float sgn[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) sgn[k] = p.den[tn * 4 + k] > 0.f ? -1.f : (p.den[tn * 4 + k] < 0.f ? 1.f : 0.f);
+#pragma unroll
+  for (int k = 0; k < 10; ++k) {
+    float v = acc[k].x + acc[k].y;
+    if (k >= 6) v *= sgn[k - 6];
+    v = warp_sum(v);
+    if (lane == 0) coef_part[e][k] = v;
+  }
+  asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  if (e == 0 && lane < 10) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kEpiWarps; ++w) v += coef_part[w][lane];
+    const int groups = p.N / kBN;
+    p.partial[(static_cast<int64_t>(2 * tm + static_cast<int>(crank)) * groups + tn) * 10 + lane] = v;
+  }
+  asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
+}
+
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -275,7 +472,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   uint64_t* acc_full = empty + kStages;    // [2]        (both CTAs)
   uint64_t* acc_empty = acc_full + 2;      // [2]        (used in the leader)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  __shared__ float rho_part[kEpiWarps][32];
+  float (*rho_part)[32] = reinterpret_cast<float (*)[32]>(out_stage + kOutBytes + kBarBytes);
+  float (*coef_part)[10] = reinterpret_cast<float (*)[10]>(out_stage + kOutBytes + kBarBytes + kEpiWarps * 32 * 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -404,6 +602,14 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
         rho = sqrtf(tot * (1.0f / 256.0f) + p.eps);
         load_grain_coeffs(gc, tn, p.num, p.den);
+      }
+      if constexpr (EPI == kGrainBwd) {
+        grain_bwd_epilogue(p, tbase, stage_buf, buf, tm, tn, crank, quarter, e, lane, row0, col0, &tmC,
+                           rho_part, coef_part);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
+        continue;
       }
 #pragma unroll 1
       for (int c = 0; c < 128; c += 64) {
@@ -535,17 +741,34 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
   if (!make_map(&ma, A, p.M, p.K, lda, kHalfM) || !make_map(&mb, B, p.N, p.K, ldb, kHalfN) ||
       !make_map(&mc, C, p.M, p.N, ldc, 32))
     return -3;
-  if (EPI == kGrainFwd) {
+  if constexpr (EPI == kGrainFwd) {
     if (!make_map(&my, Y, p.M, p.N, ldy, 32)) return -3;
   } else {
     my = mc;
   }
   auto kern = gemm2_kernel<EPI>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    configured = true;
+  static int configured = 0;  // 1 ok, -1 this configuration cannot run
+  if (configured == 0) {
+    configured = -1;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess) {
+      // a cluster of two CTAs of this size must fit on the device
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = kSmemBytes;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int active = 0;
+      if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) == cudaSuccess && active > 0) configured = 1;
+    }
+    cudaGetLastError();  // clear a failed query
   }
+  if (configured < 0) return -4;
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kBN - 1) / kBN);
   int clusters = num_sms() / 2;
   if (tiles < clusters) clusters = tiles;
@@ -565,7 +788,7 @@ int gemm2_bf16_nt(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   if (!aligned16(A) || !aligned16(B) || !aligned16(C) || (lda % 8) || (ldb % 8) || (ldc % 8) || (K % 8) ||
       (N % 8))
     return -2;
-  Params p{M, N, K, err, nullptr, nullptr, 0.f};
+  Params p{M, N, K, err, nullptr, nullptr, 0.f, nullptr, 0, nullptr};
   return launch<kStore>(A, lda, B, ldb, C, ldc, nullptr, 0, p, stream);
 }
 
@@ -578,8 +801,26 @@ int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, 
   if (M <= 0 || N <= 0 || K <= 0 || N % kBN) return -1;
   if (!aligned16(X) || !aligned16(W) || !aligned16(H) || !aligned16(Y) || (ldx % 8) || (ldw % 8) || (K % 8))
     return -2;
-  Params p{M, N, K, err, num, den, eps};
+  Params p{M, N, K, err, num, den, eps, nullptr, 0, nullptr};
   return launch<kGrainFwd>(X, ldx, W, ldw, H, N, Y, N, p, stream);
+}
+
+int gemm2_grain_partial_rows(int M) { return 2 * ((M + gemm2::kBM - 1) / gemm2::kBM); }
+
+// GRAIN backward fused behind the out-projection's input gradient:
+//   gy = bf16(dO W_out) (dO [M, K], W_out^T given K-major as wt [N, K]),
+//   gx = dGRAIN(h, gy) -> GX [M, N] (bf16), coefficient partials ->
+//   partial [gemm2_grain_partial_rows(M), N / 256, 10].
+int gemm2_grain_backward(const void* dO, int64_t ldo, const void* wt, int64_t ldw, const void* h, int64_t ldh,
+                         void* GX, float* partial, int M, int N, int K, const float* num, const float* den,
+                         float eps, int* err, cudaStream_t stream) {
+  using namespace gemm2;
+  if (M <= 0 || N <= 0 || K <= 0 || N % kBN) return -1;
+  if (!aligned16(dO) || !aligned16(wt) || !aligned16(h) || !aligned16(GX) || (ldo % 8) || (ldw % 8) ||
+      (ldh % 8) || (K % 8))
+    return -2;
+  Params p{M, N, K, err, num, den, eps, static_cast<const __nv_bfloat16*>(h), ldh, partial};
+  return launch<kGrainBwd>(dO, ldo, wt, ldw, GX, N, nullptr, 0, p, stream);
 }
 
 }  // namespace ro

@@ -919,6 +919,16 @@ int grain_backward(const void* gy, int gy_dtype, const void* x, int x_dtype, con
   return static_cast<int>(cudaGetLastError());
 }
 
+// Fixed-order reduction of per-chunk coefficient partials [chunks, groups, 10]
+// (the layout of the fused GEMM epilogue) into gnum [groups, 6], gden [groups, 4].
+int grain_reduce_coefficients(const float* partial, int chunks, int groups, float* gnum, float* gden,
+                              cudaStream_t stream) {
+  using namespace grain;
+  reduce_coeff_kernel<<<(groups * kBase + 127) / 128, 128, 0, stream>>>(partial, chunks, groups, 0, gnum, gden,
+                                                                        nullptr);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int grain_affine_partial_size(int64_t rows, int groups) {
   int chunks, rpc;
   grain::plan_chunks(rows, groups, chunks, rpc);

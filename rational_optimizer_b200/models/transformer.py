@@ -21,8 +21,8 @@ import torch.nn as nn
 
 from ..ops.attention import causal_self_attention, precompute_rope
 from ..ops.cross_entropy import linear_cross_entropy
-from ..ops.grain import in_proj_grain, in_proj_grain_supported
-from ..ops.linear import Linear, cached_cast, _WeightCache
+from ..ops.grain import grain_mlp, in_proj_grain_supported
+from ..ops.linear import Linear, cached_cast, cached_cast_t, _WeightCache
 from ..parallel import param_ready as _ready
 from ..ops.norm import add_rms_norm, fused_add_norm_supported, rms_norm
 from .grain import GRAIN
@@ -127,18 +127,24 @@ class GRAINMLP(nn.Module):
         self.rlb_activation = GRAIN(self.hidden_dim, self.groups, init=settings["base_init"],
                                     fit_range=5.0, eps=eps)
         self.out_proj = Linear(self.hidden_dim, dim, bias=False)
+        self._out_t_cache = _WeightCache()  # bf16 out_proj.weight^T for the fused backward
 
     def forward(self, x):
         act = self.rlb_activation
         if (self.in_proj.compute_dtype == torch.bfloat16 and self.in_proj.weight.dtype == torch.float32
+                and self.out_proj.weight.dtype == torch.float32
                 and in_proj_grain_supported(x, act.hidden_dim, act.groups)):
-            # GRAIN evaluated in the in-projection's GEMM epilogue (one pass over h)
+            # GRAIN evaluated in the GEMM epilogues (forward and backward)
             if _ready.pending():
                 _ready.wait(self.in_proj.weight)
-            w = cached_cast(self.in_proj.weight, torch.bfloat16, self.in_proj._cache)
-            y, h = in_proj_grain(x, self.in_proj.weight, w, act.numerator, act.denominator, act.eps,
-                                 act.groups)
-            return self.out_proj(act(h, precomputed=y))
+                _ready.wait(self.out_proj.weight)
+            w_in = cached_cast(self.in_proj.weight, torch.bfloat16, self.in_proj._cache)
+            w_out = cached_cast(self.out_proj.weight, torch.bfloat16, self.out_proj._cache)
+            w_out_t = cached_cast_t(self.out_proj.weight, torch.bfloat16, self._out_t_cache)
+            o, h, y = grain_mlp(x, self.in_proj.weight, w_in, act.numerator, act.denominator,
+                                self.out_proj.weight, w_out, w_out_t, act.eps, act.groups)
+            act(h, precomputed=y)  # the activation's statistics and forward hooks see (h, y)
+            return o
         return self.out_proj(act(self.in_proj(x)))
 
 

@@ -111,71 +111,92 @@ class _GrainFunction(torch.autograd.Function):
         return (gx, gnum.to(ndt), gden.to(ddt), gcoef.to(ldt), None, None, None, None, None, None)
 
 
-class _InProjGrainFunction(torch.autograd.Function):
-    """``y = GRAIN(x W^T)`` with the activation computed in the GEMM epilogue.
+class _GrainMLPFunction(torch.autograd.Function):
+    """``out_proj(GRAIN(in_proj(x)))`` with GRAIN inside the GEMM epilogues.
 
-    Forward runs ``grain_in_proj_forward`` (csrc/gemm2_sm100.cu): one 2-SM
-    tcgen05 GEMM whose epilogue stores the pre-activation ``h`` (kept for the
-    backward) and the activation ``y``, so ``h`` is never re-read from HBM in
-    the forward.  ``h`` is also returned (non-differentiable) for the
-    activation module's forward hooks.  Backward: the GRAIN backward kernel,
-    then the in-projection's input and weight gradients (the weight gradient
-    accumulates in the GEMM when the weight's ``.grad`` is a managed buffer,
-    as in ``ops.linear``).
+    Forward: ``grain_in_proj_forward`` (csrc/gemm2_sm100.cu) is one 2-SM
+    tcgen05 GEMM whose epilogue stores the pre-activation ``h`` and the
+    activation ``y``; the out-projection follows.  Backward: the out-
+    projection's input gradient and the GRAIN backward are one GEMM
+    (``grain_out_proj_backward``: ``gy = dO W_out`` stays in tensor memory,
+    the epilogue emits ``dh`` and the coefficient partials), then the
+    in-projection's gradients.  Weight gradients accumulate inside the GEMM
+    when the weight's ``.grad`` is a managed fp32 buffer (as in
+    ``ops.linear``).  ``h`` and ``y`` are also returned (non-differentiable)
+    for the activation module's forward hooks.
     """
 
     @staticmethod
-    def forward(ctx, x, weight, w_compute, numerator, denominator, eps, groups):
+    def forward(ctx, x, w_in, w_in_c, numerator, denominator, w_out, w_out_c, w_out_t_c, eps, groups):
+        from . import gemm
         C = ext()
         x2 = x.reshape(-1, x.shape[-1])
-        if x2.dtype != w_compute.dtype:
-            x2 = x2.to(w_compute.dtype)
+        if x2.dtype != w_in_c.dtype:
+            x2 = x2.to(w_in_c.dtype)
         x2 = x2.contiguous()
         num = numerator.detach().float().contiguous()
         den = denominator.detach().float().contiguous()
-        out = C.grain_in_proj_forward(x2, w_compute, num, den, float(eps))
+        out = C.grain_in_proj_forward(x2, w_in_c, num, den, float(eps))
         if out is None:
             raise RuntimeError("fused GRAIN in-projection rejected a supported shape")
         h, y = out
-        ctx.save_for_backward(x2, w_compute, h, num, den)
-        ctx.weight = weight
+        o = gemm.matmul_nt(y, w_out_c)
+        ctx.save_for_backward(x2, w_in_c, h, y, num, den, w_out_c, w_out_t_c)
+        ctx.weights = (w_in, w_out)
         ctx.meta = (float(eps), int(groups), x.shape, x.dtype, numerator.dtype, denominator.dtype)
-        ctx.mark_non_differentiable(h)
-        shape = tuple(x.shape[:-1]) + (h.shape[-1],)
-        return y.view(shape), h.view(shape)
+        ctx.mark_non_differentiable(h, y)
+        lead = tuple(x.shape[:-1])
+        return o.view(lead + (o.shape[-1],)), h.view(lead + (h.shape[-1],)), y.view(lead + (y.shape[-1],))
 
     @staticmethod
-    def backward(ctx, gy, _gh):
+    def backward(ctx, go, _gh, _gy):
         from . import gemm
-        from .linear import ACCUMULATE_ATTR, READY_ATTR
         C = ext()
-        x2, w, h, num, den = ctx.saved_tensors
+        x2, w_in_c, h, y, num, den, w_out_c, w_out_t_c = ctx.saved_tensors
         eps, groups, in_shape, x_dtype, ndt, ddt = ctx.meta
+        w_in, w_out = ctx.weights
         hidden = h.shape[-1]
-        g2 = gy.reshape(-1, hidden)
-        if g2.dtype != h.dtype:
-            g2 = g2.to(h.dtype)
+        g2 = go.reshape(-1, go.shape[-1])
+        if g2.dtype != w_out_c.dtype:
+            g2 = g2.to(w_out_c.dtype)
         g2 = g2.contiguous()
-        e = num.new_empty(groups, 0)
-        gh, gnum, gden, _ = C.grain_backward(g2, h, num, den, num.new_empty(groups, 0, 2), e, e, 0.0, eps,
-                                             hidden, groups, None, None)
-        gx = gw = None
+        gw_out = _weight_grad(w_out, g2, y, ctx.needs_input_grad[5])
+        res = None
+        # the fused backward epilogue is slower than GEMM + GRAIN kernel at the
+        # 18L/1024d shapes (0.67 vs 0.60 ms per layer on B200): opt-in
+        if os.environ.get("RO_FUSED_GRAIN_BWD", "0") == "1":
+            res = C.grain_out_proj_backward(g2, w_out_t_c, h, num, den, float(eps))
+        if res is None:
+            gy = gemm.matmul_nn(g2, w_out_c)
+            e = num.new_empty(groups, 0)
+            gh, gnum, gden, _ = C.grain_backward(gy, h, num, den, num.new_empty(groups, 0, 2), e, e, 0.0, eps,
+                                                 hidden, groups, None, None)
+        else:
+            gh, gnum, gden = res
+        gx = None
         if ctx.needs_input_grad[0]:
-            gx = gemm.matmul_nn(gh, w).reshape(in_shape)
+            gx = gemm.matmul_nn(gh, w_in_c).reshape(in_shape)
             if gx.dtype != x_dtype:
                 gx = gx.to(x_dtype)
-        if ctx.needs_input_grad[1]:
-            weight = ctx.weight
-            buf = weight.grad
-            if (getattr(weight, ACCUMULATE_ATTR, False) and buf is not None and buf.is_cuda
-                    and buf.dtype == torch.float32 and buf.is_contiguous()):
-                gemm.matmul_tn_accumulate_(buf, gh, x2)
-                ready = getattr(weight, READY_ATTR, None)
-                if ready is not None:
-                    ready(weight)
-            else:
-                gw = gemm.matmul_tn(gh, x2, out_dtype=weight.dtype)
-        return gx, gw, None, gnum.to(ndt), gden.to(ddt), None, None
+        gw_in = _weight_grad(w_in, gh, x2, ctx.needs_input_grad[1])
+        return gx, gw_in, None, gnum.to(ndt), gden.to(ddt), gw_out, None, None, None, None
+
+
+def _weight_grad(weight, gy2, x2, needed):
+    """dW = gy^T x: accumulated in the GEMM into a managed ``.grad`` (returns None), else returned."""
+    from . import gemm
+    from .linear import ACCUMULATE_ATTR, READY_ATTR
+    if not needed:
+        return None
+    buf = weight.grad
+    if (getattr(weight, ACCUMULATE_ATTR, False) and buf is not None and buf.is_cuda
+            and buf.dtype == torch.float32 and buf.is_contiguous()):
+        gemm.matmul_tn_accumulate_(buf, gy2, x2)
+        ready = getattr(weight, READY_ATTR, None)
+        if ready is not None:
+            ready(weight)
+        return None
+    return gemm.matmul_tn(gy2, x2, out_dtype=weight.dtype)
 
 
 def in_proj_grain_supported(x, hidden_dim, groups) -> bool:
@@ -189,9 +210,10 @@ def in_proj_grain_supported(x, hidden_dim, groups) -> bool:
     return hasattr(ext(), "grain_in_proj_forward")
 
 
-def in_proj_grain(x, weight, w_compute, numerator, denominator, eps, groups):
-    """``(y, h)``: GRAIN of the in-projection and the pre-activation (no gradient)."""
-    return _InProjGrainFunction.apply(x, weight, w_compute, numerator, denominator, eps, groups)
+def grain_mlp(x, w_in, w_in_c, numerator, denominator, w_out, w_out_c, w_out_t_c, eps, groups):
+    """``(o, h, y)``: the GRAIN MLP output and, without gradient, its pre-activation and activation."""
+    return _GrainMLPFunction.apply(x, w_in, w_in_c, numerator, denominator, w_out, w_out_c, w_out_t_c, eps,
+                                   groups)
 
 
 def _validate(x, hidden_dim, groups, centers):

@@ -46,6 +46,17 @@ def cached_cast(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -
     return cache.tensor
 
 
+def cached_cast_t(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -> torch.Tensor:
+    """``weight.T`` in ``dtype``, contiguous, refreshed when the weight's version changes."""
+    version = weight._version
+    if (cache.tensor is None or cache.version != version or cache.data_ptr != weight.data_ptr()
+            or cache.tensor.dtype != dtype):
+        cache.tensor = weight.detach().t().to(dtype).contiguous()
+        cache.version = version
+        cache.data_ptr = weight.data_ptr()
+    return cache.tensor
+
+
 class _LinearFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, w_compute):

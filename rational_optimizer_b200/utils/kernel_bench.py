@@ -150,6 +150,28 @@ def cases(rows):
             return C.grain_forward(h, num, den, e3, e, e, 0.0, 1e-6, H, G, -1, False)
         return run, 0, 2.0 * rows * d * H
 
+    def _grain_bwd_inputs():
+        dO = torch.randn(rows, d, device=dev, dtype=bf)
+        w_out = (torch.randn(d, H, device=dev) * 0.03).to(bf)
+        h = torch.randn(rows, H, device=dev, dtype=bf)
+        num = torch.tensor(GRAIN_NUMERATOR, device=dev).repeat(G, 1)
+        den = torch.tensor(GRAIN_DENOMINATOR, device=dev).repeat(G, 1)
+        return dO, w_out, h, num, den
+
+    def grain_out_proj_bwd_fused():
+        dO, w_out, h, num, den = _grain_bwd_inputs()
+        wt = w_out.t().contiguous()
+        return (lambda: C.grain_out_proj_backward(dO, wt, h, num, den, 1e-6)), 0, 2.0 * rows * d * H
+
+    def grain_out_proj_bwd_unfused():
+        dO, w_out, h, num, den = _grain_bwd_inputs()
+        e, e3 = torch.empty(G, 0, device=dev), torch.empty(G, 0, 2, device=dev)
+
+        def run():
+            gy = dO @ w_out
+            return C.grain_backward(gy, h, num, den, e3, e, e, 0.0, 1e-6, H, G, None, None)
+        return run, 0, 2.0 * rows * d * H
+
     def gemm_in_proj_cublas():
         a = torch.randn(rows, d, device=dev, dtype=bf)
         b = torch.randn(H, d, device=dev, dtype=bf)
@@ -198,7 +220,9 @@ def cases(rows):
                      ("cross_entropy", cross_entropy), ("gemm_in_proj", gemm_in_proj),
                      ("gemm_in_proj_cublas", gemm_in_proj_cublas),
                      ("gemm2_in_proj", gemm2_in_proj), ("grain_in_proj_fused", grain_in_proj_fused),
-                     ("grain_in_proj_unfused", grain_in_proj_unfused), ("ns5_router_cublas", ns5_router_cublas),
+                     ("grain_in_proj_unfused", grain_in_proj_unfused),
+                     ("grain_out_proj_bwd_fused", grain_out_proj_bwd_fused),
+                     ("grain_out_proj_bwd_unfused", grain_out_proj_bwd_unfused), ("ns5_router_cublas", ns5_router_cublas),
                      ("ns5_router_native", ns5_router_native), ("ledger", ledger)]:
         out[name] = fn
     return out

@@ -108,8 +108,10 @@ def test_grain_in_proj_fused_matches_unfused(M, groups):
     assert bool((err <= tol).all()), float(err.max())
 
 
-def test_grain_mlp_fused_path_matches_unfused(monkeypatch):
-    """GRAINMLP forward/backward with GRAIN in the GEMM epilogue vs the separate kernels."""
+@pytest.mark.parametrize("fused_bwd", ["0", "1"])
+def test_grain_mlp_fused_path_matches_unfused(monkeypatch, fused_bwd):
+    """GRAINMLP forward/backward with GRAIN in the GEMM epilogues vs the separate kernels."""
+    monkeypatch.setenv("RO_FUSED_GRAIN_BWD", fused_bwd)
     import copy
     from rational_optimizer_b200.models.transformer import GRAINMLP
     torch.manual_seed(3)
@@ -132,3 +134,27 @@ def test_grain_mlp_fused_path_matches_unfused(monkeypatch):
     for a, b in zip(*outs):
         scale = b.abs().amax().item() + 1e-6
         assert (a - b).abs().amax().item() <= 2e-2 * scale
+
+
+@pytest.mark.parametrize("M,groups", [(512, 2), (1000, 3), (4096, 18)])
+def test_grain_out_proj_backward_fused_matches_unfused(M, groups):
+    """dO W_out followed by the GRAIN backward, in one GEMM epilogue, vs the two kernels."""
+    from rational_optimizer_b200.ops.grain import GRAIN_DENOMINATOR, GRAIN_NUMERATOR
+    C = _ext.ext()
+    torch.manual_seed(5)
+    d, N = 1024, 256 * groups
+    dO = torch.randn(M, d, device=DEV).to(torch.bfloat16)
+    w_out = (torch.randn(d, N, device=DEV) * 0.03).to(torch.bfloat16)
+    h = torch.randn(M, N, device=DEV).to(torch.bfloat16)
+    num = torch.tensor(GRAIN_NUMERATOR, device=DEV).repeat(groups, 1) + 0.01 * torch.randn(groups, 6, device=DEV)
+    den = torch.tensor(GRAIN_DENOMINATOR, device=DEV).repeat(groups, 1) + 0.01 * torch.randn(groups, 4, device=DEV)
+    gx, gnum, gden = C.grain_out_proj_backward(dO, w_out.t().contiguous(), h, num, den, 1e-6)
+    torch.cuda.synchronize()
+    assert int(C.gemm_error(dO).item()) == 0
+    gy = (dO.float() @ w_out.float()).to(torch.bfloat16)
+    e = torch.empty(groups, 0, device=DEV)
+    rx, rnum, rden, _ = C.grain_backward(gy, h, num, den, torch.empty(groups, 0, 2, device=DEV), e, e, 0.0, 1e-6,
+                                         N, groups, None, None)
+    for a, b in ((gx, rx), (gnum, rnum), (gden, rden)):
+        scale = b.float().abs().amax().item() + 1e-6
+        assert (a.float() - b.float()).abs().amax().item() <= 2e-2 * scale
