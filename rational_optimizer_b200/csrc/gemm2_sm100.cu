@@ -48,23 +48,34 @@ constexpr int kBN = 256;         // columns per tile
 constexpr int kBK = 64;          // 64 bf16 = 128 B = one swizzle row
 constexpr int kHalfM = 128;      // rows per CTA
 constexpr int kHalfN = 128;      // B rows staged per CTA
-constexpr int kStages = 5;
+constexpr int kStagesMax = 5;
 constexpr int kABytes = kHalfM * kBK * 2;          // 16 KB
 constexpr int kBBytes = kHalfN * kBK * 2;          // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;     // 32 KB per CTA
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + kEpiWarps * 32;      // 320
 constexpr int kStageOut = 32 * 128;                // one 32 x 64 bf16 staging tile
-constexpr int kOutBytes = kEpiWarps * 2 * kStageOut;  // double-buffered per warp: 64 KB
-constexpr int kBarBytes = 256;
-constexpr int kExchBytes = kEpiWarps * 32 * 4 + kEpiWarps * 10 * 4;  // row-sum exchange, coefficient partials
-// dynamic shared memory only (no static __shared__), 1 KB of alignment slack
-constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + kExchBytes + 1024;
-static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
-constexpr int kTmemCols = 512;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int kOutBytes = 64 * 1024;               // output staging per CTA
+constexpr int kBarBytes = 128;
+constexpr int kMaxEpiWarps = 16;
+constexpr int kExchBytes = kMaxEpiWarps * 32 * 4 + kMaxEpiWarps * 10 * 4;  // row sums, coefficient partials
 
 enum Epilogue : int { kStore = 0, kGrainFwd = 1, kGrainBwd = 2 };
+
+// Per-epilogue shape: the GRAIN backward's epilogue is the heaviest (the
+// whole activation backward runs there), so it gets 16 warps (four per TMEM
+// lane quarter, 64 columns each, one staging tile each) and a 4-stage ring.
+template <int EPI>
+struct Traits {
+  static constexpr int kWarps = EPI == kGrainBwd ? 16 : 8;
+  static constexpr int kThreads = 64 + 32 * kWarps;
+  static constexpr int kSlice = 256 / (kWarps / 4);     // columns per warp
+  static constexpr int kStages = EPI == kGrainBwd ? 4 : kStagesMax;
+  static constexpr int kBuffers = kOutBytes / (kWarps * kStageOut);
+  // dynamic shared memory only (no static __shared__), 1 KB of alignment slack
+  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + kExchBytes + 1024;
+    static_assert(kBuffers >= 1, "staging");
+};
+constexpr int kTmemCols = 512;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 struct Params {
   int M, N, K;
@@ -226,6 +237,27 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // UMMA shared-memory descriptor, 128B swizzle, K-major (8-row core groups
 // 1024 B apart).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -270,6 +302,18 @@ __device__ __forceinline__ void stage_row32(uint8_t* stage, int lane, int c0, co
   }
 }
 
+// 16 values of one row into the swizzled 32 x 64 staging tile at column c0.
+__device__ __forceinline__ void stage_row16(uint8_t* stage, int lane, int c0, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    float w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = v[q * 8 + k];
+    const int chunk = (c0 / 8 + q) ^ (lane & 7);
+    store_vec<__nv_bfloat16, 8>(reinterpret_cast<__nv_bfloat16*>(stage + lane * 128 + chunk * 16), w);
+  }
+}
+
 // GRAIN coefficients of one group, splatted to fp32 pairs.
 struct GrainCoeffs {
   float2 a[6];  // numerator
@@ -285,62 +329,68 @@ __device__ __forceinline__ void load_grain_coeffs(GrainCoeffs& c, int g, const f
 }
 
 // GRAIN backward behind the out-projection's input-gradient GEMM.  The
-// accumulator holds gy = dL/dy for one 128-row x 256-column tile (one group);
-// this warp owns 32 rows (TMEM lanes) x 128 columns, its partner warp (e ^ 4,
-// same lanes) the other 128.  Per row, with z = h, rho = sqrt(mean z^2 + eps),
-// t = z / rho, f = P(t)/Q(|t|):
-//   pass 1  z from global (kept in registers), sum z^2 -> rho (pair exchange);
+// accumulator holds gy = dL/dy for one 128-row x 256-column tile (one group).
+// Sixteen epilogue warps: four per TMEM lane quarter (32 rows), each owning
+// 64 columns; row reductions combine the four slices through shared memory.
+// Per row, with z = h, rho = sqrt(mean z^2 + eps), t = z / rho,
+// f = P(t)/Q(|t|):
+//   pass 1  sum z^2 over the slice (HBM reads; later passes hit L2) -> rho;
 //   pass 2  gy from TMEM, rounded to bf16 as the unfused GEMM output is;
 //           coefficient partials (the factored form of
 //           ro::grain::backward_packed_kernel), the row sum of gy (f - t f'),
 //           and gy f' written back over gy in TMEM;
-//   pass 3  gx = gy f' + t * (row sum) / 256 -> bf16 -> staged TMA stores.
+//   pass 3  gx = gy f' + t * (row sum) / 256 -> bf16 -> one staged TMA store.
 // The 10 coefficient partials of the CTA's 128 rows go to
 // partial[(2 * tm + crank) * groups + tn][k] (reduced later in a fixed order).
-__device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tbase, uint8_t* stage_buf, int& buf,
-                                                   int tm, int tn, uint32_t crank, int quarter, int e, int lane,
-                                                   int row0, int col0, const CUtensorMap* tmC,
-                                                   float (*rho_part)[32], float (*coef_part)[10]) {
+template <int W>
+__device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tbase, uint8_t* stage, int tm, int tn,
+                                                   uint32_t crank, int quarter, int e, int lane, int row0, int col0,
+                                                   const CUtensorMap* tmC, float (*rho_part)[32],
+                                                   float (*coef_part)[10]) {
+  constexpr int kSlices = W / 4;
+  constexpr int kCols = 256 / kSlices;   // 64
+  constexpr int kChunks = kCols / 16;
   const int row = row0 + lane;
   const bool live = row < p.M;
-  // pass 1: sum of squares of this row's 128 pre-activations (HBM); passes
-  // 2 and 3 re-read them per 32-column chunk (L2-resident by then)
+  const int mate0 = e & 3;               // warps mate0 + 4j share these TMEM lanes
   const __nv_bfloat16* hp = p.h + static_cast<int64_t>(row) * p.ldh + col0;
-  auto load_z = [&](int ch, uint32_t (&zc)[16]) {
+  auto load_z = [&](int ch, uint32_t (&zc)[8]) {
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
+    for (int v = 0; v < 2; ++v) {
       uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-      if (live) raw = __ldg(reinterpret_cast<const uint4*>(hp + ch * 32) + v);
+      if (live) raw = __ldg(reinterpret_cast<const uint4*>(hp + ch * 16) + v);
       zc[4 * v] = raw.x;
       zc[4 * v + 1] = raw.y;
       zc[4 * v + 2] = raw.z;
       zc[4 * v + 3] = raw.w;
     }
   };
+  auto quarter_sum = [&](float v) {
+    rho_part[e][lane] = v;
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "n"(32 * kSlices) : "memory");
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < kSlices; ++j) t += rho_part[mate0 + 4 * j][lane];
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "n"(32 * kSlices) : "memory");
+    return t;
+  };
+  // pass 1
   float ss = 0.f;
 #pragma unroll
-  for (int ch = 0; ch < 4; ++ch) {
-    uint32_t zc[16];
+  for (int ch = 0; ch < kChunks; ++ch) {
+    uint32_t zc[8];
     load_z(ch, zc);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[i]));
       ss = fmaf(z.x, z.x, ss);
       ss = fmaf(z.y, z.y, ss);
     }
   }
-  rho_part[e][lane] = ss;
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-  const float tot = rho_part[e][lane] + rho_part[e ^ 4][lane];
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-  const float rho = sqrtf(tot * (1.0f / 256.0f) + p.eps);
+  const float rho = sqrtf(quarter_sum(ss) * (1.0f / 256.0f) + p.eps);
   const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
   GrainCoeffs c;
   load_grain_coeffs(c, tn, p.num, p.den);
-  const float2 da5 = mul2(splat2(5.0f), c.a[5]), da4 = mul2(splat2(4.0f), c.a[4]);
-  const float2 da3 = mul2(splat2(3.0f), c.a[3]), da2 = mul2(splat2(2.0f), c.a[2]);
-  const float2 db3 = mul2(splat2(4.0f), c.b[3]), db2 = mul2(splat2(3.0f), c.b[2]);
-  const float2 db1 = mul2(splat2(2.0f), c.b[1]);
   const float2 one = splat2(1.0f);
   float2 acc[10];
 #pragma unroll
@@ -348,13 +398,13 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
   float2 sacc = splat2(0.0f);
   // pass 2
 #pragma unroll 1
-  for (int ch = 0; ch < 4; ++ch) {
-    uint32_t zc[16];
+  for (int ch = 0; ch < kChunks; ++ch) {
+    uint32_t zc[8];
     load_z(ch, zc);
-    uint32_t r[32];
-    tmem_ld32(tbase + ch * 32, r);
+    uint32_t r[16];
+    tmem_ld16(tbase + ch * 16, r);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 8; ++j) {
       const float2 g2 = make_float2(__bfloat162float(__float2bfloat16_rn(__uint_as_float(r[2 * j]))),
                                     __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[2 * j + 1]))));
       const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[j]));
@@ -366,16 +416,18 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
       pp = fma2(pp, t, c.a[2]);
       pp = fma2(pp, t, c.a[1]);
       pp = fma2(pp, t, c.a[0]);
-      float2 dp = fma2(da5, t, da4);
-      dp = fma2(dp, t, da3);
-      dp = fma2(dp, t, da2);
+      // P'(t) = a1 + t (2 a2 + t (3 a3 + t (4 a4 + 5 a5 t)))
+      float2 dp = fma2(mul2(splat2(5.0f), c.a[5]), t, mul2(splat2(4.0f), c.a[4]));
+      dp = fma2(dp, t, mul2(splat2(3.0f), c.a[3]));
+      dp = fma2(dp, t, mul2(splat2(2.0f), c.a[2]));
       dp = fma2(dp, t, c.a[1]);
       float2 q = fma2(c.b[3], at, c.b[2]);
       q = fma2(q, at, c.b[1]);
       q = fma2(q, at, c.b[0]);
       q = fma2(q, at, one);
-      float2 hq = fma2(db3, at, db2);
-      hq = fma2(hq, at, db1);
+      // dQ/dt = sign0(t)|b0| + t (2|b1| + |t| (3|b2| + 4|b3||t|))
+      float2 hq = fma2(mul2(splat2(4.0f), c.b[3]), at, mul2(splat2(3.0f), c.b[2]));
+      hq = fma2(hq, at, mul2(splat2(2.0f), c.b[1]));
       const float2 dq = fma2(t, hq, mul2(c.b[0], sign02(t)));
       const float2 iq = rcp2(q);
       const float2 f = mul2(pp, iq);
@@ -398,71 +450,64 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
       r[2 * j] = __float_as_uint(gd.x);
       r[2 * j + 1] = __float_as_uint(gd.y);
     }
-    tmem_st32(tbase + ch * 32, r);
+    tmem_st16(tbase + ch * 16, r);
   }
-  rho_part[e][lane] = sacc.x + sacc.y;
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-  const float rowsum = rho_part[e][lane] + rho_part[e ^ 4][lane];
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-  const float2 sw = splat2(rowsum * (1.0f / 256.0f));
-  // pass 3: gx, staged as bf16 for the bulk stores (two 64-column chunks)
+  const float2 sw = splat2(quarter_sum(sacc.x + sacc.y) * (1.0f / 256.0f));
+  // pass 3: gx -> the warp's 32 x 64 staging tile -> one bulk store
+  if (lane == 0) bulk_wait_read<0>();
+  __syncwarp();
 #pragma unroll 1
-  for (int cc = 0; cc < 2; ++cc) {
-    uint8_t* st = stage_buf + buf * kStageOut;
-    if (lane == 0) bulk_wait_read<1>();
-    __syncwarp();
+  for (int ch = 0; ch < kChunks; ++ch) {
+    uint32_t zc[8];
+    load_z(ch, zc);
+    uint32_t r[16];
+    tmem_ld16(tbase + ch * 16, r);
+    float out[16];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int ch = cc * 2 + half;
-      uint32_t zc[16];
-      load_z(ch, zc);
-      uint32_t r[32];
-      tmem_ld32(tbase + ch * 32, r);
-      float out[32];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[j]));
-        const float2 t = mul2(z, ir);
-        const float2 gx = fma2(t, sw, make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])));
-        out[2 * j] = gx.x;
-        out[2 * j + 1] = gx.y;
-      }
-      stage_row32(st, lane, half * 32, out);
+    for (int j = 0; j < 8; ++j) {
+      const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[j]));
+      const float2 t = mul2(z, ir);
+      const float2 gx = fma2(t, sw, make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])));
+      out[2 * j] = gx.x;
+      out[2 * j + 1] = gx.y;
     }
-    fence_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(tmC, smem_u32(st), col0 + cc * 64, row0);
-      bulk_commit();
-    }
-    buf ^= 1;
+    stage_row16(stage, lane, ch * 16, out);
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmC, smem_u32(stage), col0, row0);
+    bulk_commit();
   }
   // coefficient partials of the CTA's rows (fixed-order reduction)
-  float sgn[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) sgn[k] = p.den[tn * 4 + k] > 0.f ? -1.f : (p.den[tn * 4 + k] < 0.f ? 1.f : 0.f);
 #pragma unroll
   for (int k = 0; k < 10; ++k) {
     float v = acc[k].x + acc[k].y;
-    if (k >= 6) v *= sgn[k - 6];
+    if (k >= 6) {
+      const float b = p.den[tn * 4 + (k - 6)];
+      v *= b > 0.f ? -1.f : (b < 0.f ? 1.f : 0.f);
+    }
     v = warp_sum(v);
     if (lane == 0) coef_part[e][k] = v;
   }
-  asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  asm volatile("bar.sync 5, %0;" ::"n"(W * 32) : "memory");
   if (e == 0 && lane < 10) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kEpiWarps; ++w) v += coef_part[w][lane];
+    for (int w = 0; w < W; ++w) v += coef_part[w][lane];
     const int groups = p.N / kBN;
     p.partial[(static_cast<int64_t>(2 * tm + static_cast<int>(crank)) * groups + tn) * 10 + lane] = v;
   }
-  asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  asm volatile("bar.sync 5, %0;" ::"n"(W * 32) : "memory");
 }
 
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Traits<EPI>::kThreads, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
              const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmY, Params p) {
+  constexpr int kStages = Traits<EPI>::kStages;
+  constexpr int kW = Traits<EPI>::kWarps;
+  constexpr int kSlice = Traits<EPI>::kSlice;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* out_stage = smem + kStages * kStageBytes;
@@ -473,7 +518,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   uint64_t* acc_empty = acc_full + 2;      // [2]        (used in the leader)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   float (*rho_part)[32] = reinterpret_cast<float (*)[32]>(out_stage + kOutBytes + kBarBytes);
-  float (*coef_part)[10] = reinterpret_cast<float (*)[10]>(out_stage + kOutBytes + kBarBytes + kEpiWarps * 32 * 4);
+  float (*coef_part)[10] = reinterpret_cast<float (*)[10]>(out_stage + kOutBytes + kBarBytes + kMaxEpiWarps * 32 * 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -493,7 +538,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&acc_full[a]), 1);
-      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * kW);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -561,10 +606,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     }
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
-    const int e = warp - 2;              // 0..7
+    const int e = warp - 2;              // 0 .. kW-1
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, +32)
-    const int chalf = e >> 2;            // column half: [128*chalf, +128)
-    uint8_t* stage_buf = out_stage + e * 2 * kStageOut;
+    const int chalf = e >> 2;            // column slice: [kSlice*chalf, +kSlice)
+    uint8_t* stage_buf = out_stage + e * Traits<EPI>::kBuffers * kStageOut;
     int buf = 0;
     const uint32_t empty_leader = map_to_rank(smem_u32(&acc_empty[0]), 0);
     GrainCoeffs gc;
@@ -578,8 +623,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       if (!mbar_wait(smem_u32(&acc_full[acc]), acc_phase, p.err, 4)) break;
       tc_fence_after();
       const int row0 = tm * kBM + static_cast<int>(crank) * kHalfM + quarter * 32;
-      const int col0 = tn * kBN + chalf * 128;
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN + chalf * 128;
+      const int col0 = tn * kBN + chalf * kSlice;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN + chalf * kSlice;
       float rho = 1.0f;
       if constexpr (EPI == kGrainFwd) {
         // pass 1: sum of squares of bf16(acc) over this warp's 128 columns,
@@ -604,8 +649,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         load_grain_coeffs(gc, tn, p.num, p.den);
       }
       if constexpr (EPI == kGrainBwd) {
-        grain_bwd_epilogue(p, tbase, stage_buf, buf, tm, tn, crank, quarter, e, lane, row0, col0, &tmC,
-                           rho_part, coef_part);
+        grain_bwd_epilogue<kW>(p, tbase, stage_buf, tm, tn, crank, quarter, e, lane, row0, col0, &tmC, rho_part,
+                               coef_part);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
@@ -750,12 +795,13 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
   static int configured = 0;  // 1 ok, -1 this configuration cannot run
   if (configured == 0) {
     configured = -1;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Traits<EPI>::kSmemBytes) ==
+        cudaSuccess) {
       // a cluster of two CTAs of this size must fit on the device
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2, 1, 1);
-      cfg.blockDim = dim3(kThreads, 1, 1);
-      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.blockDim = dim3(Traits<EPI>::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = Traits<EPI>::kSmemBytes;
       cudaLaunchAttribute attr;
       attr.id = cudaLaunchAttributeClusterDimension;
       attr.val.clusterDim.x = 2;
@@ -772,7 +818,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kBN - 1) / kBN);
   int clusters = num_sms() / 2;
   if (tiles < clusters) clusters = tiles;
-  kern<<<2 * clusters, kThreads, kSmemBytes, stream>>>(ma, mb, mc, my, p);
+  kern<<<2 * clusters, Traits<EPI>::kThreads, Traits<EPI>::kSmemBytes, stream>>>(ma, mb, mc, my, p);
   return static_cast<int>(cudaGetLastError());
 }
 

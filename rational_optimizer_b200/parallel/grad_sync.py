@@ -81,6 +81,8 @@ class GradientSynchronizer:
         self.bucket_elems = max(1, bucket_bytes // self.flat.element_size())
         self._armed = False
         self._works = []
+        self._trace = None
+        self._reported = set()
         if self.overlap:
             self._setup_buckets(model)
 
@@ -119,12 +121,18 @@ class GradientSynchronizer:
                 p.register_post_accumulate_grad_hook(self._param_ready)
         self._pending = list(self.bucket_params)
         self._next = len(self.bucket_ranges) - 1
+        # RO_GRAD_TRACE=1 records (bucket, parameter, next bucket to launch) per report
+        self._trace = [] if os.environ.get("RO_GRAD_TRACE") == "1" else None
+        self._names = {id(p): n for n, p in model.named_parameters()}
 
     def begin_backward(self):
         """Arm readiness tracking for the backward pass whose gradients are final."""
         if not self.overlap:
             return
         self._armed = True
+        self._reported = set()
+        if self._trace is not None:
+            self._trace.clear()
         self._pending = list(self.bucket_params)
         self._next = len(self.bucket_ranges) - 1
         self._works = []
@@ -133,8 +141,13 @@ class GradientSynchronizer:
         if not self._armed:
             return
         b = self._bucket_of.get(id(p))
-        if b is None:
+        if b is None or id(p) in self._reported:
+            # a weight whose gradient the GEMM accumulated also passes through
+            # an AccumulateGrad node with no gradient, whose hook reports again
             return
+        self._reported.add(id(p))
+        if self._trace is not None:
+            self._trace.append((b, self._names.get(id(p), "?"), self._next))
         self._pending[b] -= 1
         while self._next >= 0 and self._pending[self._next] <= 0:
             self._launch(self._next)
@@ -176,6 +189,7 @@ class GradientSynchronizer:
                 w.wait()
             self._works = []
             self._armed = False
+            self._reported = set()
             self._pending = list(self.bucket_params)
             self._next = len(self.bucket_ranges) - 1
             return
