@@ -54,9 +54,7 @@ constexpr int kBBytes = kHalfN * kBK * 2;          // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;     // 32 KB per CTA
 constexpr int kStageOut = 32 * 128;                // one 32 x 64 bf16 staging tile
 constexpr int kOutBytes = 64 * 1024;               // output staging per CTA
-constexpr int kBarBytes = 128;
-constexpr int kMaxEpiWarps = 16;
-constexpr int kExchBytes = kMaxEpiWarps * 32 * 4 + kMaxEpiWarps * 10 * 4;  // row sums, coefficient partials
+constexpr int kBarBytes = 256;
 
 enum Epilogue : int { kStore = 0, kGrainFwd = 1, kGrainBwd = 2 };
 
@@ -70,6 +68,7 @@ struct Traits {
   static constexpr int kSlice = 256 / (kWarps / 4);     // columns per warp
   static constexpr int kStages = EPI == kGrainBwd ? 4 : kStagesMax;
   static constexpr int kBuffers = kOutBytes / (kWarps * kStageOut);
+  static constexpr int kExchBytes = kWarps * 32 * 4 + kWarps * 10 * 4;  // row sums, coefficient partials
   // dynamic shared memory only (no static __shared__), 1 KB of alignment slack
   static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + kExchBytes + 1024;
     static_assert(kBuffers >= 1, "staging");
@@ -164,6 +163,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 2-D tiled TMA load into this CTA's shared memory, completion on a local barrier.
+__device__ __forceinline__ void tma_load_2d_local(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
 
@@ -332,14 +341,16 @@ __device__ __forceinline__ void load_grain_coeffs(GrainCoeffs& c, int g, const f
 // accumulator holds gy = dL/dy for one 128-row x 256-column tile (one group).
 // Sixteen epilogue warps: four per TMEM lane quarter (32 rows), each owning
 // 64 columns; row reductions combine the four slices through shared memory.
-// Per row, with z = h, rho = sqrt(mean z^2 + eps), t = z / rho,
+// The warp's 32 x 64 slice of h arrives in its staging tile by TMA (issued one
+// tile ahead).  Per row, with z = h, rho = sqrt(mean z^2 + eps), t = z / rho,
 // f = P(t)/Q(|t|):
-//   pass 1  sum z^2 over the slice (HBM reads; later passes hit L2) -> rho;
+//   pass 1  sum z^2 over the slice -> rho;
 //   pass 2  gy from TMEM, rounded to bf16 as the unfused GEMM output is;
 //           coefficient partials (the factored form of
 //           ro::grain::backward_packed_kernel), the row sum of gy (f - t f'),
 //           and gy f' written back over gy in TMEM;
-//   pass 3  gx = gy f' + t * (row sum) / 256 -> bf16 -> one staged TMA store.
+//   pass 3  gx = gy f' + t * (row sum) / 256 -> bf16, written over z in the
+//           staging tile -> one TMA store.
 // The 10 coefficient partials of the CTA's 128 rows go to
 // partial[(2 * tm + crank) * groups + tn][k] (reduced later in a fixed order).
 template <int W>
@@ -350,15 +361,14 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
   constexpr int kSlices = W / 4;
   constexpr int kCols = 256 / kSlices;   // 64
   constexpr int kChunks = kCols / 16;
-  const int row = row0 + lane;
-  const bool live = row < p.M;
   const int mate0 = e & 3;               // warps mate0 + 4j share these TMEM lanes
-  const __nv_bfloat16* hp = p.h + static_cast<int64_t>(row) * p.ldh + col0;
+  // z (the pre-activation h) arrived in the warp's staging tile by TMA: row
+  // `lane`, 16-byte chunk k of the row at ((k ^ (lane & 7)) * 16)
   auto load_z = [&](int ch, uint32_t (&zc)[8]) {
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
-      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-      if (live) raw = __ldg(reinterpret_cast<const uint4*>(hp + ch * 16) + v);
+      const int chunk = (ch * 2 + v) ^ (lane & 7);
+      const uint4 raw = *reinterpret_cast<const uint4*>(stage + lane * 128 + chunk * 16);
       zc[4 * v] = raw.x;
       zc[4 * v + 1] = raw.y;
       zc[4 * v + 2] = raw.z;
@@ -453,9 +463,7 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
     tmem_st16(tbase + ch * 16, r);
   }
   const float2 sw = splat2(quarter_sum(sacc.x + sacc.y) * (1.0f / 256.0f));
-  // pass 3: gx -> the warp's 32 x 64 staging tile -> one bulk store
-  if (lane == 0) bulk_wait_read<0>();
-  __syncwarp();
+  // pass 3: gx over z in the staging tile (each lane rewrites its own row) -> one bulk store
 #pragma unroll 1
   for (int ch = 0; ch < kChunks; ++ch) {
     uint32_t zc[8];
@@ -516,9 +524,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   uint64_t* empty = bars + kStages;        // [kStages]  (both CTAs)
   uint64_t* acc_full = empty + kStages;    // [2]        (both CTAs)
   uint64_t* acc_empty = acc_full + 2;      // [2]        (used in the leader)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* hbar = acc_empty + 2;         // [kW]       (GRAIN backward: h slice per warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hbar + kW);
   float (*rho_part)[32] = reinterpret_cast<float (*)[32]>(out_stage + kOutBytes + kBarBytes);
-  float (*coef_part)[10] = reinterpret_cast<float (*)[10]>(out_stage + kOutBytes + kBarBytes + kMaxEpiWarps * 32 * 4);
+  float (*coef_part)[10] = reinterpret_cast<float (*)[10]>(out_stage + kOutBytes + kBarBytes + kW * 32 * 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -540,6 +549,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       mbar_init(smem_u32(&acc_full[a]), 1);
       mbar_init(smem_u32(&acc_empty[a]), 2 * kW);
     }
+    for (int w = 0; w < kW; ++w) mbar_init(smem_u32(&hbar[w]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -612,6 +622,22 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     uint8_t* stage_buf = out_stage + e * Traits<EPI>::kBuffers * kStageOut;
     int buf = 0;
     const uint32_t empty_leader = map_to_rank(smem_u32(&acc_empty[0]), 0);
+    // GRAIN backward: TMA the warp's slice of h for a tile into its staging tile
+    auto fetch_h = [&](int tile) {
+      if constexpr (EPI == kGrainBwd) {
+        if (tile < tiles && lane == 0) {
+          int fm, fn;
+          tile_coords(tile, num_m, num_n, fm, fn);
+          bulk_wait_read<0>();  // the previous bulk store has read the tile
+          const uint32_t hb = smem_u32(&hbar[e]);
+          mbar_expect_tx(hb, kStageOut);
+          tma_load_2d_local(smem_u32(stage_buf), &tmY, hb, fn * kBN + chalf * kSlice,
+                            fm * kBM + static_cast<int>(crank) * kHalfM + quarter * 32);
+        }
+        __syncwarp();
+      }
+    };
+    fetch_h(cluster_id);
     GrainCoeffs gc;
     float2 one2 = splat2(1.0f);
     int local = 0;
@@ -649,8 +675,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         load_grain_coeffs(gc, tn, p.num, p.den);
       }
       if constexpr (EPI == kGrainBwd) {
+        if (!mbar_wait(smem_u32(&hbar[e]), local & 1, p.err, 5)) break;
         grain_bwd_epilogue<kW>(p, tbase, stage_buf, tm, tn, crank, quarter, e, lane, row0, col0, &tmC, rho_part,
                                coef_part);
+        fetch_h(tile + num_clusters);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
@@ -786,11 +814,14 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
   if (!make_map(&ma, A, p.M, p.K, lda, kHalfM) || !make_map(&mb, B, p.N, p.K, ldb, kHalfN) ||
       !make_map(&mc, C, p.M, p.N, ldc, 32))
     return -3;
-  if constexpr (EPI == kGrainFwd) {
+  if constexpr (EPI == kGrainBwd) {
+    if (!make_map(&my, p.h, p.M, p.N, p.ldh, 32)) return -3;
+  } else if constexpr (EPI == kGrainFwd) {
     if (!make_map(&my, Y, p.M, p.N, ldy, 32)) return -3;
   } else {
     my = mc;
   }
+  static_assert(Traits<EPI>::kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
   auto kern = gemm2_kernel<EPI>;
   static int configured = 0;  // 1 ok, -1 this configuration cannot run
   if (configured == 0) {

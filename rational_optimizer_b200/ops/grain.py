@@ -162,9 +162,7 @@ class _GrainMLPFunction(torch.autograd.Function):
         g2 = g2.contiguous()
         gw_out = _weight_grad(w_out, g2, y, ctx.needs_input_grad[5])
         res = None
-        # the fused backward epilogue is slower than GEMM + GRAIN kernel at the
-        # 18L/1024d shapes (0.67 vs 0.60 ms per layer on B200): opt-in
-        if os.environ.get("RO_FUSED_GRAIN_BWD", "0") == "1":
+        if os.environ.get("RO_FUSED_GRAIN_BWD", "1") != "0":
             res = C.grain_out_proj_backward(g2, w_out_t_c, h, num, den, float(eps))
         if res is None:
             gy = gemm.matmul_nn(g2, w_out_c)
