@@ -255,9 +255,11 @@ std::vector<torch::Tensor> add_rmsnorm_forward(torch::Tensor x, c10::optional<to
 }
 
 // Returns (dx fp32, ddelta bf16 or undefined, dw).
+// dw_into: the weight's fp32 gradient buffer; when given, dw is added into it
+// (in the reduction kernel) and the returned dw is undefined.
 std::vector<torch::Tensor> add_rmsnorm_backward(torch::Tensor dy, c10::optional<torch::Tensor> dres,
                                                 torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
-                                                bool want_ddelta) {
+                                                bool want_ddelta, c10::optional<torch::Tensor> dw_into) {
   check_cuda(dy, "dy");
   check_f32(x, "x");
   check_f32(w, "weight");
@@ -274,12 +276,19 @@ std::vector<torch::Tensor> add_rmsnorm_backward(torch::Tensor dy, c10::optional<
   auto dx = torch::empty_like(x);
   torch::Tensor dd;
   if (want_ddelta) dd = torch::empty(x.sizes(), x.options().dtype(torch::kBFloat16));
-  auto dw = torch::empty_like(w);
+  torch::Tensor dw;
+  if (dw_into.has_value()) {
+    check_f32(*dw_into, "dw_into");
+    TORCH_CHECK(dw_into->numel() == d, "dw_into size");
+  } else {
+    dw = torch::empty_like(w);
+  }
+  float* dwp = dw_into.has_value() ? dw_into->data_ptr<float>() : dw.data_ptr<float>();
   auto partial = torch::empty({std::max<int64_t>(1, ro::rmsnorm_backward_partial_size(rows, static_cast<int>(d)))},
                               x.options());
   check_rc(ro::add_rmsnorm_backward(dy.data_ptr(), rp, x.data_ptr<float>(), w.data_ptr<float>(),
                                     rstd.data_ptr<float>(), dx.data_ptr<float>(),
-                                    want_ddelta ? dd.data_ptr() : nullptr, dw.data_ptr<float>(),
+                                    want_ddelta ? dd.data_ptr() : nullptr, dwp, dw_into.has_value(),
                                     partial.data_ptr<float>(), rows, static_cast<int>(d),
                                     at::cuda::getCurrentCUDAStream()),
            "add_rmsnorm_backward");
@@ -439,7 +448,9 @@ c10::optional<torch::Tensor> gemm2_bf16(torch::Tensor a, torch::Tensor b) {
 // unsupported.
 c10::optional<std::vector<torch::Tensor>> grain_out_proj_backward(torch::Tensor dO, torch::Tensor w_out_t,
                                                                   torch::Tensor h, torch::Tensor num,
-                                                                  torch::Tensor den, double eps) {
+                                                                  torch::Tensor den, double eps,
+                                                                  c10::optional<torch::Tensor> gnum_into,
+                                                                  c10::optional<torch::Tensor> gden_into) {
   TORCH_CHECK(dO.is_cuda() && w_out_t.is_cuda() && h.is_cuda() && dO.dim() == 2 && w_out_t.dim() == 2 &&
                   h.dim() == 2, "expects 2-D CUDA tensors");
   TORCH_CHECK(dO.scalar_type() == torch::kBFloat16 && w_out_t.scalar_type() == torch::kBFloat16 &&
@@ -457,8 +468,19 @@ c10::optional<std::vector<torch::Tensor>> grain_out_proj_backward(torch::Tensor 
   const int chunks = ro::gemm2_grain_partial_rows(static_cast<int>(M));
   auto gx = torch::empty({M, N}, dO.options());
   auto partial = torch::empty({static_cast<int64_t>(chunks) * groups * 10}, num.options());
-  auto gnum = torch::empty({groups, 6}, num.options());
-  auto gden = torch::empty({groups, 4}, num.options());
+  // gnum_into / gden_into: the coefficients' fp32 gradient buffers; when given
+  // the gradients are added into them and the returned tensors are undefined
+  const bool into = gnum_into.has_value() && gden_into.has_value();
+  if (into) {
+    check_f32(*gnum_into, "gnum_into");
+    check_f32(*gden_into, "gden_into");
+    TORCH_CHECK(gnum_into->numel() == groups * 6 && gden_into->numel() == groups * 4, "gradient buffer sizes");
+  }
+  torch::Tensor gnum, gden;
+  if (!into) {
+    gnum = torch::empty({groups, 6}, num.options());
+    gden = torch::empty({groups, 4}, num.options());
+  }
   auto stream = at::cuda::getCurrentCUDAStream();
   static const bool trace = std::getenv("RO_TRACE_LAUNCH") != nullptr;
   if (trace) std::fprintf(stderr, "grain_out_proj_backward: M=%lld N=%lld K=%lld launch\n", (long long)M, (long long)N, (long long)K);
@@ -470,8 +492,9 @@ c10::optional<std::vector<torch::Tensor>> grain_out_proj_backward(torch::Tensor 
   if (trace) std::fprintf(stderr, "grain_out_proj_backward: rc=%d\n", rc);
   if (rc < 0) return c10::nullopt;
   check_rc(rc, "grain_out_proj_backward");
-  check_rc(ro::grain_reduce_coefficients(partial.data_ptr<float>(), chunks, groups, gnum.data_ptr<float>(),
-                                         gden.data_ptr<float>(), stream),
+  check_rc(ro::grain_reduce_coefficients(partial.data_ptr<float>(), chunks, groups,
+                                         into ? gnum_into->data_ptr<float>() : gnum.data_ptr<float>(),
+                                         into ? gden_into->data_ptr<float>() : gden.data_ptr<float>(), into, stream),
            "grain_reduce_coefficients");
   return std::vector<torch::Tensor>{gx, gnum, gden};
 }
@@ -854,7 +877,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_forward", &rmsnorm_forward);
   m.def("rmsnorm_backward", &rmsnorm_backward);
   m.def("add_rmsnorm_forward", &add_rmsnorm_forward);
-  m.def("add_rmsnorm_backward", &add_rmsnorm_backward);
+  m.def("add_rmsnorm_backward", &add_rmsnorm_backward, py::arg("dy"), py::arg("dres"), py::arg("x"), py::arg("w"),
+        py::arg("rstd"), py::arg("want_ddelta"), py::arg("dw_into") = py::none());
   m.def("rope_qkv_forward", &rope_qkv_forward);
   m.def("rope_qkv_backward", &rope_qkv_backward);
   m.def("cross_entropy_fwd_bwd", &cross_entropy_fwd_bwd);
@@ -866,7 +890,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_scale_", &clip_scale_);
   m.def("gemm2_bf16", &gemm2_bf16);
   m.def("grain_in_proj_forward", &grain_in_proj_forward);
-  m.def("grain_out_proj_backward", &grain_out_proj_backward);
+  m.def("grain_out_proj_backward", &grain_out_proj_backward, py::arg("dO"), py::arg("w_out_t"), py::arg("h"),
+        py::arg("num"), py::arg("den"), py::arg("eps"), py::arg("gnum_into") = py::none(),
+        py::arg("gden_into") = py::none());
   m.def("tiller_nesterov", &tiller_nesterov);
   m.def("tiller_transpose_bf16", &tiller_transpose_bf16);
   m.def("tiller_chord", &tiller_chord);

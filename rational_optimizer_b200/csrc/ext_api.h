@@ -40,7 +40,7 @@ int rmsnorm_backward(const void* dy, const void* x, const float* w, const float*
 int add_rmsnorm_forward(const float* x, const void* delta, const float* w, float* x_new, void* y,
                         float* rstd, int64_t rows, int d, float eps, cudaStream_t stream);
 int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, const float* w,
-                         const float* rstd, float* dx, void* ddelta, float* dw, float* partial,
+                         const float* rstd, float* dx, void* ddelta, float* dw, bool accumulate_dw, float* partial,
                          int64_t rows, int d, cudaStream_t stream);
 int rope_qkv_forward(const void* qkv, const float* cos_t, const float* sin_t, void* q, void* k,
                      void* v, int B, int S, int H, int hd, int dtype, cudaStream_t stream);
@@ -62,7 +62,7 @@ int gemm2_grain_backward(const void* dO, int64_t ldo, const void* wt, int64_t ld
                          void* GX, float* partial, int M, int N, int K, const float* num, const float* den,
                          float eps, int* err, cudaStream_t stream);
 int grain_reduce_coefficients(const float* partial, int chunks, int groups, float* gnum, float* gden,
-                              cudaStream_t stream);
+                              bool accumulate, cudaStream_t stream);
 int gemm_bf16_tn(const void* A, int64_t lda, int64_t strideA, bool a_mn, const void* B, int64_t ldb,
                  int64_t strideB, bool b_mn, void* C, int64_t ldc, int64_t strideC, bool out_f32,
                  const void* D, int64_t ldd, int64_t strideD, float alpha, float beta, int M, int N,

@@ -576,7 +576,7 @@ backward_packed_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
 // tensors (fp64 accumulation; output fp32).
 __global__ void reduce_coeff_kernel(const float* __restrict__ partial, int chunks, int groups,
                                     int nb, float* __restrict__ gnum, float* __restrict__ gden,
-                                    float* __restrict__ gcoeff) {
+                                    float* __restrict__ gcoeff, int accumulate = 0) {
   const int ngrad = kBase + 2 * nb;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= groups * ngrad) return;
@@ -585,9 +585,28 @@ __global__ void reduce_coeff_kernel(const float* __restrict__ partial, int chunk
   double s = 0.0;
   for (int ch = 0; ch < chunks; ++ch) s += partial[(static_cast<int64_t>(ch) * groups + g) * ngrad + k];
   const float v = static_cast<float>(s);
-  if (k < kNum) gnum[g * kNum + k] = v;
-  else if (k < kBase) gden[g * kDen + (k - kNum)] = v;
-  else gcoeff[g * nb * 2 + (k - kBase)] = v;
+  float* out = k < kNum ? gnum + g * kNum + k
+                        : (k < kBase ? gden + g * kDen + (k - kNum) : gcoeff + g * nb * 2 + (k - kBase));
+  *out = accumulate ? *out + v : v;
+}
+
+// The same reduction with one warp per output: lane l adds chunks l, l+32, ...
+// in fp64, then a fixed butterfly combines the lanes (deterministic).
+__global__ void __launch_bounds__(256)
+reduce_coeff_warp_kernel(const float* __restrict__ partial, int chunks, int groups, float* __restrict__ gnum,
+                         float* __restrict__ gden, int accumulate) {
+  const int idx = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (idx >= groups * kBase) return;
+  const int g = idx / kBase, k = idx % kBase;
+  double s = 0.0;
+  for (int ch = lane; ch < chunks; ch += 32) s += partial[(static_cast<int64_t>(ch) * groups + g) * kBase + k];
+  s = warp_sum_d(s);
+  if (lane == 0) {
+    const float v = static_cast<float>(s);
+    float* out = k < kNum ? gnum + g * kNum + k : gden + g * kDen + (k - kNum);
+    *out = accumulate ? *out + v : v;
+  }
 }
 
 // Affine statistics (reference K9, rational_cuda_kernel.cu:491-573): per
@@ -920,12 +939,13 @@ int grain_backward(const void* gy, int gy_dtype, const void* x, int x_dtype, con
 }
 
 // Fixed-order reduction of per-chunk coefficient partials [chunks, groups, 10]
-// (the layout of the fused GEMM epilogue) into gnum [groups, 6], gden [groups, 4].
+// (the layout of the fused GEMM epilogue) into gnum [groups, 6], gden [groups, 4]
+// (added to their contents when `accumulate`).
 int grain_reduce_coefficients(const float* partial, int chunks, int groups, float* gnum, float* gden,
-                              cudaStream_t stream) {
+                              bool accumulate, cudaStream_t stream) {
   using namespace grain;
-  reduce_coeff_kernel<<<(groups * kBase + 127) / 128, 128, 0, stream>>>(partial, chunks, groups, 0, gnum, gden,
-                                                                        nullptr);
+  reduce_coeff_warp_kernel<<<(groups * kBase + 7) / 8, 256, 0, stream>>>(partial, chunks, groups, gnum, gden,
+                                                                         accumulate ? 1 : 0);
   return static_cast<int>(cudaGetLastError());
 }
 

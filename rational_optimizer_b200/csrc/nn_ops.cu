@@ -154,13 +154,26 @@ rmsnorm_bwd_generic(const TO* __restrict__ dy, const T* __restrict__ x, const fl
   }
 }
 
-__global__ void column_reduce_kernel(const float* __restrict__ partial, int blocks, int d,
-                                     float* __restrict__ out, int accumulate) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= d) return;
+// Column sums of partial [blocks, d]: CTA x covers 32 columns with 8 warps;
+// warp w adds rows w, w+8, ... for its lane's column (coalesced 128-byte rows),
+// then the 8 warp sums are added in warp order (fixed order: deterministic).
+__global__ void __launch_bounds__(256)
+column_reduce_kernel(const float* __restrict__ partial, int blocks, int d, float* __restrict__ out,
+                     int accumulate) {
+  __shared__ float red[8][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int b = 0; b < blocks; ++b) s += partial[static_cast<int64_t>(b) * d + col];
-  out[col] = accumulate ? out[col] + s : s;
+  if (col < d)
+    for (int b = warp; b < blocks; b += 8) s += partial[static_cast<int64_t>(b) * d + col];
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && col < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][lane];
+    out[col] = accumulate ? out[col] + t : t;
+  }
 }
 
 
@@ -550,7 +563,7 @@ int rmsnorm_backward(const void* dy, const void* x, const float* w, const float*
     else if (dtype == 0 && out_dtype == 1) go(float{}, __nv_bfloat16{});
     else return -2;
   }
-  column_reduce_kernel<<<ceil_div_i(d, 256), 256, 0, stream>>>(partial, blocks, d, dw, accumulate_dw);
+  column_reduce_kernel<<<ceil_div_i(d, 32), 256, 0, stream>>>(partial, blocks, d, dw, accumulate_dw);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -575,8 +588,8 @@ int add_rmsnorm_forward(const float* x, const void* delta, const float* w, float
 }
 
 int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, const float* w,
-                         const float* rstd, float* dx, void* ddelta, float* dw, float* partial,
-                         int64_t rows, int d, cudaStream_t stream) {
+                         const float* rstd, float* dx, void* ddelta, float* dw, bool accumulate_dw,
+                         float* partial, int64_t rows, int d, cudaStream_t stream) {
   using namespace nn;
   if (d % 256 || d / 256 > 4) return -1;
   int blocks = 0, rpb = 1;
@@ -592,7 +605,7 @@ int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, cons
       default: return -1;
     }
   }
-  column_reduce_kernel<<<ceil_div_i(d, 256), 256, 0, stream>>>(partial, blocks, d, dw, 0);
+  column_reduce_kernel<<<ceil_div_i(d, 32), 256, 0, stream>>>(partial, blocks, d, dw, accumulate_dw ? 1 : 0);
   return static_cast<int>(cudaGetLastError());
 }
 

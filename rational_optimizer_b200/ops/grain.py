@@ -143,8 +143,12 @@ class _GrainMLPFunction(torch.autograd.Function):
         o = gemm.matmul_nt(y, w_out_c)
         ctx.save_for_backward(x2, w_in_c, h, y, num, den, w_out_c, w_out_t_c)
         ctx.weights = (w_in, w_out)
+        ctx.coefs = (numerator, denominator)
         ctx.meta = (float(eps), int(groups), x.shape, x.dtype, numerator.dtype, denominator.dtype)
         ctx.mark_non_differentiable(h, y)
+        # h and y never receive gradients: skip materialising two zero tensors
+        # of the activation's size for them in the backward
+        ctx.set_materialize_grads(False)
         lead = tuple(x.shape[:-1])
         return o.view(lead + (o.shape[-1],)), h.view(lead + (h.shape[-1],)), y.view(lead + (y.shape[-1],))
 
@@ -156,14 +160,25 @@ class _GrainMLPFunction(torch.autograd.Function):
         eps, groups, in_shape, x_dtype, ndt, ddt = ctx.meta
         w_in, w_out = ctx.weights
         hidden = h.shape[-1]
+        if go is None:
+            go = torch.zeros(tuple(in_shape[:-1]) + (w_out_c.shape[0],), device=h.device, dtype=w_out_c.dtype)
         g2 = go.reshape(-1, go.shape[-1])
         if g2.dtype != w_out_c.dtype:
             g2 = g2.to(w_out_c.dtype)
         g2 = g2.contiguous()
         gw_out = _weight_grad(w_out, g2, y, ctx.needs_input_grad[5])
         res = None
+        coef_into = None
         if os.environ.get("RO_FUSED_GRAIN_BWD", "1") != "0":
-            res = C.grain_out_proj_backward(g2, w_out_t_c, h, num, den, float(eps))
+            from .linear import managed_grad
+            gn_buf = managed_grad(ctx.coefs[0]) if ctx.needs_input_grad[3] else None
+            gd_buf = managed_grad(ctx.coefs[1]) if ctx.needs_input_grad[4] else None
+            if gn_buf is not None and gd_buf is not None:
+                coef_into = (gn_buf, gd_buf)
+            res = C.grain_out_proj_backward(g2, w_out_t_c, h, num, den, float(eps),
+                                            *(coef_into if coef_into else (None, None)))
+            if res is None:
+                coef_into = None
         if res is None:
             gy = gemm.matmul_nn(g2, w_out_c)
             e = num.new_empty(groups, 0)
@@ -177,6 +192,12 @@ class _GrainMLPFunction(torch.autograd.Function):
             if gx.dtype != x_dtype:
                 gx = gx.to(x_dtype)
         gw_in = _weight_grad(w_in, gh, x2, ctx.needs_input_grad[1])
+        if coef_into is not None:
+            # coefficient gradients were added into the managed buffers by the reduction
+            from .linear import report_ready
+            report_ready(ctx.coefs[0])
+            report_ready(ctx.coefs[1])
+            return gx, gw_in, None, None, None, gw_out, None, None, None, None
         return gx, gw_in, None, gnum.to(ndt), gden.to(ddt), gw_out, None, None, None, None
 
 

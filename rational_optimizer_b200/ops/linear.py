@@ -25,6 +25,22 @@ ACCUMULATE_ATTR = "_ro_accumulate_grad"
 READY_ATTR = "_ro_grad_ready"
 
 
+def managed_grad(param):
+    """The parameter's fp32 ``.grad`` buffer when kernels may add into it directly, else None."""
+    buf = param.grad
+    if (getattr(param, ACCUMULATE_ATTR, False) and buf is not None and buf.is_cuda
+            and buf.dtype == torch.float32 and buf.is_contiguous()):
+        return buf
+    return None
+
+
+def report_ready(param):
+    """Tell the gradient synchroniser that ``param``'s gradient for this backward is final."""
+    ready = getattr(param, READY_ATTR, None)
+    if ready is not None:
+        ready(param)
+
+
 class _WeightCache:
     __slots__ = ("version", "tensor", "data_ptr")
 
@@ -51,7 +67,9 @@ def cached_cast_t(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache)
     version = weight._version
     if (cache.tensor is None or cache.version != version or cache.data_ptr != weight.data_ptr()
             or cache.tensor.dtype != dtype):
-        cache.tensor = weight.detach().t().to(dtype).contiguous()
+        # one transposing, converting copy (no intermediate)
+        src = weight.detach().t()
+        cache.tensor = torch.empty(src.shape, device=weight.device, dtype=dtype).copy_(src)
         cache.version = version
         cache.data_ptr = weight.data_ptr()
     return cache.tensor

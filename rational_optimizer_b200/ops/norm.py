@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import torch
 
+from .linear import managed_grad, report_ready
 from .._ext import dtype_code, ext
 
 
@@ -44,6 +45,7 @@ class _AddRMSNormFunction(torch.autograd.Function):
         ctx.save_for_backward(x_new, w, rstd)
         ctx.shape = x.shape
         ctx.wdtype = weight.dtype
+        ctx.weight = weight
         return x_new.view(x.shape), y.view(x.shape)
 
     @staticmethod
@@ -53,8 +55,13 @@ class _AddRMSNormFunction(torch.autograd.Function):
         if dy is None:
             dy = torch.zeros(x_new.shape, device=x_new.device, dtype=torch.bfloat16)
         dres = None if dx_new is None else dx_new.reshape(-1, d).float().contiguous()
+        into = managed_grad(ctx.weight) if ctx.needs_input_grad[2] else None
         dx, ddelta, dw = ext().add_rmsnorm_backward(dy.reshape(-1, d).to(torch.bfloat16).contiguous(),
-                                                    dres, x_new, w, rstd, True)
+                                                    dres, x_new, w, rstd, True, into)
+        if into is not None:
+            # the weight gradient was added into the managed buffer by the reduction
+            report_ready(ctx.weight)
+            return dx.view(ctx.shape), ddelta.view(ctx.shape), None, None
         return dx.view(ctx.shape), ddelta.view(ctx.shape), dw.to(ctx.wdtype), None
 
 
