@@ -499,6 +499,32 @@ c10::optional<std::vector<torch::Tensor>> grain_out_proj_backward(torch::Tensor 
   return std::vector<torch::Tensor>{gx, gnum, gden};
 }
 
+// q/k/v projection with RoPE in the GEMM epilogue: x [M, K] . w [3d, K]^T,
+// rotated q and k, returned as one [3, M, d] tensor of token-major planes.
+// None when unsupported.
+c10::optional<torch::Tensor> qkv_rope_forward(torch::Tensor x, torch::Tensor w, torch::Tensor cos_t,
+                                              torch::Tensor sin_t, int64_t seq, int64_t hd) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.dim() == 2 && w.dim() == 2, "expects 2-D CUDA tensors");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16, "expects bf16");
+  TORCH_CHECK(x.size(1) == w.size(1), "inner dimensions differ");
+  check_f32(cos_t, "cos");
+  check_f32(sin_t, "sin");
+  const int64_t N = w.size(0);
+  if (x.stride(1) != 1 || w.stride(1) != 1 || N % 3 || !cos_t.is_contiguous() || !sin_t.is_contiguous() ||
+      cos_t.size(0) < seq || cos_t.size(-1) != hd / 2)
+    return c10::nullopt;
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto out = torch::empty({3, x.size(0), N / 3}, x.options());
+  const int rc = ro::gemm2_qkv_rope(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+                                    static_cast<int>(x.size(0)), static_cast<int>(N), static_cast<int>(x.size(1)),
+                                    cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), static_cast<int>(seq),
+                                    static_cast<int>(hd), gemm_error_flag(x.device()).data_ptr<int>(),
+                                    at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "qkv_rope_forward");
+  return out;
+}
+
 // In-projection with the GRAIN activation fused into the GEMM epilogue:
 // returns (h = bf16(x w^T), y = GRAIN(h)) for groups of 256 columns; None
 // when unsupported.
@@ -890,6 +916,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_scale_", &clip_scale_);
   m.def("gemm2_bf16", &gemm2_bf16);
   m.def("grain_in_proj_forward", &grain_in_proj_forward);
+  m.def("qkv_rope_forward", &qkv_rope_forward);
   m.def("grain_out_proj_backward", &grain_out_proj_backward, py::arg("dO"), py::arg("w_out_t"), py::arg("h"),
         py::arg("num"), py::arg("den"), py::arg("eps"), py::arg("gnum_into") = py::none(),
         py::arg("gden_into") = py::none());

@@ -57,6 +57,8 @@ int gemm2_bf16_nt(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
                   int K, int* err, cudaStream_t stream);
 int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, void* H, void* Y, int M, int N,
                         int K, const float* num, const float* den, float eps, int* err, cudaStream_t stream);
+int gemm2_qkv_rope(const void* X, int64_t ldx, const void* W, int64_t ldw, void* QKV, int M, int N, int K,
+                   const float* cos_t, const float* sin_t, int seq, int hd, int* err, cudaStream_t stream);
 int gemm2_grain_partial_rows(int M);
 int gemm2_grain_backward(const void* dO, int64_t ldo, const void* wt, int64_t ldw, const void* h, int64_t ldh,
                          void* GX, float* partial, int M, int N, int K, const float* num, const float* den,

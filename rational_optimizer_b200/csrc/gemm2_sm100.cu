@@ -56,7 +56,7 @@ constexpr int kStageOut = 32 * 128;                // one 32 x 64 bf16 staging t
 constexpr int kOutBytes = 64 * 1024;               // output staging per CTA
 constexpr int kBarBytes = 256;
 
-enum Epilogue : int { kStore = 0, kGrainFwd = 1, kGrainBwd = 2 };
+enum Epilogue : int { kStore = 0, kGrainFwd = 1, kGrainBwd = 2, kQkvRope = 3 };
 
 // Per-epilogue shape: the GRAIN backward's epilogue is the heaviest (the
 // whole activation backward runs there), so it gets 16 warps (four per TMEM
@@ -88,6 +88,10 @@ struct Params {
   const __nv_bfloat16* h;
   int64_t ldh;
   float* partial;
+  // q/k/v projection with RoPE: fp32 tables [seq, hd/2]; output planes of width N/3
+  const float* cos_t;
+  const float* sin_t;
+  int seq, hd;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -180,6 +184,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -700,12 +710,44 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
 #pragma unroll
           for (int j = 0; j < 32; ++j) hv[1][j] = __uint_as_float(r[j]);
         }
+        int plane = 0, pcol = col0 + c;
+        if constexpr (EPI == kQkvRope) {
+          // plane 0/1/2 = q/k/v; q and k are rotated (interleaved pairs, fp32
+          // tables, applied to the bf16-rounded projection like ro::nn's RoPE kernel)
+          const int width = p.N / 3;
+          plane = (col0 + c) / width;
+          pcol = (col0 + c) - plane * width;
+          if (plane < 2) {
+            const int row = row0 + lane;
+            const int pos = (row < p.M ? row : 0) % p.seq;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int pair0 = ((pcol + hh * 32) % p.hd) / 2;
+              const float4* cp = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * (p.hd / 2) + pair0);
+              const float4* sp = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * (p.hd / 2) + pair0);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 cv = __ldg(cp + q4), sv = __ldg(sp + q4);
+                const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int j = (q4 * 4 + u) * 2;
+                  const float ev = __bfloat162float(__float2bfloat16_rn(hv[hh][j]));
+                  const float ov = __bfloat162float(__float2bfloat16_rn(hv[hh][j + 1]));
+                  hv[hh][j] = ev * cs[u] - ov * sn[u];
+                  hv[hh][j + 1] = ev * sn[u] + ov * cs[u];
+                }
+              }
+            }
+          }
+        }
         stage_row32(st, lane, 0, hv[0]);
         stage_row32(st, lane, 32, hv[1]);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, smem_u32(st), col0 + c, row0);
+          if constexpr (EPI == kQkvRope) tma_store_3d(&tmC, smem_u32(st), pcol, row0, plane);
+          else tma_store_2d(&tmC, smem_u32(st), col0 + c, row0);
           bulk_commit();
         }
         buf ^= 1;
@@ -797,6 +839,20 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D bf16 map over planes of a [planes, rows, cols] tensor (row-major planes);
+// box = {64, 32, 1}, 128B swizzle.
+bool make_map_planes(CUtensorMap* map, const void* base, int64_t planes, int64_t rows, int64_t cols) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * 2), static_cast<cuuint64_t>(rows * cols * 2)};
+  cuuint32_t box[3] = {64u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -811,9 +867,12 @@ template <int EPI>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, void* Y, int64_t ldy,
            const Params& p, cudaStream_t stream) {
   CUtensorMap ma, mb, mc, my;
-  if (!make_map(&ma, A, p.M, p.K, lda, kHalfM) || !make_map(&mb, B, p.N, p.K, ldb, kHalfN) ||
-      !make_map(&mc, C, p.M, p.N, ldc, 32))
-    return -3;
+  if (!make_map(&ma, A, p.M, p.K, lda, kHalfM) || !make_map(&mb, B, p.N, p.K, ldb, kHalfN)) return -3;
+  if constexpr (EPI == kQkvRope) {
+    if (!make_map_planes(&mc, C, 3, p.M, p.N / 3)) return -3;
+  } else {
+    if (!make_map(&mc, C, p.M, p.N, ldc, 32)) return -3;
+  }
   if constexpr (EPI == kGrainBwd) {
     if (!make_map(&my, p.h, p.M, p.N, p.ldh, 32)) return -3;
   } else if constexpr (EPI == kGrainFwd) {
@@ -865,7 +924,7 @@ int gemm2_bf16_nt(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   if (!aligned16(A) || !aligned16(B) || !aligned16(C) || (lda % 8) || (ldb % 8) || (ldc % 8) || (K % 8) ||
       (N % 8))
     return -2;
-  Params p{M, N, K, err, nullptr, nullptr, 0.f, nullptr, 0, nullptr};
+  Params p{M, N, K, err, nullptr, nullptr, 0.f, nullptr, 0, nullptr, nullptr, nullptr, 1, 64};
   return launch<kStore>(A, lda, B, ldb, C, ldc, nullptr, 0, p, stream);
 }
 
@@ -878,7 +937,7 @@ int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, 
   if (M <= 0 || N <= 0 || K <= 0 || N % kBN) return -1;
   if (!aligned16(X) || !aligned16(W) || !aligned16(H) || !aligned16(Y) || (ldx % 8) || (ldw % 8) || (K % 8))
     return -2;
-  Params p{M, N, K, err, num, den, eps, nullptr, 0, nullptr};
+  Params p{M, N, K, err, num, den, eps, nullptr, 0, nullptr, nullptr, nullptr, 1, 64};
   return launch<kGrainFwd>(X, ldx, W, ldw, H, N, Y, N, p, stream);
 }
 
@@ -896,8 +955,23 @@ int gemm2_grain_backward(const void* dO, int64_t ldo, const void* wt, int64_t ld
   if (!aligned16(dO) || !aligned16(wt) || !aligned16(h) || !aligned16(GX) || (ldo % 8) || (ldw % 8) ||
       (ldh % 8) || (K % 8))
     return -2;
-  Params p{M, N, K, err, num, den, eps, static_cast<const __nv_bfloat16*>(h), ldh, partial};
+  Params p{M, N, K, err, num, den, eps, static_cast<const __nv_bfloat16*>(h), ldh, partial, nullptr, nullptr,
+           1, 64};
   return launch<kGrainBwd>(dO, ldo, wt, ldw, GX, N, nullptr, 0, p, stream);
+}
+
+// q, k, v = RoPE(bf16(x W_qkv^T)) split into three [M, N/3] planes of QKV
+// (token-major: row = token, columns = heads x head_dim); positions are
+// row % seq; cos/sin fp32 [seq, hd/2].  hd must be a multiple of 32.
+int gemm2_qkv_rope(const void* X, int64_t ldx, const void* W, int64_t ldw, void* QKV, int M, int N, int K,
+                   const float* cos_t, const float* sin_t, int seq, int hd, int* err, cudaStream_t stream) {
+  using namespace gemm2;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 3 || (N / 3) % kBN || hd % 32 || (N / 3) % hd || seq <= 0) return -1;
+  if (!aligned16(X) || !aligned16(W) || !aligned16(QKV) || !aligned16(cos_t) || !aligned16(sin_t) || (ldx % 8) ||
+      (ldw % 8) || (K % 8))
+    return -2;
+  Params p{M, N, K, err, nullptr, nullptr, 0.f, nullptr, 0, nullptr, cos_t, sin_t, seq, hd};
+  return launch<kQkvRope>(X, ldx, W, ldw, QKV, N / 3, nullptr, 0, p, stream);
 }
 
 }  // namespace ro

@@ -70,6 +70,24 @@ __device__ __forceinline__ unsigned long long ledger_clock() {
     if (a.timing != nullptr && threadIdx.x == 0) a.timing[k] = ledger_clock(); \
   } while (0)
 
+__device__ double block_max(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (warp == 0) {
+    t = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = fmax(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
 __device__ double block_sum(double v, double* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = warp_sum_d(v);
@@ -230,14 +248,21 @@ struct ArrowScratch {
 __device__ bool arrowhead_eigh(double* A, double* V, int n, ArrowScratch& S, double* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int ld = n + 1, m = n - 1;
-  // 1. the leading block must be diagonal
+  // 1. the leading block must be diagonal: every off-diagonal entry below 1e-6
+  // of its rows' geometric-mean norm, or below 1e-12 of the largest diagonal
+  // entry (rows of negligible energy carry rounding-level directions whose
+  // relative orthogonality is meaningless; neglecting them changes no output
+  // beyond 1e-12 relative)
+  double dmax = 0.0;
+  for (int i = tid; i < m; i += blockDim.x) dmax = fmax(dmax, fabs(A[i * ld + i]));
+  dmax = block_max(dmax, red);
   double off = 0.0;
   for (int k = tid; k < m * m; k += blockDim.x) {
     const int i = k / m, j = k - i * m;
     if (i == j) continue;
     const double aij = fabs(A[i * ld + j]);
     const double scale = sqrt(fabs(A[i * ld + i]) * fabs(A[j * ld + j]));
-    if (aij > 1e-6 * scale + 1e-300) off = 1.0;
+    if (aij > 1e-6 * scale && aij > 1e-12 * dmax) off = 1.0;
   }
   if (block_sum(off, red) > 0.0) return false;
   // 2. inputs and ranks of d (ascending, ties by index)

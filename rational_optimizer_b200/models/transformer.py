@@ -19,7 +19,7 @@ from types import SimpleNamespace
 import torch
 import torch.nn as nn
 
-from ..ops.attention import causal_self_attention, precompute_rope
+from ..ops.attention import causal_self_attention, fused_qkv_attention, precompute_rope, qkv_rope_supported
 from ..ops.cross_entropy import linear_cross_entropy
 from ..ops.grain import grain_mlp, in_proj_grain_supported
 from ..ops.linear import Linear, cached_cast, cached_cast_t, _WeightCache
@@ -60,6 +60,15 @@ class CausalSelfAttention(nn.Module):
 
     def forward(self, x):
         batch, seq_len, dim = x.shape
+        if (self.qkv.compute_dtype == torch.bfloat16 and self.qkv.weight.dtype == torch.float32
+                and seq_len <= self.rope_cos.shape[-2] and qkv_rope_supported(x, dim, self.head_dim)):
+            # projection + RoPE in one GEMM (rotation in the epilogue)
+            if _ready.pending():
+                _ready.wait(self.qkv.weight)
+            w = cached_cast(self.qkv.weight, torch.bfloat16, self.qkv._cache)
+            y = fused_qkv_attention(x, self.qkv.weight, w, batch, seq_len, self.heads, self.head_dim,
+                                    self.rope_cos[:, :, :seq_len], self.rope_sin[:, :, :seq_len])
+            return self.out(y)
         qkv = self.qkv(x)
         if seq_len > self.rope_cos.shape[-2]:
             raise ValueError("sequence longer than the precomputed RoPE table")

@@ -12,6 +12,7 @@ the ``[B, S, H*hd]`` output needed by the projection is a view, not a copy.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -46,6 +47,65 @@ class _RopeQKV(torch.autograd.Function):
         cos2d, sin2d = ctx.saved_tensors
         dqkv = _ext.ext().rope_qkv_backward(dq, dk, dv, cos2d, sin2d)
         return dqkv, None, None, None, None, None, None
+
+
+class _QKVRopeFunction(torch.autograd.Function):
+    """``q, k, v`` of ``RoPE(x W_qkv^T)`` with the rotation in the GEMM epilogue.
+
+    Forward: ``qkv_rope_forward`` (csrc/gemm2_sm100.cu) writes the rotated q, k
+    and v as three token-major ``[B*S, d]`` planes, returned as ``[B, H, S, hd]``
+    views, so neither the fused projection output nor a separate RoPE pass is
+    materialised.  Backward: the inverse rotation and re-pack
+    (``rope_qkv_backward``), then the projection's input and weight gradients
+    (the weight gradient accumulates in the GEMM into a managed ``.grad``).
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, w_compute, cos2d, sin2d, B, S, H, hd):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != w_compute.dtype:
+            x2 = x2.to(w_compute.dtype)
+        x2 = x2.contiguous()
+        planes = _ext.ext().qkv_rope_forward(x2, w_compute, cos2d, sin2d, S, hd)
+        if planes is None:
+            raise RuntimeError("fused q/k/v projection rejected a supported shape")
+        ctx.save_for_backward(x2, w_compute, cos2d, sin2d)
+        ctx.weight = weight
+        ctx.in_shape = x.shape
+        ctx.x_dtype = x.dtype
+        q, k, v = (planes[i].view(B, S, H, hd).transpose(1, 2) for i in range(3))
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        from . import gemm
+        from .linear import weight_grad
+        x2, w, cos2d, sin2d = ctx.saved_tensors
+        dqkv = _ext.ext().rope_qkv_backward(dq, dk, dv, cos2d, sin2d)
+        gx = None
+        if ctx.needs_input_grad[0]:
+            gx = gemm.matmul_nn(dqkv, w).reshape(ctx.in_shape)
+            if gx.dtype != ctx.x_dtype:
+                gx = gx.to(ctx.x_dtype)
+        gw = weight_grad(ctx.weight, dqkv, x2, ctx.needs_input_grad[1])
+        return gx, gw, None, None, None, None, None, None, None
+
+
+def qkv_rope_supported(x, dim, head_dim) -> bool:
+    if not (x.is_cuda and x.dtype == torch.bfloat16) or not _ext.available():
+        return False
+    if os.environ.get("RO_FUSED_QKV_ROPE", "1") == "0":
+        return False
+    return dim % 256 == 0 and head_dim % 32 == 0 and hasattr(_ext.ext(), "qkv_rope_forward")
+
+
+def fused_qkv_attention(x, weight, w_compute, batch, seq_len, heads, head_dim, rope_cos, rope_sin):
+    """Attention output ``[B, S, H*hd]`` (before the output projection) from the block input."""
+    cos2d = rope_cos.reshape(rope_cos.shape[-2], rope_cos.shape[-1]).float().contiguous()
+    sin2d = rope_sin.reshape(rope_sin.shape[-2], rope_sin.shape[-1]).float().contiguous()
+    q, k, v = _QKVRopeFunction.apply(x, weight, w_compute, cos2d, sin2d, batch, seq_len, heads, head_dim)
+    y = causal_attention_core(q, k, v)
+    return y.transpose(1, 2).reshape(batch, seq_len, heads * head_dim)
 
 
 def _flash():

@@ -16,6 +16,7 @@ import os
 import torch
 
 from .._ext import dtype_code, ext
+from .linear import weight_grad
 
 # SiLU fit of P5/Q4 on [-5, 5] (the published GRAIN initializer; the values
 # must be identical for checkpoints and the parameter-count contract).
@@ -166,7 +167,7 @@ class _GrainMLPFunction(torch.autograd.Function):
         if g2.dtype != w_out_c.dtype:
             g2 = g2.to(w_out_c.dtype)
         g2 = g2.contiguous()
-        gw_out = _weight_grad(w_out, g2, y, ctx.needs_input_grad[5])
+        gw_out = weight_grad(w_out, g2, y, ctx.needs_input_grad[5])
         res = None
         coef_into = None
         if os.environ.get("RO_FUSED_GRAIN_BWD", "1") != "0":
@@ -191,7 +192,7 @@ class _GrainMLPFunction(torch.autograd.Function):
             gx = gemm.matmul_nn(gh, w_in_c).reshape(in_shape)
             if gx.dtype != x_dtype:
                 gx = gx.to(x_dtype)
-        gw_in = _weight_grad(w_in, gh, x2, ctx.needs_input_grad[1])
+        gw_in = weight_grad(w_in, gh, x2, ctx.needs_input_grad[1])
         if coef_into is not None:
             # coefficient gradients were added into the managed buffers by the reduction
             from .linear import report_ready
@@ -199,23 +200,6 @@ class _GrainMLPFunction(torch.autograd.Function):
             report_ready(ctx.coefs[1])
             return gx, gw_in, None, None, None, gw_out, None, None, None, None
         return gx, gw_in, None, gnum.to(ndt), gden.to(ddt), gw_out, None, None, None, None
-
-
-def _weight_grad(weight, gy2, x2, needed):
-    """dW = gy^T x: accumulated in the GEMM into a managed ``.grad`` (returns None), else returned."""
-    from . import gemm
-    from .linear import ACCUMULATE_ATTR, READY_ATTR
-    if not needed:
-        return None
-    buf = weight.grad
-    if (getattr(weight, ACCUMULATE_ATTR, False) and buf is not None and buf.is_cuda
-            and buf.dtype == torch.float32 and buf.is_contiguous()):
-        gemm.matmul_tn_accumulate_(buf, gy2, x2)
-        ready = getattr(weight, READY_ATTR, None)
-        if ready is not None:
-            ready(weight)
-        return None
-    return gemm.matmul_tn(gy2, x2, out_dtype=weight.dtype)
 
 
 def in_proj_grain_supported(x, hidden_dim, groups) -> bool:

@@ -41,6 +41,19 @@ def report_ready(param):
         ready(param)
 
 
+def weight_grad(weight, gy2, x2, needed):
+    """dW = gy^T x: added inside the GEMM into a managed ``.grad`` (reported ready, returns
+    None), else returned for autograd to accumulate."""
+    if not needed:
+        return None
+    buf = managed_grad(weight)
+    if buf is not None:
+        gemm.matmul_tn_accumulate_(buf, gy2, x2)
+        report_ready(weight)
+        return None
+    return gemm.matmul_tn(gy2, x2, out_dtype=weight.dtype)
+
+
 class _WeightCache:
     __slots__ = ("version", "tensor", "data_ptr")
 

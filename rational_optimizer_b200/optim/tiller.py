@@ -732,6 +732,14 @@ class TILLERRouter(torch.optim.Optimizer):
         self._rfd_selection = result
         return result
 
+    @property
+    def _ledger_timing(self):
+        if os.environ.get("RO_LEDGER_TIMING") != "1":
+            return None
+        if not hasattr(self, "ledger_timings"):
+            self.ledger_timings = []
+        return torch.zeros(16, dtype=torch.int64, device=self.pairs[0]["in_weight"].device)
+
     def _fast_ledger_ok(self):
         return (self._use_fused() and not self.strict and not self._capture_telemetry_next_step
                 and hasattr(__import__("rational_optimizer_b200._ext", fromlist=["ext"]).ext(),
@@ -766,12 +774,17 @@ class TILLERRouter(torch.optim.Optimizer):
             if ref.data_ptr() != scal[3].data_ptr():
                 scal[3].copy_(ref.reshape(()))
         dd = None if functional else self._rfd_decay_derivative.reshape(1).float().contiguous()
+        timing = self._ledger_timing
         coef, cand, result = C.tiller_ledger_transaction(
             scores.float().contiguous() if functional else None,
             decay.float().contiguous() if functional else None,
             exact_by_role.float().contiguous(), momentum_by_role.float().contiguous(),
             weights.float().contiguous(), layer_ids.contiguous(), dd, pers, diag, cross, scal, ws,
-            prev_rows, len(self.pairs), float(eta))
+            prev_rows, len(self.pairs), float(eta), timing=timing)
+        if timing is not None:
+            # diagnostics (RO_LEDGER_TIMING=1): phase clock stamps and eigensolver sweeps
+            # (-1: arrowhead path) of every ledger call, kept on the host
+            self.ledger_timings.append(timing.cpu().tolist())
         new_rows = tm.CURRENT_ROWS if prev_rows == 0 else tm.PERSISTENT_ROWS
         anchor["factorized_rfd_persistent_scores"] = pers[:new_rows]
         anchor["factorized_rfd_persistent_total_diagonal"] = diag

@@ -158,3 +158,48 @@ def test_grain_out_proj_backward_fused_matches_unfused(M, groups):
     for a, b in ((gx, rx), (gnum, rnum), (gden, rden)):
         scale = b.float().abs().amax().item() + 1e-6
         assert (a.float() - b.float()).abs().amax().item() <= 2e-2 * scale
+
+
+def test_attention_fused_qkv_rope_matches_unfused(monkeypatch):
+    """q/k/v projection with RoPE in the GEMM epilogue vs projection GEMM + RoPE kernel."""
+    import copy
+    from rational_optimizer_b200.models.transformer import CausalSelfAttention
+    torch.manual_seed(6)
+    base = CausalSelfAttention(1024, 16, 512).cuda()
+    outs = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("RO_FUSED_QKV_ROPE", fused)
+        m = copy.deepcopy(base)
+        x = torch.randn(2, 512, 1024, device=DEV, generator=torch.Generator(DEV).manual_seed(7)).to(
+            torch.bfloat16).requires_grad_(True)
+        y = m(x)
+        (y.float() * torch.linspace(-1, 1, y.shape[-1], device=DEV)).sum().backward()
+        outs.append((y.float(), x.grad.float(), m.qkv.weight.grad.float(), m.out.weight.grad.float()))
+    for a, b in zip(*outs):
+        scale = b.abs().amax().item() + 1e-6
+        assert (a - b).abs().amax().item() <= 2e-2 * scale
+
+
+@pytest.mark.parametrize("M", [512, 1000])
+def test_qkv_rope_forward_matches_reference(M):
+    """Rotated planes equal RoPE applied to the bf16 projection (fp32 tables)."""
+    from rational_optimizer_b200.ops.attention import apply_rope, precompute_rope
+    C = _ext.ext()
+    torch.manual_seed(8)
+    S, d, hd = 500, 1024, 64
+    x = torch.randn(M, d, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(3 * d, d, device=DEV) * 0.03).to(torch.bfloat16)
+    cos, sin = precompute_rope(S, hd)
+    cos2d, sin2d = cos[0, 0].to(DEV).contiguous(), sin[0, 0].to(DEV).contiguous()
+    planes = C.qkv_rope_forward(x, w, cos2d, sin2d, S, hd)
+    torch.cuda.synchronize()
+    assert int(C.gemm_error(x).item()) == 0
+    qkv = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+    pos = torch.arange(M, device=DEV) % S
+    for i in range(3):
+        ref = qkv[:, i * d:(i + 1) * d].view(M, 16, hd)
+        if i < 2:
+            ref = apply_rope(ref, cos2d[pos][:, None, :], sin2d[pos][:, None, :])
+        got = planes[i].float().view(M, 16, hd)
+        scale = ref.abs().amax().item()
+        assert (got - ref).abs().amax().item() <= 1e-2 * scale
