@@ -245,7 +245,8 @@ struct ArrowScratch {
 // false, touching nothing, when the leading block is not diagonal to
 // 1e-6 relative (the caller then runs the Jacobi method).  On success the
 // eigenvalues are on A's diagonal and V holds the eigenvectors (columns).
-__device__ bool arrowhead_eigh(double* A, double* V, int n, ArrowScratch& S, double* red) {
+__device__ bool arrowhead_eigh(double* A, double* V, int n, ArrowScratch& S, double* red,
+                               double* diag = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int ld = n + 1, m = n - 1;
   // 1. the leading block must be diagonal: every off-diagonal entry below 1e-6
@@ -256,14 +257,17 @@ __device__ bool arrowhead_eigh(double* A, double* V, int n, ArrowScratch& S, dou
   double dmax = 0.0;
   for (int i = tid; i < m; i += blockDim.x) dmax = fmax(dmax, fabs(A[i * ld + i]));
   dmax = block_max(dmax, red);
-  double off = 0.0;
+  double off = 0.0, worst = 0.0;
   for (int k = tid; k < m * m; k += blockDim.x) {
     const int i = k / m, j = k - i * m;
     if (i == j) continue;
     const double aij = fabs(A[i * ld + j]);
     const double scale = sqrt(fabs(A[i * ld + i]) * fabs(A[j * ld + j]));
+    if (aij > 1e-12 * dmax) worst = fmax(worst, aij / fmax(scale, 1e-300));
     if (aij > 1e-6 * scale && aij > 1e-12 * dmax) off = 1.0;
   }
+  worst = block_max(worst, red);
+  if (diag != nullptr && threadIdx.x == 0) *diag = worst;
   if (block_sum(off, red) > 0.0) return false;
   // 2. inputs and ranks of d (ascending, ties by index)
   for (int i = tid; i < m; i += blockDim.x) {
@@ -461,6 +465,8 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
   __shared__ double sc[64];             // scalars
   __shared__ double alphas[kKrylov], betas[kKrylov], proj[kKrylov], lam[kKrylov];
   __shared__ ArrowScratch arrow_scratch;
+  __shared__ double sel_last_scale;  // the collapsed surrogate row's sqrt(32) (else 1)
+  __shared__ int sel_last_row;
   const int tid = threadIdx.x;
   const int C = a.C;
   STAMP(0);
@@ -549,6 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     nsel = prev + cur_rows;
     const float sb = static_cast<float>(sqrt(beta2)), sc1 = static_cast<float>(sqrt(1.0 - beta2));
     const double row_scale = collapse ? sqrt(static_cast<double>(kCurRows)) : 1.0;
+    if (tid == 0) {
+      sel_last_scale = row_scale;
+      sel_last_row = collapse ? prev : -1;
+    }
     for (int i = tid; i < prev * C; i += blockDim.x) sel[i] = static_cast<double>(a.pers_scores[i] * sb);
     for (int i = tid; i < cur_rows * C; i += blockDim.x)
       sel[prev * C + i] = static_cast<double>(static_cast<float>(cur[i]) * sc1) * row_scale;
@@ -578,7 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     STAMP(1);
     // surrogate rows over persistent rows from a previous decomposition: the
     // Gram is an arrowhead matrix (orthogonal rows, one new row)
-    const bool arrow = collapse && arrowhead_eigh(A, V, nsel, arrow_scratch, red);
+    double worst_ratio = 0.0;
+    const bool arrow = collapse && arrowhead_eigh(A, V, nsel, arrow_scratch, red, &worst_ratio);
+    if (a.timing != nullptr && tid == 0 && collapse)
+      a.timing[14] = static_cast<unsigned long long>(fmin(worst_ratio, 1.0) * 1e15);
     const int gram_sweeps = arrow ? -1 : jacobi_eigh(A, V, nsel, rp, rq, rc, rs, red, &rotated);
     STAMP(2);
     if (a.timing != nullptr && tid == 0) a.timing[12] = gram_sweeps;
@@ -657,13 +670,32 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
   __syncthreads();
   double prev_beta = 0.0;
   STAMP(4);
+  // The selection rows are fp32 values (the collapsed surrogate row times
+  // sqrt(32)): during the Lanczos iteration they are read from shared memory
+  // as floats (the eigenproblem's A/V space is free here), with the row scale
+  // applied to the row's coefficient, instead of twice per step from global
+  // memory.  Problems too large for shared memory read `sel` as before.
+  float* self = reinterpret_cast<float*>(sm);
+  const bool sel_smem = static_cast<size_t>(nsel) * C * sizeof(float) <= 2ull * kMaxSel * (kMaxSel + 1) * sizeof(double);
+  const int last_row = a.prev_rows == 0 ? -1 : sel_last_row;
+  const double last_scale = a.prev_rows == 0 ? 1.0 : sel_last_scale;
+  if (sel_smem)
+    for (int i2 = tid; i2 < nsel * C; i2 += blockDim.x)
+      self[i2] = static_cast<float>(i2 / C == last_row ? sel[i2] / last_scale : sel[i2]);
+  __syncthreads();
   for (int i = 0; i < steps; ++i) {
     for (int c = tid; c < C; c += blockDim.x) Q[i * C + c] = vec[c];
-    // Lv[r] = sum_c L[r,c] vec[c]
+    // Lv[r] = sum_c L[r,c] vec[c]  (stored times the row scale for the action)
     for (int r = tid >> 5; r < nsel; r += blockDim.x >> 5) {
       double s = 0.0;
-      for (int c = tid & 31; c < C; c += 32) s += sel[r * C + c] * rsw[c] * vec[c];
-      s *= inv_sqrt_m;
+      if (sel_smem) {
+        for (int c = tid & 31; c < C; c += 32) s += static_cast<double>(self[r * C + c]) * rsw[c] * vec[c];
+        const double rs2 = r == last_row ? last_scale * last_scale : 1.0;
+        s *= inv_sqrt_m * rs2;
+      } else {
+        for (int c = tid & 31; c < C; c += 32) s += sel[r * C + c] * rsw[c] * vec[c];
+        s *= inv_sqrt_m;
+      }
       s = warp_sum_d(s);
       if ((tid & 31) == 0) Lv[r] = s;
     }
@@ -672,7 +704,10 @@ __global__ void __launch_bounds__(kThreads, 1) transaction_kernel(Args a) {
     for (int c = tid; c < C; c += blockDim.x) {
       const double rw = rsw[c] * inv_sqrt_m;
       double acc = 0.0;
-      for (int r = 0; r < nsel; ++r) acc += sel[r * C + c] * Lv[r];
+      if (sel_smem)
+        for (int r = 0; r < nsel; ++r) acc += static_cast<double>(self[r * C + c]) * Lv[r];
+      else
+        for (int r = 0; r < nsel; ++r) acc += sel[r * C + c] * Lv[r];
       double s = diag_res / static_cast<double>(a.weights[c]) * vec[c] + acc * rw;
       act[c] = s;
       adot += vec[c] * s;
