@@ -11,6 +11,7 @@ experiments/protocol/method_entrypoint.py:24-171).
 """
 from __future__ import annotations
 
+import os
 import re
 
 import torch
@@ -217,6 +218,11 @@ def build_tiller(model, args, *, decay_tied_embedding=False, microbatches=None,
     if not groups:
         raise RuntimeError("TILLER found no parameters for its AdamW child")
     adamw = FusedAdamW(groups, lr=args.lr, betas=(args.beta1, args.beta2), eps=args.eps)
+    if router._shard()[2] and os.environ.get("RO_TILLER_PACK", "1") != "0":
+        # layer-sharded across ranks: one contiguous buffer per owner so the
+        # updated weights travel in one broadcast per owner
+        from .tiller import OwnerPacking
+        router.packing = OwnerPacking(router, attention)
     return TILLERCompositeOptimizer((router, attention, adamw))
 
 

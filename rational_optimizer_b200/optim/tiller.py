@@ -153,6 +153,59 @@ def sharding_enabled(world: int) -> bool:
     return world > 1 and os.environ.get("RO_TILLER_SHARD", "1") != "0"
 
 
+class OwnerPacking:
+    """TILLER-managed weights re-homed into one fp32 buffer ordered by owner.
+
+    Per layer [in_proj, out_proj, qkv, attention out]; the layers an owner
+    updates are therefore one contiguous range, replicated with one broadcast
+    per owner instead of one per tensor.
+    """
+
+    def __init__(self, router, attention):
+        L = len(router.pairs)
+        per_layer = [[router.pairs[l]["in_weight"], router.pairs[l]["out_weight"],
+                      attention.role_parameters["qkv"][l], attention.role_parameters["attn_out"][l]]
+                     for l in range(L)]
+        device = per_layer[0][0].device
+        total = sum(p.numel() for ps in per_layer for p in ps)
+        self.flat = torch.empty(total, device=device, dtype=torch.float32)
+        self.layer_ranges = []
+        self.layer_params = per_layer
+        off = 0
+        with torch.no_grad():
+            for ps in per_layer:
+                lo = off
+                for p in ps:
+                    n = p.numel()
+                    view = self.flat[off:off + n].view_as(p)
+                    view.copy_(p.data)
+                    p.data = view
+                    off += n
+                self.layer_ranges.append((lo, off))
+        self.layers = L
+        self.world = router.world_size
+        self.group = router.loss_probe_group
+
+    def broadcast(self):
+        """Replicate every owner's updated layers (one deferred broadcast per owner)."""
+        side = param_ready.side_stream(self.flat.device)
+        side.wait_stream(torch.cuda.current_stream(self.flat.device))
+        for r in range(self.world):
+            lo_l, hi_l = shard_bounds(self.layers, r, self.world)
+            if hi_l <= lo_l:
+                continue
+            lo, hi = self.layer_ranges[lo_l][0], self.layer_ranges[hi_l - 1][1]
+            src = dist.get_global_rank(self.group, r) if self.group is not None else r
+            with torch.cuda.stream(side):
+                dist.broadcast(self.flat[lo:hi], src=src, group=self.group)
+                event = torch.cuda.Event()
+                event.record(side)
+            params = [p for l in range(lo_l, hi_l) for p in self.layer_params[l]]
+            param_ready.defer(params, event)
+            for p in params:
+                increment_version(p)
+
+
 def broadcast_owned(tensors_by_layer, layers, world, group=None, *, deferred=False):
     """Replicate per-layer tensors from their owners; bumps autograd versions.
 
@@ -286,6 +339,7 @@ class TILLERRouter(torch.optim.Optimizer):
         self._last_predictive = None
         self._fused_ok = None
         self._fused_role_objs = None
+        self.packing = None  # OwnerPacking when weights are re-homed for owner broadcasts
         self._force_torch = False
         self._ledger_bufs = None
 
@@ -640,7 +694,7 @@ class TILLERRouter(torch.optim.Optimizer):
             def apply(coefficients, lr, wd):
                 for role in roles:
                     roles[role].apply(coefficients[lo:hi], decay=1.0 - lr * wd, lr=lr)
-                if sharded:
+                if sharded and self.packing is None:
                     broadcast_owned([(p["in_weight"], p["out_weight"]) for p in self.pairs], L,
                                     self.world_size, self.loss_probe_group, deferred=True)
 
@@ -1216,7 +1270,7 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
                                              congruence[lo:hi].contiguous(), update, want_selected=False)
                     fr.apply(torch.ones(hi - lo, device=first.device), decay=1.0 - lr * wd, lr=lr)
                     metas.append(tiller_fused.chord_meta(chord))
-                if sharded:
+                if sharded and self.router.packing is None:
                     broadcast_owned([(p,) for p in params], len(params), self.router.world_size,
                                     self.router.loss_probe_group, deferred=True)
                 continue
@@ -1233,6 +1287,8 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
             foreach_apply(params, restore(sel).to(parent.dtype), decay=1.0 - lr * wd,
                           alpha=-lr * adjustment)
         anchor["factorized_adaptive_tangent_updates"] = update
+        if fused and self.router.packing is not None and self.router._shard()[2]:
+            self.router.packing.broadcast()
         if self._capture_telemetry_next_step:
             safe = torch.cat([m["safe"].reshape(-1) for m in metas])
             cosine = torch.cat([m["parent_cosine"].reshape(-1) for m in metas])
