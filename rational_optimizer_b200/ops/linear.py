@@ -63,9 +63,33 @@ class _WeightCache:
         self.data_ptr = 0
 
 
+# While a CUDA graph of the forward/backward is being captured, every cast is
+# recorded into the graph (the weights change between replays), written into
+# the cache's persistent tensor; the graph object keeps those tensors alive.
+_CAPTURE = {"active": False, "keep": []}
+
+
+def capture_casts(active: bool, keep=None):
+    _CAPTURE["active"] = bool(active)
+    _CAPTURE["keep"] = keep if keep is not None else []
+
+
+def _captured_cast(weight, dtype, cache, transpose):
+    src = weight.detach().t() if transpose else weight.detach()
+    if cache.tensor is None or cache.tensor.shape != src.shape or cache.tensor.dtype != dtype:
+        cache.tensor = torch.empty(src.shape, device=weight.device, dtype=dtype)
+    cache.tensor.copy_(src)
+    cache.version = -1  # eager use after capture recasts (and replaces the tensor)
+    cache.data_ptr = weight.data_ptr()
+    _CAPTURE["keep"].append(cache.tensor)
+    return cache.tensor
+
+
 def cached_cast(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -> torch.Tensor:
     if weight.dtype == dtype:
         return weight.detach()
+    if _CAPTURE["active"]:
+        return _captured_cast(weight, dtype, cache, False)
     version = weight._version
     if (cache.tensor is None or cache.version != version or cache.data_ptr != weight.data_ptr()
             or cache.tensor.dtype != dtype):
@@ -77,6 +101,8 @@ def cached_cast(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -
 
 def cached_cast_t(weight: torch.Tensor, dtype: torch.dtype, cache: _WeightCache) -> torch.Tensor:
     """``weight.T`` in ``dtype``, contiguous, refreshed when the weight's version changes."""
+    if _CAPTURE["active"]:
+        return _captured_cast(weight, dtype, cache, True)
     version = weight._version
     if (cache.tensor is None or cache.version != version or cache.data_ptr != weight.data_ptr()
             or cache.tensor.dtype != dtype):

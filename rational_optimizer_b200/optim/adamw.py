@@ -11,6 +11,7 @@ torch implementation runs.
 from __future__ import annotations
 
 import torch
+from torch.autograd.graph import increment_version
 
 from .. import _ext
 
@@ -58,4 +59,8 @@ class FusedAdamW(torch.optim.AdamW):
             beta1, beta2 = group["betas"]
             C.adamw_multi_tensor(ps, gs, ms, vs, float(group["lr"]), float(beta1), float(beta2),
                                  float(group["eps"]), float(group["weight_decay"]), step_value)
+            # the kernel wrote the parameters in place: bump their version counters
+            # so version-keyed caches (the bf16 weight casts) see the update
+            for p in ps:
+                increment_version(p)
         return loss

@@ -161,6 +161,10 @@ class TILLERCompositeOptimizer(CompositeOptimizer):
     def router(self):
         return self.optimizers[0]
 
+    def eager_step_required(self):
+        """True when this step's forward/backward must run eagerly (response-probe refresh)."""
+        return bool(self.router._capture_response_this_transition)
+
     def record_realized_clipping(self, preclip_norm, max_norm):
         self.optimizers[0].record_realized_clipping(preclip_norm, max_norm)
 

@@ -612,7 +612,7 @@ class TILLERRouter(torch.optim.Optimizer):
         the updated weights are broadcast from their owners.
         """
         L = len(self.pairs)
-        if self._use_fused() and sharding_enabled(self.world_size):
+        if sharding_enabled(self.world_size) and self._use_fused():
             rank = dist.get_rank(group=self.loss_probe_group)
             lo, hi = shard_bounds(L, rank, self.world_size)
             return lo, hi, True

@@ -163,6 +163,10 @@ class TillerThenMuonOptimizer:
             raise RuntimeError(f"TILLER-then-Muon missing compatible momentum buffers: {missing[:4]}")
         self._activate_muon_stage()
 
+    def eager_step_required(self):
+        """True when this step's forward/backward must run eagerly (TILLER response-probe refresh)."""
+        return not self._transitioned and bool(self.tiller_router._capture_response_this_transition)
+
     def _activate_muon_stage(self):
         self._transitioned = True
         self.tiller_router.remove_hooks()

@@ -11,10 +11,12 @@ read it (the reference synchronises on ``loss.item()`` every micro-batch).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from ..parallel.grad_sync import GradientSynchronizer
+from .graphs import StepGraph, graphs_requested
 
 
 def learning_rate(step, *, lr, min_lr, warmup_steps, total_steps):
@@ -68,6 +70,44 @@ class TrainEngine:
         if clip_observer is None and hasattr(optimizer, "record_realized_clipping"):
             self.clip_observer = optimizer
         self.last_grad_norm = None
+        self._graph = None
+        self._graph_state = "off" if not graphs_requested() else "pending"
+        self._plain_steps = 0
+
+    def _graph_eligible(self, batches):
+        if self._graph_state in ("off", "failed") or len(batches) != 1:
+            return False
+        if self.sync.world > 1 and os.environ.get("RO_CUDA_GRAPH_DIST", "1") != "1":
+            return False
+        x, y = batches[0]
+        if not x.is_cuda:
+            return False
+        # only optimizers that say which steps need hooks in the forward/backward
+        eager = getattr(self.optimizer, "eager_step_required", None)
+        if eager is None or eager():
+            return False
+        if any(getattr(m, "_rlb_optimizer_track_stats", False) for m in self.model.modules()):
+            return False
+        return self._graph is None or self._graph.matches(x, y)
+
+    def _graphed_forward_backward(self, x, y):
+        """The loss via the captured graph, or None (eager path) when capture is not possible."""
+        if self._graph is None:
+            self._plain_steps += 1
+            if self._plain_steps < 3:  # let lazily-initialised state settle first
+                return None
+            try:
+                g = StepGraph(self.model, self.sync, x, y)
+                g.capture()
+                self._graph = g
+                self._graph_state = "on"
+            except Exception as exc:  # an operation that cannot be captured
+                self._graph_state = "failed"
+                self.graph_error = f"{type(exc).__name__}: {exc}"
+                self.sync.zero_grad()
+                return None
+        self.sync.zero_grad()
+        return self._graph.replay(x, y)
 
     def set_lr(self, lr):
         for group in self.optimizer.param_groups:
@@ -79,6 +119,10 @@ class TrainEngine:
             raise ValueError("expected one batch per micro-step")
         if lr is not None:
             self.set_lr(lr)
+        if self._graph_eligible(batches):
+            loss = self._graphed_forward_backward(*batches[0])
+            if loss is not None:
+                return self._finish(loss)
         self.sync.zero_grad()
         total = None
         for i, (x, y) in enumerate(batches):
@@ -88,9 +132,12 @@ class TrainEngine:
             (loss / self.grad_accum).backward()
             total = loss.detach() if total is None else total + loss.detach()
         self.sync.synchronize()
+        return self._finish(total / self.grad_accum)
+
+    def _finish(self, loss):
         norm = clip_grad_norm(self.sync.params, self.grad_clip, self.sync.flat_covering())
         self.last_grad_norm = norm
         if self.clip_observer is not None:
             self.clip_observer.record_realized_clipping(norm, self.grad_clip)
         self.optimizer.step()
-        return total / self.grad_accum
+        return loss

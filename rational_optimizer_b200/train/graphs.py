@@ -1,0 +1,82 @@
+"""CUDA graph of one training micro-batch: forward, backward and gradient reduction.
+
+With one process per GPU the host enqueues about a thousand kernels per step
+for the 18-layer model (autograd bookkeeping, Python-level ops); at the
+per-GPU batch of an 8-GPU run that host time exceeds the GPU time of the
+forward and backward.  ``StepGraph`` captures ``forward_loss`` +
+``backward`` + the data-parallel gradient reduction once (static input
+buffers, weights cast to bf16 inside the graph because they change between
+replays) and replays it on later steps; the optimizer step stays eager.
+
+Steps that need host-side work inside the forward or backward (TILLER's
+response-probe refresh, telemetry statistics, a different micro-batch shape)
+run eagerly; the graph is kept and used again on the next plain step.
+Capture failures (an operation that cannot be recorded) disable graphs for
+the run and the engine continues eagerly.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from ..ops import linear as _linear
+from ..parallel import param_ready
+
+
+def graphs_requested() -> bool:
+    return os.environ.get("RO_CUDA_GRAPH", "1") != "0"
+
+
+class StepGraph:
+    def __init__(self, model, sync, x, y, *, warmup: int = 3):
+        self.model = model
+        self.sync = sync
+        self.x = x.detach().clone()
+        self.y = y.detach().clone()
+        self.warmup = int(warmup)
+        self.graph = None
+        self.loss = None
+        self._keep = []
+
+    def matches(self, x, y) -> bool:
+        return (x.shape == self.x.shape and y.shape == self.y.shape and x.dtype == self.x.dtype
+                and y.dtype == self.y.dtype and x.device == self.x.device)
+
+    def _one(self):
+        loss = self.model.forward_loss(self.x, self.y)
+        self.sync.begin_backward()
+        loss.backward()
+        self.sync.synchronize()
+        return loss
+
+    def capture(self):
+        param_ready.wait_all()
+        side = torch.cuda.Stream(device=self.x.device)
+        side.wait_stream(torch.cuda.current_stream(self.x.device))
+        with torch.cuda.stream(side):
+            for _ in range(self.warmup):
+                self.sync.zero_grad()
+                self._one()
+        torch.cuda.current_stream(self.x.device).wait_stream(side)
+        self.sync.zero_grad()
+        graph = torch.cuda.CUDAGraph()
+        _linear.capture_casts(True, self._keep)
+        # with several ranks the process group's watchdog thread keeps querying
+        # its events while we capture: restrict capture checks to this thread
+        mode = "thread_local" if self.sync.world > 1 else "global"
+        try:
+            with torch.cuda.graph(graph, capture_error_mode=mode):
+                self.loss = self._one().detach()
+        finally:
+            _linear.capture_casts(False)
+        self.graph = graph
+
+    def replay(self, x, y):
+        param_ready.wait_all()
+        if x.data_ptr() != self.x.data_ptr():
+            self.x.copy_(x, non_blocking=True)
+        if y.data_ptr() != self.y.data_ptr():
+            self.y.copy_(y, non_blocking=True)
+        self.graph.replay()
+        return self.loss.clone()  # the graph's output tensor is overwritten by the next replay

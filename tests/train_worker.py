@@ -3,8 +3,10 @@
 Runs a 4-layer GRAIN+TILLER model for 10 steps per configuration: gradient
 all-reduce during backward (per-layer buckets) or after it, TILLER sharded by
 layer (deferred weight broadcasts) or replicated, one or two micro-batches.
-Every configuration must leave bitwise-identical replicas on all ranks, and
-the fully overlapped/sharded run must follow the plain run's loss curve.
+Every configuration must leave bitwise-identical replicas on all ranks, the
+fully overlapped/sharded run must follow the plain run's loss curve, and the
+same run with its forward/backward/reduction replayed from a CUDA graph must
+reproduce it bit for bit.
 """
 import os
 import sys
@@ -24,8 +26,9 @@ from rational_optimizer_b200.train.engine import TrainEngine  # noqa: E402
 from rational_optimizer_b200.train.integrity import model_state_sha256  # noqa: E402
 
 
-def run(info, *, overlap, shard, accum):
+def run(info, *, overlap, shard, accum, graph=False):
     os.environ["RO_TILLER_SHARD"] = "1" if shard else "0"
+    os.environ["RO_CUDA_GRAPH"] = "1" if graph else "0"
     torch.manual_seed(0)
     args = preset("18l_1024d", layers=4, seq_len=256, activation="grain")
     model = CausalTransformer(args, 50304).cuda()
@@ -53,7 +56,7 @@ def main():
     info = setup_distributed(timeout_s=120)
     configs = [dict(overlap=False, shard=False, accum=1), dict(overlap=True, shard=False, accum=1),
                dict(overlap=False, shard=True, accum=1), dict(overlap=True, shard=True, accum=1),
-               dict(overlap=True, shard=True, accum=2)]
+               dict(overlap=True, shard=True, accum=2), dict(overlap=True, shard=True, accum=1, graph=True)]
     runs = [run(info, **c) for c in configs]
     digests = [None] * info.world_size
     dist.all_gather_object(digests, [r[1] for r in runs])
@@ -64,6 +67,8 @@ def main():
         assert all(equal), equal
         rel = max(abs(x - y) / abs(y) for x, y in zip(runs[3][0], runs[0][0]))
         assert rel < 1e-2, (runs[3][0], runs[0][0])
+        # the captured forward/backward/reduction replays the overlapped run exactly
+        assert runs[5][0] == runs[3][0] and digests[0][5] == digests[0][3], (runs[5][0], runs[3][0])
         print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
     dist.barrier()
     dist.destroy_process_group()
