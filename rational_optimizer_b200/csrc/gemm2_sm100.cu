@@ -36,6 +36,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "packed.cuh"
@@ -54,7 +55,8 @@ constexpr int kBBytes = kHalfN * kBK * 2;          // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;     // 32 KB per CTA
 constexpr int kStageOut = 32 * 128;                // one 32 x 64 bf16 staging tile
 constexpr int kOutBytes = 64 * 1024;               // output staging per CTA
-constexpr int kBarBytes = 256;
+constexpr int kBarBytes = 512;   // mbarriers, TMEM slot, tile scheduler ring
+constexpr int kSched = 4;        // tile scheduler ring depth
 
 enum Epilogue : int { kStore = 0, kGrainFwd = 1, kGrainBwd = 2, kQkvRope = 3 };
 
@@ -75,6 +77,7 @@ struct Traits {
 };
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kDrainNs = 2000000ull;         // 2 ms for in-flight copies after an error
 
 struct Params {
   int M, N, K;
@@ -92,6 +95,9 @@ struct Params {
   const float* cos_t;
   const float* sin_t;
   int seq, hd;
+  // tile schedule: 0 = cluster launch control over one cluster per tile;
+  // n > 0 = static round robin over a persistent grid of n clusters
+  int static_clusters;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -157,6 +163,69 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 // Arrive on an mbarrier anywhere in the cluster (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Cluster launch control: ask the hardware to cancel the launch of a cluster
+// of this grid that has not started yet.  The 16-byte response is written to
+// `resp` (this CTA) and completes 16 transaction bytes on `bar`.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];"
+               ::"r"(resp), "r"(bar)
+               : "memory");
+}
+
+// x index of the first CTA of the cluster a response cancelled; -1 when the
+// request failed (every cluster of the grid has started).
+__device__ __forceinline__ int clc_first_cta_x(uint32_t resp) {
+  int x;
+  asm volatile(
+      "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 r, [%1];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, r;\n\t"
+      "@!p mov.s32 %0, -1;\n\t}"
+      : "=r"(x)
+      : "r"(resp)
+      : "memory");
+  return x;
+}
+
+// Tile scheduler ring (per CTA).  The leader's producer thread obtains tile
+// i+1 through cluster launch control while it loads tile i, then writes it
+// into slot i % kSched of both CTAs and arrives on both `full` barriers.
+// Every other role reads the slot and arrives on the leader's `empty`
+// barrier, which gates the slot's reuse.
+struct Sched {
+  uint32_t base;  // shared::cta address: responses [kSched x 16 B], then the CLC,
+                  // full and empty barriers [kSched each], then the tile slots
+  __device__ __forceinline__ uint32_t resp(uint32_t s) const { return base + 16 * s; }
+  __device__ __forceinline__ uint32_t clc(uint32_t s) const { return base + 16 * kSched + 8 * s; }
+  __device__ __forceinline__ uint32_t full(uint32_t s) const { return base + 24 * kSched + 8 * s; }
+  __device__ __forceinline__ uint32_t empty(uint32_t s) const { return base + 32 * kSched + 8 * s; }
+  __device__ __forceinline__ uint32_t tile(uint32_t s) const { return base + 40 * kSched + 4 * s; }
+  // tile i+1 travels through slot i % kSched, in that slot's use i / kSched
+  __device__ __forceinline__ uint32_t slot_of(int i) const { return static_cast<uint32_t>(i % kSched); }
+  __device__ __forceinline__ uint32_t parity_of(int i) const { return static_cast<uint32_t>((i / kSched) & 1); }
+};
+
+// Read tile i+1 from the ring (one thread); -1: no more tiles, -2: wait gave up.
+__device__ __forceinline__ int sched_next(const Sched& sc, int i, int* err, int code) {
+  const uint32_t slot = sc.slot_of(i);
+  if (!mbar_wait(sc.full(slot), sc.parity_of(i), err, code)) return -2;
+  int t;
+  asm volatile("ld.shared.s32 %0, [%1];" : "=r"(t) : "r"(sc.tile(slot)) : "memory");
+  mbar_arrive_cluster(map_to_rank(sc.empty(slot), 0));
+  return t;
+}
+
+// Leader producer: publish tile i+1 to both CTAs of the pair.
+__device__ __forceinline__ void sched_publish(const Sched& sc, int i, int t) {
+  const uint32_t slot = sc.slot_of(i);
+#pragma unroll
+  for (uint32_t r = 0; r < 2; ++r) {
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(map_to_rank(sc.tile(slot), r)), "r"(t) : "memory");
+    mbar_arrive_cluster(map_to_rank(sc.full(slot), r));
+  }
 }
 
 // 2-D tiled TMA load into this CTA's shared memory; the transaction bytes are
@@ -536,6 +605,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   uint64_t* acc_empty = acc_full + 2;      // [2]        (used in the leader)
   uint64_t* hbar = acc_empty + 2;         // [kW]       (GRAIN backward: h slice per warp)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hbar + kW);
+  const Sched sc{smem_u32(bars) + 256};  // tile scheduler ring (bars + 256 B)
   float (*rho_part)[32] = reinterpret_cast<float (*)[32]>(out_stage + kOutBytes + kBarBytes);
   float (*coef_part)[10] = reinterpret_cast<float (*)[10]>(out_stage + kOutBytes + kBarBytes + kW * 32 * 4);
 
@@ -544,11 +614,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   const uint32_t crank = cluster_rank();
   const bool leader = crank == 0;
   const int cluster_id = blockIdx.x >> 1;
-  const int num_clusters = gridDim.x >> 1;
   const int num_m = (p.M + kBM - 1) / kBM;
   const int num_n = (p.N + kBN - 1) / kBN;
   const int num_k = (p.K + kBK - 1) / kBK;
-  const int tiles = num_m * num_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -560,6 +628,12 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       mbar_init(smem_u32(&acc_empty[a]), 2 * kW);
     }
     for (int w = 0; w < kW; ++w) mbar_init(smem_u32(&hbar[w]), 1);
+    for (int s = 0; s < kSched; ++s) {
+      mbar_init(sc.clc(s), 1);
+      mbar_init(sc.full(s), 1);
+      // readers: leader MMA + epilogue warps, peer producer + epilogue warps
+      mbar_init(sc.empty(s), 2 + 2 * kW);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -578,7 +652,16 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = cluster_id; tile < tiles && ok; tile += num_clusters) {
+      int tile = cluster_id;
+      for (int i = 0; tile >= 0 && ok; ++i) {
+        if (leader) {
+          if (!mbar_wait(sc.empty(sc.slot_of(i)), sc.parity_of(i) ^ 1, p.err, 6)) break;
+          if (p.static_clusters == 0) {
+            // ask for the next tile now; the answer is read after this tile's loads
+            mbar_expect_tx(sc.clc(sc.slot_of(i)), 16);
+            clc_try_cancel(sc.resp(sc.slot_of(i)), sc.clc(sc.slot_of(i)));
+          }
+        }
         int tm, tn;
         tile_coords(tile, num_m, num_n, tm, tn);
         const int m0 = tm * kBM + static_cast<int>(crank) * kHalfM;
@@ -593,6 +676,20 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
           tma_load_2d(sa + kABytes, &tmB, fb, kb * kBK, n0);
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
+        if (!ok) break;
+        if (leader) {
+          if (p.static_clusters == 0) {
+            if (!mbar_wait(sc.clc(sc.slot_of(i)), sc.parity_of(i), p.err, 7)) break;
+            const int x = clc_first_cta_x(sc.resp(sc.slot_of(i)));
+            tile = x < 0 ? -1 : (x >> 1);
+          } else {
+            tile += p.static_clusters;
+            if (tile >= num_m * num_n) tile = -1;
+          }
+          sched_publish(sc, i, tile);
+        } else {
+          tile = sched_next(sc, i, p.err, 8);
+        }
       }
     }
   } else if (warp == 1) {
@@ -603,7 +700,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = cluster_id; tile < tiles && ok; tile += num_clusters, ++local) {
+      for (int tile = cluster_id; tile >= 0 && ok; ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1, p.err, 2)) { ok = false; break; }
@@ -622,6 +719,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         }
         if (!ok) break;
         tc_commit_both(smem_u32(&acc_full[acc]));
+        tile = sched_next(sc, local, p.err, 9);
       }
     }
   } else {
@@ -635,7 +733,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     // GRAIN backward: TMA the warp's slice of h for a tile into its staging tile
     auto fetch_h = [&](int tile) {
       if constexpr (EPI == kGrainBwd) {
-        if (tile < tiles && lane == 0) {
+        if (tile >= 0 && lane == 0) {
           int fm, fn;
           tile_coords(tile, num_m, num_n, fm, fn);
           bulk_wait_read<0>();  // the previous bulk store has read the tile
@@ -651,7 +749,13 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     GrainCoeffs gc;
     float2 one2 = splat2(1.0f);
     int local = 0;
-    for (int tile = cluster_id; tile < tiles; tile += num_clusters, ++local) {
+    // tile i+1 of this CTA pair, read by lane 0 and shared with the warp
+    auto next_tile = [&](int i) {
+      int t = 0;
+      if (lane == 0) t = sched_next(sc, i, p.err, 10);
+      return __shfl_sync(0xffffffffu, t, 0);
+    };
+    for (int tile = cluster_id; tile >= 0; ++local) {
       int tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
       const int acc = local & 1;
@@ -688,10 +792,12 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         if (!mbar_wait(smem_u32(&hbar[e]), local & 1, p.err, 5)) break;
         grain_bwd_epilogue<kW>(p, tbase, stage_buf, tm, tn, crank, quarter, e, lane, row0, col0, &tmC, rho_part,
                                coef_part);
-        fetch_h(tile + num_clusters);
+        const int next = next_tile(local);
+        fetch_h(next);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
+        tile = next;
         continue;
       }
 #pragma unroll 1
@@ -793,9 +899,18 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
+      tile = next_tile(local);
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
+  }
+  if (*reinterpret_cast<volatile int*>(p.err) != 0) {
+    // a wait gave up: TMA loads already issued into this pair's shared memory
+    // (operand stages, the GRAIN-backward h slices) complete without any
+    // further action, so give them a bounded interval to land before the
+    // shared memory is handed to the next cluster
+    const uint64_t t0 = global_ns();
+    while (global_ns() - t0 < kDrainNs) __nanosleep(1000);
   }
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal it
@@ -865,7 +980,7 @@ int num_sms() {
 
 template <int EPI>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, void* Y, int64_t ldy,
-           const Params& p, cudaStream_t stream) {
+           Params p, cudaStream_t stream) {
   CUtensorMap ma, mb, mc, my;
   if (!make_map(&ma, A, p.M, p.K, lda, kHalfM) || !make_map(&mb, B, p.N, p.K, ldb, kHalfN)) return -3;
   if constexpr (EPI == kQkvRope) {
@@ -906,8 +1021,20 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
   }
   if (configured < 0) return -4;
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kBN - 1) / kBN);
-  int clusters = num_sms() / 2;
-  if (tiles < clusters) clusters = tiles;
+  // default: one cluster per tile; the clusters that start first take over
+  // the tiles of clusters that have not started (cluster launch control), so
+  // SMs held by other kernels (collectives on another stream) delay no tile.
+  // RO_GEMM2_STATIC=1: a persistent grid of one cluster per SM pair.
+  static const bool static_sched = [] {
+    const char* v = std::getenv("RO_GEMM2_STATIC");
+    return v != nullptr && v[0] == '1';
+  }();
+  int clusters = tiles;
+  if (static_sched) {
+    clusters = num_sms() / 2;
+    if (tiles < clusters) clusters = tiles;
+    p.static_clusters = clusters;
+  }
   kern<<<2 * clusters, Traits<EPI>::kThreads, Traits<EPI>::kSmemBytes, stream>>>(ma, mb, mc, my, p);
   return static_cast<int>(cudaGetLastError());
 }

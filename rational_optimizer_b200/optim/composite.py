@@ -161,6 +161,18 @@ class TILLERCompositeOptimizer(CompositeOptimizer):
     def router(self):
         return self.optimizers[0]
 
+    def step(self):
+        """Router, attention, AdamW.  The router's single-CTA ledger kernel runs
+        on a side stream beside the attention and AdamW updates (they touch
+        disjoint parameters); the router's weight update is applied after."""
+        router = self.router
+        router.step(defer_apply=True)
+        try:
+            for opt in self.optimizers[1:]:
+                opt.step()
+        finally:
+            router.finish_step()
+
     def eager_step_required(self):
         """True when this step's forward/backward must run eagerly (response-probe refresh)."""
         return bool(self.router._capture_response_this_transition)

@@ -342,6 +342,9 @@ class TILLERRouter(torch.optim.Optimizer):
         self.packing = None  # OwnerPacking when weights are re-homed for owner broadcasts
         self._force_torch = False
         self._ledger_bufs = None
+        self._pending_apply = None
+        self._packing_due = False
+        self._side_stream = None
 
     # -- properties --------------------------------------------------------
     @property
@@ -651,6 +654,7 @@ class TILLERRouter(torch.optim.Optimizer):
         broadcast_owned(per_layer, L, self.world_size, self.loss_probe_group)
 
     def state_dict(self):
+        self.finish_step()
         param_ready.wait_all()
         self._sync_shards()
         return super().state_dict()
@@ -800,8 +804,14 @@ class TILLERRouter(torch.optim.Optimizer):
                             "tiller_ledger_transaction"))
 
     def _ledger_fast(self, *, functional, scores, decay, exact_by_role, momentum_by_role, weights,
-                     layer_ids, eta):
-        """Ledger advance + transaction in one single-CTA fp64 kernel (csrc/ledger.cu)."""
+                     layer_ids, eta, stream=None):
+        """Ledger advance + transaction in one single-CTA fp64 kernel (csrc/ledger.cu).
+
+        ``stream``: run the kernel there, after the work queued so far on the
+        current stream; its inputs are recorded on that stream and its outputs
+        on the current one, so the caching allocator keeps both alive across
+        the two streams.
+        """
         from .._ext import ext
         C = ext()
         anchor = self.anchor
@@ -828,13 +838,26 @@ class TILLERRouter(torch.optim.Optimizer):
             if ref.data_ptr() != scal[3].data_ptr():
                 scal[3].copy_(ref.reshape(()))
         dd = None if functional else self._rfd_decay_derivative.reshape(1).float().contiguous()
-        timing = self._ledger_timing
-        coef, cand, result = C.tiller_ledger_transaction(
-            scores.float().contiguous() if functional else None,
-            decay.float().contiguous() if functional else None,
-            exact_by_role.float().contiguous(), momentum_by_role.float().contiguous(),
-            weights.float().contiguous(), layer_ids.contiguous(), dd, pers, diag, cross, scal, ws,
-            prev_rows, len(self.pairs), float(eta), timing=timing)
+        timing = None if stream is not None else self._ledger_timing
+        inputs = [scores.float().contiguous() if functional else None,
+                  decay.float().contiguous() if functional else None,
+                  exact_by_role.float().contiguous(), momentum_by_role.float().contiguous(),
+                  weights.float().contiguous(), layer_ids.contiguous(), dd]
+        if stream is None:
+            coef, cand, result = C.tiller_ledger_transaction(*inputs, pers, diag, cross, scal, ws, prev_rows,
+                                                             len(self.pairs), float(eta), timing=timing)
+        else:
+            main = torch.cuda.current_stream(dev)
+            stream.wait_stream(main)
+            for t in inputs:
+                if t is not None:
+                    t.record_stream(stream)
+            with torch.cuda.stream(stream):
+                coef, cand, result = C.tiller_ledger_transaction(*inputs, pers, diag, cross, scal, ws,
+                                                                 prev_rows, len(self.pairs), float(eta),
+                                                                 timing=None)
+            for t in (coef, cand, result):
+                t.record_stream(main)
         if timing is not None:
             # diagnostics (RO_LEDGER_TIMING=1): phase clock stamps and eigensolver sweeps
             # (-1: arrowhead path) of every ledger call, kept on the host
@@ -924,7 +947,17 @@ class TILLERRouter(torch.optim.Optimizer):
 
     # -- step -----------------------------------------------------------------
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, *, defer_apply=False):
+        """One router transition.
+
+        ``defer_apply``: when the single-CTA ledger kernel runs, launch it on a
+        side stream and return before the weights are updated, so the caller
+        can run independent work (the attention optimizer, AdamW) beside it;
+        :meth:`finish_step` then waits for the ledger and applies the update.
+        The attention route is published before returning in both cases.
+        """
+        if self._pending_apply is not None:
+            raise RuntimeError("TILLER router step started before the previous one finished")
         if self._clip_factor is None:
             raise RuntimeError("TILLER lacks realized clipping")
         if not self._attention_consumed:
@@ -965,6 +998,9 @@ class TILLERRouter(torch.optim.Optimizer):
         exact_by_role = dirs["exact_by_role"]
         momentum_by_role = dirs["momentum_by_role"]
         layer_ids = torch.arange(L, device=weights.device, dtype=torch.int64).repeat_interleave(self.groups)
+        side = None
+        if defer_apply and weights.is_cuda and self._fast_ledger_ok() and self._ledger_timing is None:
+            side = self._ledger_side_stream(weights.device)
         if refresh:
             lo, hi, sharded = dirs["owned"]
             if sharded:
@@ -995,7 +1031,7 @@ class TILLERRouter(torch.optim.Optimizer):
                 selection = self._ledger_fast(functional=True, scores=g_scores, decay=g_decay,
                                               exact_by_role=exact_by_role,
                                               momentum_by_role=momentum_by_role, weights=weights,
-                                              layer_ids=layer_ids, eta=lr)
+                                              layer_ids=layer_ids, eta=lr, stream=side)
             else:
                 self._advance_rows(g_scores, g_decay, functional=True)
                 selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids,
@@ -1010,16 +1046,44 @@ class TILLERRouter(torch.optim.Optimizer):
                 selection = self._ledger_fast(functional=False, scores=None, decay=None,
                                               exact_by_role=exact_by_role,
                                               momentum_by_role=momentum_by_role, weights=weights,
-                                              layer_ids=layer_ids, eta=lr)
+                                              layer_ids=layer_ids, eta=lr, stream=side)
             else:
                 selection = self._transaction(exact_by_role, momentum_by_role, weights, layer_ids,
                                               eta=lr)
-        coefficients = selection.coefficients.view(L, self.groups)
-        dirs["apply"](coefficients, lr, wd)
         updates = int(anchor.get("predictive_response_transaction_updates", 0)) + 1
         anchor["predictive_response_transaction_updates"] = updates
         self._attention_update = updates
         self._attention_consumed = False
+        tail = (selection, dirs, refresh, publish, lr, wd)
+        if side is not None:
+            event = torch.cuda.Event()
+            event.record(side)
+            self._pending_apply = (event, tail)
+            return loss
+        self._complete_step(*tail)
+        return loss
+
+    def finish_step(self):
+        """Apply a deferred transition (no-op when nothing is pending)."""
+        pending, self._pending_apply = self._pending_apply, None
+        if pending is None:
+            return
+        event, tail = pending
+        torch.cuda.current_stream(self.pairs[0]["in_weight"].device).wait_event(event)
+        with torch.no_grad():
+            self._complete_step(*tail)
+        if self._packing_due:
+            self._packing_due = False
+            self.packing.broadcast()
+
+    def _ledger_side_stream(self, device):
+        if self._side_stream is None:
+            self._side_stream = torch.cuda.Stream(device=device)
+        return self._side_stream
+
+    def _complete_step(self, selection, dirs, refresh, publish, lr, wd):
+        coefficients = selection.coefficients.view(len(self.pairs), self.groups)
+        dirs["apply"](coefficients, lr, wd)
         if refresh:
             self._cache_refresh_state()
         if publish:
@@ -1028,7 +1092,6 @@ class TILLERRouter(torch.optim.Optimizer):
         self._rfd_decay_derivative = None
         self._capture_telemetry_next_step = False
         self._clip_factor = None
-        return loss
 
     def _decay_derivative(self, wd):
         """wd * sum over routed matrices of <grad, weight> (optimizer_design/_tiller/core.py:4511-4519)."""
@@ -1288,7 +1351,11 @@ class TILLERAttentionOptimizer(torch.optim.Optimizer):
                           alpha=-lr * adjustment)
         anchor["factorized_adaptive_tangent_updates"] = update
         if fused and self.router.packing is not None and self.router._shard()[2]:
-            self.router.packing.broadcast()
+            if self.router._pending_apply is not None:
+                # the router's deferred update lands in the same owner buffer
+                self.router._packing_due = True
+            else:
+                self.router.packing.broadcast()
         if self._capture_telemetry_next_step:
             safe = torch.cat([m["safe"].reshape(-1) for m in metas])
             cosine = torch.cat([m["parent_cosine"].reshape(-1) for m in metas])

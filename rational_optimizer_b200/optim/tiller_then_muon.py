@@ -178,8 +178,16 @@ class TillerThenMuonOptimizer:
         prior = self.stage
         switched = False
         child = {}
-        for opt in list(self.optimizers):
-            opt.step()
+        try:
+            for opt in list(self.optimizers):
+                if opt is self.tiller_router:
+                    # ledger kernel beside the attention and AdamW updates
+                    opt.step(defer_apply=True)
+                else:
+                    opt.step()
+        finally:
+            if prior == "tiller":
+                self.tiller_router.finish_step()
         self._completed_steps += 1
         if prior == "tiller" and self._capture_telemetry_next_step:
             for c in (self.tiller_router, self.tiller_attention):

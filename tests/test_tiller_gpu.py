@@ -45,6 +45,39 @@ def test_fused_tiller_matches_torch_path():
         torch.testing.assert_close(fa[key], ra[key], rtol=1e-3, atol=1e-9)
 
 
+class _SequentialSteps:
+    """The TILLER composite stepped child by child, without the side-stream ledger."""
+
+    def __init__(self, opt):
+        self.opt = opt
+
+    def __getattr__(self, name):
+        return getattr(self.opt, name)
+
+    def step(self):
+        for child in self.opt.optimizers:
+            child.step()
+
+
+def test_side_stream_ledger_matches_sequential_steps():
+    args = _args()
+    torch.manual_seed(0)
+    base = CausalTransformer(args, 300).cuda().set_compute_dtype(torch.float32)
+    m_seq, m_def = copy.deepcopy(base), copy.deepcopy(base)
+    o_seq = composite.configure_optimizer(m_seq, args)
+    o_def = composite.configure_optimizer(m_def, args)
+    e_seq, e_def = TrainEngine(m_seq, _SequentialSteps(o_seq)), TrainEngine(m_def, o_def)
+    gen = torch.Generator().manual_seed(11)
+    for _ in range(10):
+        t = torch.randint(0, 300, (4, 65), generator=gen).cuda()
+        e_seq.step([(t[:, :-1], t[:, 1:])], lr=3e-4)
+        e_def.step([(t[:, :-1], t[:, 1:])], lr=3e-4)
+    assert o_def.router._fast_ledger_ok() and o_def.router._side_stream is not None
+    assert o_def.router._pending_apply is None
+    for (n, a), (_, b) in zip(m_seq.named_parameters(), m_def.named_parameters()):
+        assert torch.equal(a, b), n
+
+
 def _ext():
     from rational_optimizer_b200._ext import ext
     return ext()
