@@ -1037,7 +1037,7 @@ namespace grain {
 constexpr int64_t kNoAllocScratchFloats = 65536;  // 256 KiB
 constexpr int kNoAllocMaxDevices = 64;
 
-__device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
 
 static float* noalloc_scratch_for_current_device(int* status) {
   static std::mutex lock;
