@@ -15,6 +15,7 @@ import torch.nn.functional as F
 
 from .._ext import ext
 from . import gemm
+from .linear import managed_grad, report_ready
 
 DEFAULT_CHUNK_ROWS = 8192
 
@@ -29,7 +30,7 @@ class _LinearCrossEntropy(torch.autograd.Function):
         ign = -100 if ignore_index is None else int(ignore_index)
         hc = h if h.dtype == w_compute.dtype else h.to(w_compute.dtype)
         dh = torch.empty_like(hc)
-        dw = torch.zeros(weight.shape, device=h.device, dtype=torch.float32)
+        dw = None
         loss_rows = torch.empty(n, device=h.device, dtype=torch.float32)
         for start in range(0, n, chunk_rows):
             stop = min(n, start + chunk_rows)
@@ -38,8 +39,16 @@ class _LinearCrossEntropy(torch.autograd.Function):
             loss_rows[start:stop] = C.cross_entropy_fwd_bwd(logits, target[start:stop].contiguous(),
                                                             scale, ign)
             dh[start:stop] = gemm.matmul_nn(logits, w_compute)
-            dw.add_(gemm.matmul_tn(logits, hs, out_dtype=torch.float32))
+            # the first chunk writes the fp32 weight gradient, later ones add to
+            # it inside the GEMM (no zero fill, no temporaries, no separate adds)
+            if dw is None:
+                dw = gemm.matmul_tn(logits, hs, out_dtype=torch.float32)
+            else:
+                gemm.matmul_tn_accumulate_(dw, logits, hs)
+        if dw is None:
+            dw = torch.zeros(weight.shape, device=h.device, dtype=torch.float32)
         ctx.save_for_backward(dh, dw)
+        ctx.weight = weight
         ctx.h_dtype = h.dtype
         ctx.w_dtype = weight.dtype
         return loss_rows.sum() * scale
@@ -47,9 +56,16 @@ class _LinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     def backward(ctx, go):
         dh, dw = ctx.saved_tensors
-        gh = (dh * go.to(dh.dtype)).to(ctx.h_dtype)
-        gw = (dw * go).to(ctx.w_dtype)
-        return gh, gw, None, None, None, None
+        gh = (dh * go.to(dh.dtype)).to(ctx.h_dtype) if ctx.needs_input_grad[0] else None
+        if not ctx.needs_input_grad[1]:
+            return gh, None, None, None, None, None
+        buf = managed_grad(ctx.weight)
+        if buf is not None and ctx.w_dtype == torch.float32:
+            # grad += dw * go in one pass over the managed fp32 gradient buffer
+            buf.addcmul_(dw, go.to(buf.dtype))
+            report_ready(ctx.weight)
+            return gh, None, None, None, None, None
+        return gh, (dw * go).to(ctx.w_dtype), None, None, None, None
 
 
 def linear_cross_entropy(h, weight, target, *, w_compute=None, chunk_rows=DEFAULT_CHUNK_ROWS,

@@ -169,6 +169,23 @@ def test_linear_cross_entropy(V):
     torch.testing.assert_close(w.grad, wr.grad, rtol=5e-2, atol=2e-4)
 
 
+def test_linear_cross_entropy_adds_into_managed_grad():
+    """With a managed fp32 gradient buffer the weight gradient (times the
+    incoming gradient) is added into it and autograd receives none."""
+    from rational_optimizer_b200.ops.linear import ACCUMULATE_ATTR
+    N, d, V = 700, 256, 1000
+    h = torch.randn(N, d, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    w = (0.02 * torch.randn(V, d, device=DEV)).requires_grad_(True)
+    t = torch.randint(0, V, (N,), device=DEV)
+    start = torch.randn(V, d, device=DEV)
+    w.grad = start.clone()
+    setattr(w, ACCUMULATE_ATTR, True)
+    (3.0 * linear_cross_entropy(h, w, t, chunk_rows=256)).backward()
+    wr = w.detach().to(torch.bfloat16).float().requires_grad_(True)
+    (3.0 * F.cross_entropy(h.detach().float() @ wr.t(), t)).backward()
+    torch.testing.assert_close(w.grad - start, wr.grad, rtol=5e-2, atol=6e-4)
+
+
 def test_add_rms_norm_matches_reference():
     from rational_optimizer_b200.ops.norm import add_rms_norm
     x = torch.randn(513, 1024, device=DEV, requires_grad=True)
