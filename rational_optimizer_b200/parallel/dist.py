@@ -47,6 +47,9 @@ def setup_distributed(backend: str | None = None, timeout_s: float = 300.0) -> D
 
 def cleanup_distributed(info: DistInfo):
     if info.is_distributed and dist.is_initialized():
+        # captured graphs holding NCCL calls must go before the process group
+        from ..train.graphs import release_all
+        release_all()
         dist.destroy_process_group()
 
 

@@ -92,6 +92,8 @@ class TrainEngine:
 
     def _graphed_forward_backward(self, x, y):
         """The loss via the captured graph, or None (eager path) when capture is not possible."""
+        if self._graph is not None and self._graph.graph is None:
+            self._graph = None  # released (process-group teardown): capture again if stepped
         if self._graph is None:
             self._plain_steps += 1
             if self._plain_steps < 3:  # let lazily-initialised state settle first

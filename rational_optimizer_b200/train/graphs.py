@@ -17,6 +17,7 @@ the run and the engine continues eagerly.
 from __future__ import annotations
 
 import os
+import weakref
 
 import torch
 
@@ -28,6 +29,20 @@ def graphs_requested() -> bool:
     return os.environ.get("RO_CUDA_GRAPH", "1") != "0"
 
 
+_LIVE = weakref.WeakSet()
+
+
+def release_all() -> None:
+    """Free every captured step graph of this process.
+
+    A graph that recorded NCCL collectives must be freed before the process
+    group is destroyed; otherwise process exit waits on it indefinitely.
+    ``parallel.dist.cleanup_distributed`` calls this first.
+    """
+    for g in list(_LIVE):
+        g.release()
+
+
 class StepGraph:
     def __init__(self, model, sync, x, y, *, warmup: int = 3):
         self.model = model
@@ -35,6 +50,16 @@ class StepGraph:
         self.x = x.detach().clone()
         self.y = y.detach().clone()
         self.warmup = int(warmup)
+        self.graph = None
+        self.loss = None
+        self._keep = []
+        _LIVE.add(self)
+
+    def release(self):
+        """Free the captured graph and its pinned tensors (replay needs a new capture)."""
+        if self.graph is not None:
+            torch.cuda.synchronize(self.x.device)
+            self.graph.reset()
         self.graph = None
         self.loss = None
         self._keep = []

@@ -11,6 +11,7 @@ from rational_optimizer_b200.optim import composite
 from rational_optimizer_b200.parallel import param_ready
 from rational_optimizer_b200.parallel.grad_sync import GradientSynchronizer
 from rational_optimizer_b200.train.engine import TrainEngine
+from rational_optimizer_b200.train.graphs import release_all
 
 
 def _args():
@@ -32,7 +33,11 @@ def test_graph_replay_matches_eager(monkeypatch):
         eng = TrainEngine(m, opt, grad_clip=1.0, synchronizer=GradientSynchronizer(m))
         gen = torch.Generator().manual_seed(3)
         losses = []
-        for _ in range(14):  # two response refreshes (steps 0 and 8) run eagerly
+        for i in range(14):  # two response refreshes (steps 0 and 8) run eagerly
+            if graphs == "1" and i == 10:
+                # teardown path: graphs are freed, the next plain step captures again
+                release_all()
+                assert eng._graph.graph is None
             t = torch.randint(0, 1000, (4, 257), generator=gen).cuda()
             losses.append(eng.step([(t[:, :-1], t[:, 1:])], lr=3e-4).item())
         param_ready.wait_all()
