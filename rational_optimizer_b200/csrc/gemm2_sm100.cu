@@ -1,4 +1,4 @@
-// Persistent 2-SM GEMM (tcgen05.mma.cta_group::2) with fused epilogues.
+// 2-SM GEMM (tcgen05.mma.cta_group::2) with fused epilogues.
 //
 //   acc (M x N) = A (M x K) . B (N x K)^T          bf16 operands, fp32 accumulator
 //
@@ -8,9 +8,14 @@
 // M=256 N=256 K=16 MMAs that read both CTAs' shared memory, and each CTA's
 // tensor memory receives its own 128 rows of the accumulator.
 //
-// Per CTA (320 threads, one CTA per SM, grid = 2 x #clusters, persistent):
+// Per CTA (320 threads; 576 for the GRAIN backward; one CTA per SM).  The
+// grid has one cluster per output tile; a running cluster takes over the
+// tiles of clusters that have not started (cluster launch control) and
+// passes each tile index to both CTAs through a small shared-memory ring, so
+// the clusters that run do all the work whatever SMs other kernels hold.
 //   warp 0      TMA producer: loads into this CTA's ring; the completion
-//               bytes of both CTAs land on the leader's `full` barrier;
+//               bytes of both CTAs land on the leader's `full` barrier; the
+//               leader's producer thread is also the tile scheduler;
 //   warp 1      TMEM allocation (both CTAs) and, in the leader, the MMA
 //               issuer; each K block is released to both producers with a
 //               multicast tcgen05.commit (no multicast loads are used);
@@ -27,6 +32,11 @@
 //               the RMS of H over the group, Y = rho * P(t)/Q(|t|) with
 //               t = H / rho is stored (the arithmetic of
 //               ro::grain::forward_packed_kernel).
+//   kGrainBwd   GRAIN backward fused behind the out-projection's input
+//               gradient: gy stays in TMEM, the forward H slice is fetched by
+//               TMA, dH is stored and per-tile coefficient partials written.
+//   kQkvRope    q/k/v projection with RoPE applied to q and k, stored as
+//               three token-major planes through a 3-D TMA store.
 //
 // Every mbarrier wait is bounded by a wall-clock limit; on expiry the waiting
 // role records an error code in `err` and stops.  Every thread of both CTAs
