@@ -108,6 +108,8 @@ struct Params {
   // tile schedule: 0 = cluster launch control over one cluster per tile;
   // n > 0 = static round robin over a persistent grid of n clusters
   int static_clusters;
+  // 1: readers free ring slots with release-ordered arrivals (comparison)
+  int ordered_release;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -219,12 +221,27 @@ struct Sched {
 };
 
 // Read tile i+1 from the ring (one thread); -1: no more tiles, -2: wait gave up.
-__device__ __forceinline__ int sched_next(const Sched& sc, int i, int* err, int code) {
+__device__ __forceinline__ int sched_next(const Sched& sc, int i, int* err, int code, bool ordered = false) {
   const uint32_t slot = sc.slot_of(i);
   if (!mbar_wait(sc.full(slot), sc.parity_of(i), err, code)) return -2;
   int t;
   asm volatile("ld.shared.s32 %0, [%1];" : "=r"(t) : "r"(sc.tile(slot)) : "memory");
-  mbar_arrive_cluster(map_to_rank(sc.empty(slot), 0));
+  // Free the slot with a relaxed arrival (no cluster-scope fence per reader
+  // and tile).  Its address is made to depend on the value read, so the read
+  // has completed before the arrival that lets the leader overwrite the slot.
+  // (tile indices are >= -2, so `dep` is always 0, but the assembler cannot
+  // know that and keeps the dependency)
+  uint32_t dep;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.lt.s32 q, %1, -2;\n\tselp.u32 %0, 8, 0, q;\n\t}"
+      : "=r"(dep)
+      : "r"(t));
+  if (ordered)
+    mbar_arrive_cluster(map_to_rank(sc.empty(slot), 0));
+  else
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                     map_to_rank(sc.empty(slot), 0) + dep)
+                 : "memory");
   return t;
 }
 
@@ -698,7 +715,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
           }
           sched_publish(sc, i, tile);
         } else {
-          tile = sched_next(sc, i, p.err, 8);
+          tile = sched_next(sc, i, p.err, 8, p.ordered_release != 0);
         }
       }
     }
@@ -729,7 +746,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         }
         if (!ok) break;
         tc_commit_both(smem_u32(&acc_full[acc]));
-        tile = sched_next(sc, local, p.err, 9);
+        tile = sched_next(sc, local, p.err, 9, p.ordered_release != 0);
       }
     }
   } else {
@@ -762,7 +779,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     // tile i+1 of this CTA pair, read by lane 0 and shared with the warp
     auto next_tile = [&](int i) {
       int t = 0;
-      if (lane == 0) t = sched_next(sc, i, p.err, 10);
+      if (lane == 0) t = sched_next(sc, i, p.err, 10, p.ordered_release != 0);
       return __shfl_sync(0xffffffffu, t, 0);
     };
     for (int tile = cluster_id; tile >= 0; ++local) {
@@ -1039,6 +1056,11 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
     const char* v = std::getenv("RO_GEMM2_STATIC");
     return v != nullptr && v[0] == '1';
   }();
+  static const bool ordered = [] {
+    const char* v = std::getenv("RO_GEMM2_ORDERED_RELEASE");
+    return v != nullptr && v[0] == '1';
+  }();
+  p.ordered_release = ordered ? 1 : 0;
   int clusters = tiles;
   if (static_sched) {
     clusters = num_sms() / 2;
