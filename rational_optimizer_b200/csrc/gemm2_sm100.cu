@@ -110,6 +110,8 @@ struct Params {
   int static_clusters;
   // 1: readers free ring slots with release-ordered arrivals (comparison)
   int ordered_release;
+  // 1: epilogue warps free accumulator buffers with cluster-scope releases
+  int acc_release_cluster;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -253,6 +255,17 @@ __device__ __forceinline__ void sched_publish(const Sched& sc, int i, int t) {
     asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(map_to_rank(sc.tile(slot), r)), "r"(t) : "memory");
     mbar_arrive_cluster(map_to_rank(sc.full(slot), r));
   }
+}
+
+// Release an accumulator buffer to the leader's MMA issuer (remote arrive).
+// After tcgen05.wait::ld and tcgen05.fence::before_thread_sync the TMEM reads
+// are complete, so the arrival needs no cluster-scope fence: the default
+// (CTA-scope release) form is used, the cluster-scope release on request.
+__device__ __forceinline__ void acc_release(uint32_t cluster_addr, bool cluster_scope) {
+  if (cluster_scope)
+    mbar_arrive_cluster(cluster_addr);
+  else
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-D tiled TMA load into this CTA's shared memory; the transaction bytes are
@@ -823,7 +836,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         fetch_h(next);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
+        if (lane == 0) acc_release(empty_leader + acc * 8, p.acc_release_cluster != 0);
         tile = next;
         continue;
       }
@@ -925,7 +938,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       // accumulator buffer drained: release it to the leader's MMA issuer
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(empty_leader + acc * 8);
+      if (lane == 0) acc_release(empty_leader + acc * 8, p.acc_release_cluster != 0);
       tile = next_tile(local);
     }
     if (lane == 0) bulk_wait_all();
@@ -1061,6 +1074,11 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int6
     return v != nullptr && v[0] == '1';
   }();
   p.ordered_release = ordered ? 1 : 0;
+  static const bool acc_cluster = [] {
+    const char* v = std::getenv("RO_GEMM2_ACC_CLUSTER_RELEASE");
+    return v != nullptr && v[0] == '1';
+  }();
+  p.acc_release_cluster = acc_cluster ? 1 : 0;
   int clusters = tiles;
   if (static_sched) {
     clusters = num_sms() / 2;

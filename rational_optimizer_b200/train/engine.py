@@ -96,7 +96,10 @@ class TrainEngine:
             self._graph = None  # released (process-group teardown): capture again if stepped
         if self._graph is None:
             self._plain_steps += 1
-            if self._plain_steps < 3:  # let lazily-initialised state settle first
+            # one complete plain step first (lazily created optimizer state,
+            # weight casts); capture on the second, so any run with three or
+            # more warm-up steps has captured before it is timed
+            if self._plain_steps < 2:
                 return None
             try:
                 g = StepGraph(self.model, self.sync, x, y)

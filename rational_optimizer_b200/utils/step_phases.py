@@ -46,6 +46,8 @@ class PhaseTimer:
 
     # -- markers ------------------------------------------------------------
     def mark(self, name):
+        if self.cuda and torch.cuda.is_current_stream_capturing():
+            return  # inside a step-graph capture: its replays carry no markers
         if self.cuda:
             e = torch.cuda.Event(enable_timing=True)
             e.record(torch.cuda.current_stream(self.device))
