@@ -42,7 +42,7 @@ ZIPF_TOKENS = 8_000_000
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=24)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--optimizer", default="tiller_v1")
@@ -54,7 +54,11 @@ def parse():
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region.
+
+    nvidia-smi writes straight into a temporary file and is parsed after the
+    region, so no thread of the benchmark process wakes up while it is timed.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -62,27 +66,19 @@ class ClockSampler:
 
     def __init__(self, index):
         self.index = index
-        self.samples = []
         self.proc = None
-        self.thread = None
+        self.file = None
 
     def start(self):
+        import tempfile
+        self.file = tempfile.TemporaryFile(mode="w+")
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                stdout=self.file, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
-
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append(parts)
 
     def stop(self):
         if self.proc is not None:
@@ -91,11 +87,17 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=2)
+        samples = []
+        if self.file is not None:
+            self.file.seek(0)
+            for line in self.file:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    samples.append(parts)
+            self.file.close()
         mhz, maxes, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for s in self.samples:
+        for s in samples:
             try:
                 mhz.append(float(s[1]))
                 maxes.append(float(s[2]))
@@ -126,29 +128,44 @@ def count_own_launches(step_fn):
     return own, total
 
 
-def timed(step_fn, steps, device, dist_on, flush=None):
+def timed(step_fn, steps, device, dist_on, flush=None, kind=None):
+    """Mean device ms per step over exactly ``steps`` steps, MAX over ranks.
+
+    An event is also recorded after every step (no synchronisation), so the
+    per-step device times can be split by ``kind()`` (called before each
+    step, e.g. ``"plain"`` / ``"refresh"``); returns (ms, {kind: [median ms,
+    count]}) with each median also reduced with MAX over ranks.
+    """
     import torch
     import torch.distributed as dist
     if dist_on:
         dist.barrier()
     torch.cuda.synchronize(device)
-    start = torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     end = torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
+    kinds = []
+    marks[0].record()
+    for i in range(steps):
+        kinds.append(kind() if kind is not None else "step")
         step_fn()
+        marks[i + 1].record()
     if flush is not None:
         flush()  # side-stream work of the last step (deferred weight broadcasts) inside the region
     end.record()
     torch.cuda.synchronize(device)
     if dist_on:
         dist.barrier()
-    ms = start.elapsed_time(end) / steps
+    ms = marks[0].elapsed_time(end) / steps
+    per = {}
+    for i, k in enumerate(kinds):
+        per.setdefault(k, []).append(marks[i].elapsed_time(marks[i + 1]))
+    names = sorted(per)
+    med = [sorted(per[k])[len(per[k]) // 2] for k in names]
     if dist_on:
-        t = torch.tensor([ms], device=device)
+        t = torch.tensor([ms] + med, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return ms
+        ms, med = float(t[0].item()), t[1:].tolist()
+    return ms, {k: [round(m, 3), len(per[k])] for k, m in zip(names, med)}
 
 
 def run_ours(a, info):
@@ -194,26 +211,40 @@ def run_ours(a, info):
         loss = engine.step([(x, y)], lr=3e-4)
         return float(loss.item())
 
+    from rational_optimizer_b200.utils.step_phases import step_kind
+
+    def kind():
+        return step_kind(engine)
+
     for _ in range(a.warmup):
         device_step()
     sampler = ClockSampler(device.index or 0) if info.rank == 0 else None
     if sampler:
         sampler.start()
-    ms = timed(device_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all)
+    start_step = counter["i"]
+    ms, split = timed(device_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all,
+                      kind=kind)
     clocks = sampler.stop() if sampler else None
-    e2e_ms = None
+    e2e_ms = e2e_split = None
     if not a.no_e2e:
-        for _ in range(2):
+        # start the end-to-end window at the same phase of the optimizer's
+        # 8-step refresh cadence as the device-timed window, so both hold the
+        # same number of refresh steps
+        done = a.warmup + a.steps
+        extra = 2 + (start_step - (done + 2)) % 8
+        for _ in range(extra):
             e2e_step()
-        e2e_ms = timed(e2e_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all)
+        e2e_ms, e2e_split = timed(e2e_step, a.steps, device, info.is_distributed,
+                                  flush=param_ready.wait_all, kind=kind)
     launches = None
-    if not a.no_count_launches and not info.is_distributed:
+    if not a.no_count_launches:  # every rank profiles one step (same collective sequence)
         own, total = count_own_launches(device_step)
         launches = {"own_per_step": own, "all_per_step": total}
     loss = float(engine.step([staged[0]], lr=3e-4).item())
     if sync.communicator is not None:
         sync.communicator.check()
-    return ms, e2e_ms, clocks, launches, loss, batcher.bytes_per_batch, sync.transport
+    return (ms, e2e_ms, clocks, launches, loss, batcher.bytes_per_batch, sync.transport,
+            {"device": split, "e2e": e2e_split})
 
 
 def run_reference(a, info):
@@ -279,9 +310,12 @@ def run_reference(a, info):
     sampler = ClockSampler(device.index or 0) if info.rank == 0 else None
     if sampler:
         sampler.start()
-    ms = timed(lambda: one_step(True), a.steps, device, info.is_distributed)
+    ms, split = timed(lambda: one_step(True), a.steps, device, info.is_distributed)
     clocks = sampler.stop() if sampler else None
-    return ms, clocks
+    # the timed loop is already end to end: each step copies its batch from
+    # pinned host memory (sample_batch) and reads the loss back (loss.item())
+    h2d = 2 * args.batch_size * SEQ * tokens.element_size()
+    return ms, clocks, h2d
 
 
 def main():
@@ -312,7 +346,7 @@ def main():
                 print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
             cleanup_distributed(info)
             return
-        ms, clocks = res
+        ms, clocks, h2d = res
         value = tokens_per_step / (ms / 1000.0)
         if info.rank == 0:
             print(json.dumps({
@@ -321,10 +355,14 @@ def main():
                 "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": value / BASELINE_TOKENS_PER_S, "dtype": "fp32+tf32",
                 "data": "synthetic Zipf(1.1) token ids, seed 0; random-init weights",
-                "config": cfg, "clocks": clocks}), flush=True)
+                "config": cfg, "clocks": clocks,
+                "e2e": {"value": value, "unit": "tokens/s", "ms_per_step": ms,
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                        "note": "the reference's own step loop: sample_batch H2D copy and "
+                                "loss.item() inside every timed step"}}), flush=True)
         cleanup_distributed(info)
         return
-    ms, e2e_ms, clocks, launches, loss, h2d, transport = run_ours(a, info)
+    ms, e2e_ms, clocks, launches, loss, h2d, transport, split = run_ours(a, info)
     value = tokens_per_step / (ms / 1000.0)
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
@@ -334,6 +372,9 @@ def main():
         "config": cfg, "clocks": clocks, "final_loss": loss,
     }
     out["config"]["grad_transport"] = transport
+    # per-step device time by step kind: {kind: [median ms, steps]}; "refresh"
+    # steps run the optimizer's response-probe refresh (one in eight)
+    out["step_ms_by_kind"] = split
     if e2e_ms is not None:
         out["e2e"] = {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                       "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4}

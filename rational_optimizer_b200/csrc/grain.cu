@@ -1068,46 +1068,60 @@ extern "C" int ro_grain_backward_noalloc(const float* gy, const float* x, const 
                                          float* grad_den, int64_t rows, int hidden, int groups,
                                          float eps, cudaStream_t stream) {
   using namespace ro::grain;
-  if (gy == nullptr || x == nullptr || num == nullptr || den == nullptr || gx == nullptr ||
-      grad_num == nullptr || grad_den == nullptr)
-    return -1;
+  if (num == nullptr || den == nullptr || grad_num == nullptr || grad_den == nullptr) return -1;
+  // empty [0, hidden] tensors may come with null data pointers
+  if (rows > 0 && (gy == nullptr || x == nullptr || gx == nullptr)) return -1;
   if (groups <= 0 || hidden <= 0 || hidden % groups || rows < 0) return -1;
   const int w = hidden / groups;
   if (w > 256) return -1;
-  if (rows == 0) return 0;
-  int chunks, rpc;
-  plan_chunks(rows, groups, chunks, rpc);
+  int chunks = 0, rpc = 0;
+  if (rows > 0) plan_chunks(rows, groups, chunks, rpc);
   if (static_cast<int64_t>(chunks) * groups * kBase > kNoAllocScratchFloats) return -2;
   int setup = 0;
   float* partial = noalloc_scratch_for_current_device(&setup);
   if (partial == nullptr) return setup;
-  const bool aligned = (hidden % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(gy) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(gx) % 16 == 0);
-  const dim3 grid(chunks, groups);
-  bool ok = false;
-  if (aligned && (w == 256 || w == 128 || w == 64)) {
-    // same kernel choice as grain_backward, so both entry points agree bitwise
-    auto launch = [&](auto e) {
-      constexpr int E = decltype(e)::value;
-      backward_packed_kernel<float, float, float, E><<<grid, kThreads, 0, stream>>>(
-          gy, x, num, den, gx, partial, rows, hidden, groups, eps, rpc);
-    };
-    if (w == 256) launch(std::integral_constant<int, 8>{});
-    else if (w == 128) launch(std::integral_constant<int, 4>{});
-    else launch(std::integral_constant<int, 2>{});
-    ok = true;
-  } else {
-    ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
-      constexpr int E = decltype(e)::value;
-      constexpr bool C = decltype(contig)::value;
-      backward_kernel<float, float, float, E, C, kBase, false><<<grid, kThreads, 0, stream>>>(
-          gy, x, num, den, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, gx, partial, rows,
-          hidden, groups, 0, 0.0f, eps, rpc);
-    });
+  // Every launch goes through cudaLaunchKernelEx, which returns that launch's
+  // own status; an error left pending by some earlier, unrelated call is
+  // neither reported as this call's failure nor cleared.
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = stream;
+  cfg.blockDim = dim3(kThreads);
+  cfg.gridDim = dim3(chunks, groups);
+  cudaError_t err = cudaSuccess;
+  if (rows > 0) {
+    const bool aligned = (hidden % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(gy) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(gx) % 16 == 0);
+    bool ok = false;
+    if (aligned && (w == 256 || w == 128 || w == 64)) {
+      // same kernel choice as grain_backward, so both entry points agree bitwise
+      auto launch = [&](auto e) {
+        constexpr int E = decltype(e)::value;
+        err = cudaLaunchKernelEx(&cfg, backward_packed_kernel<float, float, float, E>, gy, x, num,
+                                 den, gx, partial, rows, hidden, groups, eps, rpc);
+      };
+      if (w == 256) launch(std::integral_constant<int, 8>{});
+      else if (w == 128) launch(std::integral_constant<int, 4>{});
+      else launch(std::integral_constant<int, 2>{});
+      ok = true;
+    } else {
+      ok = dispatch_layout(w, aligned, [&](auto e, auto contig) {
+        constexpr int E = decltype(e)::value;
+        constexpr bool C = decltype(contig)::value;
+        const float* none = nullptr;
+        float* none_out = nullptr;
+        err = cudaLaunchKernelEx(&cfg, backward_kernel<float, float, float, E, C, kBase, false>,
+                                 gy, x, num, den, none, none, none, none, none, none_out, gx,
+                                 partial, rows, hidden, groups, 0, 0.0f, eps, rpc);
+      });
+    }
+    if (!ok) return -1;
+    if (err != cudaSuccess) return static_cast<int>(err);
   }
-  if (!ok) return -1;
-  reduce_coeff_kernel<<<(groups * kBase + 127) / 128, 128, 0, stream>>>(partial, chunks, groups, 0,
-                                                                        grad_num, grad_den, nullptr);
-  return static_cast<int>(cudaGetLastError());
+  // With rows == 0 there are no partials (chunks == 0) and this writes zeros.
+  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3((groups * kBase + 127) / 128);
+  err = cudaLaunchKernelEx(&cfg, reduce_coeff_kernel, static_cast<const float*>(partial), chunks,
+                           groups, 0, grad_num, grad_den, static_cast<float*>(nullptr), 0);
+  return static_cast<int>(err);
 }

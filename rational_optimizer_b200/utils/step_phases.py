@@ -40,6 +40,8 @@ class PhaseTimer:
     def __init__(self, device=None):
         self.device = torch.device(device) if device is not None else None
         self.cuda = self.device is not None and self.device.type == "cuda"
+        self._kind = None
+        self._host0 = 0.0
         self._marks = []
         self._samples = {}
         self._patched = []
@@ -93,26 +95,38 @@ class PhaseTimer:
         self._patched = []
 
     # -- steps --------------------------------------------------------------
-    def begin_step(self):
+    def begin_step(self, kind=None):
+        """Open a step; ``kind`` (e.g. ``"plain"`` / ``"refresh"``) keys its samples separately."""
         self._marks = []
+        self._kind = kind
+        self._host0 = time.perf_counter()
         self.mark("step")
 
     def end_step(self, record=True):
         """Close the step; ``record=False`` discards it (warm-up)."""
+        host_ms = (time.perf_counter() - self._host0) * 1000.0
         self.mark("end")
         if self.cuda:
             torch.cuda.synchronize(self.device)
         if not record:
             return
+        prefix = f"{self._kind}:" if self._kind else ""
         for (a, ta), (b, tb) in zip(self._marks, self._marks[1:]):
-            self._samples.setdefault(f"{a}->{b}", []).append(self._elapsed_ms(ta, tb))
-        self._samples.setdefault("total", []).append(self._elapsed_ms(self._marks[0][1], self._marks[-1][1]))
+            self._samples.setdefault(f"{prefix}{a}->{b}", []).append(self._elapsed_ms(ta, tb))
+        self._samples.setdefault(f"{prefix}total", []).append(
+            self._elapsed_ms(self._marks[0][1], self._marks[-1][1]))
+        # host time to enqueue the step (no synchronisation inside the step)
+        self._samples.setdefault(f"{prefix}host_enqueue", []).append(host_ms)
 
     def _elapsed_ms(self, a, b):
         return a.elapsed_time(b) if self.cuda else (b - a) * 1000.0
 
     def summary(self, group=None):
-        """{interval: median ms}, MAX over ranks when a process group is up."""
+        """{interval: median ms}, MAX over ranks when a process group is up.
+
+        Every rank must have recorded the same interval names (the same step
+        kinds), since the reduction is one collective over the sorted names.
+        """
         names = sorted(self._samples)
         med = []
         for n in names:
@@ -124,6 +138,12 @@ class PhaseTimer:
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
             med = t.tolist()
         return dict(zip(names, med))
+
+
+def step_kind(engine):
+    """``"refresh"`` when the next step of ``engine`` runs the TILLER response refresh, else ``"plain"``."""
+    probe = getattr(engine.optimizer, "eager_step_required", None)
+    return "refresh" if probe is not None and probe() else "plain"
 
 
 def main(argv=None):
@@ -138,7 +158,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=MODEL["layers"])
     ap.add_argument("--global-batch", type=int, default=32)
-    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--warmup", type=int, default=4)
     a = ap.parse_args(argv)
     info = setup_distributed()
@@ -159,7 +179,7 @@ def main(argv=None):
     staged = [batcher.to_device(info.device, batcher.next_host().clone()) for _ in range(4)]
     timer = PhaseTimer.attach(engine)
     for i in range(a.warmup + a.steps):
-        timer.begin_step()
+        timer.begin_step(step_kind(engine))
         engine.step([staged[i % len(staged)]], lr=3e-4)
         param_ready.wait_all()  # owners' deferred broadcasts inside the step
         timer.end_step(record=i >= a.warmup)

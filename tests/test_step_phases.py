@@ -28,12 +28,40 @@ def test_phase_timer_on_tiller_engine():
     out = timer.summary()
     timer.detach()
     assert engine.optimizer.optimizers[0].step == original
-    names = [n for n in out if n != "total"]
+    names = [n for n in out if n not in ("total", "host_enqueue")]
     assert "step->grad_sync>" in names and "router_apply>->router_apply<" in names
     assert any(n.startswith("TILLERRouter[0]>") for n in names)
     assert all(v >= 0.0 for v in out.values())
     # consecutive intervals add up to the whole step
     assert abs(sum(out[n] for n in names) - out["total"]) <= 1e-6 * out["total"] + 1e-6
+
+
+def test_phase_timer_keys_samples_by_step_kind():
+    from rational_optimizer_b200.utils.step_phases import step_kind
+
+    args = model_args(layers=2, d_model=64, heads=4, ffn_dim=128, seq_len=16, activation="grain",
+                      rational_group_size=32, optimizer="tiller_v1", lr=3e-4, weight_decay=0.1,
+                      muon_momentum=0.95, muon_ns_steps=5, beta1=0.9, beta2=0.95, eps=1e-8,
+                      muon_adjust_lr_fn="match_rms_adamw", grad_accum=1)
+    torch.manual_seed(0)
+    model = CausalTransformer(args, 100)
+    engine = TrainEngine(model, composite.configure_optimizer(model, args),
+                         synchronizer=GradientSynchronizer(model))
+    timer = PhaseTimer.attach(engine)
+    gen = torch.Generator().manual_seed(1)
+    kinds = []
+    for _ in range(10):
+        t = torch.randint(0, 100, (2, 17), generator=gen)
+        kinds.append(step_kind(engine))
+        timer.begin_step(kinds[-1])
+        engine.step([(t[:, :-1], t[:, 1:])], lr=3e-4)
+        timer.end_step()
+    out = timer.summary()
+    timer.detach()
+    # the response refresh runs on router transitions 0 and 8 (cadence 8)
+    assert kinds == ["refresh"] + ["plain"] * 7 + ["refresh", "plain"]
+    assert "refresh:total" in out and "plain:total" in out
+    assert "plain:host_enqueue" in out and "total" not in out
 
 
 def test_composite_step_matches_children_in_order():

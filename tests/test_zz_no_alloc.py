@@ -77,3 +77,18 @@ def test_noalloc_rejects_oversized_problem_without_launching():
     assert torch.isnan(gnum).all()  # nothing was written
     rc, *_ = _call(fn, x, gy, num, den, 7, 1e-6)  # 7000 / 7 = 1000 > 256: unsupported width
     assert rc == -1
+
+
+def test_noalloc_zero_rows_writes_zero_coefficient_gradients():
+    fn = _entry()
+    x = torch.zeros(0, 768, device="cuda")
+    gy = torch.zeros_like(x)
+    num = torch.ones(3, 6, device="cuda")
+    den = torch.ones(3, 4, device="cuda")
+    for _ in range(2):
+        rc, gx, gnum, gden = _call(fn, x, gy, num, den, 3, 1e-6)
+        torch.cuda.synchronize()
+        assert rc == 0
+        assert gx.numel() == 0
+        assert torch.equal(gnum, torch.zeros_like(gnum))  # NaN-filled before the call
+        assert torch.equal(gden, torch.zeros_like(gden))
