@@ -81,13 +81,27 @@ class Attention(nn.Module):
 
 
 class SwiGLU(nn.Module):
+    """``down(silu(gate(x)) * value(x))``.
+
+    ``tap``: optional instrumentation callable; when set, every forward calls
+    ``tap(self, x, gate, value, features, output)`` with the tensors the
+    forward actually computed (the SwiGLU-TILLER optimizer records its probe
+    rows this way).  It does not change the computation.
+    """
+
     def __init__(self, c):
         super().__init__()
         d, h = c["hidden_size"], c["intermediate_size"]
         self.gate, self.value, self.down = Linear(d, h), Linear(d, h), Linear(h, d)
+        self.tap = None
 
     def forward(self, x):
-        return self.down(F.silu(self.gate(x)) * self.value(x))
+        g, v = self.gate(x), self.value(x)
+        h = F.silu(g) * v
+        y = self.down(h)
+        if self.tap is not None:
+            self.tap(self, x, g, v, h, y)
+        return y
 
 
 class GrainMLP(nn.Module):

@@ -1,24 +1,27 @@
-"""Portable torchrun trainer of the MHA study (reference experiments/mha_1b_tokens/train.py:1-278).
+"""Portable torchrun trainer of the MHA study (behaviour of
+experiments/mha_1b_tokens/train.py:1-278; same CLI, outputs and checkpoints).
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m rational_optimizer_b200.mha.train \\
         --condition grain_tiller --data caches/manifest.json --output runs/grain_tiller \\
         [--config config.json] [--resume latest] [--microbatch M --accumulation A] \\
         [--max-hours H] [--stop-after U] [--device cpu]
 
-Every update reads disjoint packed windows (:class:`PackedBatches`), the LR
-follows warm-up + cosine to ``min_lr_ratio`` at the schedule horizon, the
-gradient norm is clipped once at 1.0, validation runs every
-``validation_every`` updates on a fixed prefix of the validation cache, and
-checkpoints are atomic and checksum-verified at update boundaries
-(periodic / switch / final / continuation).  A resumed run verifies the
-run identity (config, data manifest, world size, condition) and that the
-next batch is the one the interrupted run would have read; metric records
-past the durable checkpoint are archived, never silently kept.  Each rank
-runs on its own GPU with gradients averaged by the package's synchroniser.
+:class:`StudyRun` owns one run: it verifies the token caches, fixes the run
+identity (condition, config digest, data-manifest digest, world size,
+precision) and the output directory, builds the seeded model and the
+condition's optimizer, and optionally resumes from a verified checkpoint.
+``StudyRun.update`` performs one optimizer update over ``accumulation``
+disjoint packed micro-batches (gradients averaged by the package's
+synchroniser, clip at 1.0, warm-up + cosine LR); validation runs every
+``validation_every`` updates on a fixed prefix of the validation cache;
+checkpoints (periodic / switch / final / continuation) go through
+:class:`~.checkpoint.CheckpointStore`.  On resume, metric records past the
+durable checkpoint are archived to ``metrics-abandoned-*.jsonl``, never kept.
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import fcntl
 import hashlib
 import json
@@ -40,274 +43,369 @@ from .data import PackedBatches, atomic_json, digest, object_digest
 from .model import ModernMHADecoder, copy_shared
 from .optim import build_optimizer
 
+TELEMETRY_EVERY = 100
 
-def initial_model(cfg, condition):
-    """Seeded SwiGLU model; GRAIN conditions copy its shared tensors so every condition starts alike."""
-    random.seed(cfg["seed"])
-    np.random.seed(cfg["seed"])
-    torch.manual_seed(cfg["seed"])
-    base = ModernMHADecoder(cfg["model"])
-    if condition in GRAIN_CONDITIONS:
-        model = ModernMHADecoder(cfg["model"], grain=True, groups=cfg["grain"]["groups"])
-        copied = copy_shared(base, model)
-    else:
-        model = base
-        copied = [n for n, _ in model.named_parameters() if ".mlp." not in n]
+
+def _shared_digest(model, names):
+    """SHA-256 over (name, raw bytes) of the named parameters, in model order."""
     h = hashlib.sha256()
+    wanted = set(names)
     for name, p in model.named_parameters():
-        if name in copied:
+        if name in wanted:
             h.update(name.encode())
             h.update(p.detach().contiguous().numpy().tobytes())
-    return model, h.hexdigest()
+    return h.hexdigest()
+
+
+def initial_model(cfg, condition):
+    """(model, digest of its shared initial tensors).
+
+    Every condition starts from the same seeded SwiGLU decoder; GRAIN
+    conditions take over its attention, norm and embedding tensors, so the
+    digest of the tensors the conditions share is equal across conditions.
+    """
+    seed = cfg["seed"]
+    random.seed(seed)
+    np.random.seed(seed)
+    torch.manual_seed(seed)
+    swiglu = ModernMHADecoder(cfg["model"])
+    if condition not in GRAIN_CONDITIONS:
+        return swiglu, _shared_digest(swiglu, [n for n, _ in swiglu.named_parameters() if ".mlp." not in n])
+    grain = ModernMHADecoder(cfg["model"], grain=True, groups=cfg["grain"]["groups"])
+    return grain, _shared_digest(grain, copy_shared(swiglu, grain))
 
 
 def batch_hash(data, update, rank):
+    """Digest of this rank's first micro-batch of ``update`` ("END" past the cache)."""
     try:
-        x, y, mask = data.batch(update, 0, rank)
+        arrays = data.batch(update, 0, rank)
     except IndexError:
         return "END"
-    return hashlib.sha256(x.tobytes() + y.tobytes() + mask.tobytes()).hexdigest()
-
-
-def train_step(model, optimizer, sync, data, completed, cfg, device, rank, world):
-    optimizer.zero_grad()
-    sync.zero_grad()
-    if optimizer.router is not None and (completed + 1) % 100 == 0:
-        optimizer.router.set_telemetry_capture(True)
-        optimizer.attention.set_telemetry_capture(True)
-    lr = schedule(completed, cfg, cfg["conditions"][optimizer.condition]["lr"])
-    for g in optimizer.param_groups:
-        g["lr"] = lr
-    count = 0
-    summed = torch.zeros((), device=device)
-    for micro in range(cfg["accumulation"]):
-        x, y, mask = data.batch(completed, micro, rank)
-        if not mask.all():
-            raise RuntimeError("the packing protocol requires every target to be loss-bearing")
-        count += int(mask.sum())
-        value = model.forward_loss(torch.from_numpy(x).to(device), torch.from_numpy(y).to(device))
-        if micro == cfg["accumulation"] - 1:
-            sync.begin_backward()
-        (value / cfg["accumulation"]).backward()
-        summed += value.detach().float() / cfg["accumulation"]
-    sync.synchronize()
-    total = torch.tensor([count], device=device, dtype=torch.int64)
-    if dist.is_initialized():
-        dist.all_reduce(total)
-    if int(total.item()) != cfg["loss_tokens_per_update"]:
-        raise RuntimeError("actual mask count differs")
-    norm = optimizer.clip_grad_norm()
-    if device.type == "cuda":
-        torch.cuda.synchronize(device)
-    t0 = time.perf_counter()
-    optimizer.step()
-    if device.type == "cuda":
-        torch.cuda.synchronize(device)
-    opt_seconds = time.perf_counter() - t0
-    if dist.is_initialized():
-        dist.all_reduce(summed)
-    value = float(summed / world)
-    if not math.isfinite(value):
-        raise RuntimeError("nonfinite training loss")
-    return dict(loss=value, lr=lr, loss_tokens_this_update=int(total.item()), gradient_norm=float(norm),
-                optimizer_seconds=opt_seconds,
-                phase=getattr(optimizer, "phase", "tiller" if optimizer.router is not None else "baseline"),
-                optimizer_child_lrs={role: [g["lr"] for g in child.param_groups]
-                                     for role, child in zip(optimizer.roles, optimizer.children)})
-
-
-@torch.no_grad()
-def validation(model, path, cfg, device, rank, world):
-    ids = np.memmap(path, dtype="<u4", mode="r")
-    context, tokens = cfg["context"], cfg["small_validation_tokens"]
-    if tokens % context or len(ids) <= tokens:
-        raise ValueError("validation cache too short or unaligned")
-    total = torch.zeros(2, device=device, dtype=torch.float64)
-    was_training = model.training
-    model.eval()
-    try:
-        for index in range(rank, tokens // context, world):
-            block = torch.from_numpy(np.array(ids[index * context:(index + 1) * context + 1], dtype=np.int64)).to(device)[None]
-            value = model.forward_loss(block[:, :-1], block[:, 1:])
-            total += torch.stack((value.double() * context, value.new_tensor(context).double()))
-    finally:
-        model.train(was_training)
-    if dist.is_initialized():
-        dist.all_reduce(total)
-    if int(total[1]) != tokens:
-        raise RuntimeError("validation token count differs")
-    value = float(total[0] / total[1])
-    if not math.isfinite(value):
-        raise RuntimeError("nonfinite validation loss")
-    return value
+    return hashlib.sha256(b"".join(a.tobytes() for a in arrays)).hexdigest()
 
 
 def reconcile_metrics(path: Path, completed: int):
-    """Keep records up to the durable checkpoint; archive the rest."""
+    """Keep the records up to the durable checkpoint; archive the others (a torn
+    last line included) to ``metrics-abandoned-<ns>.jsonl``."""
     if not path.exists():
         return
     lines = path.read_text().splitlines(True)
-    kept, abandoned = [], []
+    keep, drop = [], []
     for i, line in enumerate(lines):
         try:
-            rec = json.loads(line)
+            step = json.loads(line)["step"]
         except json.JSONDecodeError:
-            if i != len(lines) - 1:
-                raise RuntimeError("corrupt metrics before the final line")
-            abandoned.append(line)
+            if i + 1 != len(lines):
+                raise RuntimeError(f"{path}: unreadable record on line {i + 1} of {len(lines)}")
+            drop.append(line)
             continue
-        (kept if rec["step"] <= completed else abandoned).append(line)
-    if abandoned:
-        with path.with_name(f"metrics-abandoned-{time.time_ns()}.jsonl").open("x") as fh:
-            fh.writelines(abandoned)
+        (keep if step <= completed else drop).append(line)
+    if not drop:
+        return
+
+    def durable(target, records):
+        with target.open("x") as fh:
+            fh.writelines(records)
             fh.flush()
             os.fsync(fh.fileno())
-        tmp = path.with_name(f".metrics-{time.time_ns()}.partial")
-        with tmp.open("x") as fh:
-            fh.writelines(kept)
-            fh.flush()
-            os.fsync(fh.fileno())
-        os.replace(tmp, path)
+
+    stamp = time.time_ns()
+    durable(path.with_name(f"metrics-abandoned-{stamp}.jsonl"), drop)
+    staged = path.with_name(f".metrics-{stamp}.partial")
+    durable(staged, keep)
+    os.replace(staged, path)
+
+
+class StudyRun:
+    """One condition's training run on this rank."""
+
+    def __init__(self, a):
+        self.started = time.monotonic()
+        self.args = a
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.rank = int(os.environ.get("RANK", 0))
+        local = int(os.environ.get("LOCAL_RANK", 0))
+        self.device = torch.device("cuda", local) if a.device == "cuda" else torch.device("cpu")
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        if self.world > 1 and not dist.is_initialized():
+            dist.init_process_group("nccl" if self.device.type == "cuda" else "gloo",
+                                    timeout=datetime.timedelta(seconds=600))
+        self.cfg = self._config()
+        self.paths = self._verified_caches()
+        cfg = self.cfg
+        self.data = PackedBatches(self.paths["train"], world_size=self.world, microbatch=cfg["microbatch"],
+                                  accumulation=cfg["accumulation"], context=cfg["context"])
+        # the whole schedule must be readable before the first update
+        self.data.batch(cfg["updates"] - 1, cfg["accumulation"] - 1, self.world - 1)
+        precision = "bf16_gemm_fp32_master" if self.device.type == "cuda" else "cpu_fp32"
+        self.identity = {"schema": 1, "condition": a.condition, "config": object_digest(cfg),
+                         "data": digest(a.data), "world_size": self.world, "precision": precision}
+        self.output = a.output
+        self._lock = self._claim_output()
+        model, self.shared_digest = initial_model(cfg, a.condition)
+        self.parameter_count = sum(p.numel() for p in model.parameters())
+        self.model = model.to(self.device)
+        if self.device.type == "cpu":  # fp32 GEMM outputs on the CPU oracle path
+            for m in self.model.modules():
+                if hasattr(m, "out_dtype"):
+                    m.out_dtype = None
+        self.sync = GradientSynchronizer(self.model)
+        self.optimizer = build_optimizer(self.model, a.condition, cfg["conditions"][a.condition]["lr"],
+                                         cfg["accumulation"])
+        self.store = checkpoint.CheckpointStore(self.output, self.identity)
+        self.completed = 0
+        self.last_saved = -1
+
+    # -- set-up -------------------------------------------------------------
+    def _config(self):
+        a = self.args
+        cfg = json.loads(a.config.read_text()) if a.config else default_config()
+        cfg["world_size"] = self.world
+        for key in ("microbatch", "accumulation"):
+            if getattr(a, key) is not None:
+                cfg[key] = getattr(a, key)
+        validate_config(cfg)
+        if a.max_hours is not None and a.max_hours * 3600 <= a.checkpoint_margin_seconds:
+            raise ValueError("--max-hours leaves no time beyond the checkpoint margin")
+        if a.stop_after is not None and not 1 <= a.stop_after <= cfg["updates"]:
+            raise ValueError(f"--stop-after must be within 1..{cfg['updates']}")
+        return cfg
+
+    def _verified_caches(self):
+        manifest = json.loads(self.args.data.read_text())
+        if manifest["dtype"] != "<u4":
+            raise ValueError(f"token caches must be little-endian uint32, manifest says {manifest['dtype']}")
+        paths = {}
+        for split in ("train", "validation"):
+            entry = manifest["splits"][split]
+            p = Path(entry["path"])
+            p = p if p.is_absolute() else self.args.data.parent / p
+            if self.rank == 0 and (p.stat().st_size != 4 * entry["tokens"] or digest(p) != entry["sha256"]):
+                raise RuntimeError(f"{split} cache {p} does not match its manifest entry")
+            paths[split] = p
+        checkpoint.barrier()
+        return paths
+
+    def _claim_output(self):
+        """Lock the output directory (rank 0) and record or check the run identity."""
+        self.output.mkdir(parents=True, exist_ok=True)
+        lock = None
+        if self.rank == 0:
+            lock = (self.output / "trainer.lock").open("a")
+            fcntl.flock(lock, fcntl.LOCK_EX | fcntl.LOCK_NB)
+            recorded = self.output / "identity.json"
+            if recorded.exists():
+                if not self.args.resume or json.loads(recorded.read_text()) != self.identity:
+                    raise RuntimeError(f"{self.output} holds another run; resume it with a matching "
+                                       "identity or choose a new output")
+            elif self.args.resume:
+                raise RuntimeError(f"nothing to resume in {self.output}")
+            else:
+                atomic_json(recorded, self.identity)
+                atomic_json(self.output / "resolved_config.json", self.cfg)
+        checkpoint.barrier()
+        return lock
+
+    def resume(self):
+        spec = self.args.resume
+        if not spec:
+            return
+        manifest = (json.loads((self.output / "latest.json").read_text())["manifest"] if spec == "latest"
+                    else spec)
+        self.completed = self.store.load(manifest, self.model, self.optimizer,
+                                         lambda u: batch_hash(self.data, u, self.rank))
+        self.last_saved = self.completed
+        if self.rank == 0:
+            reconcile_metrics(self.output / "metrics.jsonl", self.completed)
+        checkpoint.barrier()
+
+    # -- one update ------------------------------------------------------------
+    def update(self):
+        cfg, opt, device = self.cfg, self.optimizer, self.device
+        accum = cfg["accumulation"]
+        opt.zero_grad()
+        self.sync.zero_grad()
+        if opt.router is not None and (self.completed + 1) % TELEMETRY_EVERY == 0:
+            opt.router.set_telemetry_capture(True)
+            opt.attention.set_telemetry_capture(True)
+        lr = schedule(self.completed, cfg, cfg["conditions"][opt.condition]["lr"])
+        for g in opt.param_groups:
+            g["lr"] = lr
+        tokens = 0
+        loss_sum = torch.zeros((), device=device)
+        for micro in range(accum):
+            x, y, mask = self.data.batch(self.completed, micro, self.rank)
+            if not mask.all():
+                raise RuntimeError("packed batches must have every target loss-bearing")
+            tokens += int(mask.sum())
+            loss = self.model.forward_loss(torch.from_numpy(x).to(device), torch.from_numpy(y).to(device))
+            if micro + 1 == accum:
+                self.sync.begin_backward()  # the last backward's gradients are final
+            (loss / accum).backward()
+            loss_sum += loss.detach().float() / accum
+        self.sync.synchronize()
+        counts = torch.tensor([tokens], device=device, dtype=torch.int64)
+        if dist.is_initialized():
+            dist.all_reduce(counts)
+        if int(counts.item()) != cfg["loss_tokens_per_update"]:
+            raise RuntimeError(f"{int(counts.item())} loss tokens this update, the config says "
+                               f"{cfg['loss_tokens_per_update']}")
+        norm = opt.clip_grad_norm()
+        seconds = self._timed(opt.step)
+        if dist.is_initialized():
+            dist.all_reduce(loss_sum)
+        loss = float(loss_sum / self.world)
+        if not math.isfinite(loss):
+            raise RuntimeError(f"training loss became {loss} at update {self.completed + 1}")
+        self.completed += 1
+        phase = getattr(opt, "phase", "tiller" if opt.router is not None else "baseline")
+        return {"loss": loss, "lr": lr, "loss_tokens_this_update": int(counts.item()),
+                "gradient_norm": float(norm), "optimizer_seconds": seconds, "phase": phase,
+                "optimizer_child_lrs": {role: [g["lr"] for g in child.param_groups]
+                                        for role, child in zip(opt.roles, opt.children)}}
+
+    def _timed(self, fn):
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        t0 = time.perf_counter()
+        fn()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        return time.perf_counter() - t0
+
+    @torch.no_grad()
+    def validate(self):
+        cfg = self.cfg
+        ids = np.memmap(self.paths["validation"], dtype="<u4", mode="r")
+        ctx, want = cfg["context"], cfg["small_validation_tokens"]
+        if want % ctx or len(ids) <= want:
+            raise ValueError(f"validation cache of {len(ids)} tokens cannot give {want} in windows of {ctx}")
+        acc = torch.zeros(2, device=self.device, dtype=torch.float64)
+        training = self.model.training
+        self.model.eval()
+        try:
+            for w in range(self.rank, want // ctx, self.world):
+                window = np.array(ids[w * ctx:(w + 1) * ctx + 1], dtype=np.int64)
+                block = torch.from_numpy(window).to(self.device)[None]
+                loss = self.model.forward_loss(block[:, :-1], block[:, 1:])
+                acc += torch.stack((loss.double() * ctx, loss.new_tensor(ctx).double()))
+        finally:
+            self.model.train(training)
+        if dist.is_initialized():
+            dist.all_reduce(acc)
+        if int(acc[1]) != want:
+            raise RuntimeError(f"validated {int(acc[1])} tokens, expected {want}")
+        value = float(acc[0] / acc[1])
+        if not math.isfinite(value):
+            raise RuntimeError(f"validation loss became {value}")
+        return value
+
+    # -- checkpoints -------------------------------------------------------------
+    def save(self, kind):
+        cfg = self.cfg
+        manifest = self.store.save(self.completed, kind, self.model, self.optimizer,
+                                   batch_hash(self.data, self.completed, self.rank))
+        if self.rank == 0:
+            atomic_json(self.output / "latest.json",
+                        {"manifest": str(manifest.resolve()), "update": self.completed,
+                         "tokens": self.completed * cfg["loss_tokens_per_update"]})
+            self.store.prune(cfg["checkpoint_keep_recent"])
+        checkpoint.barrier()
+        self.last_saved = self.completed
+
+    def _checkpoint_kind(self):
+        if self.completed == self.cfg["updates"]:
+            return "final"
+        if self.args.condition == MHA_SWITCH and self.completed in (C.SWITCH_UPDATE, C.SWITCH_UPDATE + 1):
+            return "switch"  # both sides of the TILLER -> Muon hand-off
+        if self.completed % self.cfg["checkpoint_every"] == 0:
+            return "periodic"
+        return None
+
+    def _should_stop(self):
+        a = self.args
+        by_count = a.stop_after is not None and self.completed >= a.stop_after
+        by_time = (a.max_hours is not None and time.monotonic() - self.started
+                   >= a.max_hours * 3600 - a.checkpoint_margin_seconds)
+        flag = torch.tensor(int(by_count or by_time), device=self.device)
+        if dist.is_initialized():
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)  # every rank stops at the same update
+        return bool(flag.item())
+
+    def _log(self, record):
+        if self.rank != 0:
+            return
+        line = json.dumps(record, allow_nan=False, default=float)
+        with (self.output / "metrics.jsonl").open("a") as fh:
+            fh.write(line + "\n")
+        print(line, flush=True)
+
+    # -- driver ------------------------------------------------------------------
+    def run(self):
+        cfg = self.cfg
+        if self.rank == 0:
+            atomic_json(self.output / "startup.json",
+                        {"parameter_count": self.parameter_count,
+                         "shared_initial_sha256": self.shared_digest,
+                         "resumed_update": self.completed, "identity": self.identity})
+        while self.completed < cfg["updates"]:
+            t0 = time.perf_counter()
+            record = self.update()
+            record.update(step=self.completed, loss_tokens=self.completed * cfg["loss_tokens_per_update"],
+                          seconds=time.perf_counter() - t0,
+                          peak_memory_bytes=(torch.cuda.max_memory_allocated(self.device)
+                                             if self.device.type == "cuda" else 0))
+            if self.completed % cfg["validation_every"] == 0 or self.completed == cfg["updates"]:
+                record["validation_loss"] = self.validate()
+            if self.optimizer.router is not None and self.completed % TELEMETRY_EVERY == 0:
+                record["tiller_telemetry"] = self.optimizer.router.telemetry()
+                record["attention_telemetry"] = self.optimizer.attention.telemetry()
+            self._log(record)
+            kind = self._checkpoint_kind()
+            if kind is not None:
+                self.save(kind)
+            if self._should_stop():
+                break
+        if 0 < self.completed != self.last_saved and self.completed != cfg["updates"]:
+            self.save("continuation")
+        if self.rank == 0:
+            atomic_json(self.output / "result.json",
+                        {"completed": self.completed == cfg["updates"], "update": self.completed,
+                         "loss_tokens": self.completed * cfg["loss_tokens_per_update"],
+                         "identity": self.identity})
+        checkpoint.barrier()
+
+    def close(self):
+        if getattr(self.sync, "communicator", None) is not None:
+            self.sync.communicator.close()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--condition", required=True, choices=C.CONDITIONS)
+    p.add_argument("--data", type=Path, required=True, help="manifest of the local uint32 token caches")
+    p.add_argument("--output", type=Path, required=True)
+    p.add_argument("--config", type=Path, default=None)
+    p.add_argument("--resume", help="a checkpoint manifest path, or 'latest' under --output")
+    p.add_argument("--microbatch", type=int)
+    p.add_argument("--accumulation", type=int)
+    p.add_argument("--max-hours", type=float, help="wall-time budget of this launch, margin included")
+    p.add_argument("--checkpoint-margin-seconds", type=float, default=900)
+    p.add_argument("--stop-after", type=int, help="stop (with a checkpoint) after this update")
+    p.add_argument("--device", choices=("cuda", "cpu"), default="cuda")
+    return p.parse_args(argv)
 
 
 def main(argv=None):
-    launch_started = time.monotonic()
-    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("--condition", required=True, choices=("swiglu_muon", "swiglu_adamw", "grain_tiller", MHA_SWITCH))
-    p.add_argument("--data", type=Path, required=True, help="local uint32 cache manifest")
-    p.add_argument("--output", type=Path, required=True)
-    p.add_argument("--config", type=Path, default=None)
-    p.add_argument("--resume", help="verified manifest path, or 'latest' under --output")
-    p.add_argument("--microbatch", type=int)
-    p.add_argument("--accumulation", type=int)
-    p.add_argument("--max-hours", type=float)
-    p.add_argument("--checkpoint-margin-seconds", type=float, default=900)
-    p.add_argument("--stop-after", type=int)
-    p.add_argument("--device", choices=("cuda", "cpu"), default="cuda")
-    a = p.parse_args(argv)
-    world = int(os.environ.get("WORLD_SIZE", 1))
-    rank = int(os.environ.get("RANK", 0))
-    local = int(os.environ.get("LOCAL_RANK", 0))
-    device = torch.device("cuda", local) if a.device == "cuda" else torch.device("cpu")
-    if device.type == "cuda":
-        torch.cuda.set_device(device)
-    if world > 1 and not dist.is_initialized():
-        import datetime
-        dist.init_process_group("nccl" if device.type == "cuda" else "gloo",
-                                timeout=datetime.timedelta(seconds=600))
-    cfg = json.loads(a.config.read_text()) if a.config else default_config()
-    cfg["world_size"] = world
-    if a.microbatch is not None:
-        cfg["microbatch"] = a.microbatch
-    if a.accumulation is not None:
-        cfg["accumulation"] = a.accumulation
-    validate_config(cfg)
-    if a.max_hours is not None and a.max_hours * 3600 <= a.checkpoint_margin_seconds:
-        raise ValueError("walltime is shorter than the checkpoint margin")
-    if a.stop_after is not None and not 1 <= a.stop_after <= cfg["updates"]:
-        raise ValueError("invalid stop boundary")
-    manifest = json.loads(a.data.read_text())
-    if manifest["dtype"] != "<u4":
-        raise ValueError("cache dtype differs")
-    paths = {}
-    for split in ("train", "validation"):
-        item = manifest["splits"][split]
-        path = Path(item["path"])
-        paths[split] = path if path.is_absolute() else a.data.parent / path
-        if rank == 0 and (digest(paths[split]) != item["sha256"] or paths[split].stat().st_size != 4 * item["tokens"]):
-            raise RuntimeError("cache checksum/size mismatch")
-    checkpoint.barrier()
-    data = PackedBatches(paths["train"], world_size=world, microbatch=cfg["microbatch"],
-                         accumulation=cfg["accumulation"], context=cfg["context"])
-    data.batch(cfg["updates"] - 1, cfg["accumulation"] - 1, world - 1)  # the whole horizon must be local
-    identity = dict(schema=1, condition=a.condition, config=object_digest(cfg), data=digest(a.data),
-                    world_size=world, precision="bf16_gemm_fp32_master" if device.type == "cuda" else "cpu_fp32")
-    a.output.mkdir(parents=True, exist_ok=True)
-    lock = None
-    if rank == 0:
-        lock = (a.output / "trainer.lock").open("a")
-        fcntl.flock(lock, fcntl.LOCK_EX | fcntl.LOCK_NB)
-        old = a.output / "identity.json"
-        if old.exists():
-            if not a.resume or json.loads(old.read_text()) != identity:
-                raise RuntimeError("existing output requires explicit resume with a matching identity")
-        elif a.resume:
-            raise RuntimeError("resume requires the original output directory")
-        else:
-            atomic_json(old, identity)
-            atomic_json(a.output / "resolved_config.json", cfg)
-    checkpoint.barrier()
-    model, shared_hash = initial_model(cfg, a.condition)
-    count = sum(p.numel() for p in model.parameters())
-    model = model.to(device)
-    if device.type == "cpu":
-        for m in model.modules():
-            if hasattr(m, "out_dtype"):
-                m.out_dtype = None
-    sync = GradientSynchronizer(model)
-    optimizer = build_optimizer(model, a.condition, cfg["conditions"][a.condition]["lr"], cfg["accumulation"])
-    completed = 0
-    if a.resume:
-        saved = json.loads((a.output / "latest.json").read_text())["manifest"] if a.resume == "latest" else a.resume
-        completed = checkpoint.load(saved, model, optimizer, identity, lambda u: batch_hash(data, u, rank))
-        if rank == 0:
-            reconcile_metrics(a.output / "metrics.jsonl", completed)
-        checkpoint.barrier()
-    if rank == 0:
-        atomic_json(a.output / "startup.json", dict(parameter_count=count, shared_initial_sha256=shared_hash,
-                                                    resumed_update=completed, identity=identity))
-    saved_update = completed if a.resume else -1
-
-    def save(kind):
-        nonlocal saved_update
-        mp = checkpoint.save(a.output / f"checkpoint-{completed:06d}-{kind}", model, optimizer, completed, identity,
-                             batch_hash(data, completed, rank))
-        if rank == 0:
-            atomic_json(a.output / "latest.json", dict(manifest=str(mp.resolve()), update=completed,
-                                                       tokens=completed * cfg["loss_tokens_per_update"]))
-            checkpoint.prune_periodic(a.output, identity, cfg["checkpoint_keep_recent"])
-        checkpoint.barrier()
-        saved_update = completed
-
-    while completed < cfg["updates"]:
-        tick = time.perf_counter()
-        metrics = train_step(model, optimizer, sync, data, completed, cfg, device, rank, world)
-        completed += 1
-        metrics.update(step=completed, loss_tokens=completed * cfg["loss_tokens_per_update"],
-                       seconds=time.perf_counter() - tick,
-                       peak_memory_bytes=torch.cuda.max_memory_allocated(device) if device.type == "cuda" else 0)
-        if completed % cfg["validation_every"] == 0 or completed == cfg["updates"]:
-            metrics["validation_loss"] = validation(model, paths["validation"], cfg, device, rank, world)
-        if optimizer.router is not None and completed % 100 == 0:
-            metrics["tiller_telemetry"] = optimizer.router.telemetry()
-            metrics["attention_telemetry"] = optimizer.attention.telemetry()
-        if rank == 0:
-            with (a.output / "metrics.jsonl").open("a") as fh:
-                fh.write(json.dumps(metrics, allow_nan=False, default=float) + "\n")
-            print(json.dumps(metrics, allow_nan=False, default=float), flush=True)
-        boundary = a.condition == MHA_SWITCH and completed in (C.SWITCH_UPDATE, C.SWITCH_UPDATE + 1)
-        final = completed == cfg["updates"]
-        if boundary or final or completed % cfg["checkpoint_every"] == 0:
-            save("final" if final else "switch" if boundary else "periodic")
-        stop = torch.tensor(int((a.stop_after is not None and completed >= a.stop_after) or
-                                (a.max_hours is not None and
-                                 time.monotonic() - launch_started >= a.max_hours * 3600 - a.checkpoint_margin_seconds)),
-                            device=device)
-        if dist.is_initialized():
-            dist.all_reduce(stop, op=dist.ReduceOp.MAX)
-        if stop.item():
-            break
-    if completed > 0 and completed != saved_update and completed != cfg["updates"]:
-        save("continuation")
-    if rank == 0:
-        atomic_json(a.output / "result.json", dict(completed=completed == cfg["updates"], update=completed,
-                                                   loss_tokens=completed * cfg["loss_tokens_per_update"],
-                                                   identity=identity))
-    checkpoint.barrier()
-    if getattr(sync, "communicator", None) is not None:
-        sync.communicator.close()
-    if dist.is_initialized():
-        dist.destroy_process_group()
+    run = StudyRun(parse_args(argv))
+    run.resume()
+    try:
+        run.run()
+    finally:
+        run.close()
     return 0
 
 

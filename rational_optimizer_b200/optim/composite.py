@@ -174,8 +174,12 @@ class TILLERCompositeOptimizer(CompositeOptimizer):
             router.finish_step()
 
     def eager_step_required(self):
-        """True when this step's forward/backward must run eagerly (response-probe refresh)."""
+        """True when this step's forward/backward records response probes (refresh step)."""
         return bool(self.router._capture_response_this_transition)
+
+    def probe_recorder(self):
+        """The child whose forward/backward hooks record probes (see ``train.graphs``)."""
+        return self.router
 
     def record_realized_clipping(self, preclip_norm, max_norm):
         self.optimizers[0].record_realized_clipping(preclip_norm, max_norm)

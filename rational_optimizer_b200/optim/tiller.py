@@ -30,6 +30,7 @@ parameter order are those of the reference so ``state_dict`` round-trips.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 import os
 
@@ -409,6 +410,33 @@ class TILLERRouter(torch.optim.Optimizer):
             output.register_hook(capture_gradient)
             return None
         return capture
+
+    # -- probe records for captured steps ------------------------------------
+    @contextlib.contextmanager
+    def probes_forced(self, enabled=True):
+        """Switch the probe hooks on or off regardless of the cadence (graph captures)."""
+        saved = self._capture_response_this_transition
+        self._capture_response_this_transition = bool(enabled)
+        try:
+            yield
+        finally:
+            self._capture_response_this_transition = saved
+
+    def take_probe_records(self):
+        """Detach and return the records the hooks made; the router holds none afterwards."""
+        if any(p is not None for p in self._pending_inputs):
+            raise RuntimeError("TILLER probe input remained unmatched")
+        records = (self._functional_records, self._cotangent_records)
+        self._functional_records = [[] for _ in self.pairs]
+        self._cotangent_records = [[] for _ in self.pairs]
+        return records
+
+    def restore_probe_records(self, records):
+        """Install records made by a captured forward/backward (their tensors are
+        rewritten by every replay of that graph) as this step's probes."""
+        functional, cotangent = records
+        self._functional_records = [list(r) for r in functional]
+        self._cotangent_records = [list(r) for r in cotangent]
 
     def remove_hooks(self):
         for h in self._hook_handles:

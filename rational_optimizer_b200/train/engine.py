@@ -70,49 +70,81 @@ class TrainEngine:
         if clip_observer is None and hasattr(optimizer, "record_realized_clipping"):
             self.clip_observer = optimizer
         self.last_grad_norm = None
-        self._graph = None
+        self._graphs = {}  # "plain" / "refresh" -> StepGraph
         self._graph_state = "off" if not graphs_requested() else "pending"
-        self._plain_steps = 0
+        self._eligible_steps = 0
 
-    def _graph_eligible(self, batches):
+    def _graph_kind(self, batches):
+        """``"plain"`` or ``"refresh"`` when this step may replay a captured graph, else None."""
         if self._graph_state in ("off", "failed") or len(batches) != 1:
-            return False
+            return None
         if self.sync.world > 1 and os.environ.get("RO_CUDA_GRAPH_DIST", "1") != "1":
-            return False
+            return None
         x, y = batches[0]
         if not x.is_cuda:
-            return False
-        # only optimizers that say which steps need hooks in the forward/backward
-        eager = getattr(self.optimizer, "eager_step_required", None)
-        if eager is None or eager():
-            return False
+            return None
+        # only optimizers that say which steps record probes in the forward/backward
+        probes = getattr(self.optimizer, "eager_step_required", None)
+        if probes is None:
+            return None
+        kind = "plain"
+        if probes():
+            if os.environ.get("RO_REFRESH_GRAPH", "1") != "1" or self._recorder() is None:
+                return None
+            kind = "refresh"
         if any(getattr(m, "_rlb_optimizer_track_stats", False) for m in self.model.modules()):
-            return False
-        return self._graph is None or self._graph.matches(x, y)
+            return None
+        graph = self._graphs.get("plain")
+        if graph is not None and not graph.matches(x, y):
+            return None
+        return kind
 
-    def _graphed_forward_backward(self, x, y):
-        """The loss via the captured graph, or None (eager path) when capture is not possible."""
-        if self._graph is not None and self._graph.graph is None:
-            self._graph = None  # released (process-group teardown): capture again if stepped
-        if self._graph is None:
-            self._plain_steps += 1
-            # one complete plain step first (lazily created optimizer state,
-            # weight casts); capture on the second, so any run with three or
-            # more warm-up steps has captured before it is timed
-            if self._plain_steps < 2:
+    def _recorder(self):
+        get = getattr(self.optimizer, "probe_recorder", None)
+        return get() if get is not None else None
+
+    def _capture_graphs(self, x, y):
+        recorder = self._recorder()
+        graphs = {"plain": StepGraph(self.model, self.sync, x, y, recorder=recorder, probes=False)}
+        if recorder is not None and os.environ.get("RO_REFRESH_GRAPH", "1") == "1":
+            # the plain graph's capture warmed everything up; one warm-up
+            # pass initialises the probe hooks' own work
+            graphs["refresh"] = StepGraph(self.model, self.sync, x, y, warmup=1, recorder=recorder,
+                                          probes=True)
+        for g in graphs.values():
+            g.capture()
+        return graphs
+
+    def _graphed_forward_backward(self, x, y, kind):
+        """The loss via a captured graph, or None (eager path) when capture is not possible."""
+        if any(g.graph is None for g in self._graphs.values()):
+            self._graphs = {}  # released (process-group teardown): capture again if stepped
+        if not self._graphs:
+            self._eligible_steps += 1
+            # one complete step first (lazily created optimizer state, weight
+            # casts); capture on the second, so any run with three or more
+            # warm-up steps has captured before it is timed
+            if self._eligible_steps < 2:
                 return None
             try:
-                g = StepGraph(self.model, self.sync, x, y)
-                g.capture()
-                self._graph = g
+                self._graphs = self._capture_graphs(x, y)
                 self._graph_state = "on"
             except Exception as exc:  # an operation that cannot be captured
+                for g in self._graphs.values():
+                    g.release()
+                self._graphs = {}
                 self._graph_state = "failed"
                 self.graph_error = f"{type(exc).__name__}: {exc}"
+                recorder = self._recorder()
+                if recorder is not None:
+                    recorder.take_probe_records()
                 self.sync.zero_grad()
                 return None
+        graph = self._graphs.get(kind)
+        if graph is None:
+            return None
         self.sync.zero_grad()
-        return self._graph.replay(x, y)
+        return graph.replay(x, y)
 
     def set_lr(self, lr):
         for group in self.optimizer.param_groups:
@@ -124,8 +156,9 @@ class TrainEngine:
             raise ValueError("expected one batch per micro-step")
         if lr is not None:
             self.set_lr(lr)
-        if self._graph_eligible(batches):
-            loss = self._graphed_forward_backward(*batches[0])
+        kind = self._graph_kind(batches)
+        if kind is not None:
+            loss = self._graphed_forward_backward(*batches[0], kind)
             if loss is not None:
                 return self._finish(loss)
         self.sync.zero_grad()

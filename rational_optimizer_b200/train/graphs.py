@@ -8,14 +8,20 @@ forward and backward.  ``StepGraph`` captures ``forward_loss`` +
 buffers, weights cast to bf16 inside the graph because they change between
 replays) and replays it on later steps; the optimizer step stays eager.
 
-Steps that need host-side work inside the forward or backward (TILLER's
-response-probe refresh, telemetry statistics, a different micro-batch shape)
-run eagerly; the graph is kept and used again on the next plain step.
-Capture failures (an operation that cannot be recorded) disable graphs for
-the run and the engine continues eagerly.
+TILLER's response-probe refresh steps get a graph of their own: with a
+``recorder`` (the optimizer child whose hooks record probe rows) and
+``probes=True`` the capture runs with the hooks forced on, and the probe
+records it made - index selects of fixed rows into tensors owned by the
+graph - are handed back to the recorder after every replay; the plain
+step's graph is captured with the hooks forced off.  Steps that still need host-side work
+inside the forward or backward (telemetry statistics, a different
+micro-batch shape) run eagerly; the graphs are kept for the next eligible
+step.  Capture failures (an operation that cannot be recorded) disable
+graphs for the run and the engine continues eagerly.
 """
 from __future__ import annotations
 
+import contextlib
 import os
 import weakref
 
@@ -44,14 +50,18 @@ def release_all() -> None:
 
 
 class StepGraph:
-    def __init__(self, model, sync, x, y, *, warmup: int = 3):
+    def __init__(self, model, sync, x, y, *, warmup: int = 3, recorder=None, probes=False):
         self.model = model
         self.sync = sync
         self.x = x.detach().clone()
         self.y = y.detach().clone()
         self.warmup = int(warmup)
+        self.recorder = recorder
+        self.probes = bool(probes) and recorder is not None
+        self.records = None
         self.graph = None
         self.loss = None
+        self.replays = 0
         self._keep = []
         _LIVE.add(self)
 
@@ -62,6 +72,7 @@ class StepGraph:
             self.graph.reset()
         self.graph = None
         self.loss = None
+        self.records = None
         self._keep = []
 
     def matches(self, x, y) -> bool:
@@ -76,6 +87,13 @@ class StepGraph:
         return loss
 
     def capture(self):
+        """Capture with the recorder's probe hooks forced on (``probes``) or off."""
+        forced = (self.recorder.probes_forced(self.probes) if self.recorder is not None
+                  else contextlib.nullcontext())
+        with forced:
+            self._capture()
+
+    def _capture(self):
         param_ready.wait_all()
         side = torch.cuda.Stream(device=self.x.device)
         side.wait_stream(torch.cuda.current_stream(self.x.device))
@@ -83,6 +101,8 @@ class StepGraph:
             for _ in range(self.warmup):
                 self.sync.zero_grad()
                 self._one()
+                if self.probes:
+                    self.recorder.take_probe_records()  # warm-up records are not used
         torch.cuda.current_stream(self.x.device).wait_stream(side)
         self.sync.zero_grad()
         graph = torch.cuda.CUDAGraph()
@@ -95,6 +115,8 @@ class StepGraph:
                 self.loss = self._one().detach()
         finally:
             _linear.capture_casts(False)
+            if self.probes:
+                self.records = self.recorder.take_probe_records()
         self.graph = graph
 
     def replay(self, x, y):
@@ -104,4 +126,7 @@ class StepGraph:
         if y.data_ptr() != self.y.data_ptr():
             self.y.copy_(y, non_blocking=True)
         self.graph.replay()
+        self.replays += 1
+        if self.probes:
+            self.recorder.restore_probe_records(self.records)
         return self.loss.clone()  # the graph's output tensor is overwritten by the next replay

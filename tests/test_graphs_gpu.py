@@ -33,15 +33,20 @@ def test_graph_replay_matches_eager(monkeypatch):
         eng = TrainEngine(m, opt, grad_clip=1.0, synchronizer=GradientSynchronizer(m))
         gen = torch.Generator().manual_seed(3)
         losses = []
-        for i in range(14):  # two response refreshes (steps 0 and 8) run eagerly
+        refresh_replays = 0
+        for i in range(20):  # response refreshes at steps 0 (eager), 8 and 16 (refresh graph)
             if graphs == "1" and i == 10:
-                # teardown path: graphs are freed, the next plain step captures again
+                # teardown path: graphs are freed, the next step captures again
+                refresh_replays += eng._graphs["refresh"].replays
                 release_all()
-                assert eng._graph.graph is None
+                assert all(g.graph is None for g in eng._graphs.values())
             t = torch.randint(0, 1000, (4, 257), generator=gen).cuda()
             losses.append(eng.step([(t[:, :-1], t[:, 1:])], lr=3e-4).item())
         param_ready.wait_all()
         torch.cuda.synchronize()
+        if graphs == "1":
+            refresh_replays += eng._graphs["refresh"].replays
+            assert refresh_replays == 2
         runs.append((losses, [p.detach().clone() for p in m.parameters()], eng._graph_state))
     assert runs[0][2] == "off" and runs[1][2] == "on", (runs[0][2], runs[1][2])
     assert runs[0][0] == runs[1][0]

@@ -61,3 +61,42 @@ def test_training_steps_and_checkpoint_round_trip():
     for p, q in zip(model.parameters(), twin_model.parameters()):
         assert torch.equal(p, q)
     assert [m["preclip_norm"] for m in a] == [m["preclip_norm"] for m in b]
+
+
+def test_trajectory_matches_reference_extension():
+    """Ten updates (refreshes at 1 and 9) of ours against the reference extension
+    (experiments/swiglu_tiller/tiller_swiglu.py) on the same weights and batches."""
+    import importlib
+
+    from reference_oracle import require_reference
+    require_reference()
+    ref_ts = importlib.import_module("experiments.swiglu_tiller.tiller_swiglu")
+    ref_model_mod = importlib.import_module("experiments.swiglu_tiller.model")
+    mine = _model()
+    theirs = ref_model_mod.ModernMHADecoder(mine.config)
+    theirs.load_state_dict(mine.state_dict())
+    my_opt = TS.SwiGLUTILLER(mine, group_width=32)
+    ref_opt = ref_ts.SwiGLUTILLER(theirs, group_width=32)
+    gen = torch.Generator().manual_seed(4)
+    for step in range(10):
+        x = torch.randint(0, 128, (4, 16), generator=gen)
+        y = torch.randint(0, 128, (4, 16), generator=gen)
+        mask = torch.rand(4, 16, generator=gen) > 0.2
+        got = []
+        for model, opt in ((mine, my_opt), (theirs, ref_opt)):
+            opt.zero_grad()
+            opt.begin_step([mask])
+            opt.backward(_per_token_loss(model, x, y))
+            got.append(opt.step())
+        for key in ("functional_refresh", "ledger_step", "proposal_accepted", "total_loss_tokens"):
+            assert got[0][key] == got[1][key], (step, key)
+        assert abs(got[0]["preclip_norm"] - got[1]["preclip_norm"]) <= 1e-5 * got[1]["preclip_norm"]
+        for (n, p), (_, q) in zip(mine.named_parameters(), theirs.named_parameters()):
+            torch.testing.assert_close(p, q, rtol=2e-4, atol=2e-6, msg=f"step {step} {n}")
+    # checkpoints interchange
+    ref_opt.close()
+    twin = ref_model_mod.ModernMHADecoder(mine.config)
+    twin.load_state_dict(mine.state_dict())
+    ref_twin = ref_ts.SwiGLUTILLER(twin, group_width=32)
+    ref_twin.load_state_dict(copy.deepcopy(my_opt.state_dict()))
+    assert ref_twin.completed_steps == my_opt.completed_steps == 10
