@@ -553,6 +553,66 @@ c10::optional<std::vector<torch::Tensor>> grain_in_proj_forward(torch::Tensor x,
   return std::vector<torch::Tensor>{h, y};
 }
 
+// Flash attention forward over token-major planes: q, k, v [B, S, ld] bf16
+// (head h at columns h*hd), returns (o [B, S, H*hd] bf16, lse2 [B, H, S] fp32);
+// None for unsupported shapes or strides.
+c10::optional<std::vector<torch::Tensor>> attention_forward(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                                            int64_t heads, int64_t hd, double scale,
+                                                            bool causal) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "attention_forward expects CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k.scalar_type() == torch::kBFloat16 &&
+                  v.scalar_type() == torch::kBFloat16, "attention_forward expects bf16");
+  TORCH_CHECK(q.dim() == 3 && k.sizes() == q.sizes() && v.sizes() == q.sizes(), "q, k, v must be [B, S, ld]");
+  const int64_t B = q.size(0), S = q.size(1), ld = q.stride(1);
+  for (const auto& t : {q, k, v})
+    if (t.stride(2) != 1 || t.stride(1) != ld || t.stride(0) != ld * S) return c10::nullopt;
+  if (q.size(2) < heads * hd) return c10::nullopt;
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto o = torch::empty({B, S, heads * hd}, q.options());
+  auto lse2 = torch::empty({B, heads, S}, q.options().dtype(torch::kFloat32));
+  const int rc = ro::attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                       lse2.data_ptr<float>(), static_cast<int>(B), static_cast<int>(S),
+                                       static_cast<int>(heads), static_cast<int>(hd), ld, heads * hd,
+                                       static_cast<float>(scale), causal,
+                                       gemm_error_flag(q.device()).data_ptr<int>(),
+                                       at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "attention_forward");
+  return std::vector<torch::Tensor>{o, lse2};
+}
+
+// Backward of attention_forward: (dq, dk, dv) as [B, S, H*hd] bf16 planes, or
+// None for unsupported arguments.  o, dout: [B, S, H*hd] (made contiguous).
+c10::optional<std::vector<torch::Tensor>> attention_backward(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                                             torch::Tensor o, torch::Tensor dout,
+                                                             torch::Tensor lse2, int64_t heads, int64_t hd,
+                                                             double scale, bool causal) {
+  TORCH_CHECK(q.is_cuda() && q.dim() == 3 && k.sizes() == q.sizes() && v.sizes() == q.sizes(),
+              "q, k, v must be CUDA [B, S, ld]");
+  const int64_t B = q.size(0), S = q.size(1), ld = q.stride(1), cols = heads * hd;
+  for (const auto& t : {q, k, v})
+    if (t.stride(2) != 1 || t.stride(1) != ld || t.stride(0) != ld * S || t.scalar_type() != torch::kBFloat16)
+      return c10::nullopt;
+  o = o.contiguous();
+  dout = dout.contiguous();
+  TORCH_CHECK(o.sizes() == dout.sizes() && o.size(0) == B && o.size(1) == S && o.size(2) == cols,
+              "o and dout must be [B, S, H*hd]");
+  TORCH_CHECK(lse2.is_contiguous() && lse2.scalar_type() == torch::kFloat32 && lse2.numel() == B * heads * S,
+              "lse2 must be fp32 [B, H, S]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto dq = torch::empty_like(o), dk = torch::empty_like(o), dv = torch::empty_like(o);
+  auto delta = torch::empty({B, heads, S}, lse2.options());
+  const int rc = ro::attention_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, o.data_ptr(), dout.data_ptr(),
+                                        lse2.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), cols,
+                                        delta.data_ptr<float>(), static_cast<int>(B), static_cast<int>(S),
+                                        static_cast<int>(heads), static_cast<int>(hd), static_cast<float>(scale),
+                                        causal, gemm_error_flag(q.device()).data_ptr<int>(),
+                                        at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return c10::nullopt;
+  check_rc(rc, "attention_backward");
+  return std::vector<torch::Tensor>{dq, dk, dv};
+}
+
 void adamw_multi_tensor(std::vector<torch::Tensor> p, std::vector<torch::Tensor> g,
                         std::vector<torch::Tensor> m, std::vector<torch::Tensor> v, double lr,
                         double beta1, double beta2, double eps, double wd, double step) {
@@ -917,6 +977,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2_bf16", &gemm2_bf16);
   m.def("grain_in_proj_forward", &grain_in_proj_forward);
   m.def("qkv_rope_forward", &qkv_rope_forward);
+  m.def("attention_forward", &attention_forward);
+  m.def("attention_backward", &attention_backward);
   m.def("grain_out_proj_backward", &grain_out_proj_backward, py::arg("dO"), py::arg("w_out_t"), py::arg("h"),
         py::arg("num"), py::arg("den"), py::arg("eps"), py::arg("gnum_into") = py::none(),
         py::arg("gden_into") = py::none());

@@ -60,6 +60,11 @@ int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, 
 int gemm2_qkv_rope(const void* X, int64_t ldx, const void* W, int64_t ldw, void* QKV, int M, int N, int K,
                    const float* cos_t, const float* sin_t, int seq, int hd, int* err, cudaStream_t stream);
 int gemm2_grain_partial_rows(int M);
+int attention_backward(const void* q, const void* k, const void* v, int64_t ld, const void* o, const void* dout,
+                       const float* lse2, void* dq, void* dk, void* dv, int64_t ld2, float* delta, int B, int S,
+                       int H, int hd, float scale, bool causal, int* err, cudaStream_t stream);
+int attention_forward(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int S, int H,
+                      int hd, int64_t ld, int64_t ldo, float scale, bool causal, int* err, cudaStream_t stream);
 int gemm2_grain_backward(const void* dO, int64_t ldo, const void* wt, int64_t ldw, const void* h, int64_t ldh,
                          void* GX, float* partial, int M, int N, int K, const float* num, const float* den,
                          float eps, int* err, cudaStream_t stream);

@@ -104,39 +104,60 @@ def fused_qkv_attention(x, weight, w_compute, batch, seq_len, heads, head_dim, r
     cos2d = rope_cos.reshape(rope_cos.shape[-2], rope_cos.shape[-1]).float().contiguous()
     sin2d = rope_sin.reshape(rope_sin.shape[-2], rope_sin.shape[-1]).float().contiguous()
     q, k, v = _QKVRopeFunction.apply(x, weight, w_compute, cos2d, sin2d, batch, seq_len, heads, head_dim)
+    if own_attention_supported(q):
+        # the [B, H, S, hd] views are token-major planes: hand the planes over as they are
+        planes = [t.transpose(1, 2).reshape(batch, seq_len, heads * head_dim) for t in (q, k, v)]
+        return _OwnAttention.apply(*planes, heads, head_dim, True)
     y = causal_attention_core(q, k, v)
     return y.transpose(1, 2).reshape(batch, seq_len, heads * head_dim)
 
 
-def _flash():
-    if not _ext.available():
-        return None
-    C = _ext.ext()
-    return C if hasattr(C, "flash_attn_fwd") else None
+class _OwnAttention(torch.autograd.Function):
+    """Attention over token-major ``[B, S, H*hd]`` planes on the package's
+    tcgen05 kernels (csrc/attention_sm100.cu): forward saves (o, lse2); the
+    backward is deterministic (query-stationary dQ pass, key-stationary dK/dV
+    pass, no atomics)."""
 
-
-class _FlashAttention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, scale):
-        C = _ext.ext()
-        o, lse = C.flash_attn_fwd(q, k, v, float(scale), True)
-        ctx.save_for_backward(q, k, v, o, lse)
-        ctx.scale = float(scale)
+    def forward(ctx, q, k, v, heads, head_dim, causal):
+        scale = 1.0 / math.sqrt(head_dim)
+        out = _ext.ext().attention_forward(q, k, v, int(heads), int(head_dim), scale, bool(causal))
+        if out is None:
+            raise RuntimeError("attention_forward rejected a shape own_attention_supported accepted")
+        o, lse2 = out
+        ctx.save_for_backward(q, k, v, o, lse2)
+        ctx.cfg = (int(heads), int(head_dim), scale, bool(causal))
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, o, lse = ctx.saved_tensors
-        dq, dk, dv = _ext.ext().flash_attn_bwd(do.contiguous(), q, k, v, o, lse, ctx.scale, True)
-        return dq, dk, dv, None
+        q, k, v, o, lse2 = ctx.saved_tensors
+        heads, head_dim, scale, causal = ctx.cfg
+        out = _ext.ext().attention_backward(q, k, v, o, do, lse2, heads, head_dim, scale, causal)
+        if out is None:
+            raise RuntimeError("attention_backward rejected the forward's tensors")
+        dq, dk, dv = out
+        return dq, dk, dv, None, None, None
+
+
+def own_attention_supported(q) -> bool:
+    """The package's attention kernels take this ``[B, H, S, hd]`` token-major view.
+
+    Opt-in (``RO_OWN_ATTENTION=1``): at the 18-layer shape the kernels are
+    still slower than cuDNN's (forward 0.207 against 0.138 ms, backward 0.775
+    against 0.394 ms per layer at 32 x 1024 tokens, one B200).
+    """
+    if os.environ.get("RO_OWN_ATTENTION", "0") != "1" or not (q.is_cuda and q.dtype == torch.bfloat16):
+        return False
+    if not _ext.available() or not hasattr(_ext.ext(), "attention_forward"):
+        return False
+    B, H, S, hd = q.shape
+    return hd in (64, 128) and q.stride(3) == 1 and q.stride(1) == hd and q.stride(2) == H * hd \
+        and q.stride(0) == S * H * hd
 
 
 def causal_attention_core(q, k, v):
     """softmax(q k^T / sqrt(hd) + causal mask) v for [B, H, S, hd] tensors."""
-    scale = 1.0 / math.sqrt(q.shape[-1])
-    C = _flash()
-    if C is not None and q.is_cuda and q.dtype == torch.bfloat16 and C.flash_attn_supported(q):
-        return _FlashAttention.apply(q, k, v, scale)
     return F.scaled_dot_product_attention(q, k, v, is_causal=True)
 
 
@@ -160,3 +181,34 @@ def causal_self_attention(qkv, batch, seq_len, heads, head_dim, rope_cos, rope_s
     k = apply_rope(k, cos, sin)
     y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
     return y.transpose(1, 2).reshape(batch, seq_len, d)
+
+
+def flash_attention_forward(q, k, v, heads, head_dim, *, causal=True, scale=None):
+    """Own tcgen05 attention forward over token-major planes.
+
+    ``q``, ``k``, ``v``: bf16 ``[B, S, ld]`` (head ``h`` at columns
+    ``h*head_dim``).  Returns ``(o [B, S, heads*head_dim] bf16, lse2 [B, heads, S]
+    fp32)`` with ``lse2`` in log2 units of the scaled scores, or None when the
+    kernel does not support the arguments.
+    """
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
+    out = _ext.ext().attention_forward(q, k, v, int(heads), int(head_dim), scale, bool(causal))
+    return None if out is None else (out[0], out[1])
+
+
+def attention_reference(q, k, v, heads, head_dim, *, causal=True, scale=None):
+    """fp32 oracle of :func:`flash_attention_forward`: (o, lse2) from ``[B, S, ld]`` planes."""
+    B, S, _ = q.shape
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
+
+    def split(t):
+        return t[..., : heads * head_dim].float().reshape(B, S, heads, head_dim).transpose(1, 2)
+
+    qf, kf, vf = split(q), split(k), split(v)
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    if causal:
+        mask = torch.ones(S, S, dtype=torch.bool, device=q.device).triu(1)
+        s = s.masked_fill(mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.softmax(s, dim=-1) @ vf
+    return o.transpose(1, 2).reshape(B, S, heads * head_dim), lse / math.log(2.0)

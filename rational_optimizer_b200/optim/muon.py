@@ -3,8 +3,9 @@ training/train.py:1808-1850).
 
 Same constructor, defaults, parameter-group keys and ``momentum_buffer``
 state as ``torch.optim.Muon``; the step groups parameters of equal shape and
-runs one batched NS5 per shape (tcgen05 batched GEMMs on CUDA) instead of one
-small NS5 per matrix.
+runs one batched NS5 per shape
+(:func:`~rational_optimizer_b200.optim.newton_schulz.batched_zero_power`)
+instead of one small NS5 per matrix.
 """
 from __future__ import annotations
 

@@ -51,13 +51,6 @@ def zeropower_via_newton_schulz(matrix: torch.Tensor, steps: int = 5) -> torch.T
     return value.T if transposed else value
 
 
-def _native_ns():
-    if not _ext.available():
-        return None
-    C = _ext.ext()
-    return C if hasattr(C, "ns5_batched") else None
-
-
 def _ns5_torch_bf16(work: torch.Tensor) -> torch.Tensor:
     a, b, c = NS_COEFFICIENTS
     for _ in range(5):
@@ -125,11 +118,10 @@ def batched_zero_power(momentum: torch.Tensor, steps: int = 5) -> torch.Tensor:
         raise RuntimeError(f"expected [batch, rows, cols], got {tuple(momentum.shape)}")
     transposed = momentum.shape[-2] > momentum.shape[-1]
     work = momentum.transpose(-2, -1) if transposed else momentum
-    C = _native_ns()
-    if C is not None and work.is_cuda and int(steps) == 5:
-        out = C.ns5_batched(work.contiguous() if work.dtype != torch.float32 else work.contiguous())
-        if out is not None:
-            return out.transpose(-2, -1) if transposed else out
+    if work.is_cuda and int(steps) == 5:
+        # normalisation kernel + batched GEMMs (same arithmetic as below)
+        out = ns5_grouped_bf16(work.to(dtype=torch.bfloat16).contiguous())
+        return out.transpose(-2, -1) if transposed else out
     work = work.to(dtype=torch.bfloat16)
     norm = torch.linalg.vector_norm(work.float(), dim=(-2, -1), keepdim=True).clamp_min(NS_EPS)
     work = work / norm.to(dtype=work.dtype)

@@ -50,8 +50,8 @@ class GradientSynchronizer:
             overlap = os.environ.get("RO_GRAD_OVERLAP", "1") == "1"
         self.overlap = bool(overlap and self.world > 1 and device.type == "cuda" and transport == "nccl")
         if (communicator is None and self.world > 1 and transport == "p2p" and device.type == "cuda"):
-            from .comm import maybe_communicator
-            communicator = maybe_communicator(device, total, group=group)
+            from .p2p import P2PCommunicator
+            communicator = P2PCommunicator.create(device, total, group=group)
         self.communicator = communicator
         if communicator is not None:
             self.transport = "p2p"

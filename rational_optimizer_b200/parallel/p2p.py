@@ -55,7 +55,12 @@ class P2PCommunicator:
 
     @classmethod
     def create(cls, device, numel=None, *, group=None, mode="f32"):
+        """A communicator over ``group`` (2..16 ranks), or None when the process
+        group, the peer-memory kernels of the extension, or enough ranks are missing
+        (callers then use NCCL through torch.distributed)."""
         if not (dist.is_available() and dist.is_initialized()):
+            return None
+        if not _ext.available() or not hasattr(_ext.ext(), "comm_allreduce_f32"):
             return None
         world = dist.get_world_size(group)
         if world < 2 or world > 16:

@@ -141,11 +141,17 @@ def save(path: Path, *, args, rank, world_size, is_distributed, device, model, o
             "active_seconds": float(active_seconds),
         }, mtmp)
     faults.maybe_inject("checkpoint_written", rank, completed_step)
+    if rank == 0:
+        # the manifest describes one generation: drop the old one before any of
+        # its files is replaced, write the new one after the last promotion
+        Manifest.path_for(path).unlink(missing_ok=True)
     _barrier(is_distributed)
     rtmp.replace(rpath)
     _barrier(is_distributed)
     if rank == 0:
         mtmp.replace(path)
+    faults.maybe_inject("checkpoint_promoted", rank, completed_step)
+    if rank == 0:
         Manifest.write(path, [path] + [rank_path(path, r) for r in range(int(world_size))])
     _barrier(is_distributed)
 

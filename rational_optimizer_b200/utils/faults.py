@@ -7,9 +7,10 @@ environment variable ``RO_INJECT_FAULT`` selects one fault as
 ``train_step:1:3:raise`` makes rank 1 raise at the start of step 3.
 
 Points: ``train_step`` (start of a training step, before any collective of
-that step) and ``checkpoint_written`` (after this rank's temporary
-checkpoint files are written, before they are promoted).  Unset, every call
-is a no-op.
+that step), ``checkpoint_written`` (after this rank's temporary checkpoint
+files are written, before they are promoted) and ``checkpoint_promoted``
+(after the files are promoted, before the new manifest is written).  Unset,
+every call is a no-op.
 """
 from __future__ import annotations
 

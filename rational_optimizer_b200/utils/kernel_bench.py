@@ -190,6 +190,45 @@ def cases(rows):
     def ns5_router_native():
         return _ns5(True)
 
+    def _attn_planes():
+        B, S, Hh, hd = rows // 1024, 1024, 16, 64
+        q, k, v = (torch.randn(B, S, Hh * hd, device=dev, dtype=bf) for _ in range(3))
+        flops = 4.0 * B * Hh * hd * S * (S + 1) / 2  # causal: QK^T and PV over the lower triangle
+        return q, k, v, B, S, Hh, hd, flops
+
+    def attn_fwd():
+        from ..ops.attention import flash_attention_forward
+        q, k, v, B, S, Hh, hd, flops = _attn_planes()
+        return (lambda: flash_attention_forward(q, k, v, Hh, hd)), 0, flops
+
+    def attn_fwd_sdpa():
+        q, k, v, B, S, Hh, hd, flops = _attn_planes()
+        views = [t.view(B, S, Hh, hd).transpose(1, 2) for t in (q, k, v)]
+
+        def run():
+            with torch.no_grad():
+                torch.nn.functional.scaled_dot_product_attention(*views, is_causal=True)
+        return run, 0, flops
+
+    def attn_bwd():
+        from ..ops.attention import flash_attention_forward
+        q, k, v, B, S, Hh, hd, flops = _attn_planes()
+        o, lse2 = flash_attention_forward(q, k, v, Hh, hd)
+        do = torch.randn_like(o)
+        # algorithmic FLOPs of the backward (5 products; the two-pass kernel
+        # recomputes two of them, not counted)
+        return (lambda: C.attention_backward(q, k, v, o, do, lse2, Hh, hd, hd ** -0.5, True)), 0, flops * 2.5
+
+    def attn_bwd_sdpa():
+        q, k, v, B, S, Hh, hd, flops = _attn_planes()
+        views = [t.view(B, S, Hh, hd).transpose(1, 2).detach().requires_grad_() for t in (q, k, v)]
+        out = torch.nn.functional.scaled_dot_product_attention(*views, is_causal=True)
+        do = torch.randn_like(out)
+
+        def run():
+            torch.autograd.grad(out, views, do, retain_graph=True)
+        return run, 0, flops * 2.5
+
     def ledger():
         L = 18
         n = L * G
@@ -223,7 +262,9 @@ def cases(rows):
                      ("grain_in_proj_unfused", grain_in_proj_unfused),
                      ("grain_out_proj_bwd_fused", grain_out_proj_bwd_fused),
                      ("grain_out_proj_bwd_unfused", grain_out_proj_bwd_unfused), ("ns5_router_cublas", ns5_router_cublas),
-                     ("ns5_router_native", ns5_router_native), ("ledger", ledger)]:
+                     ("ns5_router_native", ns5_router_native), ("ledger", ledger),
+                     ("attn_fwd", attn_fwd), ("attn_fwd_sdpa", attn_fwd_sdpa), ("attn_bwd", attn_bwd),
+                     ("attn_bwd_sdpa", attn_bwd_sdpa)]:
         out[name] = fn
     return out
 

@@ -126,6 +126,24 @@ def test_exact_resume_is_bitwise(tmp_path):
         assert a["loss"] == b["loss"] and a["grad_global_norm_before_clip"] == b["grad_global_norm_before_clip"]
 
 
+def test_crash_between_promotion_and_manifest_still_resumes(tmp_path, monkeypatch):
+    """A save that stops after its files are promoted but before the new manifest
+    is written leaves no stale manifest behind, so the run resumes from it."""
+    from rational_optimizer_b200.utils import faults
+    ck = tmp_path / "ck" / "state.pt"
+    common = ["--optimizer", "adamw", "--resume-checkpoint", str(ck), "--resume-checkpoint-interval", "2",
+              "--eval-interval", "2"]  # checkpoints are written at evaluation steps 2 and 4
+    monkeypatch.setenv(faults.ENV, "checkpoint_promoted:0:4:raise")
+    with pytest.raises(faults.InjectedFault):
+        trainer.main(_tiny_args(tmp_path, "a", *common))
+    monkeypatch.delenv(faults.ENV)
+    assert torch.load(ck, weights_only=False)["completed_step"] == 4
+    assert not Manifest.path_for(ck).is_file()  # the step-2 manifest is gone, not stale
+    assert trainer.main(_tiny_args(tmp_path, "b", *common)) == 0
+    recs = _records(tmp_path / "runs" / "b" / "silu.jsonl")
+    assert recs[0]["event"] == "resumed" and recs[0]["step"] == 4
+
+
 def test_resume_rejects_changed_contract_and_corruption(tmp_path):
     ck = tmp_path / "ck" / "state.pt"
     common = ["--optimizer", "adamw", "--resume-checkpoint", str(ck), "--resume-checkpoint-interval", "3"]
