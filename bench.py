@@ -192,7 +192,8 @@ def run_ours(a, info):
         for p in model.parameters():
             dist.broadcast(p.data, 0)
     optimizer = composite.configure_optimizer(model, args)
-    sync = GradientSynchronizer(model)
+    layers, owner_of = composite.owner_layers(optimizer)
+    sync = GradientSynchronizer(model, owner_layers=layers, layer_owner=owner_of)
     engine = TrainEngine(model, optimizer, grad_clip=1.0, grad_accum=1, synchronizer=sync)
     tokens = zipf_tokens(ZIPF_TOKENS, VOCAB, alpha=1.1, seed=0)
     batcher = PinnedBatcher(tokens, local_batch, SEQ, seed=0, rank=info.rank)

@@ -613,6 +613,62 @@ c10::optional<std::vector<torch::Tensor>> attention_backward(torch::Tensor q, to
   return std::vector<torch::Tensor>{dq, dk, dv};
 }
 
+// Reduce-to-owner (csrc/owner_comm.cu).  `dst` and `counter` are addresses in
+// the owner's memory (CUDA IPC mappings); the kernels run on the current stream.
+void owner_send(torch::Tensor src, int64_t dst, bool bf16, int64_t counter, int64_t ctas) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat32 && src.is_contiguous(),
+              "owner_send expects a contiguous fp32 CUDA tensor");
+  const c10::cuda::CUDAGuard guard(src.device());
+  check_rc(ro::owner_send(src.data_ptr<float>(), reinterpret_cast<void*>(dst), src.numel(), bf16,
+                          reinterpret_cast<unsigned int*>(counter), static_cast<int>(ctas),
+                          at::cuda::getCurrentCUDAStream()),
+           "owner_send");
+}
+
+void owner_reduce(torch::Tensor grad, int64_t recv, torch::Tensor counters, torch::Tensor offsets,
+                  torch::Tensor sizes, torch::Tensor recv_offsets, torch::Tensor sumsq, int64_t rank,
+                  int64_t world, int64_t expected, double scale, bool bf16, torch::Tensor err,
+                  int64_t timeout_ns) {
+  TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == torch::kFloat32, "owner_reduce: fp32 gradient buffer");
+  TORCH_CHECK(offsets.scalar_type() == torch::kInt64 && sizes.scalar_type() == torch::kInt64 &&
+                  recv_offsets.scalar_type() == torch::kInt64 && offsets.is_cuda(),
+              "owner_reduce: int64 CUDA layout tensors");
+  TORCH_CHECK(sumsq.scalar_type() == torch::kFloat32 && err.scalar_type() == torch::kInt32, "owner_reduce dtypes");
+  const c10::cuda::CUDAGuard guard(grad.device());
+  check_rc(ro::owner_reduce(grad.data_ptr<float>(), reinterpret_cast<const void*>(recv),
+                            reinterpret_cast<unsigned int*>(counters.data_ptr()), offsets.data_ptr<int64_t>(),
+                            sizes.data_ptr<int64_t>(), recv_offsets.data_ptr<int64_t>(), sumsq.data_ptr<float>(),
+                            static_cast<int>(sumsq.numel()), static_cast<int>(offsets.numel()),
+                            static_cast<int>(rank), static_cast<int>(world), static_cast<unsigned int>(expected),
+                            static_cast<float>(scale), bf16, err.data_ptr<int>(),
+                            static_cast<uint64_t>(timeout_ns), at::cuda::getCurrentCUDAStream()),
+           "owner_reduce");
+}
+
+// Owner weight all-gather (csrc/owner_comm.cu): publish bumps this rank's
+// counter; pull copies `dst.numel()` fp32 values from a peer address into
+// `dst` once the peer's counter (address `published`) has reached this rank's
+// own counter `mine`.
+void owner_publish(torch::Tensor published) {
+  const c10::cuda::CUDAGuard guard(published.device());
+  check_rc(ro::owner_publish(reinterpret_cast<unsigned int*>(published.data_ptr()),
+                             at::cuda::getCurrentCUDAStream()),
+           "owner_publish");
+}
+
+void owner_pull(int64_t src, torch::Tensor dst, int64_t published, torch::Tensor mine, torch::Tensor err,
+                int64_t timeout_ns, int64_t ctas) {
+  TORCH_CHECK(dst.is_cuda() && dst.scalar_type() == torch::kFloat32 && dst.is_contiguous(),
+              "owner_pull: contiguous fp32 destination");
+  const c10::cuda::CUDAGuard guard(dst.device());
+  check_rc(ro::owner_pull(reinterpret_cast<const float*>(src), dst.data_ptr<float>(), nullptr, dst.numel(),
+                          reinterpret_cast<const unsigned int*>(published),
+                          reinterpret_cast<const unsigned int*>(mine.data_ptr()), err.data_ptr<int>(),
+                          static_cast<uint64_t>(timeout_ns), static_cast<int>(ctas),
+                          at::cuda::getCurrentCUDAStream()),
+           "owner_pull");
+}
+
 void adamw_multi_tensor(std::vector<torch::Tensor> p, std::vector<torch::Tensor> g,
                         std::vector<torch::Tensor> m, std::vector<torch::Tensor> v, double lr,
                         double beta1, double beta2, double eps, double wd, double step) {
@@ -977,6 +1033,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2_bf16", &gemm2_bf16);
   m.def("grain_in_proj_forward", &grain_in_proj_forward);
   m.def("qkv_rope_forward", &qkv_rope_forward);
+  m.def("owner_send", &owner_send);
+  m.def("owner_reduce", &owner_reduce);
+  m.def("owner_publish", &owner_publish);
+  m.def("owner_pull", &owner_pull);
   m.def("attention_forward", &attention_forward);
   m.def("attention_backward", &attention_backward);
   m.def("grain_out_proj_backward", &grain_out_proj_backward, py::arg("dO"), py::arg("w_out_t"), py::arg("h"),

@@ -60,6 +60,15 @@ int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, 
 int gemm2_qkv_rope(const void* X, int64_t ldx, const void* W, int64_t ldw, void* QKV, int M, int N, int K,
                    const float* cos_t, const float* sin_t, int seq, int hd, int* err, cudaStream_t stream);
 int gemm2_grain_partial_rows(int M);
+int owner_send(const float* src, void* dst, int64_t n, bool bf16, unsigned int* counter, int ctas,
+               cudaStream_t stream);
+int owner_reduce(float* grad, const void* recv, unsigned int* counters, const int64_t* offsets,
+                 const int64_t* sizes, const int64_t* recv_offsets, float* sumsq, int ctas, int layers,
+                 int rank, int world, unsigned int expected, float scale, bool bf16, int* err,
+                 uint64_t timeout_ns, cudaStream_t stream);
+int owner_publish(unsigned int* published, cudaStream_t stream);
+int owner_pull(const float* src, float* dst, __nv_bfloat16* dst16, int64_t n, const unsigned int* published,
+               const unsigned int* mine, int* err, uint64_t timeout_ns, int ctas, cudaStream_t stream);
 int attention_backward(const void* q, const void* k, const void* v, int64_t ld, const void* o, const void* dout,
                        const float* lse2, void* dq, void* dk, void* dv, int64_t ld2, float* delta, int B, int S,
                        int H, int hd, float scale, bool causal, int* err, cudaStream_t stream);

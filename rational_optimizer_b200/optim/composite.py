@@ -207,6 +207,24 @@ class TILLERCompositeOptimizer(CompositeOptimizer):
             opt.load_state_dict(st)
 
 
+def owner_layers(optimizer):
+    """(per-layer matrices, layer -> owner rank) when ``optimizer`` updates each
+    layer's structural matrices on one rank only (the layer-sharded TILLER
+    composite), else (None, None).  This is what the reduce-to-owner gradient
+    transport needs (``parallel.grad_sync``)."""
+    if not isinstance(optimizer, TILLERCompositeOptimizer):
+        return None, None
+    router, attention = optimizer.optimizers[0], optimizer.optimizers[1]
+    if not router._shard()[2]:
+        return None, None
+    from .tiller import layer_owner
+    L, world = len(router.pairs), router.world_size
+    layers = [[router.pairs[l]["in_weight"], router.pairs[l]["out_weight"],
+               attention.role_parameters["qkv"][l], attention.role_parameters["attn_out"][l]]
+              for l in range(L)]
+    return layers, (lambda layer: layer_owner(layer, L, world))
+
+
 def _adam_groups(decay, no_decay, weight_decay):
     groups = []
     if decay:

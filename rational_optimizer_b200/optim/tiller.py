@@ -169,7 +169,16 @@ class OwnerPacking:
                      for l in range(L)]
         device = per_layer[0][0].device
         total = sum(p.numel() for ps in per_layer for p in ps)
-        self.flat = torch.empty(total, device=device, dtype=torch.float32)
+        self.world = router.world_size
+        self.group = router.loss_probe_group
+        from ..parallel import owner_gather
+        self.gather = None
+        use_gather = (device.type == "cuda" and self.world > 1 and owner_gather.available()
+                      and os.environ.get("RO_WEIGHT_TRANSPORT", "nccl") == "p2p")
+        if use_gather:
+            raw, self.flat = owner_gather.shared_buffer(total, device)
+        else:
+            self.flat = torch.empty(total, device=device, dtype=torch.float32)
         self.layer_ranges = []
         self.layer_params = per_layer
         off = 0
@@ -184,11 +193,24 @@ class OwnerPacking:
                     off += n
                 self.layer_ranges.append((lo, off))
         self.layers = L
-        self.world = router.world_size
-        self.group = router.loss_probe_group
+        if use_gather:
+            ranges, params = [], []
+            for r in range(self.world):
+                lo_l, hi_l = shard_bounds(L, r, self.world)
+                if hi_l > lo_l:
+                    ranges.append((self.layer_ranges[lo_l][0], self.layer_ranges[hi_l - 1][1]))
+                else:
+                    ranges.append((0, 0))
+                params.append([p for l in range(lo_l, hi_l) for p in per_layer[l]])
+            self.gather = owner_gather.OwnerGather(raw, self.flat, ranges, params, group=self.group)
 
     def broadcast(self):
-        """Replicate every owner's updated layers (one deferred broadcast per owner)."""
+        """Replicate every owner's updated layers: the peer-memory pull
+        (:class:`~rational_optimizer_b200.parallel.owner_gather.OwnerGather`) or,
+        without it, one deferred NCCL broadcast per owner."""
+        if self.gather is not None:
+            self.gather.publish()  # the copies are pulled by the next reader (lazily, or in the step graph)
+            return
         side = param_ready.side_stream(self.flat.device)
         side.wait_stream(torch.cuda.current_stream(self.flat.device))
         for r in range(self.world):
@@ -1122,7 +1144,25 @@ class TILLERRouter(torch.optim.Optimizer):
         self._clip_factor = None
 
     def _decay_derivative(self, wd):
-        """wd * sum over routed matrices of <grad, weight> (optimizer_design/_tiller/core.py:4511-4519)."""
+        """wd * sum over routed matrices of <grad, weight> (optimizer_design/_tiller/core.py:4511-4519).
+
+        Layer-sharded: each rank sums over the layers it owns (whose averaged
+        gradient it holds, whatever the gradient transport) and the partial
+        sums are all-reduced, so every rank gets the same value.
+        """
+        lo, hi, sharded = self._shard()
+        if sharded:
+            pairs = self.pairs[lo:hi]
+            tensors = [(p[k].grad.detach(), p[k].detach()) for p in pairs for k in ("in_weight", "out_weight")]
+            device = self.pairs[0]["in_weight"].device
+            if tensors:
+                from .._ext import ext
+                part = ext().multi_tensor_dot([g for g, _ in tensors], [w for _, w in tensors], float(wd))
+                part = part.reshape(1).clone()
+            else:
+                part = torch.zeros(1, device=device, dtype=torch.float32)
+            dist.all_reduce(part, group=self.loss_probe_group)
+            return part.reshape(())
         tensors = [(p[k].grad.detach(), p[k].detach()) for p in self.pairs for k in ("in_weight", "out_weight")]
         if self._use_fused() and all(g.dtype == torch.float32 and g.is_contiguous() and w.is_contiguous()
                                      for g, w in tensors):

@@ -18,6 +18,15 @@ training/train.py:2366-2371).  Two ways to average it across ranks:
   GPU, peer memory mapped through CUDA IPC), otherwise NCCL in fixed-size
   buckets.
 
+* reduce-to-owner (``transport="owner"`` / ``"owner-bf16"``, the default
+  with several ranks when ``owner_layers`` names the matrices of layer-sharded
+  optimizers): those matrices are laid out first in the buffer, one
+  contiguous segment per layer, and each segment goes only to the rank that
+  owns the layer (:class:`~.owner_reduce.OwnerReduce`, own NVLink kernels,
+  sent during backward); the remaining parameters (embeddings, norms, GRAIN
+  coefficients - the replicated optimizer's) are one contiguous range
+  averaged with a single NCCL all-reduce after backward.
+
 With one rank the synchroniser only manages the buffer.
 """
 from __future__ import annotations
@@ -27,34 +36,56 @@ import os
 import torch
 import torch.distributed as dist
 
+from .. import _ext
 from ..ops.linear import ACCUMULATE_ATTR, READY_ATTR
 
 
 class GradientSynchronizer:
     def __init__(self, model: torch.nn.Module, *, group=None, bucket_bytes: int = 256 << 20,
-                 communicator=None, transport: str | None = None, overlap: bool | None = None):
+                 communicator=None, transport: str | None = None, overlap: bool | None = None,
+                 owner_layers=None, layer_owner=None):
+        """``owner_layers``: per layer, the parameters a layer-sharded optimizer updates
+        on the layer's owner only; ``layer_owner(layer) -> rank``.  Both are required
+        for the reduce-to-owner transport."""
         seen, params = set(), []
         for p in model.parameters():
             if p.requires_grad and id(p) not in seen:
                 seen.add(id(p))
                 params.append(p)
-        self.params = params
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         dtype = params[0].dtype
         device = params[0].device
         total = sum(p.numel() for p in params)
         if transport is None:
-            transport = os.environ.get("RO_GRAD_TRANSPORT", "nccl")
+            default = "nccl"
+            if (owner_layers is not None and self.world > 1 and device.type == "cuda" and _ext.available()
+                    and hasattr(_ext.ext(), "owner_send")):
+                default = "owner"
+            transport = os.environ.get("RO_GRAD_TRANSPORT", default)
+        self.owner = None
+        owned_matrices = []
+        if transport.startswith("owner"):
+            if owner_layers is None or layer_owner is None or self.world < 2 or device.type != "cuda":
+                transport = "nccl"
+            else:
+                # managed matrices first, one contiguous segment per layer
+                owned_matrices = [list(ps) for ps in owner_layers]
+                managed = {id(p) for ps in owned_matrices for p in ps}
+                params = [p for ps in owned_matrices for p in ps] + [p for p in params if id(p) not in managed]
+        self.params = params
         if overlap is None:
             overlap = os.environ.get("RO_GRAD_OVERLAP", "1") == "1"
         self.overlap = bool(overlap and self.world > 1 and device.type == "cuda" and transport == "nccl")
+        self.owner_mode = transport.startswith("owner")
         if (communicator is None and self.world > 1 and transport == "p2p" and device.type == "cuda"):
             from .p2p import P2PCommunicator
             communicator = P2PCommunicator.create(device, total, group=group)
         self.communicator = communicator
         if communicator is not None:
             self.transport = "p2p"
+        elif self.owner_mode:
+            self.transport = "owner-bf16" if transport == "owner-bf16" else "owner-f32"
         elif self.world > 1:
             self.transport = "nccl-overlap" if self.overlap else "nccl"
         else:
@@ -85,6 +116,52 @@ class GradientSynchronizer:
         self._reported = set()
         if self.overlap:
             self._setup_buckets(model)
+        if self.owner_mode:
+            self._setup_owner(owned_matrices, layer_owner)
+
+    # -- reduce-to-owner ---------------------------------------------------------
+    def _setup_owner(self, layers, layer_owner):
+        from .owner_reduce import OwnerReduce
+        index = {id(p): i for i, p in enumerate(self.params)}
+        segments, self._layer_of, self._layer_left = [], {}, []
+        for layer, ps in enumerate(layers):
+            lo = self.offsets[index[id(ps[0])]]
+            n = sum(p.numel() for p in ps)
+            segments.append((lo, n))
+            for p in ps:
+                self._layer_of[id(p)] = layer
+                setattr(p, READY_ATTR, self._owner_ready)
+                p.register_post_accumulate_grad_hook(self._owner_ready)
+            self._layer_left.append(len(ps))
+        self._layer_size = list(self._layer_left)
+        self._tail = segments[-1][0] + segments[-1][1] if segments else 0
+        owners = [int(layer_owner(l)) for l in range(len(layers))]
+        self.owner = OwnerReduce(self.flat, segments, owners, group=self.group,
+                                 transport="bf16" if self.transport == "owner-bf16" else "f32")
+        self._reported = set()
+
+    def _owner_ready(self, p):
+        if not self._armed:
+            return
+        layer = self._layer_of.get(id(p))
+        if layer is None or id(p) in self._reported:
+            return
+        self._reported.add(id(p))
+        self._layer_left[layer] -= 1
+        if self._layer_left[layer] == 0:
+            self.owner.send(layer)
+
+    def grad_sumsq(self):
+        """Sum of squares of the averaged gradient (device scalar, identical on every
+        rank) when gradients are not replicated everywhere; None otherwise."""
+        if not self.owner_mode:
+            return None
+        from .. import _ext as ext
+        tail = self.flat[self._tail:]
+        owned = self.owner.owned_sumsq().reshape(1).clone()
+        dist.all_reduce(owned, group=self.group)
+        rest = ext.ext().multi_tensor_dot([tail], [tail], 1.0) if tail.numel() else owned.new_zeros(1)
+        return (owned + rest.reshape(1)).reshape(())
 
     # -- overlapped buckets ----------------------------------------------------
     def _setup_buckets(self, model):
@@ -127,6 +204,12 @@ class GradientSynchronizer:
 
     def begin_backward(self):
         """Arm readiness tracking for the backward pass whose gradients are final."""
+        if self.owner_mode:
+            self._armed = True
+            self._reported = set()
+            self._layer_left = list(self._layer_size)
+            self.owner.begin()
+            return
         if not self.overlap:
             return
         self._armed = True
@@ -175,6 +258,17 @@ class GradientSynchronizer:
     def synchronize(self):
         """Average gradients across ranks (no-op for one rank)."""
         if self.world == 1:
+            return
+        if self.owner_mode:
+            work = None
+            if self._tail < self.flat.numel():
+                work = dist.all_reduce(self.flat[self._tail:], op=dist.ReduceOp.AVG, group=self.group,
+                                       async_op=True)
+            self.owner.reduce()
+            if work is not None:
+                work.wait()
+            self._armed = False
+            self._reported = set()
             return
         if self.overlap:
             # buckets whose readiness was not reported (e.g. unused parameters)

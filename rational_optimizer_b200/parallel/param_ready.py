@@ -15,6 +15,30 @@ import torch
 
 _PENDING: dict[int, torch.cuda.Event] = {}
 _STREAMS: dict[int, torch.cuda.Stream] = {}
+# objects with a ``pending`` flag and ``pull()``: replication that is enqueued
+# lazily, by the first reader of a parameter (see ``parallel.owner_gather``)
+_PULLERS: list = []
+
+
+def register_puller(obj) -> None:
+    if obj not in _PULLERS:
+        _PULLERS.append(obj)
+
+
+def _flush_pullers() -> None:
+    for obj in _PULLERS:
+        if obj.pending:
+            obj.pending = False
+            obj.pull()
+
+
+def claim_pullers() -> list:
+    """Mark every pending lazy replication as taken by the caller (a captured
+    step graph that performs the pulls itself) and return the claimed objects."""
+    claimed = [obj for obj in _PULLERS if obj.pending]
+    for obj in claimed:
+        obj.pending = False
+    return claimed
 
 
 def side_stream(device: torch.device) -> torch.cuda.Stream:
@@ -37,7 +61,21 @@ def pending() -> bool:
     return bool(_PENDING)
 
 
+def pullers() -> list:
+    return list(_PULLERS)
+
+
+def forget_events(events) -> None:
+    """Drop pending entries whose events are in ``events`` (recorded inside a
+    graph capture: the graph carries those dependencies itself)."""
+    ids = {id(e) for e in events}
+    for key in [k for k, ev in _PENDING.items() if id(ev) in ids]:
+        del _PENDING[key]
+
+
 def wait(param) -> None:
+    if _PULLERS:
+        _flush_pullers()
     if _PENDING:
         ev = _PENDING.pop(id(param), None)
         if ev is not None:
@@ -45,6 +83,8 @@ def wait(param) -> None:
 
 
 def wait_all() -> None:
+    if _PULLERS:
+        _flush_pullers()
     if not _PENDING:
         return
     for ev in set(_PENDING.values()):

@@ -28,19 +28,23 @@ def learning_rate(step, *, lr, min_lr, warmup_steps, total_steps):
     return min_lr + 0.5 * (1.0 + math.cos(math.pi * progress)) * (lr - min_lr)
 
 
-def clip_grad_norm(params, max_norm, flat=None):
+def clip_grad_norm(params, max_norm, flat=None, sumsq=None):
     """Global L2 norm of all gradients (fp32) and in-place clipping; returns the device norm.
 
     ``flat``: the single fp32 buffer every gradient is a view of (the data-
     parallel synchroniser's); on CUDA the norm is then one fixed-order
     reduction kernel over the buffer and the clip one scaling pass, instead of
     per-tensor norms (torch.nn.utils.clip_grad_norm_, used by the reference
-    trainer, training/train.py:957).
+    trainer, training/train.py:957).  ``sumsq``: the squared norm when the
+    caller has it already (reduce-to-owner: the buffer then holds averaged
+    gradients only for this rank's layers, so the norm comes from the owners'
+    partial sums).
     """
     if flat is not None and flat.is_cuda and flat.dtype == torch.float32 and _has_dot():
         from .. import _ext
         C = _ext.ext()
-        sumsq = C.multi_tensor_dot([flat], [flat], 1.0)
+        if sumsq is None:
+            sumsq = C.multi_tensor_dot([flat], [flat], 1.0)
         if max_norm > 0:
             C.clip_scale_(flat, sumsq.reshape(1), float(max_norm))
         return sumsq.sqrt()
@@ -173,7 +177,8 @@ class TrainEngine:
         return self._finish(total / self.grad_accum)
 
     def _finish(self, loss):
-        norm = clip_grad_norm(self.sync.params, self.grad_clip, self.sync.flat_covering())
+        norm = clip_grad_norm(self.sync.params, self.grad_clip, self.sync.flat_covering(),
+                              sumsq=self.sync.grad_sumsq())
         self.last_grad_norm = norm
         if self.clip_observer is not None:
             self.clip_observer.record_realized_clipping(norm, self.grad_clip)

@@ -63,6 +63,8 @@ class StepGraph:
         self.loss = None
         self.replays = 0
         self._keep = []
+        self._pullers = []
+        self._captured_events = []
         _LIVE.add(self)
 
     def release(self):
@@ -79,11 +81,23 @@ class StepGraph:
         return (x.shape == self.x.shape and y.shape == self.y.shape and x.dtype == self.x.dtype
                 and y.dtype == self.y.dtype and x.device == self.x.device)
 
-    def _one(self):
+    def _one(self, pull=False):
+        pulled = []
+        if pull:
+            # replicate the owners' weights inside the graph: each layer's
+            # forward waits only for the copy from its own owner
+            param_ready.claim_pullers()
+            for obj in self._pullers:
+                ev = obj.pull()
+                if ev is not None:
+                    pulled.append(ev)
         loss = self.model.forward_loss(self.x, self.y)
         self.sync.begin_backward()
         loss.backward()
         self.sync.synchronize()
+        if pulled:
+            torch.cuda.current_stream(self.x.device).wait_stream(param_ready.side_stream(self.x.device))
+            self._captured_events = pulled
         return loss
 
     def capture(self):
@@ -94,6 +108,8 @@ class StepGraph:
             self._capture()
 
     def _capture(self):
+        self._pullers = param_ready.pullers()
+        self._captured_events = []
         param_ready.wait_all()
         side = torch.cuda.Stream(device=self.x.device)
         side.wait_stream(torch.cuda.current_stream(self.x.device))
@@ -112,14 +128,17 @@ class StepGraph:
         mode = "thread_local" if self.sync.world > 1 else "global"
         try:
             with torch.cuda.graph(graph, capture_error_mode=mode):
-                self.loss = self._one().detach()
+                self.loss = self._one(pull=bool(self._pullers)).detach()
         finally:
             _linear.capture_casts(False)
+            param_ready.forget_events(self._captured_events)
             if self.probes:
                 self.records = self.recorder.take_probe_records()
         self.graph = graph
 
     def replay(self, x, y):
+        if self._pullers:
+            param_ready.claim_pullers()  # the graph pulls the owners' weights itself
         param_ready.wait_all()
         if x.data_ptr() != self.x.data_ptr():
             self.x.copy_(x, non_blocking=True)

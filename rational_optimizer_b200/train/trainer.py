@@ -182,7 +182,7 @@ def build_parser() -> argparse.ArgumentParser:
                    help="vocabulary of the synthetic/zipf and synthetic/uniform sources")
     p.add_argument("--zipf-alpha", type=float, default=1.1)
     p.add_argument("--compute-dtype", choices=["bf16", "fp32"], default="bf16")
-    p.add_argument("--grad-transport", choices=["p2p", "nccl"], default=None)
+    p.add_argument("--grad-transport", choices=["p2p", "nccl", "owner", "owner-bf16"], default=None)
     p.add_argument("--strict-exact-resume", action="store_true",
                    help="run-local checkpoint, interrupted-commit recovery, argument-digest contract")
     p.add_argument("--dist-timeout-s", type=float, default=600.0)
@@ -296,12 +296,15 @@ class Run:
                 for t in list(model.parameters()) + list(model.buffers()):
                     torch.distributed.broadcast(t, src=0)
         self.model = model
-        self.sync = GradientSynchronizer(model, transport=args.grad_transport)
         self.rational_param_count = sum(
             p.numel() for n, p in model.named_parameters()
             if p.requires_grad and (".rlb_activation." in n or n.endswith(".numerator")
                                     or n.endswith(".denominator")))
         self.optimizer = configure_optimizer(model, args)
+        from ..optim.composite import owner_layers
+        layers, owner_of = owner_layers(self.optimizer)
+        self.sync = GradientSynchronizer(model, transport=args.grad_transport, owner_layers=layers,
+                                         layer_owner=owner_of)
         self.clip_observer = self.optimizer if hasattr(self.optimizer, "record_realized_clipping") else None
         self.fairness = audit.audit_optimizer_lr_wd_fairness(model, self.optimizer, args)
         self.offsets = torch.arange(args.seq_len + 1)

@@ -35,3 +35,4 @@ def test_overlapped_sharded_training_matches_replicated():
     res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert f"TRAIN_OK {n}" in res.stdout
+    assert "OWNER_OK" in res.stdout

@@ -26,7 +26,7 @@ from rational_optimizer_b200.train.engine import TrainEngine  # noqa: E402
 from rational_optimizer_b200.train.integrity import model_state_sha256  # noqa: E402
 
 
-def run(info, *, overlap, shard, accum, graph=False):
+def run(info, *, overlap, shard, accum, graph=False, transport="nccl"):
     os.environ["RO_TILLER_SHARD"] = "1" if shard else "0"
     os.environ["RO_CUDA_GRAPH"] = "1" if graph else "0"
     torch.manual_seed(0)
@@ -36,8 +36,14 @@ def run(info, *, overlap, shard, accum, graph=False):
                          muon_momentum=0.95, muon_ns_steps=5, muon_adjust_lr_fn="match_rms_adamw",
                          grad_accum=accum, layers=4, steps=100)
     opt = configure_optimizer(model, ns)
-    sync = GradientSynchronizer(model, transport="nccl", overlap=overlap)
-    assert sync.transport == ("nccl-overlap" if overlap else "nccl")
+    if transport.startswith("owner"):
+        from rational_optimizer_b200.optim.composite import owner_layers
+        layers, owner_of = owner_layers(opt)
+        sync = GradientSynchronizer(model, transport=transport, owner_layers=layers, layer_owner=owner_of)
+        assert sync.transport == ("owner-bf16" if transport == "owner-bf16" else "owner-f32")
+    else:
+        sync = GradientSynchronizer(model, transport="nccl", overlap=overlap)
+        assert sync.transport == ("nccl-overlap" if overlap else "nccl")
     eng = TrainEngine(model, opt, grad_clip=1.0, grad_accum=accum, synchronizer=sync)
     gen = torch.Generator().manual_seed(100 + info.rank)
     losses = []
@@ -49,6 +55,8 @@ def run(info, *, overlap, shard, accum, graph=False):
         losses.append(eng.step(batches, lr=3e-4))
     param_ready.wait_all()
     torch.cuda.synchronize()
+    if sync.owner is not None:
+        sync.owner.check()
     return [float(v) for v in losses], model_state_sha256(model)
 
 
@@ -56,7 +64,10 @@ def main():
     info = setup_distributed(timeout_s=120)
     configs = [dict(overlap=False, shard=False, accum=1), dict(overlap=True, shard=False, accum=1),
                dict(overlap=False, shard=True, accum=1), dict(overlap=True, shard=True, accum=1),
-               dict(overlap=True, shard=True, accum=2), dict(overlap=True, shard=True, accum=1, graph=True)]
+               dict(overlap=True, shard=True, accum=2), dict(overlap=True, shard=True, accum=1, graph=True),
+               dict(overlap=False, shard=True, accum=1, transport="owner"),
+               dict(overlap=False, shard=True, accum=1, transport="owner", graph=True),
+               dict(overlap=False, shard=True, accum=1, transport="owner-bf16")]
     runs = [run(info, **c) for c in configs]
     digests = [None] * info.world_size
     dist.all_gather_object(digests, [r[1] for r in runs])
@@ -69,6 +80,14 @@ def main():
         assert rel < 1e-2, (runs[3][0], runs[0][0])
         # the captured forward/backward/reduction replays the overlapped run exactly
         assert runs[5][0] == runs[3][0] and digests[0][5] == digests[0][3], (runs[5][0], runs[3][0])
+        # reduce-to-owner (fp32 transport) follows the all-reduce runs; its graph replays it exactly;
+        # bf16 transport stays close
+        rel_owner = max(abs(x - y) / abs(y) for x, y in zip(runs[6][0], runs[0][0]))
+        assert rel_owner < 1e-2, (runs[6][0], runs[0][0])
+        assert runs[7][0] == runs[6][0] and digests[0][7] == digests[0][6], (runs[7][0], runs[6][0])
+        rel_bf16 = max(abs(x - y) / abs(y) for x, y in zip(runs[8][0], runs[0][0]))
+        assert rel_bf16 < 2e-2, (runs[8][0], runs[0][0])
+        print("OWNER_OK max rel loss diff f32", rel_owner, "bf16", rel_bf16, flush=True)
         print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
     dist.barrier()
     dist.destroy_process_group()
