@@ -34,6 +34,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -589,6 +590,345 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Forward with eight softmax warps (two per TMEM lane quarter).  The warp
+// pair of a lane quarter splits every 128-column score row into two 64-column
+// halves: each half keeps its own running sum and the output columns
+// [half * HD/2, (half + 1) * HD/2) in registers, and the two halves agree on
+// the row maximum through shared memory once per tile.  Twice the warps of
+// the four-warp kernel and half the work per warp: the softmax, which bounds
+// this kernel, hides its latencies with two warps per SM sub-partition.
+// Waits that gate a whole tile are done by one thread and published with a
+// barrier reduction, so every softmax thread leaves a tile loop at the same
+// point and the named barriers that follow always see all 256 threads.
+constexpr int kThreads8 = 320;
+
+__device__ __forceinline__ bool group256_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "barrier.cta.red.and.pred p, 1, 256, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void group256_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads8, 1)
+    attn_fwd8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
+  using C = Cfg<HD>;
+  constexpr int kHalfO = HD / 2;  // output columns per warp of a pair
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + C::kQBytes;
+  uint8_t* sP = sKV + C::kStages * C::kStageBytes;
+  uint8_t* sOut = C::kOutInP ? sP : sP + 2 * C::kPBytes;
+  // row maxima / sums exchanged by the two halves: [2 buffers][2 halves][128 rows]
+  float* sX = reinterpret_cast<float*>(sP + 2 * C::kPBytes + C::kOutBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + 2 * 2 * 128);
+  const uint32_t q_full = smem_u32(bars + 0), q_empty = smem_u32(bars + 1);
+  auto kv_full = [&](int s) { return smem_u32(bars + 2 + s); };
+  auto kv_empty = [&](int s) { return smem_u32(bars + 5 + s); };
+  auto s_full = [&](int i) { return smem_u32(bars + 8 + i); };
+  auto s_empty = [&](int i) { return smem_u32(bars + 10 + i); };
+  auto p_full = [&](int i) { return smem_u32(bars + 12 + i); };
+  auto o_full = [&](int i) { return smem_u32(bars + 14 + i); };
+  auto o_empty = [&](int i) { return smem_u32(bars + 16 + i); };
+  const uint32_t done_bar = smem_u32(bars + 18);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_qt = (p.S + kBM - 1) / kBM;
+  const int items = num_qt * p.H * p.B;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_empty(i), 256);
+      mbar_init(p_full(i), 256);
+      mbar_init(o_full(i), 1);
+      mbar_init(o_empty(i), 256);
+    }
+    mbar_init(done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_async_smem();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto coords = [&](int t, int& qt, int& h, int& b) {
+    const int hb = p.H * p.B;
+    qt = num_qt - 1 - t / hb;
+    const int r = t % hb;
+    b = r / p.H;
+    h = r % p.H;
+  };
+  auto kv_tiles = [&](int qt) {
+    if (!p.causal) return (p.S + kBN - 1) / kBN;
+    const int last_row = min(qt * kBM + kBM - 1, p.S - 1);
+    return last_row / kBN + 1;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer (as in attn_fwd_kernel) ----------------
+    if (lane == 0) {
+      int stage = 0, local = 0, issued = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < items && ok; t += gridDim.x, ++local) {
+        int qt, h, b;
+        coords(t, qt, h, b);
+        if (!mbar_wait(q_empty, (local & 1) ^ 1, p.err, 1)) { ok = false; break; }
+        mbar_expect_tx(q_full, C::kQBytes);
+#pragma unroll
+        for (int a = 0; a < C::kAtoms; ++a)
+          tma_load_3d(smem_u32(sQ) + a * kBM * 128, &tmQ, q_full, h * HD + 64 * a, qt * kBM, b);
+        const int n = kv_tiles(qt);
+        for (int j = 0; j < n; ++j) {
+          if (!mbar_wait(kv_empty(stage), phase ^ 1, p.err, 2)) { ok = false; break; }
+          const uint32_t fb = kv_full(stage);
+          mbar_expect_tx(fb, C::kStageBytes);
+          const uint32_t sk = smem_u32(sKV) + stage * C::kStageBytes;
+          const uint32_t sv = sk + C::kKBytes;
+#pragma unroll
+          for (int a = 0; a < C::kAtoms; ++a) {
+            tma_load_3d(sk + a * kBN * 128, &tmK, fb, h * HD + 64 * a, j * kBN, b);
+            tma_load_3d(sv + a * kBN * 128, &tmV, fb, h * HD + 64 * a, j * kBN, b);
+          }
+          ++issued;
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < C::kStages && i < issued; ++i) {
+          if (--s < 0) { s = C::kStages - 1; ph ^= 1; }
+          mbar_wait(kv_full(s), ph, p.err, 0, kDrainNs);
+        }
+        mbar_wait(q_full, local & 1, p.err, 0, kDrainNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (as in attn_fwd_kernel) ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = instr_desc<kBN, false>();
+      constexpr uint32_t idesc_o = instr_desc<HD, true>();
+      int stage = 0, g = 0, local = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint32_t sq = smem_u32(sQ);
+      const uint32_t sp = smem_u32(sP);
+      auto issue_o = [&](int gj, int stage_j) -> bool {
+        const int buf = gj & 1;
+        const uint32_t par = (gj >> 1) & 1;
+        if (!mbar_wait(p_full(buf), par, p.err, 5)) return false;
+        if (!mbar_wait(o_empty(buf), par ^ 1, p.err, 6)) return false;
+        tc_fence_after();
+        const uint32_t tmem_o = tmem_base + C::kTmemO + buf * HD;
+        const uint32_t pa = sp + buf * C::kPBytes;
+        const uint32_t vb = smem_u32(sKV) + stage_j * C::kStageBytes + C::kKBytes;
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          const uint64_t ad = smem_desc(pa + (k >> 2) * (kBM * 128) + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc(vb + k * 16 * 128, kBN * 128, 1024);
+          tc_mma(tmem_o, ad, bd, idesc_o, k != 0 ? 1u : 0u);
+        }
+        tc_commit(o_full(buf));
+        tc_commit(kv_empty(stage_j));
+        return true;
+      };
+      for (int t = blockIdx.x; t < items && ok; t += gridDim.x, ++local) {
+        int qt, h, b;
+        coords(t, qt, h, b);
+        const int n = kv_tiles(qt);
+        if (!mbar_wait(q_full, local & 1, p.err, 3)) { ok = false; break; }
+        int prev_stage = -1;
+        for (int j = 0; j < n; ++j, ++g) {
+          const int buf = g & 1;
+          const uint32_t par = (g >> 1) & 1;
+          if (!mbar_wait(kv_full(stage), phase, p.err, 4)) { ok = false; break; }
+          if (!mbar_wait(s_empty(buf), par ^ 1, p.err, 7)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tmem_s = tmem_base + C::kTmemS + buf * kBN;
+          const uint32_t kb = smem_u32(sKV) + stage * C::kStageBytes;
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint32_t off = (k >> 2) * (kBM * 128) + (k & 3) * 32;
+            tc_mma(tmem_s, smem_desc(sq + off, 16, 1024), smem_desc(kb + (k >> 2) * (kBN * 128) + (k & 3) * 32, 16, 1024),
+                   idesc_s, k != 0 ? 1u : 0u);
+          }
+          tc_commit(s_full(buf));
+          if (j == n - 1) tc_commit(q_empty);
+          if (j > 0 && !issue_o(g - 1, prev_stage)) { ok = false; break; }
+          prev_stage = stage;
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (!issue_o(g - 1, prev_stage)) { ok = false; break; }
+      }
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, p.err, 0, kDrainNs);
+    }
+  } else {
+    // ---------------- softmax (warps 2..9) ----------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;             // warps 2..5: columns 0..63, warps 6..9: 64..127
+    const int row = quarter * 32 + lane;
+    const int tid = threadIdx.x - 64;             // 0..255
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t sp = smem_u32(sP);
+    const uint32_t so = smem_u32(sOut);
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < items && ok; t += gridDim.x) {
+      int qt, h, b;
+      coords(t, qt, h, b);
+      const int n = kv_tiles(qt);
+      const int q_index = qt * kBM + row;
+      float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+      float o[kHalfO];
+#pragma unroll
+      for (int c = 0; c < kHalfO; ++c) o[c] = 0.f;
+      if constexpr (C::kOutInP) {
+        if (tid == 0) bulk_wait_read_all();
+        group256_sync();
+      }
+      // o = o * a + (this half's columns of O_gj)
+      auto take_o = [&](int gj, float a) {
+        const int buf = gj & 1;
+        float v[kHalfO];
+        tmem_ld32xN<kHalfO / 32>(tmem_base + lane_off + C::kTmemO + buf * HD + half * kHalfO, v);
+#pragma unroll
+        for (int i = 0; i < kHalfO; ++i) o[i] = fmaf(o[i], a, v[i]);
+        tc_fence_before();
+        mbar_arrive(o_empty(buf));
+      };
+      bool good = true;
+      for (int j = 0; j < n; ++j, ++g) {
+        const int buf = g & 1;
+        // one thread waits for S_g (and for O_{g-1}, issued right after S_g)
+        bool w = true;
+        if (tid == 0) {
+          w = mbar_wait(s_full(buf), (g >> 1) & 1, p.err, 8);
+          if (w && j > 0) w = mbar_wait(o_full((g - 1) & 1), ((g - 1) >> 1) & 1, p.err, 9);
+        }
+        if (!group256_all(w)) { good = false; break; }
+        tc_fence_after();
+        if (j > 0) take_o(g - 1, alpha_prev);
+        const uint32_t ts = tmem_base + lane_off + C::kTmemS + buf * kBN + half * 64;
+        const int kv0 = j * kBN + half * 64;
+        int limit = 64;
+        if (p.causal) limit = min(limit, q_index - kv0 + 1);
+        limit = min(limit, p.S - kv0);
+        float sv[64];
+        tmem_ld32xN<2>(ts, sv);
+        if (limit < 64) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i >= limit) sv[i] = -INFINITY;
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
+        // buffer g % 2: the write two tiles later comes after the consensus barrier
+        // that every thread passes only once it has read this one
+        float* xb = sX + buf * 256;
+        xb[half * 128 + row] = mx;
+        group256_sync();
+        mx = fmaxf(mx, xb[(half ^ 1) * 128 + row]);
+        const float m_new = fmaxf(m, mx * p.scale_log2);
+        const float alpha = fast_exp2(m - m_new);
+        float sum = 0.f;
+        const uint32_t atom = sp + buf * C::kPBytes + half * (kBM * 128) + row * 128;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = fast_exp2(fmaf(sv[32 * c + i], p.scale_log2, -m_new));
+            const float p1 = fast_exp2(fmaf(sv[32 * c + i + 1], p.scale_log2, -m_new));
+            sum += p0 + p1;
+            packed[i / 2] = pack_bf16(p0, p1);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t chunk = static_cast<uint32_t>((c * 4 + q) ^ (row & 7));
+            st_shared_v4(atom + chunk * 16, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(s_empty(buf));
+        fence_async_smem();
+        mbar_arrive(p_full(buf));
+        l = fmaf(l, alpha, sum);
+        alpha_prev = alpha;
+        m = m_new;
+      }
+      if (!good) { ok = false; break; }
+      bool w = true;
+      if (tid == 0) w = mbar_wait(o_full((g - 1) & 1), ((g - 1) >> 1) & 1, p.err, 9);
+      if (!group256_all(w)) { ok = false; break; }
+      tc_fence_after();
+      take_o(g - 1, alpha_prev);
+      // ---- epilogue: the row sum is the sum of the halves' sums
+      sX[half * 128 + row] = l;
+      if constexpr (!C::kOutInP) {
+        if (tid == 0) bulk_wait_read_all();
+      }
+      group256_sync();
+      const float l_all = l + sX[(half ^ 1) * 128 + row];
+      const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
+      // this half's HD/2 columns: atom (half * HD/2) / 64, chunks (half * HD/2 % 64) / 8 ...
+#pragma unroll
+      for (int c0 = 0; c0 < kHalfO; c0 += 8) {
+        const int col = half * kHalfO + c0;
+        const uint32_t base = so + (col / 64) * (kBM * 128) + row * 128;
+        const uint32_t chunk = static_cast<uint32_t>(((col % 64) / 8) ^ (row & 7));
+        st_shared_v4(base + chunk * 16, pack_bf16(o[c0] * inv, o[c0 + 1] * inv),
+                     pack_bf16(o[c0 + 2] * inv, o[c0 + 3] * inv), pack_bf16(o[c0 + 4] * inv, o[c0 + 5] * inv),
+                     pack_bf16(o[c0 + 6] * inv, o[c0 + 7] * inv));
+      }
+      if (half == 0 && q_index < p.S)
+        p.lse2[(static_cast<int64_t>(b) * p.H + h) * p.S + q_index] = m + log2f(l_all);
+      fence_async_smem();
+      group256_sync();
+      if (tid == 0) {
+#pragma unroll
+        for (int a = 0; a < C::kAtoms; ++a) tma_store_3d(&tmO, so + a * (kBM * 128), h * HD + 64 * a, qt * kBM, b);
+        bulk_commit();
+      }
+    }
+    if (tid == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::kTmemCols));
+}
+
+// ---------------------------------------------------------------------------
 // Backward.  Deterministic (no atomics): two passes that each own their output
 // tile, with the usual recomputation of P from lse2.
 //
@@ -667,6 +1007,20 @@ __device__ __forceinline__ void stage_row(uint32_t staging, int row, const float
   }
 }
 
+// The HD/2 columns [half * HD/2, (half + 1) * HD/2) of `row` (values in `v`)
+// as bf16 into a 128B-swizzled staging tile.
+template <int HD>
+__device__ __forceinline__ void stage_row_half(uint32_t staging, int row, int half, const float (&v)[HD / 2]) {
+#pragma unroll
+  for (int c0 = 0; c0 < HD / 2; c0 += 8) {
+    const int col = half * (HD / 2) + c0;
+    const uint32_t base = staging + (col / 64) * (128 * 128) + row * 128;
+    const uint32_t chunk = static_cast<uint32_t>(((col % 64) / 8) ^ (row & 7));
+    st_shared_v4(base + chunk * 16, pack_bf16(v[c0], v[c0 + 1]), pack_bf16(v[c0 + 2], v[c0 + 3]),
+                 pack_bf16(v[c0 + 4], v[c0 + 5]), pack_bf16(v[c0 + 6], v[c0 + 7]));
+  }
+}
+
 // Write 32 bf16 values (16 packed words) of columns [32c, 32c+32) of `row`
 // into a [128 x 128] K-major 128B-swizzled operand tile.
 __device__ __forceinline__ void store_operand_chunk(uint32_t tile, int row, int c, const uint32_t (&w)[16]) {
@@ -691,7 +1045,7 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[HD]) {
 
 // ---- dQ: query-stationary ------------------------------------------------------
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads8, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                        const __grid_constant__ CUtensorMap tmDQ, BwdParams p) {
@@ -724,11 +1078,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_empty(s), 1);
     }
     mbar_init(st_full, 1);
-    mbar_init(st_empty, 128);
-    mbar_init(ds_full, 128);
+    mbar_init(st_empty, 256);
+    mbar_init(ds_full, 256);
     mbar_init(ds_empty, 1);
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    mbar_init(acc_empty, 256);
     mbar_init(done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
@@ -856,8 +1210,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(done_bar, 0, p.err, 0, kDrainNs);
     }
   } else {
+    // eight compute warps: the pair of a lane quarter splits the 128 key columns
+    // (and the head_dim columns of dQ) into two halves
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
+    const int tid = threadIdx.x - 64;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t sds = smem_u32(sDS);
     int g = 0, local = 0;
@@ -871,65 +1229,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float lse = q_index < p.S ? p.lse2[stat] : INFINITY;
       const float dlt = q_index < p.S ? p.delta[stat] : 0.f;
       // the previous item's dQ store reads the dS buffer (it doubles as staging)
-      if (threadIdx.x == 64) bulk_wait_read_all();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid == 0) bulk_wait_read_all();
+      group256_sync();
       bool good = true;
       for (int j = 0; j < n; ++j, ++g) {
-        if (!mbar_wait(st_full, g & 1, p.err, 28)) { good = false; break; }
-        if (!mbar_wait(ds_empty, (g & 1) ^ 1, p.err, 29)) { good = false; break; }
+        bool w = true;
+        if (tid == 0) w = mbar_wait(st_full, g & 1, p.err, 28) && mbar_wait(ds_empty, (g & 1) ^ 1, p.err, 29);
+        if (!group256_all(w)) { good = false; break; }
         tc_fence_after();
-        const int kv0 = j * 128;
-        int limit = 128;
+        const int kv0 = j * 128 + half * 64;
+        int limit = 64;
         if (p.causal) limit = min(limit, q_index - kv0 + 1);
         limit = min(limit, p.S - kv0);
-        const bool full = limit >= 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float s[32], dp[32];
-          tmem_ld32(tmem_base + lane_off + C::kTmemS + 32 * c, s);
-          tmem_ld32(tmem_base + lane_off + C::kTmemDP + 32 * c, dp);
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float p0 = fast_exp2(fmaf(s[i], p.scale_log2, -lse));
-            float p1 = fast_exp2(fmaf(s[i + 1], p.scale_log2, -lse));
-            if (!full) {
-              p0 = 32 * c + i < limit ? p0 : 0.f;
-              p1 = 32 * c + i + 1 < limit ? p1 : 0.f;
-            }
-            w[i / 2] = pack_bf16(p0 * (dp[i] - dlt), p1 * (dp[i + 1] - dlt));
-          }
-          store_operand_chunk(sds, row, c, w);
-        }
+        const bool full = limit >= 64;
+        float s[64], dp[64];
+        tmem_ld32xN<2>(tmem_base + lane_off + C::kTmemS + half * 64, s);
+        tmem_ld32xN<2>(tmem_base + lane_off + C::kTmemDP + half * 64, dp);
         tc_fence_before();
         mbar_arrive(st_empty);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t w2[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int col = 32 * c + i;
+            float p0 = fast_exp2(fmaf(s[col], p.scale_log2, -lse));
+            float p1 = fast_exp2(fmaf(s[col + 1], p.scale_log2, -lse));
+            if (!full) {
+              p0 = col < limit ? p0 : 0.f;
+              p1 = col + 1 < limit ? p1 : 0.f;
+            }
+            w2[i / 2] = pack_bf16(p0 * (dp[col] - dlt), p1 * (dp[col + 1] - dlt));
+          }
+          store_operand_chunk(sds, row, 2 * half + c, w2);
+        }
         fence_async_smem();
         mbar_arrive(ds_full);
       }
-      ok = group_all(good);
-      if (!ok) break;
-      // epilogue: dQ = scale * acc -> bf16 -> staging (the dS buffer) -> TMA store
-      if (!mbar_wait(acc_full, local & 1, p.err, 30)) good = false;
-      // the last dQ MMA read dS: it is complete once acc_full fired
-      ok = group_all(good);
-      if (!ok) break;
+      if (!good) { ok = false; break; }
+      // epilogue: dQ = scale * acc -> bf16 -> staging (the dS buffer) -> TMA store;
+      // the last dQ product read dS, and it has completed once acc_full fired
+      bool w = true;
+      if (tid == 0) w = mbar_wait(acc_full, local & 1, p.err, 30);
+      if (!group256_all(w)) { ok = false; break; }
       tc_fence_after();
-      float v[HD];
-      tmem_ld_row<HD>(tmem_base + lane_off + C::kTmemAcc, v);
+      float v[HD / 2];
+      tmem_ld32xN<HD / 64>(tmem_base + lane_off + C::kTmemAcc + half * (HD / 2), v);
       tc_fence_before();
       mbar_arrive(acc_empty);
 #pragma unroll
-      for (int c = 0; c < HD; ++c) v[c] *= p.scale;
-      stage_row<HD>(sds, row, v);
+      for (int c = 0; c < HD / 2; ++c) v[c] *= p.scale;
+      stage_row_half<HD>(sds, row, half, v);
       fence_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
+      group256_sync();
+      if (tid == 0) {
 #pragma unroll
         for (int a = 0; a < C::kAtoms; ++a) tma_store_3d(&tmDQ, sds + a * 16384, h * HD + 64 * a, qt * 128, b);
         bulk_commit();
       }
     }
-    if (threadIdx.x == 64) bulk_wait_all();
+    if (tid == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -940,7 +1299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---- dK, dV: key-stationary ----------------------------------------------------------
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads8, 1)
     attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                          const __grid_constant__ CUtensorMap tmDK, const __grid_constant__ CUtensorMap tmDV,
@@ -976,11 +1335,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(qd_empty(s), 1);
     }
     mbar_init(st_full, 1);
-    mbar_init(st_empty, 128);
-    mbar_init(pd_full, 128);
+    mbar_init(st_empty, 256);
+    mbar_init(pd_full, 256);
     mbar_init(pd_empty, 1);
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    mbar_init(acc_empty, 256);
     mbar_init(done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
@@ -1111,10 +1470,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(done_bar, 0, p.err, 0, kDrainNs);
     }
   } else {
+    // eight compute warps: the pair of a lane quarter splits the 128 query
+    // columns (and the head_dim columns of dK and dV) into two halves
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;          // key row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int tid = threadIdx.x - 64;             // 0..127
+    const int tid = threadIdx.x - 64;             // 0..255
     const uint32_t spt = smem_u32(sPT), sdst = smem_u32(sDST);
     int g = 0, local = 0;
     bool ok = true;
@@ -1126,69 +1488,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int k_index = kt * 128 + row;
       const int64_t stat_row = (static_cast<int64_t>(b) * p.H + h) * p.S;
       // the previous item's dK / dV stores read the P^T and dS^T buffers
-      if (threadIdx.x == 64) bulk_wait_read_all();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid == 0) bulk_wait_read_all();
+      group256_sync();
       bool good = true;
       for (int i = 0; i < n; ++i, ++g) {
         const int q0 = (i0 + i) * 128;
-        // lse2 / delta of this query tile (buffer g % 2); masked rows get lse = inf
+        // lse2 / delta of this query tile (buffer g % 2); masked columns get lse = inf
         float* st = sStat + (g & 1) * 256;
-        const int qi = q0 + tid;
-        st[tid] = qi < p.S ? p.lse2[stat_row + qi] : INFINITY;
-        st[128 + tid] = qi < p.S ? p.delta[stat_row + qi] : 0.f;
+        if (tid < 128) {
+          const int qi = q0 + tid;
+          st[tid] = qi < p.S ? p.lse2[stat_row + qi] : INFINITY;
+          st[128 + tid] = qi < p.S ? p.delta[stat_row + qi] : 0.f;
+        }
         // one thread waits for the products and the free operand buffers; the
-        // group barrier publishes the statistics and the outcome to all 128
+        // group barrier publishes the statistics and the outcome to all 256
         bool w = true;
         if (tid == 0) w = mbar_wait(st_full, g & 1, p.err, 48) && mbar_wait(pd_empty, (g & 1) ^ 1, p.err, 49);
-        if (!group_all(w)) { good = false; break; }
+        if (!group256_all(w)) { good = false; break; }
         tc_fence_after();
-        // query column c is allowed for this key when q0 + c >= k_index (causal)
-        const int lo = p.causal ? k_index - q0 : 0;
+        float s2[64], dp[64];
+        tmem_ld32xN<2>(tmem_base + lane_off + C::kTmemS + half * 64, s2);
+        tmem_ld32xN<2>(tmem_base + lane_off + C::kTmemDP + half * 64, dp);
+        tc_fence_before();
+        mbar_arrive(st_empty);
+        // query column c (of this half) is allowed for this key when q0 + c >= k_index
+        const int lo = p.causal ? k_index - q0 - half * 64 : 0;
+        const float* lse = st + half * 64;
+        const float* dlt = st + 128 + half * 64;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float s[32], dp[32];
-          tmem_ld32(tmem_base + lane_off + C::kTmemS + 32 * c, s);
-          tmem_ld32(tmem_base + lane_off + C::kTmemDP + 32 * c, dp);
+        for (int c = 0; c < 2; ++c) {
           uint32_t wp[16], wd[16];
 #pragma unroll
           for (int i2 = 0; i2 < 32; i2 += 2) {
             const int col = 32 * c + i2;
-            float p0 = fast_exp2(fmaf(s[i2], p.scale_log2, -st[col]));
-            float p1 = fast_exp2(fmaf(s[i2 + 1], p.scale_log2, -st[col + 1]));
+            float p0 = fast_exp2(fmaf(s2[col], p.scale_log2, -lse[col]));
+            float p1 = fast_exp2(fmaf(s2[col + 1], p.scale_log2, -lse[col + 1]));
             if (lo > 0) {
               p0 = col >= lo ? p0 : 0.f;
               p1 = col + 1 >= lo ? p1 : 0.f;
             }
             wp[i2 / 2] = pack_bf16(p0, p1);
-            wd[i2 / 2] = pack_bf16(p0 * (dp[i2] - st[128 + col]), p1 * (dp[i2 + 1] - st[128 + col + 1]));
+            wd[i2 / 2] = pack_bf16(p0 * (dp[col] - dlt[col]), p1 * (dp[col + 1] - dlt[col + 1]));
           }
-          store_operand_chunk(spt, row, c, wp);
-          store_operand_chunk(sdst, row, c, wd);
+          store_operand_chunk(spt, row, 2 * half + c, wp);
+          store_operand_chunk(sdst, row, 2 * half + c, wd);
         }
-        tc_fence_before();
-        mbar_arrive(st_empty);
         fence_async_smem();
         mbar_arrive(pd_full);
       }
-      // every thread left the tile loop at the same point (uniform outcome)
       if (!good) { ok = false; break; }
-      if (!mbar_wait(acc_full, local & 1, p.err, 50)) good = false;
-      ok = group_all(good);
-      if (!ok) break;
+      bool w = true;
+      if (tid == 0) w = mbar_wait(acc_full, local & 1, p.err, 50);
+      if (!group256_all(w)) { ok = false; break; }
       tc_fence_after();
-      float v[HD];
-      tmem_ld_row<HD>(tmem_base + lane_off + C::kTmemAcc, v);        // dV
-      stage_row<HD>(spt, row, v);
-      tmem_ld_row<HD>(tmem_base + lane_off + C::kTmemAcc + HD, v);   // dK
+      float v[HD / 2];
+      tmem_ld32xN<HD / 64>(tmem_base + lane_off + C::kTmemAcc + half * (HD / 2), v);        // dV
+      stage_row_half<HD>(spt, row, half, v);
+      tmem_ld32xN<HD / 64>(tmem_base + lane_off + C::kTmemAcc + HD + half * (HD / 2), v);   // dK
       tc_fence_before();
       mbar_arrive(acc_empty);
 #pragma unroll
-      for (int c = 0; c < HD; ++c) v[c] *= p.scale;
-      stage_row<HD>(sdst, row, v);
-      (void)k_index;
+      for (int c = 0; c < HD / 2; ++c) v[c] *= p.scale;
+      stage_row_half<HD>(sdst, row, half, v);
       fence_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
+      group256_sync();
+      if (tid == 0) {
 #pragma unroll
         for (int a = 0; a < C::kAtoms; ++a) {
           tma_store_3d(&tmDV, spt + a * 16384, h * HD + 64 * a, kt * 128, b);
@@ -1197,7 +1561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_commit();
       }
     }
-    if (threadIdx.x == 64) bulk_wait_all();
+    if (tid == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -1260,16 +1624,35 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, int6
       !make_plane_map(&mv, v, p.B, p.S, cols, ld) || !make_plane_map(&mo, o, p.B, p.S, cols, ldo))
     return -3;
   static_assert(C::kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
+  // the eight-softmax-warp kernel needs 2 KB more shared memory (row exchange);
+  // RO_ATTN_FWD_WARPS=4 selects the four-warp kernel (comparison)
+  // (head_dim 128 leaves no room for it: that size runs the four-warp kernel)
+  constexpr int kSmem8 = C::kSmemBytes + 2 * 2 * 128 * 4;
+  constexpr bool kHas8 = HD == 64;
+  static_assert(!kHas8 || kSmem8 <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
+  static const bool four_warps = [] {
+    const char* v = std::getenv("RO_ATTN_FWD_WARPS");
+    return v != nullptr && v[0] == '4';
+  }();
   static int configured = 0;
   if (configured == 0) {
-    configured = cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      C::kSmemBytes) == cudaSuccess ? 1 : -1;
+    const bool a = cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::kSmemBytes) == cudaSuccess;
+    const bool b = !kHas8 || cudaFuncSetAttribute(attn_fwd8_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  kSmem8) == cudaSuccess;
+    configured = a && b ? 1 : -1;
     cudaGetLastError();
   }
   if (configured < 0) return -4;
   const int items = ((p.S + kBM - 1) / kBM) * p.H * p.B;
   int grid = num_sms();
   if (items < grid) grid = items;
+  if constexpr (kHas8) {
+    if (!four_warps) {
+      attn_fwd8_kernel<HD><<<grid, kThreads8, kSmem8, stream>>>(mq, mk, mv, mo, p);
+      return static_cast<int>(cudaGetLastError());
+    }
+  }
   attn_fwd_kernel<HD><<<grid, kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, mo, p);
   return static_cast<int>(cudaGetLastError());
 }
@@ -1309,10 +1692,10 @@ static int launch_bwd(const void* q, const void* k, const void* v, int64_t ld, c
   const int items = ((p.S + 127) / 128) * p.H * p.B;
   int grid = num_sms();
   if (items < grid) grid = items;
-  attn_bwd_dkdv_kernel<HD><<<grid, kThreads, kSmemKV, stream>>>(mq, mk, mv, mdo, mdk, mdv, p);
+  attn_bwd_dkdv_kernel<HD><<<grid, kThreads8, kSmemKV, stream>>>(mq, mk, mv, mdo, mdk, mdv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
-  attn_bwd_dq_kernel<HD><<<grid, kThreads, kSmemDQ, stream>>>(mq, mk, mv, mdo, mdq, p);
+  attn_bwd_dq_kernel<HD><<<grid, kThreads8, kSmemDQ, stream>>>(mq, mk, mv, mdo, mdq, p);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -69,6 +69,7 @@ class OwnerGather:
         self.published = C.comm_alloc(16, self.device.index)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.pending = False
+        param_ready.register_puller(self, replace=True)
         local = (C.comm_handle(raw), C.comm_handle(self.published))
         gathered = [None] * self.world
         dist.all_gather_object(gathered, local, group=group)
@@ -88,7 +89,6 @@ class OwnerGather:
     def publish(self):
         _ext.ext().owner_publish(self.published)
         self.pending = True
-        param_ready.register_puller(self)
         for r in range(self.world):
             if r != self.rank:
                 for p in self.params_by_owner[r]:

@@ -20,7 +20,11 @@ _STREAMS: dict[int, torch.cuda.Stream] = {}
 _PULLERS: list = []
 
 
-def register_puller(obj) -> None:
+def register_puller(obj, *, replace=False) -> None:
+    """Add ``obj``; ``replace=True`` first drops every other puller on the same device
+    (a newly built model's replication supersedes the previous model's)."""
+    if replace:
+        _PULLERS[:] = [o for o in _PULLERS if getattr(o, "device", None) != getattr(obj, "device", None)]
     if obj not in _PULLERS:
         _PULLERS.append(obj)
 
@@ -58,7 +62,9 @@ def defer(params, event: torch.cuda.Event) -> None:
 
 
 def pending() -> bool:
-    return bool(_PENDING)
+    """True while some parameter may still be waiting for its replication
+    (an event to wait on, or a lazy pull not enqueued yet)."""
+    return bool(_PENDING) or any(obj.pending for obj in _PULLERS)
 
 
 def pullers() -> list:

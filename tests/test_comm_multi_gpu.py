@@ -36,3 +36,4 @@ def test_overlapped_sharded_training_matches_replicated():
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert f"TRAIN_OK {n}" in res.stdout
     assert "OWNER_OK" in res.stdout
+    assert "PULL_OK" in res.stdout

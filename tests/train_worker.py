@@ -26,8 +26,9 @@ from rational_optimizer_b200.train.engine import TrainEngine  # noqa: E402
 from rational_optimizer_b200.train.integrity import model_state_sha256  # noqa: E402
 
 
-def run(info, *, overlap, shard, accum, graph=False, transport="nccl"):
+def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="nccl"):
     os.environ["RO_TILLER_SHARD"] = "1" if shard else "0"
+    os.environ["RO_WEIGHT_TRANSPORT"] = weights
     os.environ["RO_CUDA_GRAPH"] = "1" if graph else "0"
     torch.manual_seed(0)
     args = preset("18l_1024d", layers=4, seq_len=256, activation="grain")
@@ -67,7 +68,9 @@ def main():
                dict(overlap=True, shard=True, accum=2), dict(overlap=True, shard=True, accum=1, graph=True),
                dict(overlap=False, shard=True, accum=1, transport="owner"),
                dict(overlap=False, shard=True, accum=1, transport="owner", graph=True),
-               dict(overlap=False, shard=True, accum=1, transport="owner-bf16")]
+               dict(overlap=False, shard=True, accum=1, transport="owner-bf16"),
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p"),
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", graph=True)]
     runs = [run(info, **c) for c in configs]
     digests = [None] * info.world_size
     dist.all_gather_object(digests, [r[1] for r in runs])
@@ -88,6 +91,11 @@ def main():
         rel_bf16 = max(abs(x - y) / abs(y) for x, y in zip(runs[8][0], runs[0][0]))
         assert rel_bf16 < 2e-2, (runs[8][0], runs[0][0])
         print("OWNER_OK max rel loss diff f32", rel_owner, "bf16", rel_bf16, flush=True)
+        # weights pulled from their owners over peer memory: the same numbers as the
+        # NCCL broadcasts, eagerly and from the step graph
+        assert runs[9][0] == runs[6][0] and digests[0][9] == digests[0][6], (runs[9][0], runs[6][0])
+        assert runs[10][0] == runs[6][0] and digests[0][10] == digests[0][6], (runs[10][0], runs[6][0])
+        print("PULL_OK", flush=True)
         print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
     dist.barrier()
     dist.destroy_process_group()
