@@ -1625,14 +1625,15 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, int6
     return -3;
   static_assert(C::kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
   // the eight-softmax-warp kernel needs 2 KB more shared memory (row exchange);
-  // RO_ATTN_FWD_WARPS=4 selects the four-warp kernel (comparison)
+  // RO_ATTN_FWD_WARPS=8 selects it (measured slower than the four-warp kernel
+  // at the 18-layer shape: 0.270 against 0.207 ms)
   // (head_dim 128 leaves no room for it: that size runs the four-warp kernel)
   constexpr int kSmem8 = C::kSmemBytes + 2 * 2 * 128 * 4;
   constexpr bool kHas8 = HD == 64;
   static_assert(!kHas8 || kSmem8 <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
   static const bool four_warps = [] {
     const char* v = std::getenv("RO_ATTN_FWD_WARPS");
-    return v != nullptr && v[0] == '4';
+    return !(v != nullptr && v[0] == '8');
   }();
   static int configured = 0;
   if (configured == 0) {

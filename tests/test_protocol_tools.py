@@ -124,3 +124,65 @@ def test_source_freeze_agrees_with_the_reference_tool(tmp_path, monkeypatch):
     ours = FZ.Freeze.collect(root, manifests=ref.MANIFESTS,
                              output="experiments/protocol/SOURCE_FREEZE.sha256").render()
     assert ours == theirs
+
+
+def _arm_records(row, arm, losses, *, lr_digest="d" * 64, fingerprint="f" * 64, seconds=100.0):
+    from rational_optimizer_b200.protocol import rows as R
+    side = "control" if arm == "control" else "candidate"
+    cfg = {"event": "config", "activation": row[f"{side}_activation"], "optimizer": row[f"{side}_optimizer"],
+           "dataset": row["dataset_name"], "dataset_config": row["dataset_config"],
+           "dataset_revision": row["dataset_revision"], "tokenizer": row["tokenizer"],
+           "tokenizer_revision": row["tokenizer_revision"], "steps": row["steps"], "seed": row["seed"],
+           "train_tokens": row["max_train_tokens"], "val_tokens": row["max_val_tokens"],
+           "optimizer_lr_wd_fairness": {"passed": True, "base_lr": row["lr"], "minimum_lr": row["min_lr"],
+                                        "base_weight_decay": row["weight_decay"],
+                                        "groups": [{"group_index": 0, "lr_scale": 1.0, "weight_decay": 0.1}]},
+           "train_token_sample_sha256": fingerprint, "val_token_sample_sha256": "v" * 64,
+           "first_batch_index_sha256": "b" * 64, "validation_index_sha256": "i" * 64}
+    if arm == "candidate":
+        cfg["experiment_identity"] = R.experiment_identity(row)
+        cfg["tiller_experiment_identity"] = {"passed": True, "matrix_index": row["matrix_index"],
+                                             "source_manifest_row_index": row["source_manifest_row_index"],
+                                             "source_manifest_row_id": row["source_manifest_row_id"]}
+    recs = [cfg] + [{"event": "eval", "step": s, "val_loss": v} for s, v in losses.items()]
+    recs.append({"event": "summary", "realized_lr_audit_steps": row["steps"],
+                 "realized_lr_trace_sha256": lr_digest, "total_seconds": seconds})
+    return recs
+
+
+def _write_jsonl(path, recs):
+    path.write_text("".join(json.dumps(r) + "\n" for r in recs))
+    return path
+
+
+def test_endpoint_analysis_and_aggregate(tmp_path):
+    from test_protocol import _row
+    from rational_optimizer_b200.protocol import analyze as AN
+    row = _row()
+    ctrl = _write_jsonl(tmp_path / "c.jsonl", _arm_records(row, "control", {1000: 4.5, 3050: 4.29}, seconds=100.0))
+    cand = _write_jsonl(tmp_path / "k.jsonl", _arm_records(row, "candidate", {1000: 4.4, 3050: 4.22}, seconds=104.0))
+    res = AN.endpoint_result(row, ctrl, cand)
+    assert res["status"] == "complete" and res["schema"] == AN.SCHEMA
+    assert abs(res["absolute_endpoint_lead"] - 0.07) < 1e-12 and abs(res["step1000_absolute_lead"] - 0.1) < 1e-12
+    assert abs(res["exact_matched_hardware_end_to_end_total_time_ratio"] - 1.04) < 1e-12
+    assert res["passes_final_1_05_time_gate"] and res["time_scope"] == "training_loop"
+    AN.write_result(tmp_path / "r.json", res)
+    assert (tmp_path / "r.json.sha256").read_text().split()[0] == AN._sha(tmp_path / "r.json")
+    # a candidate that trails at the screen step is an invalid (uninterrupted) row
+    bad = _write_jsonl(tmp_path / "k2.jsonl", _arm_records(row, "candidate", {1000: 4.6, 3050: 4.2}))
+    assert AN.endpoint_result(row, ctrl, bad)["status"] == "invalid_not_interrupted"
+    summary = AN.aggregate([res, AN.endpoint_result(row, ctrl, bad)])
+    g = summary["groups"][0]
+    assert g["rows"] == 2 and g["complete_rows"] == 1 and g["candidate_endpoint_wins"] == 1
+    # different data order or LR schedule between the arms is rejected
+    other = _write_jsonl(tmp_path / "k3.jsonl", _arm_records(row, "candidate", {1000: 4.4, 3050: 4.2},
+                                                              fingerprint="0" * 64))
+    with pytest.raises(RuntimeError, match="same data"):
+        AN.endpoint_result(row, ctrl, other)
+    sched = _write_jsonl(tmp_path / "k4.jsonl", _arm_records(row, "candidate", {1000: 4.4, 3050: 4.2},
+                                                              lr_digest="e" * 64))
+    with pytest.raises(RuntimeError, match="LR schedule"):
+        AN.endpoint_result(row, ctrl, sched)
+    missing = _write_jsonl(tmp_path / "k5.jsonl", _arm_records(row, "candidate", {1000: 4.4}))
+    with pytest.raises(RuntimeError, match="lacks evaluations"):
+        AN.endpoint_result(row, ctrl, missing)
