@@ -37,3 +37,19 @@ def test_overlapped_sharded_training_matches_replicated():
     assert f"TRAIN_OK {n}" in res.stdout
     assert "OWNER_OK" in res.stdout
     assert "PULL_OK" in res.stdout
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs at least two GPUs")
+def test_transport_smoke():
+    n = min(torch.cuda.device_count(), 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29519",
+           "-m", "rational_optimizer_b200.protocol.smoke"]
+    res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    line = [l for l in res.stdout.splitlines() if l.startswith("{")][-1]
+    import json
+    out = json.loads(line)
+    assert out["passed"] is True and out["world_size"] == n

@@ -186,3 +186,146 @@ def test_endpoint_analysis_and_aggregate(tmp_path):
     missing = _write_jsonl(tmp_path / "k5.jsonl", _arm_records(row, "candidate", {1000: 4.4}))
     with pytest.raises(RuntimeError, match="lacks evaluations"):
         AN.endpoint_result(row, ctrl, missing)
+
+
+def test_fairness_audit_of_both_arms():
+    from test_protocol import _row
+    from rational_optimizer_b200.protocol import fairness as FA
+    row = _row()
+    row.update(layers=2, d_model=128, heads=4, ffn_dim=256)  # the audit logic, not the size, is under test
+    payload = FA.audit_rows([row])
+    assert payload["schema"] == FA.SCHEMA and payload["passed"] is True
+    arms = {r["arm"]: r for r in payload["reports"]}
+    assert arms["control"]["optimizer"] == "muon" and arms["candidate"]["optimizer"] == "tiller_v1"
+    assert all(r["covered_parameter_elements"] == r["trainable_parameter_elements"] for r in payload["reports"])
+
+
+def test_results_summary_reproduces_every_published_summary_table():
+    """summary.csv of each optimizer, recomputed from its published runs.csv, byte for byte."""
+    import csv
+    import io
+    from rational_optimizer_b200.protocol import results as RS
+    _need_data()
+    tables = [d for d in sorted(os.listdir(RESULTS)) if os.path.isfile(os.path.join(RESULTS, d, "runs.csv"))]
+    assert set(tables) == set(RS.TABLE_DIRS.values())
+    for d in tables:
+        with open(os.path.join(RESULTS, d, "runs.csv"), newline="") as fh:
+            reader = csv.DictReader(fh)
+            assert tuple(reader.fieldnames) == RS.RUN_FIELDS
+            runs = list(reader)
+        buf = io.StringIO()
+        w = csv.DictWriter(buf, fieldnames=list(RS.SUMMARY_FIELDS), lineterminator="\n")
+        w.writeheader()
+        w.writerows(RS.summarize(runs))
+        with open(os.path.join(RESULTS, d, "summary.csv"), newline="") as fh:
+            assert buf.getvalue() == fh.read(), d
+        with open(os.path.join(RESULTS, d, "checkpoints.csv"), newline="") as fh:
+            assert tuple(csv.DictReader(fh).fieldnames) == RS.CHECKPOINT_FIELDS
+
+
+def _write_run(path, *, steps, losses, summary=True, stopped=False, torn=False, tps=1000.0):
+    import json
+    path.parent.mkdir(parents=True, exist_ok=True)
+    recs = [{"event": "config", "optimizer_lr_wd_fairness": {"passed": True}, "slurm_job_id": "7"}]
+    recs += [{"event": "eval", "step": s, "val_loss": v, "val_ppl": 2.0 ** v, "active_seconds_at_val_loss": s / 10}
+             for s, v in losses.items()]
+    if stopped:
+        recs.append({"event": "stopped_early", "step": max(losses)})
+    if summary:
+        recs.append({"event": "summary", "completed_steps": max(losses), "stopped_early": stopped,
+                     "total_seconds": 50.0, "mean_seconds_per_step": 0.01, "tokens_per_second": tps,
+                     "realized_lr_trace_sha256": "ab" * 32, "slurm_job_id": "7"})
+    text = "".join(json.dumps(r) + "\n" for r in recs)
+    if torn:
+        text += '{"event": "train", "st'
+    path.write_text(text)
+
+
+def test_results_tables_from_trainer_jsonl(tmp_path):
+    import csv
+    import json
+    from rational_optimizer_b200.protocol import results as RS
+    manifest = []
+    for i, (act, loss) in enumerate((("silu", 4.0), ("rlb_fused_global_rational", 3.9))):
+        manifest.append({"row_index": str(i), "row_id": f"r{i}", "phase": "12l_768d_100m_tokens_3050_steps",
+                         "model": "12l_768d", "dataset": "c4_en", "seed": "1337", "train_tokens": "100",
+                         "steps": "20", "activation": act, "optimizer": "muon", "method": f"{act}_muon"})
+    runs = tmp_path / "runs"
+    for m, loss in zip(manifest, (4.0, 3.9)):
+        _write_run(runs / m["phase"] / m["dataset"] / m["row_id"] / f"{m['activation']}.jsonl",
+                   steps=20, losses={10: loss + 1, 20: loss}, torn=m["activation"] == "silu")
+    # the GRAIN arm's launcher recorded its process time
+    grain = runs / manifest[1]["phase"] / "c4_en" / "r1" / "rlb_fused_global_rational.wall_clock.json"
+    grain.write_text(json.dumps({"schema": "rationalopt_process_wall_clock_v1", "return_code": 0,
+                                 "elapsed_seconds": 60.0}))
+    by_opt, points = RS.manifest_tables(manifest, runs)
+    silu, g = by_opt["muon"]
+    assert silu["status"] == g["status"] == "complete"
+    assert silu["time_scope"] == "training_loop" and g["time_scope"] == "end_to_end_process"
+    assert g["total_seconds"] == 60.0 and g["training_loop_total_seconds"] == 50.0
+    assert abs(g["lead_vs_matched_control"] - 0.1) < 1e-12 and g["matched_control_total_seconds"] == 50.0
+    assert g["total_time_ratio_vs_matched_control"] == ""  # the control has no process time
+    assert g["method_display_name"] == "GRAIN + Muon" and len(points["muon"]) == 4
+    out = RS.publish(tmp_path / "tables", "muon", by_opt["muon"], points["muon"])
+    with (out / "summary.csv").open() as fh:
+        cells = list(csv.DictReader(fh))
+    assert [c["status"] for c in cells] == ["complete", "complete"]
+    assert cells[0]["activation"] == "rlb_fused_global_rational" and cells[0]["lead_vs_matched_control_mean"]
+
+
+def test_results_run_states(tmp_path):
+    from rational_optimizer_b200.protocol import results as RS
+    spec = dict(run_index=3, model="18l_1024d", dataset="dclm", seed=1337, train_tokens=10, steps=20,
+                activation="rlb_fused_global_rational", optimizer="tiller_v1", method="tiller",
+                phase="p", source_row_index=3, source_row_id="x")
+    assert RS.run_record(spec, tmp_path / "none.jsonl")[0]["status"] == "pending"
+    p = tmp_path / "a.jsonl"
+    _write_run(p, steps=20, losses={10: 5.0}, summary=False)
+    row, _ = RS.run_record(spec, p)
+    assert row["status"] == "incomplete" and row["steps_completed"] == 10
+    _write_run(p, steps=20, losses={10: 5.0, 20: float("nan")})
+    assert RS.run_record(spec, p)[0]["status"] == "non_finite"
+    _write_run(p, steps=20, losses={10: 5.0}, stopped=True)
+    assert RS.run_record(spec, p)[0]["status"] == "stopped_early"
+    _write_run(p, steps=20, losses={10: 5.0, 20: 4.0})
+    (tmp_path / "a.wall_clock.json").write_text('{"schema": "rationalopt_process_wall_clock_v1", '
+                                                 '"return_code": 1, "elapsed_seconds": 9.0}')
+    row, _ = RS.run_record(spec, p)
+    assert row["status"] == "incomplete" and row["final_validation_loss"] == ""
+    p.write_text('{"event": "config"}\nnot json\n{"event": "summary"}\n')
+    with pytest.raises(RS.ResultsError):
+        RS.run_record(spec, p)
+    cells = RS.summarize([dict(RS.run_record(spec, tmp_path / "none.jsonl")[0])])
+    assert cells[0]["status"] == "pending" and cells[0]["validation_loss_mean"] == ""
+
+
+def test_results_matrix_candidates_pair_with_their_control(tmp_path):
+    import json
+    from rational_optimizer_b200.protocol import results as RS
+    from rational_optimizer_b200.protocol import rows as R
+    _need_data()
+    matrix = R.load_matrix(os.path.join(PROTO, "matrix.json"))
+    row = matrix["rows"][0]
+    steps = int(row["steps"])
+    small = {"rows": [row]}
+    runs, analysis = tmp_path / "runs", tmp_path / "analysis"
+    got, _ = RS.matrix_tables(small, runs, analysis)
+    assert got[0]["status"] == "pending" and got[0]["optimizer"] == row["candidate_optimizer"]
+    _write_run(R.jsonl_path(row, "candidate", runs), steps=steps, losses={1000: 5.0, steps: 4.0})
+    got, pts = RS.matrix_tables(small, runs, analysis)
+    published = row["matched_control"]["endpoint_validation_loss"]
+    assert got[0]["status"] == "complete" and len(pts) == 2
+    assert abs(got[0]["lead_vs_matched_control"] - (published - 4.0)) < 1e-12
+    # a negative step-1,000 screen stops the run
+    screen = runs / f"{R.run_name(row, 'candidate')}.step1000.json"
+    screen.write_text(json.dumps({"matrix_index": row["matrix_index"], "status": "failed_negative_interrupted",
+                                  "candidate_step1000_loss": 5.0}))
+    got, _ = RS.matrix_tables(small, runs, analysis)
+    assert got[0]["status"] == "stopped_early" and got[0]["final_validation_loss"] == ""
+    # an endpoint result beside a stopped screen is a contradiction
+    (analysis / f"row-{row['matrix_index']:02d}").mkdir(parents=True)
+    (analysis / f"row-{row['matrix_index']:02d}" / "RESULT.json").write_text(json.dumps({
+        "schema": "tiller_matched_endpoint_result_v1", "status": "complete", "matrix_index": row["matrix_index"],
+        "model": row["model"], "dataset": row["dataset"], "seed": int(row["seed"]), "steps": steps}))
+    with pytest.raises(RS.ResultsError):
+        RS.matrix_tables(small, runs, analysis)
