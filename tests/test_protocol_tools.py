@@ -329,3 +329,34 @@ def test_results_matrix_candidates_pair_with_their_control(tmp_path):
         "model": row["model"], "dataset": row["dataset"], "seed": int(row["seed"]), "steps": steps}))
     with pytest.raises(RS.ResultsError):
         RS.matrix_tables(small, runs, analysis)
+
+
+def test_verify_passes_on_the_published_package_and_catches_edits(tmp_path):
+    import shutil
+    from rational_optimizer_b200.protocol import verify as V
+    _need_data()
+    checks = dict(V.verify_package(PROTO, RESULTS))
+    assert checks["activation/optimizer manifest"] == 640 and checks["TILLER matrix"] == 60
+    assert checks["optimizer result directories"] == 8
+    results = tmp_path / "results"
+    shutil.copytree(RESULTS, results)
+    runs = results / "tiller" / "runs.csv"
+    original = runs.read_text()
+    lines = original.splitlines(keepends=True)
+    cells = lines[1].split(",")
+    i = lines[0].split(",").index("lead_vs_matched_control")
+    cells[i] = str(float(cells[i]) + 1e-3)
+    runs.write_text(lines[0] + ",".join(cells) + "".join(lines[2:]))
+    with pytest.raises(V.VerificationError, match="control minus candidate"):
+        V.verify_results(results)
+    runs.write_text(original)
+    summary = results / "muon" / "summary.csv"
+    summary.write_text(summary.read_text().replace("complete", "pending", 1))
+    with pytest.raises(V.VerificationError, match="summary of its runs"):
+        V.verify_results(results)
+    package = tmp_path / "package"
+    shutil.copytree(PROTO, package)
+    manifest = package / "activation_optimizer_manifest.csv"
+    manifest.write_text(manifest.read_text().replace("3407", "3408", 1))
+    with pytest.raises(V.VerificationError):
+        V.verify_package(package, RESULTS, quick=True)
