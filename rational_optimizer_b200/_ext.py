@@ -1,4 +1,6 @@
-"""Loader for the in-tree sm_100a extension (``rational_optimizer_b200._C``).
+"""Loader for the in-tree sm_100a extension (``rational_optimizer_b200._C``;
+``rational_optimizer_b200._C_checked``, the bounds-checked build, when
+``RO_CHECKED=1``).
 
 CUDA tensors always go through the native kernels: if the extension is
 missing on a machine with a GPU, :func:`ext` raises instead of silently
@@ -8,6 +10,7 @@ double as the fp32 oracles of the test-suite.
 from __future__ import annotations
 
 import importlib
+import os
 
 _C = None
 _ERR: Exception | None = None
@@ -18,9 +21,15 @@ def _load():
     if _C is not None or _ERR is not None:
         return
     try:
-        _C = importlib.import_module("rational_optimizer_b200._C")
+        import torch  # noqa: F401  (loads libc10 / libtorch that the extension links against)
+        _C = importlib.import_module(module_name())
     except Exception as exc:  # pragma: no cover - depends on the build
         _ERR = exc
+
+
+def module_name() -> str:
+    checked = os.environ.get("RO_CHECKED", "0") == "1"
+    return "rational_optimizer_b200._C_checked" if checked else "rational_optimizer_b200._C"
 
 
 def available() -> bool:
@@ -33,8 +42,8 @@ def ext():
     _load()
     if _C is None:
         raise RuntimeError(
-            "rational_optimizer_b200._C is not built; run "
-            "`python setup.py build_ext --inplace` (sm_100a) before using CUDA tensors"
+            f"{module_name()} is not built; run `python setup.py build_ext --inplace` (sm_100a; "
+            "with RO_BOUNDS_CHECK=1 for the checked build) before using CUDA tensors"
         ) from _ERR
     return _C
 

@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -615,11 +616,14 @@ c10::optional<std::vector<torch::Tensor>> attention_backward(torch::Tensor q, to
 
 // Reduce-to-owner (csrc/owner_comm.cu).  `dst` and `counter` are addresses in
 // the owner's memory (CUDA IPC mappings); the kernels run on the current stream.
-void owner_send(torch::Tensor src, int64_t dst, bool bf16, int64_t counter, int64_t ctas) {
+// mode: 0 fp32, 1 bf16, 2 int8 (per-256 fp32 scales); see owner_slot_bytes.
+int64_t owner_slot_bytes(int64_t n, int64_t mode) { return ro::owner_slot_bytes(n, static_cast<int>(mode)); }
+
+void owner_send(torch::Tensor src, int64_t dst, int64_t mode, int64_t counter, int64_t ctas) {
   TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat32 && src.is_contiguous(),
               "owner_send expects a contiguous fp32 CUDA tensor");
   const c10::cuda::CUDAGuard guard(src.device());
-  check_rc(ro::owner_send(src.data_ptr<float>(), reinterpret_cast<void*>(dst), src.numel(), bf16,
+  check_rc(ro::owner_send(src.data_ptr<float>(), reinterpret_cast<void*>(dst), src.numel(), static_cast<int>(mode),
                           reinterpret_cast<unsigned int*>(counter), static_cast<int>(ctas),
                           at::cuda::getCurrentCUDAStream()),
            "owner_send");
@@ -627,7 +631,7 @@ void owner_send(torch::Tensor src, int64_t dst, bool bf16, int64_t counter, int6
 
 void owner_reduce(torch::Tensor grad, int64_t recv, torch::Tensor counters, torch::Tensor offsets,
                   torch::Tensor sizes, torch::Tensor recv_offsets, torch::Tensor sumsq, int64_t rank,
-                  int64_t world, int64_t expected, double scale, bool bf16, torch::Tensor err,
+                  int64_t world, int64_t expected, double scale, int64_t mode, torch::Tensor err,
                   int64_t timeout_ns) {
   TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == torch::kFloat32, "owner_reduce: fp32 gradient buffer");
   TORCH_CHECK(offsets.scalar_type() == torch::kInt64 && sizes.scalar_type() == torch::kInt64 &&
@@ -640,7 +644,7 @@ void owner_reduce(torch::Tensor grad, int64_t recv, torch::Tensor counters, torc
                             sizes.data_ptr<int64_t>(), recv_offsets.data_ptr<int64_t>(), sumsq.data_ptr<float>(),
                             static_cast<int>(sumsq.numel()), static_cast<int>(offsets.numel()),
                             static_cast<int>(rank), static_cast<int>(world), static_cast<unsigned int>(expected),
-                            static_cast<float>(scale), bf16, err.data_ptr<int>(),
+                            static_cast<float>(scale), static_cast<int>(mode), err.data_ptr<int>(),
                             static_cast<uint64_t>(timeout_ns), at::cuda::getCurrentCUDAStream()),
            "owner_reduce");
 }
@@ -1007,10 +1011,33 @@ std::vector<torch::Tensor> tiller_ledger_transaction(
 
 int64_t tiller_ledger_workspace(int64_t C) { return ro::ledger_workspace_doubles(static_cast<int>(C)); }
 
+// Failed RO_CHECKs per kernel file since the last call (0 = none; always 0
+// unless the module was built with -DRO_BOUNDS_CHECK).  Synchronises.
+std::map<std::string, uint64_t> bounds_faults() {
+  check_rc(static_cast<int>(cudaDeviceSynchronize()), "bounds_faults");
+  return {{"grain", ro::grain_bounds_word()}, {"nn_ops", ro::nn_ops_bounds_word()},
+          {"optim", ro::optim_bounds_word()}};
+}
+
+void bounds_selftest(torch::Tensor buf, int64_t index) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == torch::kFloat32 && buf.is_contiguous(),
+              "bounds_selftest: contiguous fp32 CUDA tensor expected");
+  const int rc = ro::bounds_selftest(buf.data_ptr<float>(), buf.numel(), index, stream());
+  TORCH_CHECK(rc != -1, "bounds_selftest needs a -DRO_BOUNDS_CHECK build");
+  check_rc(rc, "bounds_selftest");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels for rational_optimizer_b200";
+#ifdef RO_BOUNDS_CHECK
+  m.attr("bounds_checked") = true;
+#else
+  m.attr("bounds_checked") = false;
+#endif
+  m.def("bounds_faults", &bounds_faults);
+  m.def("bounds_selftest", &bounds_selftest);
   m.def("grain_forward", &grain_forward);
   m.def("grain_backward", &grain_backward);
   m.def("grain_affine_statistics", &grain_affine_statistics);
@@ -1033,6 +1060,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2_bf16", &gemm2_bf16);
   m.def("grain_in_proj_forward", &grain_in_proj_forward);
   m.def("qkv_rope_forward", &qkv_rope_forward);
+  m.def("owner_slot_bytes", &owner_slot_bytes);
   m.def("owner_send", &owner_send);
   m.def("owner_reduce", &owner_reduce);
   m.def("owner_publish", &owner_publish);

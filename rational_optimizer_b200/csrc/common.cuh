@@ -127,4 +127,44 @@ __device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&in)[N
 
 inline int ceil_div_i(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
+// ---------------------------------------------------------------------------
+// Bounds-checked builds.  Compiled with -DRO_BOUNDS_CHECK, RO_CHECK(cond, site)
+// evaluates `cond`; when it is false the first such failure of this source
+// file is recorded in a device word as (site << 32) | source line and the
+// macro yields false, so the caller skips the access it guards instead of
+// touching memory it does not own (no trap, the context stays usable).  In
+// normal builds RO_CHECK is the constant true and costs nothing.  Every .cu
+// file that uses it defines a host query with RO_BOUNDS_QUERY(name), which
+// returns the word and clears it (0 = no failure).
+#ifdef RO_BOUNDS_CHECK
+static __device__ unsigned long long g_bounds_word = 0ull;
+
+static __device__ __noinline__ void bounds_record(unsigned site, unsigned line) {
+  atomicCAS(&g_bounds_word, 0ull, (static_cast<unsigned long long>(site) << 32) | line);
+}
+
+#define RO_CHECK(cond, site) \
+  (__builtin_expect(!!(cond), 1) ? true : (::ro::bounds_record((site), __LINE__), false))
+
+#define RO_BOUNDS_QUERY(name)                                                          \
+  unsigned long long name() {                                                          \
+    unsigned long long word = 0ull;                                                    \
+    const unsigned long long zero = 0ull;                                              \
+    if (cudaMemcpyFromSymbol(&word, ::ro::g_bounds_word, sizeof(word)) != cudaSuccess) \
+      return ~0ull;                                                                    \
+    cudaMemcpyToSymbol(::ro::g_bounds_word, &zero, sizeof(zero));                      \
+    return word;                                                                       \
+  }
+#else
+#define RO_CHECK(cond, site) true
+#define RO_BOUNDS_QUERY(name) \
+  unsigned long long name() { return 0ull; }
+#endif
+
+// Row r, columns [c0, c1) of a [rows, cols] row-major plane.
+__device__ __forceinline__ bool span_ok(int64_t r, int64_t c0, int64_t c1, int64_t rows, int64_t cols,
+                                        unsigned site) {
+  return RO_CHECK(r >= 0 && r < rows && c0 >= 0 && c0 <= c1 && c1 <= cols, site);
+}
+
 }  // namespace ro

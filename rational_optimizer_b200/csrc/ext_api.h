@@ -7,6 +7,15 @@
 
 namespace ro {
 
+// First failed RO_CHECK of each kernel file in a -DRO_BOUNDS_CHECK build,
+// (site << 32) | line, cleared by the read; always 0 in normal builds.
+unsigned long long grain_bounds_word();
+unsigned long long nn_ops_bounds_word();
+unsigned long long optim_bounds_word();
+// Checked builds only: a kernel that guards buf[index] (n elements) with
+// RO_CHECK and writes 1 there when the check passes; returns the launch status.
+int bounds_selftest(float* buf, int64_t n, int64_t index, cudaStream_t stream);
+
 // grain.cu
 int grain_forward(const void* x, int x_dtype, const float* num, const float* den,
                   const float* logits, const float* centers, const float* beta, void* y,
@@ -60,11 +69,14 @@ int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, 
 int gemm2_qkv_rope(const void* X, int64_t ldx, const void* W, int64_t ldw, void* QKV, int M, int N, int K,
                    const float* cos_t, const float* sin_t, int seq, int hd, int* err, cudaStream_t stream);
 int gemm2_grain_partial_rows(int M);
-int owner_send(const float* src, void* dst, int64_t n, bool bf16, unsigned int* counter, int ctas,
+// Reduce-to-owner transport formats: mode 0 fp32, 1 bf16, 2 int8 with one
+// fp32 scale per 256 elements.  recv_offsets are byte offsets.
+int64_t owner_slot_bytes(int64_t n, int mode);
+int owner_send(const float* src, void* dst, int64_t n, int mode, unsigned int* counter, int ctas,
                cudaStream_t stream);
 int owner_reduce(float* grad, const void* recv, unsigned int* counters, const int64_t* offsets,
                  const int64_t* sizes, const int64_t* recv_offsets, float* sumsq, int ctas, int layers,
-                 int rank, int world, unsigned int expected, float scale, bool bf16, int* err,
+                 int rank, int world, unsigned int expected, float scale, int mode, int* err,
                  uint64_t timeout_ns, cudaStream_t stream);
 int owner_publish(unsigned int* published, cudaStream_t stream);
 int owner_pull(const float* src, float* dst, __nv_bfloat16* dst16, int64_t n, const unsigned int* published,

@@ -207,12 +207,14 @@ forward_kernel(const TI* __restrict__ x, const float* __restrict__ num,
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
-      if (r < r1) load_seg<TI, E, CONTIG>(x + r * hidden + static_cast<int64_t>(g) * w, w, lane, v[u]);
+      if (r < r1 && span_ok(r, static_cast<int64_t>(g) * w, static_cast<int64_t>(g + 1) * w, rows, hidden, 1))
+        load_seg<TI, E, CONTIG>(x + r * hidden + static_cast<int64_t>(g) * w, w, lane, v[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
       if (r >= r1) break;
+      if (!span_ok(r, static_cast<int64_t>(g) * w, static_cast<int64_t>(g + 1) * w, rows, hidden, 1)) continue;
       float ss = 0.f;
 #pragma unroll
       for (int j = 0; j < E; ++j) ss = fmaf(v[u][j], v[u][j], ss);
@@ -267,7 +269,7 @@ backward_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
-      if (r < r1) {
+      if (r < r1 && span_ok(r, static_cast<int64_t>(g) * w, static_cast<int64_t>(g + 1) * w, rows, hidden, 2)) {
         const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
         load_seg<TI, E, CONTIG>(x + off, w, lane, z[u]);
         load_seg<TG, E, CONTIG>(gy_ptr + off, w, lane, gy[u]);
@@ -277,6 +279,7 @@ backward_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
       if (r >= r1) break;
+      if (!span_ok(r, static_cast<int64_t>(g) * w, static_cast<int64_t>(g + 1) * w, rows, hidden, 2)) continue;
       const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
       float ss = 0.f;
 #pragma unroll
@@ -364,7 +367,7 @@ backward_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
     if (lane == 0) red[warp][k] = v;
   }
   __syncthreads();
-  if (threadIdx.x < ngrad) {
+  if (threadIdx.x < ngrad && RO_CHECK(ngrad <= kMaxGrad && g < groups, 2)) {
     float v = 0.f;
 #pragma unroll
     for (int wi = 0; wi < kWarps; ++wi) v += red[wi][threadIdx.x];
@@ -415,12 +418,14 @@ forward_packed_kernel(const TI* __restrict__ x, const float* __restrict__ num,
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
-      if (r < r1) load_pairs<TI, E>(x + r * hidden + col, v[u]);
+      if (r < r1 && span_ok(r, col, col + E, rows, hidden, 3)) load_pairs<TI, E>(x + r * hidden + col, v[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
       if (r >= r1) break;
+      // the whole warp takes the same branch: a failure anywhere skips the row
+      if (!__all_sync(0xffffffffu, span_ok(r, col, col + E, rows, hidden, 3))) continue;
       float2 s2 = splat2(0.0f);
 #pragma unroll
       for (int i = 0; i < P; ++i) s2 = fma2(v[u][i], v[u][i], s2);
@@ -486,7 +491,7 @@ backward_packed_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
-      if (r < r1) {
+      if (r < r1 && span_ok(r, col, col + E, rows, hidden, 4)) {
         load_pairs<TI, E>(x + r * hidden + col, z[u]);
         load_pairs<TG, E>(gy_ptr + r * hidden + col, gy[u]);
       }
@@ -495,6 +500,7 @@ backward_packed_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
     for (int u = 0; u < U; ++u) {
       const int64_t r = rb + static_cast<int64_t>(u) * kWarps;
       if (r >= r1) break;
+      if (!__all_sync(0xffffffffu, span_ok(r, col, col + E, rows, hidden, 4))) continue;
       float2 s2 = splat2(0.0f);
 #pragma unroll
       for (int i = 0; i < P; ++i) s2 = fma2(z[u][i], z[u][i], s2);
@@ -564,7 +570,7 @@ backward_packed_kernel(const TG* __restrict__ gy_ptr, const TI* __restrict__ x,
     if (lane == 0) red[warp][k] = v;
   }
   __syncthreads();
-  if (threadIdx.x < kBase) {
+  if (threadIdx.x < kBase && RO_CHECK(g < groups, 4)) {
     float v = 0.f;
 #pragma unroll
     for (int wi = 0; wi < kWarps; ++wi) v += red[wi][threadIdx.x];
@@ -579,7 +585,7 @@ __global__ void reduce_coeff_kernel(const float* __restrict__ partial, int chunk
                                     float* __restrict__ gcoeff, int accumulate = 0) {
   const int ngrad = kBase + 2 * nb;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= groups * ngrad) return;
+  if (idx >= groups * ngrad || !RO_CHECK(nb >= 0 && nb <= kMaxBasis && chunks >= 0, 5)) return;
   const int g = idx / ngrad;
   const int k = idx % ngrad;
   double s = 0.0;
@@ -628,6 +634,7 @@ affine_stats_kernel(const T* __restrict__ x, const T* __restrict__ feature,
   const float inv_w = 1.0f / static_cast<float>(w);
   double acc[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t r = r0 + warp; r < r1; r += kWarps) {
+    if (!span_ok(r, static_cast<int64_t>(g) * w, static_cast<int64_t>(g + 1) * w, rows, hidden, 6)) continue;
     const int64_t off = r * hidden + static_cast<int64_t>(g) * w;
     float z[E], h[E];
     load_seg<T, E, CONTIG>(x + off, w, lane, z);
@@ -738,6 +745,7 @@ legacy_backward_kernel(const float* __restrict__ gy, const float* __restrict__ x
                        const float* __restrict__ a, const float* __restrict__ b,
                        float* __restrict__ gx, float* __restrict__ partial, int64_t n) {
   __shared__ float red[8][kBase];
+  if (!RO_CHECK(blockDim.x <= 256, 7)) return;  // red[] holds 8 warps
   float ca[kNum], cb[kDen];
 #pragma unroll
   for (int j = 0; j < kNum; ++j) ca[j] = a[j];
@@ -1021,6 +1029,8 @@ int legacy_rational_backward(const float* gy, const float* x, const float* a, co
   grain::legacy_reduce_kernel<<<1, 32, 0, stream>>>(partial, blocks, ga, gb);
   return static_cast<int>(cudaGetLastError());
 }
+
+RO_BOUNDS_QUERY(grain_bounds_word)
 
 }  // namespace ro
 

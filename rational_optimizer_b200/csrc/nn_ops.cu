@@ -22,7 +22,7 @@ rmsnorm_fwd_fast(const T* __restrict__ x, const float* __restrict__ w, TO* __res
   constexpr int d = NCH * 256;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  if (row >= rows || !span_ok(row, lane * 8, (NCH - 1) * 256 + lane * 8 + 8, rows, d, 1)) return;
   float v[NCH][8];
   float ss = 0.f;
 #pragma unroll
@@ -188,7 +188,7 @@ add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_bfloat16* __restr
   constexpr int d = NCH * 256;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  if (row >= rows || !span_ok(row, lane * 8, (NCH - 1) * 256 + lane * 8 + 8, rows, d, 1)) return;
   float v[NCH][8];
   float ss = 0.f;
 #pragma unroll
@@ -330,6 +330,11 @@ __global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __re
   const int rem = t - which * H * vec;
   const int h = rem / vec, jv = rem - h * vec;
   const int d = H * hd;
+  const int64_t tokens = static_cast<int64_t>(B) * S;
+  if (!(span_ok(static_cast<int64_t>(token) * 3 + which, h * hd + jv * 8, h * hd + jv * 8 + 8, tokens * 3, d, 2) &&
+        span_ok(static_cast<int64_t>(token) * H + h, jv * 8, jv * 8 + 8, tokens * H, hd, 2) &&
+        span_ok(s, jv * 4, jv * 4 + 4, S, hd / 2, 2)))
+    return;
   float val[8];
   load_vec<T, 8>(qkv + (static_cast<int64_t>(token) * 3 + which) * d + h * hd + jv * 8, val);
   if (which < 2) {
@@ -354,6 +359,11 @@ __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restric
   const int rem = t - which * H * vec;
   const int h = rem / vec, jv = rem - h * vec;
   const int d = H * hd;
+  const int64_t tokens = static_cast<int64_t>(B) * S;
+  if (!(span_ok(static_cast<int64_t>(token) * 3 + which, h * hd + jv * 8, h * hd + jv * 8 + 8, tokens * 3, d, 3) &&
+        span_ok(static_cast<int64_t>(token) * H + h, jv * 8, jv * 8 + 8, tokens * H, hd, 3) &&
+        span_ok(s, jv * 4, jv * 4 + 4, S, hd / 2, 3)))
+    return;
   const T* in = which == 0 ? dq : (which == 1 ? dk : dv);
   float val[8];
   load_vec<T, 8>(in + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
@@ -450,7 +460,7 @@ ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
   __syncthreads();
   const float lse = bcast;
   const bool ignored = (tgt == ignore_index) || tgt < 0 || tgt >= V;
-  if (tid == 0) {
+  if (tid == 0 && RO_CHECK(ignored || (tgt >= 0 && tgt < V), 4)) {
     const float xt = ignored ? 0.f : to_f<T>(use_smem ? srow[tgt] : lr[tgt]);
     loss_row[row] = ignored ? 0.f : (lse - xt);
   }
@@ -671,5 +681,24 @@ int cross_entropy_fwd_bwd(void* logits, const int64_t* target, float* loss_row, 
   else return -2;
   return static_cast<int>(cudaGetLastError());
 }
+
+RO_BOUNDS_QUERY(nn_ops_bounds_word)
+
+#ifdef RO_BOUNDS_CHECK
+namespace nn {
+// Writes buf[index] = 1 only when 0 <= index < n; otherwise records site 99.
+__global__ void bounds_selftest_kernel(float* buf, int64_t n, int64_t index) {
+  if (RO_CHECK(index >= 0 && index < n, 99)) buf[index] = 1.0f;
+}
+}  // namespace nn
+
+int bounds_selftest(float* buf, int64_t n, int64_t index, cudaStream_t stream) {
+  nn::bounds_selftest_kernel<<<1, 1, 0, stream>>>(buf, n, index);
+  return static_cast<int>(cudaGetLastError());
+}
+#else
+// Without the checks the guarded store would not be skipped: refuse.
+int bounds_selftest(float*, int64_t, int64_t, cudaStream_t) { return -1; }
+#endif
 
 }  // namespace ro

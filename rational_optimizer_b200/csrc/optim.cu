@@ -63,6 +63,7 @@ adamw_kernel(const __grid_constant__ TensorList tl, AdamScalars a) {
   const int t = chunk_owner(tl.cstart, tl.count, blockIdx.x);
   const int64_t start = (static_cast<int64_t>(blockIdx.x) - tl.cstart[t]) * kChunk;
   const int64_t end = start + kChunk < tl.n[t] ? start + kChunk : tl.n[t];
+  if (!RO_CHECK(t >= 0 && t < tl.count && start >= 0 && end <= tl.n[t], 1)) return;
   float* __restrict__ P = tl.p[t];
   const float* __restrict__ G = tl.g[t];
   float* __restrict__ M = tl.m[t];
@@ -110,6 +111,8 @@ dot_chunks_kernel(const __grid_constant__ DotList dl, float* __restrict__ part) 
   const int t = chunk_owner(dl.cstart, dl.count, blockIdx.x);
   const int64_t start = (static_cast<int64_t>(blockIdx.x) - dl.cstart[t]) * kChunk;
   const int64_t end = start + kChunk < dl.n[t] ? start + kChunk : dl.n[t];
+  // uniform per CTA, so the __syncthreads below is reached by all or none
+  if (!RO_CHECK(t >= 0 && t < dl.count && start >= 0 && end <= dl.n[t], 2)) return;
   const float* __restrict__ A = dl.a[t];
   const float* __restrict__ B = dl.b[t];
   float s = 0.f;
@@ -244,5 +247,7 @@ int multi_tensor_dot(const float* const* a, const float* const* b, const int64_t
   sum_partials_kernel<<<1, 1024, 0, stream>>>(part, offset, scale, out);
   return static_cast<int>(cudaGetLastError());
 }
+
+RO_BOUNDS_QUERY(optim_bounds_word)
 
 }  // namespace ro

@@ -7,14 +7,19 @@
 //
 //   send   (every non-owner, per layer, on the communication stream as soon
 //          as backward has produced the layer's gradient): read the fp32
-//          gradient, convert to the transport type (bf16 or fp32), store it
-//          into slot [sender rank] of the owner's receive buffer with plain
-//          16-byte peer stores, then per CTA: __syncthreads, a system-scope
-//          fence and one atomic increment of the owner's counter for the layer;
+//          gradient, convert to the transport format, store it into slot
+//          [sender rank] of the owner's receive buffer with plain peer stores,
+//          then per CTA: __syncthreads, a system-scope fence and one atomic
+//          increment of the owner's counter for the layer.  Formats: fp32,
+//          bf16, or int8 with one fp32 scale per 256-element block (a warp
+//          quantises one block: scale = max|g| / 127, q = round(g / scale)
+//          clamped to [-127, 127]; the slot holds the n int8 values, padded
+//          to 16 bytes, then the block scales);
 //   reduce (owner, after backward): wait until every sender CTA of every owned
 //          layer has arrived (bounded; on expiry an error code is recorded and
-//          the reduction is skipped), then sum the slots in rank order with its
-//          own fp32 gradient in its rank position, scale by 1/world, write the
+//          the reduction is skipped), then sum the slots (int8: dequantised,
+//          q * scale) in rank order with its own fp32 gradient in its rank
+//          position, scale by 1/world, write the
 //          fp32 result over its own gradient, return each counter to zero for
 //          the next step and emit per-CTA sums of squares of the result (the
 //          owned part of the global gradient norm).
@@ -29,6 +34,32 @@ namespace ro {
 namespace owner {
 
 constexpr int kThreads = 512;
+constexpr int kF32 = 0, kBF16 = 1, kI8 = 2;  // transport formats
+constexpr int kQBlock = 256;                   // int8: elements per fp32 scale
+
+__host__ __device__ __forceinline__ int64_t round16(int64_t bytes) { return (bytes + 15) / 16 * 16; }
+
+// Bytes of one sender's slot of an n-element layer (n a multiple of 8).
+__host__ __device__ __forceinline__ int64_t slot_bytes(int64_t n, int mode) {
+  if (mode == kF32) return 4 * n;
+  if (mode == kBF16) return 2 * n;
+  return round16(n) + round16(4 * ((n + kQBlock - 1) / kQBlock));
+}
+
+__device__ __forceinline__ uint32_t pack_i8x4(const float* q) {
+  return (static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(q[0])))) |
+         (static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(q[1]))) << 8) |
+         (static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(q[2]))) << 16) |
+         (static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(q[3]))) << 24);
+}
+
+__device__ __forceinline__ void unpack_i8x8(uint2 raw, float scale, float (&x)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[i] = static_cast<float>(static_cast<int8_t>((raw.x >> (8 * i)) & 0xffu)) * scale;
+    x[4 + i] = static_cast<float>(static_cast<int8_t>((raw.y >> (8 * i)) & 0xffu)) * scale;
+  }
+}
 
 __device__ __forceinline__ uint64_t now_ns() {
   uint64_t t;
@@ -42,21 +73,47 @@ __device__ __forceinline__ unsigned int load_acquire_sys(const unsigned int* p) 
   return v;
 }
 
-template <bool BF16>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads)
 send_kernel(const float* __restrict__ src, void* __restrict__ dst, int64_t n, unsigned int* counter) {
   const int64_t nvec = n / 8;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-    float x[8];
-    load_vec<float, 8>(src + v * 8, x);
-    if constexpr (BF16) store_vec<__nv_bfloat16, 8>(static_cast<__nv_bfloat16*>(dst) + v * 8, x);
-    else store_vec<float, 8>(static_cast<float*>(dst) + v * 8, x);
-  }
-  if (blockIdx.x == 0 && threadIdx.x < n - nvec * 8) {
-    const int64_t i = nvec * 8 + threadIdx.x;
-    if constexpr (BF16) static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(src[i]);
-    else static_cast<float*>(dst)[i] = src[i];
+  if constexpr (MODE == kI8) {
+    // one warp per 256-element block; lane l owns elements [8l, 8l + 8)
+    int8_t* q8 = static_cast<int8_t*>(dst);
+    float* scales = reinterpret_cast<float*>(q8 + round16(n));
+    const int lane = threadIdx.x & 31;
+    const int64_t blocks = (n + kQBlock - 1) / kQBlock;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    for (int64_t b = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); b < blocks;
+         b += warps) {
+      const int64_t e0 = b * kQBlock + lane * 8;
+      const bool valid = e0 < n;  // n is a multiple of 8: a lane's 8 elements are all in or all out
+      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (valid) load_vec<float, 8>(src + e0, x);
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      amax = warp_max(amax);
+      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+      float q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = fminf(fmaxf(rintf(x[i] * inv), -127.f), 127.f);
+      if (valid) *reinterpret_cast<uint2*>(q8 + e0) = make_uint2(pack_i8x4(q), pack_i8x4(q + 4));
+      if (lane == 0) scales[b] = amax / 127.0f;
+    }
+  } else {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+      float x[8];
+      load_vec<float, 8>(src + v * 8, x);
+      if constexpr (MODE == kBF16) store_vec<__nv_bfloat16, 8>(static_cast<__nv_bfloat16*>(dst) + v * 8, x);
+      else store_vec<float, 8>(static_cast<float*>(dst) + v * 8, x);
+    }
+    if (blockIdx.x == 0 && threadIdx.x < n - nvec * 8) {
+      const int64_t i = nvec * 8 + threadIdx.x;
+      if constexpr (MODE == kBF16) static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(src[i]);
+      else static_cast<float*>(dst)[i] = src[i];
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -71,7 +128,7 @@ struct ReduceArgs {
   unsigned int* counters;  // [owned layers]
   const int64_t* offsets;  // [owned layers] element offset of the layer in `grad`
   const int64_t* sizes;    // [owned layers] elements
-  const int64_t* recv_offsets;  // [owned layers] element offset of the layer's slots in `recv`
+  const int64_t* recv_offsets;  // [owned layers] byte offset of the layer's slots in `recv`
   float* sumsq;            // [gridDim.x] partial sums of squares of the reduced gradient
   int layers, rank, world;
   unsigned int expected;   // arrivals per layer: (world - 1) * sender CTAs
@@ -80,7 +137,7 @@ struct ReduceArgs {
   uint64_t timeout_ns;
 };
 
-template <bool BF16>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads) reduce_kernel(const __grid_constant__ ReduceArgs a) {
   __shared__ int ok;
   __shared__ float red[kThreads / 32];
@@ -104,6 +161,8 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(const __grid_constant_
       const int64_t n = a.sizes[l];
       float* g = a.grad + a.offsets[l];
       const int64_t nvec = n / 8;
+      const int64_t slot = slot_bytes(n, MODE);
+      const uint8_t* base = static_cast<const uint8_t*>(a.recv) + a.recv_offsets[l];
       const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
       for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
         float s[8];
@@ -111,12 +170,16 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(const __grid_constant_
         for (int i = 0; i < 8; ++i) s[i] = 0.f;
         for (int r = 0; r < a.world; ++r) {
           float x[8];
+          const uint8_t* from = base + r * slot;
           if (r == a.rank) {
             load_vec<float, 8>(g + v * 8, x);
-          } else if constexpr (BF16) {
-            load_vec<__nv_bfloat16, 8>(static_cast<const __nv_bfloat16*>(a.recv) + a.recv_offsets[l] + r * n + v * 8, x);
+          } else if constexpr (MODE == kI8) {
+            const float scale = reinterpret_cast<const float*>(from + round16(n))[v / (kQBlock / 8)];
+            unpack_i8x8(*reinterpret_cast<const uint2*>(from + v * 8), scale, x);
+          } else if constexpr (MODE == kBF16) {
+            load_vec<__nv_bfloat16, 8>(reinterpret_cast<const __nv_bfloat16*>(from) + v * 8, x);
           } else {
-            load_vec<float, 8>(static_cast<const float*>(a.recv) + a.recv_offsets[l] + r * n + v * 8, x);
+            load_vec<float, 8>(reinterpret_cast<const float*>(from) + v * 8, x);
           }
 #pragma unroll
           for (int i = 0; i < 8; ++i) s[i] += x[i];
@@ -128,14 +191,15 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(const __grid_constant_
         }
         store_vec<float, 8>(g + v * 8, s);
       }
-      if (blockIdx.x == 0 && threadIdx.x < n - nvec * 8) {
+      if (MODE != kI8 && blockIdx.x == 0 && threadIdx.x < n - nvec * 8) {
         const int64_t i = nvec * 8 + threadIdx.x;
         float s = 0.f;
         for (int r = 0; r < a.world; ++r) {
+          const uint8_t* from = base + r * slot;
           float x;
           if (r == a.rank) x = g[i];
-          else if constexpr (BF16) x = __bfloat162float(static_cast<const __nv_bfloat16*>(a.recv)[a.recv_offsets[l] + r * n + i]);
-          else x = static_cast<const float*>(a.recv)[a.recv_offsets[l] + r * n + i];
+          else if constexpr (MODE == kBF16) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(from)[i]);
+          else x = reinterpret_cast<const float*>(from)[i];
           s += x;
         }
         s *= a.scale;
@@ -163,27 +227,31 @@ __global__ void release_kernel(unsigned int* counters, int layers, unsigned int 
 
 }  // namespace owner
 
-int owner_send(const float* src, void* dst, int64_t n, bool bf16, unsigned int* counter, int ctas,
+int64_t owner_slot_bytes(int64_t n, int mode) { return owner::slot_bytes(n, mode); }
+
+int owner_send(const float* src, void* dst, int64_t n, int mode, unsigned int* counter, int ctas,
                cudaStream_t stream) {
   using namespace owner;
-  if (n <= 0 || ctas <= 0) return -1;
-  if (!aligned16(src) || !aligned16(dst)) return -2;
-  if (bf16) send_kernel<true><<<ctas, kThreads, 0, stream>>>(src, dst, n, counter);
-  else send_kernel<false><<<ctas, kThreads, 0, stream>>>(src, dst, n, counter);
+  if (n <= 0 || ctas <= 0 || mode < kF32 || mode > kI8) return -1;
+  if (!aligned16(src) || !aligned16(dst) || (mode == kI8 && n % 8 != 0)) return -2;
+  if (mode == kI8) send_kernel<kI8><<<ctas, kThreads, 0, stream>>>(src, dst, n, counter);
+  else if (mode == kBF16) send_kernel<kBF16><<<ctas, kThreads, 0, stream>>>(src, dst, n, counter);
+  else send_kernel<kF32><<<ctas, kThreads, 0, stream>>>(src, dst, n, counter);
   return static_cast<int>(cudaGetLastError());
 }
 
 int owner_reduce(float* grad, const void* recv, unsigned int* counters, const int64_t* offsets,
                  const int64_t* sizes, const int64_t* recv_offsets, float* sumsq, int ctas, int layers,
-                 int rank, int world, unsigned int expected, float scale, bool bf16, int* err,
+                 int rank, int world, unsigned int expected, float scale, int mode, int* err,
                  uint64_t timeout_ns, cudaStream_t stream) {
   using namespace owner;
   if (layers <= 0) return 0;
-  if (ctas <= 0 || world < 2) return -1;
+  if (ctas <= 0 || world < 2 || mode < kF32 || mode > kI8) return -1;
   ReduceArgs a{grad, recv, counters, offsets, sizes, recv_offsets, sumsq, layers, rank, world, expected,
                scale, err, timeout_ns};
-  if (bf16) reduce_kernel<true><<<ctas, kThreads, 0, stream>>>(a);
-  else reduce_kernel<false><<<ctas, kThreads, 0, stream>>>(a);
+  if (mode == kI8) reduce_kernel<kI8><<<ctas, kThreads, 0, stream>>>(a);
+  else if (mode == kBF16) reduce_kernel<kBF16><<<ctas, kThreads, 0, stream>>>(a);
+  else reduce_kernel<kF32><<<ctas, kThreads, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
   release_kernel<<<(layers + 31) / 32, 32, 0, stream>>>(counters, layers, expected);

@@ -21,6 +21,10 @@ class FusedAdamW(torch.optim.AdamW):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          foreach=False, **kw)
 
+    def eager_step_required(self):
+        """No probes are recorded in the forward/backward: always graph-eligible."""
+        return False
+
     def _native(self):
         if not _ext.available():
             return None

@@ -140,6 +140,11 @@ class CompositeOptimizer:
         for opt in self.optimizers:
             opt.step()
 
+    def eager_step_required(self):
+        """No step records forward/backward probes, so every step's
+        forward/backward may replay a captured graph."""
+        return False
+
     def state_dict(self):
         return [opt.state_dict() for opt in self.optimizers]
 
@@ -210,10 +215,15 @@ class TILLERCompositeOptimizer(CompositeOptimizer):
 def owner_layers(optimizer):
     """(per-layer matrices, layer -> owner rank) when ``optimizer`` updates each
     layer's structural matrices on one rank only (the layer-sharded TILLER
-    composite), else (None, None).  This is what the reduce-to-owner gradient
+    composite, or a Muon composite whose Muon is layer-sharded), else
+    (None, None).  This is what the reduce-to-owner gradient
     transport needs (``parallel.grad_sync``)."""
     if not isinstance(optimizer, TILLERCompositeOptimizer):
-        return None, None
+        shard = getattr(optimizer.optimizers[0], "shard", None) if isinstance(optimizer, CompositeOptimizer) \
+            and optimizer.optimizers else None
+        if shard is None:
+            return None, None
+        return shard.per_layer, shard.owner
     router, attention = optimizer.optimizers[0], optimizer.optimizers[1]
     if not router._shard()[2]:
         return None, None
@@ -260,7 +270,7 @@ def build_tiller(model, args, *, decay_tied_embedding=False, microbatches=None,
         # layer-sharded across ranks: one contiguous buffer per owner so the
         # updated weights travel in one broadcast per owner
         from .tiller import OwnerPacking
-        router.packing = OwnerPacking(router, attention)
+        router.packing = OwnerPacking.for_tiller(router, attention)
     return TILLERCompositeOptimizer((router, attention, adamw))
 
 
@@ -293,9 +303,12 @@ def configure_optimizer(model, args):
                 adam_decay.append(p)
         opts = []
         if muon_named:
-            opts.append(Muon(muon_named, lr=args.lr, weight_decay=args.weight_decay,
-                             momentum=args.muon_momentum, ns_steps=args.muon_ns_steps,
-                             adjust_lr_fn=args.muon_adjust_lr_fn))
+            from .muon import shard_muon
+            muon = Muon(muon_named, lr=args.lr, weight_decay=args.weight_decay,
+                        momentum=args.muon_momentum, ns_steps=args.muon_ns_steps,
+                        adjust_lr_fn=args.muon_adjust_lr_fn)
+            shard_muon(muon)
+            opts.append(muon)
         ag = _adam_groups(adam_decay, adam_no_decay, args.weight_decay)
         if ag:
             opts.append(FusedAdamW(ag, lr=args.lr, betas=(args.beta1, args.beta2), eps=args.eps))

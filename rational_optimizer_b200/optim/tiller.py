@@ -155,22 +155,29 @@ def sharding_enabled(world: int) -> bool:
 
 
 class OwnerPacking:
-    """TILLER-managed weights re-homed into one fp32 buffer ordered by owner.
+    """Layer-sharded weights re-homed into one fp32 buffer ordered by owner.
 
-    Per layer [in_proj, out_proj, qkv, attention out]; the layers an owner
-    updates are therefore one contiguous range, replicated with one broadcast
-    per owner instead of one per tensor.
+    ``per_layer[l]`` lists the matrices of layer ``l`` (TILLER: [in_proj,
+    out_proj, qkv, attention out]); layer ``l`` is updated on rank
+    ``layer_owner(l)``, so the layers an owner updates form one contiguous
+    range, replicated with one peer-memory pull (or one broadcast) per owner
+    instead of one per tensor.
     """
 
-    def __init__(self, router, attention):
+    @classmethod
+    def for_tiller(cls, router, attention):
         L = len(router.pairs)
         per_layer = [[router.pairs[l]["in_weight"], router.pairs[l]["out_weight"],
                       attention.role_parameters["qkv"][l], attention.role_parameters["attn_out"][l]]
                      for l in range(L)]
+        return cls(per_layer, router.world_size, router.loss_probe_group)
+
+    def __init__(self, per_layer, world, group=None):
+        L = len(per_layer)
         device = per_layer[0][0].device
         total = sum(p.numel() for ps in per_layer for p in ps)
-        self.world = router.world_size
-        self.group = router.loss_probe_group
+        self.world = int(world)
+        self.group = group
         from ..parallel import owner_gather
         self.gather = None
         use_gather = (device.type == "cuda" and self.world > 1 and owner_gather.available()

@@ -18,7 +18,8 @@ training/train.py:2366-2371).  Two ways to average it across ranks:
   GPU, peer memory mapped through CUDA IPC), otherwise NCCL in fixed-size
   buckets.
 
-* reduce-to-owner (``transport="owner"`` / ``"owner-bf16"``, the default
+* reduce-to-owner (``transport="owner"`` / ``"owner-bf16"`` /
+  ``"owner-int8"`` (per-256 fp32 block scales; lossy, opt-in), the default
   with several ranks when ``owner_layers`` names the matrices of layer-sharded
   optimizers): those matrices are laid out first in the buffer, one
   contiguous segment per layer, and each segment goes only to the rank that
@@ -85,7 +86,7 @@ class GradientSynchronizer:
         if communicator is not None:
             self.transport = "p2p"
         elif self.owner_mode:
-            self.transport = "owner-bf16" if transport == "owner-bf16" else "owner-f32"
+            self.transport = transport if transport in ("owner-bf16", "owner-int8") else "owner-f32"
         elif self.world > 1:
             self.transport = "nccl-overlap" if self.overlap else "nccl"
         else:
@@ -137,7 +138,7 @@ class GradientSynchronizer:
         self._tail = segments[-1][0] + segments[-1][1] if segments else 0
         owners = [int(layer_owner(l)) for l in range(len(layers))]
         self.owner = OwnerReduce(self.flat, segments, owners, group=self.group,
-                                 transport="bf16" if self.transport == "owner-bf16" else "f32")
+                                 transport=self.transport.split("-", 1)[1])
         self._reported = set()
 
     def _owner_ready(self, p):

@@ -6,8 +6,9 @@ all-reduce of those gradients (the reference runs DDP's fp32 all-reduce,
 training/train.py:2366-2371) by
 
 * ``send(layer)``: as soon as backward has produced a layer's gradient, every
-  other rank writes it (fp32, or bf16 with ``transport="bf16"``) into its slot
-  of the owner's receive buffer with peer stores, on a communication stream,
+  other rank writes it (fp32; bf16 with ``transport="bf16"``; int8 with one
+  fp32 scale per 256 elements with ``transport="int8"``) into its slot of the
+  owner's receive buffer with peer stores, on a communication stream,
   overlapped with the rest of backward;
 * ``reduce()``: after backward the owner waits (bounded) for every sender,
   sums the slots in rank order together with its own gradient, scales by
@@ -37,17 +38,32 @@ from .. import _ext
 
 SEND_CTAS = 16
 REDUCE_CTAS = 296
+MODES = {"f32": 0, "bf16": 1, "int8": 2}
+QBLOCK = 256  # int8: elements per fp32 scale
 
 
-def receive_layout(sizes, owners, world):
-    """Per owner: {layer: element offset of the layer's first slot} in its receive
-    buffer (slots ``[world][n_layer]`` back to back in layer order), and the
-    buffer's total elements."""
+def slot_bytes(n: int, transport: str) -> int:
+    """Bytes of one sender's slot of an ``n``-element layer (the kernels'
+    layout: fp32 / bf16 values, or int8 values padded to 16 bytes followed by
+    the per-256 fp32 scales padded to 16 bytes)."""
+    n = int(n)
+    if transport == "f32":
+        return 4 * n
+    if transport == "bf16":
+        return 2 * n
+    r16 = lambda b: (b + 15) // 16 * 16  # noqa: E731
+    return r16(n) + r16(4 * ((n + QBLOCK - 1) // QBLOCK))
+
+
+def receive_layout(sizes, owners, world, transport="f32"):
+    """Per owner: {layer: byte offset of the layer's first slot} in its receive
+    buffer (``world`` slots per layer back to back, layers in order), and the
+    buffer's total bytes."""
     offsets, totals = {}, {}
     for layer, (n, owner) in enumerate(zip(sizes, owners)):
         table = offsets.setdefault(owner, {})
         table[layer] = totals.get(owner, 0)
-        totals[owner] = totals.get(owner, 0) + world * int(n)
+        totals[owner] = totals.get(owner, 0) + world * slot_bytes(n, transport)
     return offsets, totals
 
 
@@ -59,8 +75,8 @@ def counter_index(layer, owners):
 class OwnerReduce:
     def __init__(self, flat: torch.Tensor, segments, owners, *, group=None, transport="f32",
                  timeout_s=None):
-        if transport not in ("f32", "bf16"):
-            raise ValueError(f"owner transport must be f32 or bf16, got {transport!r}")
+        if transport not in MODES:
+            raise ValueError(f"owner transport must be one of {sorted(MODES)}, got {transport!r}")
         C = _ext.ext()
         self.flat = flat
         self.device = flat.device
@@ -69,8 +85,8 @@ class OwnerReduce:
         self.world = dist.get_world_size(group)
         self.segments = [(int(o), int(n)) for o, n in segments]
         self.owners = [int(r) for r in owners]
-        self.bf16 = transport == "bf16"
-        self.elem = 2 if self.bf16 else 4
+        self.transport = transport
+        self.mode = MODES[transport]
         for off, n in self.segments:
             if off % 8 or n % 8:
                 raise ValueError("owner-reduce segments must start and end on 32-byte boundaries")
@@ -78,9 +94,9 @@ class OwnerReduce:
             timeout_s = float(os.environ.get("RO_COMM_TIMEOUT_S", "10"))
         self.timeout_ns = int(timeout_s * 1e9)
         sizes = [n for _, n in self.segments]
-        self.recv_offsets, totals = receive_layout(sizes, self.owners, self.world)
+        self.recv_offsets, totals = receive_layout(sizes, self.owners, self.world, transport)
         self.owned = [l for l, r in enumerate(self.owners) if r == self.rank]
-        self.recv = C.comm_alloc(max(16, totals.get(self.rank, 0) * self.elem), self.device.index)
+        self.recv = C.comm_alloc(max(16, totals.get(self.rank, 0)), self.device.index)
         self.counters = C.comm_alloc(max(16, 4 * len(self.owned)), self.device.index)
         local = (C.comm_handle(self.recv), C.comm_handle(self.counters))
         gathered = [None] * self.world
@@ -120,12 +136,12 @@ class OwnerReduce:
         if owner == self.rank:
             return
         off, n = self.segments[layer]
-        dst = self.peer_recv[owner] + (self.recv_offsets[owner][layer] + self.rank * n) * self.elem
+        dst = self.peer_recv[owner] + self.recv_offsets[owner][layer] + self.rank * slot_bytes(n, self.transport)
         counter = self.peer_counters[owner] + 4 * counter_index(layer, self.owners)
         current = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(current)
         with torch.cuda.stream(self.stream):
-            _ext.ext().owner_send(self.flat[off:off + n], dst, self.bf16, counter, SEND_CTAS)
+            _ext.ext().owner_send(self.flat[off:off + n], dst, self.mode, counter, SEND_CTAS)
 
     def reduce(self):
         """Send what backward did not report, then reduce the owned layers (current stream)."""
@@ -137,7 +153,7 @@ class OwnerReduce:
         if self.owned:
             _ext.ext().owner_reduce(self.flat, self.recv.data_ptr(), self.counters, self.dev_offsets,
                                     self.dev_sizes, self.dev_recv_offsets, self.sumsq, self.rank,
-                                    self.world, (self.world - 1) * SEND_CTAS, 1.0 / self.world, self.bf16,
+                                    self.world, (self.world - 1) * SEND_CTAS, 1.0 / self.world, self.mode,
                                     self.err, self.timeout_ns)
         else:
             self.sumsq.zero_()

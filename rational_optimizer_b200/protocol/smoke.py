@@ -8,14 +8,18 @@ Run once per node, one process per GPU:
 Checks, with exact expected values (every rank fills with rank + 1):
 
 * NCCL broadcast and all-reduce of a 256 MiB fp32 buffer;
-* the reduce-to-owner kernels (:class:`~rational_optimizer_b200.parallel.owner_reduce.OwnerReduce`):
-  every rank owns one segment, receives the others' copies over NVLink peer
-  memory and must hold the mean;
+* the reduce-to-owner kernels (:class:`~rational_optimizer_b200.parallel.owner_reduce.OwnerReduce`)
+  in each transport format (fp32, bf16, int8 with per-256 scales): every
+  rank owns one segment, receives the others' copies over NVLink peer memory
+  and must hold the mean (exactly; int8 to one rounding of the scale);
 * the owner weight pull (:class:`~rational_optimizer_b200.parallel.owner_gather.OwnerGather`):
   after a publish every rank must hold every owner's values.
 
-Rank 0 prints one JSON line with the measured bus bandwidths (device time,
-max over ranks) and ``passed``; any mismatch raises.  Every collective wait
+Rank 0 prints one JSON line with the measured bandwidths (device time, max
+over ranks): NCCL bus bandwidth, and for the peer-memory kernels the bytes
+each rank receives per second and that figure as a fraction of the measured
+770 GB/s per-direction NVLink peer-copy bandwidth; and ``passed``.  Any
+mismatch raises.  Every collective wait
 inside the package's kernels is bounded (``RO_COMM_TIMEOUT_S``).
 """
 from __future__ import annotations
@@ -57,48 +61,48 @@ def nccl_checks(rank, world, device):
     return {"nccl_allreduce_ms": ms, "nccl_allreduce_busbw_gbs": 2 * (world - 1) / world * value.numel() * 4 / ms / 1e6}
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction per B200 on this class of node
+
+
 def owner_checks(rank, world, device):
-    from ..parallel.owner_reduce import OwnerReduce
     from ..parallel import owner_gather
-    seg = ELEMS // world // 8 * 8
-    flat = torch.full((seg * world,), float(rank + 1), device=device)
-    red = OwnerReduce(flat, [(r * seg, seg) for r in range(world)], list(range(world)))
-    red.begin()
-    for layer in range(world):
-        red.send(layer)
-    red.reduce()
-    torch.cuda.synchronize(device)
-    red.check()
-    mine = flat[rank * seg:(rank + 1) * seg]
-    want = (world + 1) / 2
-    if not torch.all(mine == want):
-        raise RuntimeError(f"reduce-to-owner: rank {rank} holds {mine[0].item()}, expected {want}")
+    from ..parallel.owner_reduce import OwnerReduce, slot_bytes
+    seg = ELEMS // world // 256 * 256
+    out = {}
+    flat = torch.empty(seg * world, device=device)
+    for transport in ("f32", "bf16", "int8"):
+        red = OwnerReduce(flat, [(r * seg, seg) for r in range(world)], list(range(world)), transport=transport)
 
-    def once():
-        flat.fill_(float(rank + 1))
-        red.begin()
-        for layer in range(world):
-            red.send(layer)
-        red.reduce()
+        def once():
+            flat.fill_(float(rank + 1))
+            red.begin()
+            for layer in range(world):
+                red.send(layer)
+            red.reduce()
 
-    ms_red = _time(once, device)
-    red.close()
+        once()
+        torch.cuda.synchronize(device)
+        red.check()
+        mine = flat[rank * seg:(rank + 1) * seg]
+        want = torch.full_like(mine, (world + 1) / 2)
+        if transport == "int8":  # one rounding of the per-block scale
+            ok = torch.allclose(mine, want, rtol=1e-5, atol=0.0)
+        else:
+            ok = torch.equal(mine, want)
+        if not ok:
+            raise RuntimeError(f"reduce-to-owner ({transport}): rank {rank} holds {mine[0].item()}, "
+                               f"expected {(world + 1) / 2}")
+        ms = _time(once, device)
+        red.close()
+        moved = (world - 1) * slot_bytes(seg, transport)  # bytes each rank receives (and sends)
+        out[f"owner_reduce_{transport}_ms"] = ms
+        out[f"owner_reduce_{transport}_ingress_gbs"] = moved / ms / 1e6
+        out[f"owner_reduce_{transport}_frac_nvlink"] = moved / ms / 1e6 / NVLINK_GBS
     raw, weights = owner_gather.shared_buffer(seg * world, device)
-    weights.copy_(torch.arange(world, device=device, dtype=torch.float32).repeat_interleave(seg) + 1.0)
-    weights[rank * seg:(rank + 1) * seg] = float(rank + 1)
     gather = owner_gather.OwnerGather(raw, weights, [(r * seg, (r + 1) * seg) for r in range(world)],
                                       [[] for _ in range(world)])
     weights.zero_()
     weights[rank * seg:(rank + 1) * seg] = float(rank + 1)
-    gather.publish()
-    gather.pending = False
-    gather.pull()
-    torch.cuda.current_stream(device).wait_stream(owner_gather.param_ready.side_stream(device))
-    torch.cuda.synchronize(device)
-    gather.check()
-    expect = torch.arange(world, device=device, dtype=torch.float32).repeat_interleave(seg) + 1.0
-    if not torch.equal(weights, expect):
-        raise RuntimeError(f"weight pull: rank {rank} holds the wrong values")
 
     def pull_once():
         gather.publish()
@@ -106,11 +110,18 @@ def owner_checks(rank, world, device):
         gather.pull()
         torch.cuda.current_stream(device).wait_stream(owner_gather.param_ready.side_stream(device))
 
+    pull_once()
+    torch.cuda.synchronize(device)
+    gather.check()
+    expect = torch.arange(world, device=device, dtype=torch.float32).repeat_interleave(seg) + 1.0
+    if not torch.equal(weights, expect):
+        raise RuntimeError(f"weight pull: rank {rank} holds the wrong values")
     ms_pull = _time(pull_once, device)
     gather.close()
-    moved = (world - 1) * seg * 4  # bytes each rank receives
-    return {"owner_reduce_ms": ms_red, "owner_reduce_ingress_gbs": moved / ms_red / 1e6,
-            "owner_pull_ms": ms_pull, "owner_pull_ingress_gbs": moved / ms_pull / 1e6}
+    moved = (world - 1) * seg * 4
+    out.update(owner_pull_ms=ms_pull, owner_pull_ingress_gbs=moved / ms_pull / 1e6,
+               owner_pull_frac_nvlink=moved / ms_pull / 1e6 / NVLINK_GBS)
+    return out
 
 
 def main() -> int:

@@ -182,7 +182,7 @@ def build_parser() -> argparse.ArgumentParser:
                    help="vocabulary of the synthetic/zipf and synthetic/uniform sources")
     p.add_argument("--zipf-alpha", type=float, default=1.1)
     p.add_argument("--compute-dtype", choices=["bf16", "fp32"], default="bf16")
-    p.add_argument("--grad-transport", choices=["p2p", "nccl", "owner", "owner-bf16"], default=None)
+    p.add_argument("--grad-transport", choices=["p2p", "nccl", "owner", "owner-bf16", "owner-int8"], default=None)
     p.add_argument("--strict-exact-resume", action="store_true",
                    help="run-local checkpoint, interrupted-commit recovery, argument-digest contract")
     p.add_argument("--dist-timeout-s", type=float, default=600.0)

@@ -190,6 +190,20 @@ def cases(rows):
     def ns5_router_native():
         return _ns5(True)
 
+    def _ns5_muon(native):
+        # Muon's MLP matrices of all layers in one batch, wide orientation
+        from ..optim.newton_schulz import ns5_grouped_bf16
+        B, r, c = 18, d, H
+        x = torch.randn(B, r, c, device=dev, dtype=bf)
+        flops = 5 * B * (2.0 * r * r * c + 2.0 * r * r * r + 2.0 * r * r * c)
+        return (lambda: ns5_grouped_bf16(x, native=native)), 0, flops
+
+    def ns5_muon_mlp_cublas():
+        return _ns5_muon(False)
+
+    def ns5_muon_mlp_native():
+        return _ns5_muon(True)
+
     def _attn_planes():
         B, S, Hh, hd = rows // 1024, 1024, 16, 64
         q, k, v = (torch.randn(B, S, Hh * hd, device=dev, dtype=bf) for _ in range(3))
@@ -262,7 +276,8 @@ def cases(rows):
                      ("grain_in_proj_unfused", grain_in_proj_unfused),
                      ("grain_out_proj_bwd_fused", grain_out_proj_bwd_fused),
                      ("grain_out_proj_bwd_unfused", grain_out_proj_bwd_unfused), ("ns5_router_cublas", ns5_router_cublas),
-                     ("ns5_router_native", ns5_router_native), ("ledger", ledger),
+                     ("ns5_router_native", ns5_router_native), ("ns5_muon_mlp_cublas", ns5_muon_mlp_cublas),
+                     ("ns5_muon_mlp_native", ns5_muon_mlp_native), ("ledger", ledger),
                      ("attn_fwd", attn_fwd), ("attn_fwd_sdpa", attn_fwd_sdpa), ("attn_bwd", attn_bwd),
                      ("attn_bwd_sdpa", attn_bwd_sdpa)]:
         out[name] = fn

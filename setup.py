@@ -3,6 +3,11 @@
 All CUDA sources are compiled for Blackwell only
 (``-gencode arch=compute_100a,code=sm_100a``); torch's own arch list is
 bypassed because explicit ``-gencode`` flags are given.
+
+``RO_BOUNDS_CHECK=1 python setup.py build_ext --inplace --build-temp build/checked``
+builds the bounds-checked variant ``rational_optimizer_b200._C_checked``
+(``-DRO_BOUNDS_CHECK``: failed index checks are recorded in a device word and
+the guarded access is skipped; ``RO_CHECKED=1`` makes the package load it).
 """
 import glob
 import os
@@ -19,8 +24,11 @@ NVCC_FLAGS = [
     "--expt-relaxed-constexpr",
     "-DNDEBUG",
 ]
-if os.environ.get("RO_BOUNDS_CHECK") == "1":
+CXX_FLAGS = ["-O3", "-std=c++17"]
+CHECKED = os.environ.get("RO_BOUNDS_CHECK") == "1"
+if CHECKED:
     NVCC_FLAGS.append("-DRO_BOUNDS_CHECK")
+    CXX_FLAGS.append("-DRO_BOUNDS_CHECK")
 
 
 def sources():
@@ -34,10 +42,10 @@ setup(
     packages=[],
     ext_modules=[
         CUDAExtension(
-            name="rational_optimizer_b200._C",
+            name="rational_optimizer_b200._C_checked" if CHECKED else "rational_optimizer_b200._C",
             sources=sources(),
             include_dirs=[os.path.join(HERE, CSRC)],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

@@ -25,3 +25,18 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """Under the bounds-checked build (RO_CHECKED=1), write the failed-check
+    words of the session's kernels to RO_CHECKED_REPORT (JSON)."""
+    report = os.environ.get("RO_CHECKED_REPORT")
+    if os.environ.get("RO_CHECKED") != "1" or not report:
+        return
+    import json
+
+    from rational_optimizer_b200 import _ext
+    C = _ext.ext()
+    with open(report, "w") as fh:
+        json.dump({"module": C.__file__, "checked": bool(C.bounds_checked), "faults": C.bounds_faults(),
+                   "exitstatus": int(exitstatus)}, fh)

@@ -91,3 +91,12 @@ def test_resume_with_another_world_size_is_rejected(tmp_path):
     assert torch.load(ck, weights_only=False)["contract"]["world_size"] == 2
     res = _launch(tmp_path, "ws1", 1, *common)
     assert res.returncode != 0 and "contract differs" in res.stderr
+
+
+def test_sharded_muon_ownership_and_state_replication():
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(ROOT, "tests", "muon_shard_worker.py")]
+    res = subprocess.run(cmd, cwd=ROOT, env=dict(os.environ, OMP_NUM_THREADS="1"), capture_output=True, text=True,
+                         timeout=240)
+    assert res.returncode == 0, res.stderr[-3000:]
+    assert "MUON_STATE_OK 2" in res.stdout

@@ -2,7 +2,9 @@
 
 Runs a 4-layer GRAIN+TILLER model for 10 steps per configuration: gradient
 all-reduce during backward (per-layer buckets) or after it, TILLER sharded by
-layer (deferred weight broadcasts) or replicated, one or two micro-batches.
+layer (deferred weight broadcasts) or replicated, one or two micro-batches;
+then Muon replicated against Muon layer-sharded (reduce-to-owner gradients,
+owner update, peer-memory weight pull), eager and graphed.
 Every configuration must leave bitwise-identical replicas on all ranks, the
 fully overlapped/sharded run must follow the plain run's loss curve, and the
 same run with its forward/backward/reduction replayed from a CUDA graph must
@@ -26,14 +28,15 @@ from rational_optimizer_b200.train.engine import TrainEngine  # noqa: E402
 from rational_optimizer_b200.train.integrity import model_state_sha256  # noqa: E402
 
 
-def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="nccl"):
+def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="nccl", optimizer="tiller_v1"):
     os.environ["RO_TILLER_SHARD"] = "1" if shard else "0"
+    os.environ["RO_MUON_SHARD"] = "1" if shard else "0"
     os.environ["RO_WEIGHT_TRANSPORT"] = weights
     os.environ["RO_CUDA_GRAPH"] = "1" if graph else "0"
     torch.manual_seed(0)
     args = preset("18l_1024d", layers=4, seq_len=256, activation="grain")
     model = CausalTransformer(args, 50304).cuda()
-    ns = SimpleNamespace(optimizer="tiller_v1", lr=3e-4, weight_decay=0.1, beta1=0.9, beta2=0.95, eps=1e-8,
+    ns = SimpleNamespace(optimizer=optimizer, lr=3e-4, weight_decay=0.1, beta1=0.9, beta2=0.95, eps=1e-8,
                          muon_momentum=0.95, muon_ns_steps=5, muon_adjust_lr_fn="match_rms_adamw",
                          grad_accum=accum, layers=4, steps=100)
     opt = configure_optimizer(model, ns)
@@ -41,7 +44,7 @@ def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="
         from rational_optimizer_b200.optim.composite import owner_layers
         layers, owner_of = owner_layers(opt)
         sync = GradientSynchronizer(model, transport=transport, owner_layers=layers, layer_owner=owner_of)
-        assert sync.transport == ("owner-bf16" if transport == "owner-bf16" else "owner-f32")
+        assert sync.transport == (transport if transport in ("owner-bf16", "owner-int8") else "owner-f32")
     else:
         sync = GradientSynchronizer(model, transport="nccl", overlap=overlap)
         assert sync.transport == ("nccl-overlap" if overlap else "nccl")
@@ -70,7 +73,12 @@ def main():
                dict(overlap=False, shard=True, accum=1, transport="owner", graph=True),
                dict(overlap=False, shard=True, accum=1, transport="owner-bf16"),
                dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p"),
-               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", graph=True)]
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", graph=True),
+               dict(overlap=True, shard=False, accum=1, optimizer="muon"),
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", optimizer="muon"),
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", graph=True,
+                    optimizer="muon"),
+               dict(overlap=False, shard=True, accum=1, transport="owner-int8", weights="p2p")]
     runs = [run(info, **c) for c in configs]
     digests = [None] * info.world_size
     dist.all_gather_object(digests, [r[1] for r in runs])
@@ -96,6 +104,16 @@ def main():
         assert runs[9][0] == runs[6][0] and digests[0][9] == digests[0][6], (runs[9][0], runs[6][0])
         assert runs[10][0] == runs[6][0] and digests[0][10] == digests[0][6], (runs[10][0], runs[6][0])
         print("PULL_OK", flush=True)
+        # layer-sharded Muon (reduce-to-owner, owner update, weight pull) follows the
+        # replicated Muon; its graphed forward/backward replays it exactly
+        rel_muon = max(abs(x - y) / abs(y) for x, y in zip(runs[12][0], runs[11][0]))
+        assert rel_muon < 1e-2, (runs[12][0], runs[11][0])
+        assert runs[13][0] == runs[12][0] and digests[0][13] == digests[0][12], (runs[13][0], runs[12][0])
+        print("MUON_SHARD_OK max rel loss diff", rel_muon, flush=True)
+        # int8 gradients with per-256 fp32 scales stay close to the fp32 transport
+        rel_i8 = max(abs(x - y) / abs(y) for x, y in zip(runs[14][0], runs[0][0]))
+        assert rel_i8 < 3e-2, (runs[14][0], runs[0][0])
+        print("INT8_OK max rel loss diff", rel_i8, flush=True)
         print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
     dist.barrier()
     dist.destroy_process_group()
