@@ -8,6 +8,7 @@ supports are routed to it; anything else uses cuBLAS through PyTorch.
 from __future__ import annotations
 
 import os
+import warnings
 
 import torch
 
@@ -67,15 +68,25 @@ def matmul_tn(a: torch.Tensor, b: torch.Tensor, out_dtype=None) -> torch.Tensor:
 
 
 _ADDMM_DTYPE_OUT = True
+# Which form the last CUDA weight-gradient accumulation took: "addmm_fp32_out"
+# (one GEMM with beta = 1 writing fp32 in place) or "gemm_then_add" (a
+# separate fp32 GEMM output added into the buffer: 8 more bytes per element).
+ACCUMULATE_PATH = None
 
 
 def matmul_tn_accumulate_(out: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """``out += a^T @ b`` with bf16 operands and an fp32 ``out`` (weight-gradient
     accumulation straight into a gradient buffer, beta = 1 in the GEMM)."""
-    global _ADDMM_DTYPE_OUT
+    global _ADDMM_DTYPE_OUT, ACCUMULATE_PATH
     if _ADDMM_DTYPE_OUT and a.is_cuda and out.dtype == torch.float32 and a.dtype != torch.float32:
         try:
-            return torch.addmm(out, a.t(), b, out_dtype=torch.float32, out=out)
-        except (RuntimeError, TypeError):
+            result = torch.addmm(out, a.t(), b, out_dtype=torch.float32, out=out)
+            ACCUMULATE_PATH = "addmm_fp32_out"
+            return result
+        except (RuntimeError, TypeError) as exc:
             _ADDMM_DTYPE_OUT = False
+            warnings.warn(f"fp32-output addmm is unavailable ({exc}); weight gradients fall back to a "
+                          "separate GEMM and an add", RuntimeWarning)
+    if a.is_cuda:
+        ACCUMULATE_PATH = "gemm_then_add"
     return out.add_(matmul_tn(a, b, out_dtype=out.dtype))

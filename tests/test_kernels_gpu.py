@@ -225,3 +225,15 @@ def test_fused_residual_model_matches_unfused():
     assert abs(float(l1) - float(l2)) < 1e-2
     for a, b in zip(g1, [p.grad for p in m.parameters()]):
         torch.testing.assert_close(a, b, rtol=5e-2, atol=5e-3)
+
+
+def test_weight_gradient_accumulates_in_one_fp32_gemm():
+    from rational_optimizer_b200.ops import gemm
+    torch.manual_seed(0)
+    dy = torch.randn(4096, 768, device=DEV).to(torch.bfloat16)
+    x = torch.randn(4096, 1024, device=DEV).to(torch.bfloat16)
+    out = torch.randn(768, 1024, device=DEV)
+    want = out + dy.float().t() @ x.float()
+    gemm.matmul_tn_accumulate_(out, dy, x)
+    assert gemm.ACCUMULATE_PATH == "addmm_fp32_out"  # beta = 1 into the fp32 buffer, no extra pass
+    torch.testing.assert_close(out, want, rtol=1e-3, atol=1e-2)
