@@ -456,6 +456,25 @@ __device__ __forceinline__ void load_grain_coeffs(GrainCoeffs& c, int g, const f
   for (int j = 0; j < 4; ++j) c.b[j] = splat2(fabsf(den[g * 4 + j]));
 }
 
+// Derivative coefficients, formed once per tile: P'(t) = a1 + t (2 a2 + t (3 a3
+// + t (4 a4 + 5 a5 t))) and dQ/dt = sign0(t)|b0| + t (2|b1| + |t| (3|b2| + 4|b3||t|)).
+struct GrainDerivCoeffs {
+  float2 da5, da4, da3, da2;
+  float2 db3, db2, db1;
+};
+
+__device__ __forceinline__ GrainDerivCoeffs grain_deriv_coeffs(const GrainCoeffs& c) {
+  GrainDerivCoeffs d;
+  d.da5 = mul2(splat2(5.0f), c.a[5]);
+  d.da4 = mul2(splat2(4.0f), c.a[4]);
+  d.da3 = mul2(splat2(3.0f), c.a[3]);
+  d.da2 = mul2(splat2(2.0f), c.a[2]);
+  d.db3 = mul2(splat2(4.0f), c.b[3]);
+  d.db2 = mul2(splat2(3.0f), c.b[2]);
+  d.db1 = mul2(splat2(2.0f), c.b[1]);
+  return d;
+}
+
 // GRAIN backward behind the out-projection's input-gradient GEMM.  The
 // accumulator holds gy = dL/dy for one 128-row x 256-column tile (one group).
 // Sixteen epilogue warps: four per TMEM lane quarter (32 rows), each owning
@@ -520,6 +539,7 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
   const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
   GrainCoeffs c;
   load_grain_coeffs(c, tn, p.num, p.den);
+  const GrainDerivCoeffs dc = grain_deriv_coeffs(c);
   const float2 one = splat2(1.0f);
   float2 acc[10];
 #pragma unroll
@@ -534,8 +554,9 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
     tmem_ld16(tbase + ch * 16, r);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float2 g2 = make_float2(__bfloat162float(__float2bfloat16_rn(__uint_as_float(r[2 * j]))),
-                                    __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[2 * j + 1]))));
+      // gy rounded to bf16 as the unfused GEMM output is (one paired conversion)
+      const float2 g2 = __bfloat1622float2(__floats2bfloat162_rn(__uint_as_float(r[2 * j]),
+                                                                 __uint_as_float(r[2 * j + 1])));
       const float2 z = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zc[j]));
       const float2 t = mul2(z, ir);
       const float2 at = abs2(t);
@@ -545,18 +566,16 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
       pp = fma2(pp, t, c.a[2]);
       pp = fma2(pp, t, c.a[1]);
       pp = fma2(pp, t, c.a[0]);
-      // P'(t) = a1 + t (2 a2 + t (3 a3 + t (4 a4 + 5 a5 t)))
-      float2 dp = fma2(mul2(splat2(5.0f), c.a[5]), t, mul2(splat2(4.0f), c.a[4]));
-      dp = fma2(dp, t, mul2(splat2(3.0f), c.a[3]));
-      dp = fma2(dp, t, mul2(splat2(2.0f), c.a[2]));
+      float2 dp = fma2(dc.da5, t, dc.da4);
+      dp = fma2(dp, t, dc.da3);
+      dp = fma2(dp, t, dc.da2);
       dp = fma2(dp, t, c.a[1]);
       float2 q = fma2(c.b[3], at, c.b[2]);
       q = fma2(q, at, c.b[1]);
       q = fma2(q, at, c.b[0]);
       q = fma2(q, at, one);
-      // dQ/dt = sign0(t)|b0| + t (2|b1| + |t| (3|b2| + 4|b3||t|))
-      float2 hq = fma2(mul2(splat2(4.0f), c.b[3]), at, mul2(splat2(3.0f), c.b[2]));
-      hq = fma2(hq, at, mul2(splat2(2.0f), c.b[1]));
+      float2 hq = fma2(dc.db3, at, dc.db2);
+      hq = fma2(hq, at, dc.db1);
       const float2 dq = fma2(t, hq, mul2(c.b[0], sign02(t)));
       const float2 iq = rcp2(q);
       const float2 f = mul2(pp, iq);

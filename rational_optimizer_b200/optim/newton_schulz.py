@@ -23,6 +23,7 @@ import torch
 from .. import _ext
 
 NS_COEFFICIENTS = (3.4445, -4.775, 2.0315)
+LAST_PATH = None  # "native" (tcgen05 GEMMs) or "cublas": the last CUDA ns5_grouped_bf16
 NS_EPS = 1e-7
 ATTENTION_HEADS = 16
 ATTENTION_HEAD_GROUP_SIZE = 4
@@ -66,9 +67,12 @@ def ns5_grouped_bf16(x16: torch.Tensor, *, native: bool | None = None) -> torch.
     CUDA: the Frobenius normalisation kernel followed by, per iteration,
     ``A = X X^T``; ``P = b A + c A A``; ``X = a X + P X``.  ``native`` selects
     the package's batched tcgen05 GEMMs, whose epilogue reads the addend
-    directly (``RO_NATIVE_NS=1`` by default; cuBLAS batched GEMMs otherwise,
-    which first copy the addend into the output).
+    directly (the default; ``RO_NATIVE_NS=0`` selects cuBLAS batched GEMMs,
+    which first copy the addend into the output).  Shapes the kernel does
+    not take (row strides that are not a multiple of 16 bytes) use cuBLAS;
+    :data:`LAST_PATH` records which ran last.
     """
+    global LAST_PATH
     if x16.shape[-2] > x16.shape[-1]:
         raise RuntimeError("ns5_grouped_bf16 expects wide blocks")
     if _ext.available() and x16.is_cuda and hasattr(_ext.ext(), "ns_normalize"):
@@ -79,7 +83,9 @@ def ns5_grouped_bf16(x16: torch.Tensor, *, native: bool | None = None) -> torch.
         if native and hasattr(C, "gemm_bf16_ex"):
             out = _ns5_native_bf16(C, work)
             if out is not None:
+                LAST_PATH = "native"
                 return out
+        LAST_PATH = "cublas"
         return _ns5_torch_bf16(work)
     work = x16.to(torch.bfloat16)
     norm = torch.linalg.vector_norm(work.float(), dim=(-2, -1), keepdim=True).clamp_min(NS_EPS)
@@ -99,12 +105,7 @@ def _ns5_native_bf16(C, work):
 
 
 def _native_ns_enabled() -> bool:
-    return os.environ.get("RO_NATIVE_NS", _native_default()) == "1"
-
-
-def _native_default() -> str:
-    from ..ops import gemm as _g
-    return "1" if _g._NATIVE else "0"
+    return os.environ.get("RO_NATIVE_NS", "1") == "1"
 
 
 def _native_gemm_enabled() -> bool:
