@@ -425,6 +425,32 @@ c10::optional<torch::Tensor> gemm_bf16_ex(torch::Tensor a, torch::Tensor b, bool
 
 torch::Tensor gemm_error(torch::Tensor like) { return gemm_error_flag(like.device()); }
 
+// fp32 c = a . b (layouts as gemm_bf16, 2-D) written to a raw device address
+// with row stride ldc - which may be a peer GPU's memory mapped through CUDA
+// IPC: every epilogue tile then travels over NVLink as plain 16-byte stores
+// while later tiles are still being multiplied.  False when the layout is
+// unsupported (nothing is written).
+bool gemm_bf16_to(torch::Tensor a, torch::Tensor b, bool a_km, bool b_nk, int64_t c_addr, int64_t ldc) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.dim() == 2 && b.dim() == 2, "gemm_bf16_to expects 2-D CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
+              "gemm_bf16_to expects bfloat16 operands");
+  if (a.stride(-1) != 1 || b.stride(-1) != 1 || (c_addr & 15) != 0 || ldc % 4 != 0) return false;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int64_t M = a_km ? a.size(1) : a.size(0);
+  const int64_t K = a_km ? a.size(0) : a.size(1);
+  const int64_t N = b_nk ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == (b_nk ? b.size(1) : b.size(0)), "gemm_bf16_to inner dimensions differ");
+  TORCH_CHECK(ldc >= N, "gemm_bf16_to: ldc < N");
+  auto& flag = gemm_error_flag(a.device());
+  const int rc = ro::gemm_bf16_tn(a.data_ptr(), a.stride(0), 0, a_km, b.data_ptr(), b.stride(0), 0, !b_nk,
+                                  reinterpret_cast<void*>(c_addr), ldc, 0, true, nullptr, 0, 0, 1.0f, 0.0f,
+                                  static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), 1,
+                                  flag.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+  if (rc < 0) return false;
+  check_rc(rc, "gemm_bf16_to");
+  return true;
+}
+
 // 2-SM tcgen05 GEMM: c[M, N] = a[M, K] . b[N, K]^T (bf16, both K-major).
 // None when the shape or alignment is unsupported (callers fall back).
 c10::optional<torch::Tensor> gemm2_bf16(torch::Tensor a, torch::Tensor b) {
@@ -618,6 +644,13 @@ c10::optional<std::vector<torch::Tensor>> attention_backward(torch::Tensor q, to
 // the owner's memory (CUDA IPC mappings); the kernels run on the current stream.
 // mode: 0 fp32, 1 bf16, 2 int8 (per-256 fp32 scales); see owner_slot_bytes.
 int64_t owner_slot_bytes(int64_t n, int64_t mode) { return ro::owner_slot_bytes(n, static_cast<int>(mode)); }
+
+// counter 0: no arrival (a later owner_signal accounts for the data).
+void owner_signal(int64_t counter, int64_t count) {
+  check_rc(ro::owner_signal(reinterpret_cast<unsigned int*>(counter), static_cast<unsigned int>(count),
+                            at::cuda::getCurrentCUDAStream()),
+           "owner_signal");
+}
 
 void owner_send(torch::Tensor src, int64_t dst, int64_t mode, int64_t counter, int64_t ctas) {
   TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat32 && src.is_contiguous(),
@@ -1053,6 +1086,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd_bwd", &cross_entropy_fwd_bwd);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_bf16_ex", &gemm_bf16_ex);
+  m.def("gemm_bf16_to", &gemm_bf16_to);
   m.def("gemm_error", &gemm_error);
   m.def("adamw_multi_tensor", &adamw_multi_tensor);
   m.def("multi_tensor_dot", &multi_tensor_dot);
@@ -1062,6 +1096,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_rope_forward", &qkv_rope_forward);
   m.def("owner_slot_bytes", &owner_slot_bytes);
   m.def("owner_send", &owner_send);
+  m.def("owner_signal", &owner_signal);
   m.def("owner_reduce", &owner_reduce);
   m.def("owner_publish", &owner_publish);
   m.def("owner_pull", &owner_pull);

@@ -15,6 +15,9 @@
 //          quantises one block: scale = max|g| / 127, q = round(g / scale)
 //          clamped to [-127, 127]; the slot holds the n int8 values, padded
 //          to 16 bytes, then the block scales);
+//          A sender may instead let the layer's weight-gradient GEMMs store
+//          their fp32 tiles straight into the slot (peer stores from the GEMM
+//          epilogue, tile by tile) and then signal the arrivals (signal_kernel);
 //   reduce (owner, after backward): wait until every sender CTA of every owned
 //          layer has arrived (bounded; on expiry an error code is recorded and
 //          the reduction is skipped), then sum the slots (int8: dequantised,
@@ -116,10 +119,19 @@ send_kernel(const float* __restrict__ src, void* __restrict__ dst, int64_t n, un
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && counter != nullptr) {
     __threadfence_system();
     atomicAdd_system(counter, 1u);
   }
+}
+
+// Arrival for data that reached the owner's slot by other kernels earlier on
+// this stream (a weight-gradient GEMM storing its tiles there, sends without
+// a counter): the system-scope fence orders those stores (stream order makes
+// them precede this kernel) before the counter increment the owner acquires.
+__global__ void signal_kernel(unsigned int* counter, unsigned int count) {
+  __threadfence_system();
+  atomicAdd_system(counter, count);
 }
 
 struct ReduceArgs {
@@ -228,6 +240,11 @@ __global__ void release_kernel(unsigned int* counters, int layers, unsigned int 
 }  // namespace owner
 
 int64_t owner_slot_bytes(int64_t n, int mode) { return owner::slot_bytes(n, mode); }
+
+int owner_signal(unsigned int* counter, unsigned int count, cudaStream_t stream) {
+  owner::signal_kernel<<<1, 1, 0, stream>>>(counter, count);
+  return static_cast<int>(cudaGetLastError());
+}
 
 int owner_send(const float* src, void* dst, int64_t n, int mode, unsigned int* counter, int ctas,
                cudaStream_t stream) {

@@ -23,6 +23,11 @@ ACCUMULATE_ATTR = "_ro_accumulate_grad"
 # Optional callable on such parameters, invoked once the in-GEMM accumulation
 # for the current backward pass has been issued (gradient bucketing).
 READY_ATTR = "_ro_grad_ready"
+# Optional callable ``route(gy2, x2) -> bool`` on such parameters: when it
+# returns True it has computed dW = gy^T x itself and delivered it elsewhere
+# (the reduce-to-owner transport: the GEMM stores its tiles straight into the
+# layer owner's receive slot over NVLink), so nothing is added locally.
+ROUTE_ATTR = "_ro_grad_route"
 
 
 def managed_grad(param):
@@ -41,6 +46,14 @@ def report_ready(param):
         ready(param)
 
 
+def accumulate_weight_grad(weight, buf, gy2, x2):
+    """dW = gy^T x into the managed buffer ``buf`` (or routed, see ROUTE_ATTR); reports ready."""
+    route = getattr(weight, ROUTE_ATTR, None)
+    if route is None or not route(gy2, x2):
+        gemm.matmul_tn_accumulate_(buf, gy2, x2)
+    report_ready(weight)
+
+
 def weight_grad(weight, gy2, x2, needed):
     """dW = gy^T x: added inside the GEMM into a managed ``.grad`` (reported ready, returns
     None), else returned for autograd to accumulate."""
@@ -48,8 +61,7 @@ def weight_grad(weight, gy2, x2, needed):
         return None
     buf = managed_grad(weight)
     if buf is not None:
-        gemm.matmul_tn_accumulate_(buf, gy2, x2)
-        report_ready(weight)
+        accumulate_weight_grad(weight, buf, gy2, x2)
         return None
     return gemm.matmul_tn(gy2, x2, out_dtype=weight.dtype)
 
@@ -145,10 +157,7 @@ class _LinearFunction(torch.autograd.Function):
                     and buf.dtype == torch.float32 and buf.is_contiguous()):
                 # dW accumulates in the GEMM (beta = 1) straight into the
                 # parameter's gradient buffer; autograd then has nothing to add.
-                gemm.matmul_tn_accumulate_(buf, g2, x2)
-                ready = getattr(ctx.weight, READY_ATTR, None)
-                if ready is not None:
-                    ready(ctx.weight)
+                accumulate_weight_grad(ctx.weight, buf, g2, x2)
             else:
                 gw = gemm.matmul_tn(g2, x2, out_dtype=ctx.w_dtype)
         return gx, gw, None

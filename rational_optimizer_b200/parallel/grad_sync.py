@@ -38,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _ext
-from ..ops.linear import ACCUMULATE_ATTR, READY_ATTR
+from ..ops.linear import ACCUMULATE_ATTR, READY_ATTR, ROUTE_ATTR
 
 
 class GradientSynchronizer:
@@ -140,9 +140,41 @@ class GradientSynchronizer:
         self.owner = OwnerReduce(self.flat, segments, owners, group=self.group,
                                  transport=self.transport.split("-", 1)[1])
         self._reported = set()
+        self._delivered = {}   # layer -> [(start, length)] stored in the owner's slot by GEMMs
+        self._dirty = False    # a backward ran since zero_grad (gradient accumulation)
+        self._route_ok = False
+        self.fused_wgrad = (self.transport == "owner-f32"
+                            and os.environ.get("RO_FUSED_WGRAD_SEND", "0") == "1"
+                            and hasattr(_ext.ext(), "gemm_bf16_to"))
+        if self.fused_wgrad:
+            for layer, ps in enumerate(layers):
+                if owners[layer] == self.owner.rank:
+                    continue
+                lo = segments[layer][0]
+                for p in ps:
+                    if p.dim() == 2:
+                        start = self.offsets[index[id(p)]] - lo
+                        setattr(p, ROUTE_ATTR, self._make_route(p, layer, start))
 
+    def _make_route(self, p, layer, start):
+        """dW of ``p`` computed by the package's GEMM straight into the owner's
+        slot (fp32 tiles stored over NVLink from the epilogue) when this is the
+        only backward of the step; False (compute locally) otherwise."""
+        addr = self.owner.slot_address(layer, start)
+        rows, cols, n = p.shape[0], p.shape[1], p.numel()
+        C = _ext.ext()
+
+        def route(gy2, x2):
+            if not (self._armed and self._route_ok) or gy2.shape[-1] != rows or x2.shape[-1] != cols:
+                return False
+            if not C.gemm_bf16_to(gy2, x2, True, False, addr, cols):
+                return False
+            self._delivered.setdefault(layer, []).append((start, n))
+            return True
+        return route
     def _owner_ready(self, p):
         if not self._armed:
+            self._dirty = True  # a gradient-accumulation micro-step: later GEMMs must add locally
             return
         layer = self._layer_of.get(id(p))
         if layer is None or id(p) in self._reported:
@@ -150,7 +182,7 @@ class GradientSynchronizer:
         self._reported.add(id(p))
         self._layer_left[layer] -= 1
         if self._layer_left[layer] == 0:
-            self.owner.send(layer)
+            self.owner.send(layer, self._delivered.pop(layer, ()))
 
     def grad_sumsq(self):
         """Sum of squares of the averaged gradient (device scalar, identical on every
@@ -209,6 +241,8 @@ class GradientSynchronizer:
             self._armed = True
             self._reported = set()
             self._layer_left = list(self._layer_size)
+            self._delivered = {}
+            self._route_ok = self.fused_wgrad and not self._dirty
             self.owner.begin()
             return
         if not self.overlap:
@@ -255,6 +289,7 @@ class GradientSynchronizer:
             if p.grad is None or p.grad.data_ptr() != v.data_ptr():
                 p.grad = v
         self.flat.zero_()
+        self._dirty = False
 
     def synchronize(self):
         """Average gradients across ranks (no-op for one rank)."""

@@ -123,12 +123,26 @@ class OwnerReduce:
         self.stream = torch.cuda.Stream(device=dev)
         self._sent = set()
 
+    def slot_address(self, layer: int, element: int) -> int:
+        """Device address (in the owner's memory) of element ``element`` of this
+        rank's fp32 slot for ``layer`` - where a weight-gradient GEMM may store
+        its tiles directly (fp32 transport only)."""
+        if self.transport != "f32":
+            raise RuntimeError("direct slot stores need the fp32 transport")
+        owner = self.owners[layer]
+        n = self.segments[layer][1]
+        return (self.peer_recv[owner] + self.recv_offsets[owner][layer] + self.rank * slot_bytes(n, "f32")
+                + 4 * int(element))
+
     # -- per step ---------------------------------------------------------------
     def begin(self):
         self._sent = set()
 
-    def send(self, layer: int):
-        """Ship this rank's gradient of ``layer`` to its owner (no-op for owned layers)."""
+    def send(self, layer: int, delivered=()):
+        """Ship this rank's gradient of ``layer`` to its owner (no-op for owned
+        layers).  ``delivered``: (start, length) element ranges of the layer that
+        already sit in the owner's slot (stored there by the weight-gradient
+        GEMMs); the rest is sent, then the arrival is signalled once."""
         if layer in self._sent:
             return
         self._sent.add(layer)
@@ -140,8 +154,18 @@ class OwnerReduce:
         counter = self.peer_counters[owner] + 4 * counter_index(layer, self.owners)
         current = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(current)
+        C = _ext.ext()
         with torch.cuda.stream(self.stream):
-            _ext.ext().owner_send(self.flat[off:off + n], dst, self.mode, counter, SEND_CTAS)
+            if not delivered:
+                C.owner_send(self.flat[off:off + n], dst, self.mode, counter, SEND_CTAS)
+                return
+            cursor = 0
+            for start, length in sorted(delivered) + [(n, 0)]:
+                if start > cursor:  # a gap the GEMMs did not store: send it without an arrival
+                    C.owner_send(self.flat[off + cursor:off + start], dst + 4 * cursor, self.mode, 0, SEND_CTAS)
+                cursor = max(cursor, start + length)
+            # one arrival worth a full send, after everything this stream ordered before it
+            C.owner_signal(counter, SEND_CTAS)
 
     def reduce(self):
         """Send what backward did not report, then reduce the owned layers (current stream)."""

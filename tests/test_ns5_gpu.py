@@ -29,12 +29,16 @@ def test_native_ns5_matches_oracle_and_cublas(shape):
     cublas = NS.ns5_grouped_bf16(x, native=False)
     assert NS.LAST_PATH == "cublas"
     want = _oracle(x)
-    # bf16 iterates: compare the polar factors' entries at the scale of their RMS
+    # bf16 iterates amplify rounding: judge the native path by the cuBLAS form of
+    # the same bf16 arithmetic (entry-wise error, relative to the RMS entry), and
+    # both by the fp32 oracle in the Frobenius norm
     scale = want.pow(2).mean().sqrt().item()
     err_native = (native.float() - want).abs().max().item() / scale
     err_cublas = (cublas.float() - want).abs().max().item() / scale
-    assert err_native < 0.1 and err_native < 2.0 * err_cublas + 0.02, (err_native, err_cublas)
-    assert (native.float() - cublas.float()).abs().max().item() / scale < 0.1
+    assert err_native <= 1.25 * err_cublas + 0.02, (err_native, err_cublas)
+    frob = lambda t: (t.float() - want).norm().item() / want.norm().item()  # noqa: E731
+    assert frob(native) < 0.1 and frob(cublas) < 0.1, (frob(native), frob(cublas))
+    assert (native.float() - cublas.float()).norm().item() / want.norm().item() < 0.05
 
 
 def test_native_ns5_is_the_default():

@@ -28,7 +28,9 @@ from rational_optimizer_b200.train.engine import TrainEngine  # noqa: E402
 from rational_optimizer_b200.train.integrity import model_state_sha256  # noqa: E402
 
 
-def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="nccl", optimizer="tiller_v1"):
+def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="nccl", optimizer="tiller_v1",
+        fused=False):
+    os.environ["RO_FUSED_WGRAD_SEND"] = "1" if fused else "0"
     os.environ["RO_TILLER_SHARD"] = "1" if shard else "0"
     os.environ["RO_MUON_SHARD"] = "1" if shard else "0"
     os.environ["RO_WEIGHT_TRANSPORT"] = weights
@@ -45,6 +47,7 @@ def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="
         layers, owner_of = owner_layers(opt)
         sync = GradientSynchronizer(model, transport=transport, owner_layers=layers, layer_owner=owner_of)
         assert sync.transport == (transport if transport in ("owner-bf16", "owner-int8") else "owner-f32")
+        assert sync.fused_wgrad == fused
     else:
         sync = GradientSynchronizer(model, transport="nccl", overlap=overlap)
         assert sync.transport == ("nccl-overlap" if overlap else "nccl")
@@ -78,7 +81,10 @@ def main():
                dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", optimizer="muon"),
                dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", graph=True,
                     optimizer="muon"),
-               dict(overlap=False, shard=True, accum=1, transport="owner-int8", weights="p2p")]
+               dict(overlap=False, shard=True, accum=1, transport="owner-int8", weights="p2p"),
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", fused=True),
+               dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", fused=True, graph=True),
+               dict(overlap=False, shard=True, accum=2, transport="owner", weights="p2p", fused=True)]
     runs = [run(info, **c) for c in configs]
     digests = [None] * info.world_size
     dist.all_gather_object(digests, [r[1] for r in runs])
@@ -114,6 +120,13 @@ def main():
         rel_i8 = max(abs(x - y) / abs(y) for x, y in zip(runs[14][0], runs[0][0]))
         assert rel_i8 < 3e-2, (runs[14][0], runs[0][0])
         print("INT8_OK max rel loss diff", rel_i8, flush=True)
+        # weight-gradient GEMMs storing their tiles straight into the owners' slots
+        rel_fused = max(abs(x - y) / abs(y) for x, y in zip(runs[15][0], runs[9][0]))
+        assert rel_fused < 1e-2, (runs[15][0], runs[9][0])
+        assert runs[16][0] == runs[15][0] and digests[0][16] == digests[0][15], (runs[16][0], runs[15][0])
+        rel_fused2 = max(abs(x - y) / abs(y) for x, y in zip(runs[17][0], runs[4][0]))
+        assert rel_fused2 < 1e-2, (runs[17][0], runs[4][0])
+        print("FUSED_WGRAD_OK max rel loss diff", rel_fused, rel_fused2, flush=True)
         print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
     dist.barrier()
     dist.destroy_process_group()
