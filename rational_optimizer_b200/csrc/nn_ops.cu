@@ -4,6 +4,8 @@
 // gradient in place.  Semantics follow training/train.py:24-45 (RMSNorm,
 // precompute_rope/apply_rope) and the F.cross_entropy mean loss of
 // training/train.py:2868-2870.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace ro {
@@ -220,8 +222,11 @@ add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_bfloat16* __restr
 
 // Backward of the fused op: dx = dres + r * (w dy - xhat * mean(w dy xhat)) (fp32); optionally
 // also written as bf16 (the gradient of the bf16 delta branch).  dres may be null.
-template <int NCH>
-__global__ void __launch_bounds__(kNormWarps * 32)
+// MINB = 2 asks for two CTAs per SM (at most 128 registers a thread, some
+// spilled) so 16 warps keep row loads in flight; MINB = 1 lets the compiler
+// hold 171 registers (one CTA per SM, deeper prefetch per warp).
+template <int NCH, int MINB>
+__global__ void __launch_bounds__(kNormWarps * 32, MINB)
 add_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ dres,
                        const float* __restrict__ x, const float* __restrict__ w,
                        const float* __restrict__ rstd, float* __restrict__ dx,
@@ -607,13 +612,23 @@ int add_rmsnorm_backward(const void* dy, const float* dres, const float* x, cons
     rmsnorm_backward_plan(rows, blocks, rpb);
     const auto* dyp = static_cast<const __nv_bfloat16*>(dy);
     auto* ddp = static_cast<__nv_bfloat16*>(ddelta);
+    static const bool two = [] {
+      const char* v = std::getenv("RO_NORM_BWD_CTAS");
+      return v != nullptr && v[0] == '2';
+    }();
+#define RO_NORM_BWD(N)                                                                                      \
+  (two ? add_rmsnorm_bwd_kernel<N, 2><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, \
+                                                                              partial, rows, rpb)            \
+       : add_rmsnorm_bwd_kernel<N, 1><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, \
+                                                                              partial, rows, rpb))
     switch (d / 256) {
-      case 1: add_rmsnorm_bwd_kernel<1><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
-      case 2: add_rmsnorm_bwd_kernel<2><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
-      case 3: add_rmsnorm_bwd_kernel<3><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
-      case 4: add_rmsnorm_bwd_kernel<4><<<blocks, kNormWarps * 32, 0, stream>>>(dyp, dres, x, w, rstd, dx, ddp, partial, rows, rpb); break;
+      case 1: RO_NORM_BWD(1); break;
+      case 2: RO_NORM_BWD(2); break;
+      case 3: RO_NORM_BWD(3); break;
+      case 4: RO_NORM_BWD(4); break;
       default: return -1;
     }
+#undef RO_NORM_BWD
   }
   column_reduce_kernel<<<ceil_div_i(d, 32), 256, 0, stream>>>(partial, blocks, d, dw, accumulate_dw ? 1 : 0);
   return static_cast<int>(cudaGetLastError());
@@ -666,7 +681,13 @@ int cross_entropy_fwd_bwd(void* logits, const int64_t* target, float* loss_row, 
                           cudaStream_t stream) {
   if (rows <= 0) return 0;
   const size_t elem = dtype == 1 ? 2 : 4;
-  const int use_smem = static_cast<size_t>(V) * elem <= kCeMaxSmemBytes ? 1 : 0;
+  // RO_CE_SMEM=0: re-read the row from L2 for the gradient pass instead of
+  // staging it in shared memory (no shared-memory limit on resident CTAs)
+  static const bool smem_ok = [] {
+    const char* v = std::getenv("RO_CE_SMEM");
+    return v == nullptr || v[0] != '0';
+  }();
+  const int use_smem = smem_ok && static_cast<size_t>(V) * elem <= kCeMaxSmemBytes ? 1 : 0;
   const size_t smem = use_smem ? (static_cast<size_t>(V) * elem + 15) / 16 * 16 : 0;
   auto go = [&](auto tv) {
     using T = decltype(tv);
