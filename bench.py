@@ -161,11 +161,20 @@ def timed(step_fn, steps, device, dist_on, flush=None, kind=None):
         per.setdefault(k, []).append(marks[i].elapsed_time(marks[i + 1]))
     names = sorted(per)
     med = [sorted(per[k])[len(per[k]) // 2] for k in names]
+    global LAST_RANK_MS
+    LAST_RANK_MS = [round(ms, 3)]
     if dist_on:
+        every = torch.zeros(dist.get_world_size(), device=device)
+        dist.all_gather_into_tensor(every, torch.tensor([ms], device=device))
+        LAST_RANK_MS = [round(v, 3) for v in every.tolist()]
         t = torch.tensor([ms] + med, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, med = float(t[0].item()), t[1:].tolist()
     return ms, {k: [round(m, 3), len(per[k])] for k, m in zip(names, med)}
+
+
+# device ms per step of every rank in the last timed() window (which rank sets the MAX)
+LAST_RANK_MS = []
 
 
 def run_ours(a, info):
@@ -225,6 +234,7 @@ def run_ours(a, info):
     start_step = counter["i"]
     ms, split = timed(device_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all,
                       kind=kind)
+    split = dict(split, ms_per_rank=list(LAST_RANK_MS))
     clocks = sampler.stop() if sampler else None
     e2e_ms = e2e_split = None
     if not a.no_e2e:
