@@ -360,3 +360,69 @@ def test_verify_passes_on_the_published_package_and_catches_edits(tmp_path):
     manifest.write_text(manifest.read_text().replace("3407", "3408", 1))
     with pytest.raises(V.VerificationError):
         V.verify_package(package, RESULTS, quick=True)
+
+
+def _flag_map(argv):
+    out, i = {}, 0
+    while i < len(argv):
+        a = argv[i]
+        if i + 1 < len(argv) and not argv[i + 1].startswith("--"):
+            out[a] = argv[i + 1]
+            i += 2
+        else:
+            out[a] = True
+            i += 1
+    return out
+
+
+def test_sweep_row_argv_matches_the_reference_row_runner(tmp_path):
+    import importlib
+    from rational_optimizer_b200.protocol import rows as R
+    from rational_optimizer_b200.protocol import sweep as SW
+    _need_data()
+    ref = importlib.import_module("experiments.protocol.run_activation_row")
+    manifest = R.load_manifest(os.path.join(PROTO, "activation_optimizer_manifest.csv"))
+    for row in manifest[::53]:
+        theirs = _flag_map(ref.training_arguments(row, tmp_path)[1:])
+        theirs.pop("--hf-cache")
+        assert _flag_map(SW.training_argv(row, tmp_path)) == theirs, row["row_id"]
+        assert SW.trajectory_path(row, tmp_path) == ref.result_path(row, tmp_path)
+        assert SW.row_sha256(row) == ref.row_sha256(row)
+    # re-derived for 8 GPUs at the same global tokens per step
+    row = manifest[12]
+    flags = _flag_map(SW.training_argv(row, tmp_path, gpus=8))
+    assert int(flags["--batch-size"]) * int(flags["--grad-accum"]) * 8 * int(row["seq_len"]) == int(
+        row["global_tokens_per_step"])
+
+
+def test_sweep_accepts_only_a_matching_finished_trajectory(tmp_path):
+    import json
+    from rational_optimizer_b200.protocol import rows as R
+    from rational_optimizer_b200.protocol import sweep as SW
+    _need_data()
+    manifest_path = os.path.join(PROTO, "activation_optimizer_manifest.csv")
+    row = R.load_manifest(manifest_path)[12]
+    identity = SW.source_identity(manifest_path, row, os.path.join(PROTO, "SOURCE_FREEZE.sha256"))
+    cfg = {"event": "config", **identity, "experiment_identity": "none",
+           "optimizer_lr_wd_fairness": {"contract": "exact_lr_wd_v1", "passed": True, "base_lr": float(row["lr"]),
+                                        "minimum_lr": float(row["min_lr"]),
+                                        "base_weight_decay": float(row["weight_decay"])}}
+    cfg.update({k: row[c] for k, c in SW.EXACT_FIELDS})
+    cfg.update({k: int(row[c]) for k, c in SW.INTEGER_FIELDS})
+    cfg.update({k: float(row[c]) for k, c in SW.NUMBER_FIELDS})
+    path = SW.trajectory_path(row, tmp_path)
+    path.parent.mkdir(parents=True)
+
+    def write(config, steps):
+        path.write_text(json.dumps(config) + "\n" + json.dumps({"event": "summary", "completed_steps": steps}) + "\n")
+
+    write(cfg, int(row["steps"]))
+    assert SW.matches(path, row, identity)
+    write(cfg, int(row["steps"]) - 1)
+    assert not SW.matches(path, row, identity)
+    write(dict(cfg, optimizer_lr=1e-3), int(row["steps"]))
+    assert not SW.matches(path, row, identity)
+    write(dict(cfg, source_freeze_sha256="0" * 64), int(row["steps"]))
+    assert not SW.matches(path, row, identity)
+    moved = SW.archive(path)
+    assert moved.name.startswith(f"{row['activation']}.superseded-") and not path.exists()
