@@ -489,9 +489,8 @@ __device__ __forceinline__ GrainDerivCoeffs grain_deriv_coeffs(const GrainCoeffs
 //           and gy f' written back over gy in TMEM;
 //   pass 3  gx = gy f' + t * (row sum) / 256 -> bf16, written over z in the
 //           staging tile -> one TMA store.
-// Each epilogue warp writes the 10 coefficient partials of its slice to
-// partial[((2 * tm + crank) * W + warp) * groups + tn][k] (reduced later in a
-// fixed order), so no CTA-wide barrier is needed per tile.
+// The 10 coefficient partials of the CTA's 128 rows go to
+// partial[(2 * tm + crank) * groups + tn][k] (reduced later in a fixed order).
 template <int W>
 __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tbase, uint8_t* stage, int tm, int tn,
                                                    uint32_t crank, int quarter, int e, int lane, int row0, int col0,
@@ -626,9 +625,7 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
     tma_store_2d(tmC, smem_u32(stage), col0, row0);
     bulk_commit();
   }
-  // this warp's coefficient partials (fixed-order reduction later)
-  const int groups = p.N / kBN;
-  float* out = p.partial + ((static_cast<int64_t>(2 * tm + static_cast<int>(crank)) * W + e) * groups + tn) * 10;
+  // coefficient partials of the CTA's rows (fixed-order reduction)
 #pragma unroll
   for (int k = 0; k < 10; ++k) {
     float v = acc[k].x + acc[k].y;
@@ -637,8 +634,17 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
       v *= b > 0.f ? -1.f : (b < 0.f ? 1.f : 0.f);
     }
     v = warp_sum(v);
-    if (lane == 0) out[k] = v;
+    if (lane == 0) coef_part[e][k] = v;
   }
+  asm volatile("bar.sync 5, %0;" ::"n"(W * 32) : "memory");
+  if (e == 0 && lane < 10) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) v += coef_part[w][lane];
+    const int groups = p.N / kBN;
+    p.partial[(static_cast<int64_t>(2 * tm + static_cast<int>(crank)) * groups + tn) * 10 + lane] = v;
+  }
+  asm volatile("bar.sync 5, %0;" ::"n"(W * 32) : "memory");
 }
 
 template <int EPI>
@@ -1131,9 +1137,7 @@ int gemm2_grain_forward(const void* X, int64_t ldx, const void* W, int64_t ldw, 
   return launch<kGrainFwd>(X, ldx, W, ldw, H, N, Y, N, p, stream);
 }
 
-int gemm2_grain_partial_rows(int M) {
-  return 2 * gemm2::Traits<gemm2::kGrainBwd>::kWarps * ((M + gemm2::kBM - 1) / gemm2::kBM);
-}
+int gemm2_grain_partial_rows(int M) { return 2 * ((M + gemm2::kBM - 1) / gemm2::kBM); }
 
 // GRAIN backward fused behind the out-projection's input gradient:
 //   gy = bf16(dO W_out) (dO [M, K], W_out^T given K-major as wt [N, K]),
