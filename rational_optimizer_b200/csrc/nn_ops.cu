@@ -462,13 +462,14 @@ ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
     }
     if (lane == 0) bcast = wm + __logf(ws);
   }
+  // The target logit is read before the barrier: after it, every thread
+  // overwrites its elements of the row with the gradient.
+  const bool ignored = (tgt == ignore_index) || tgt < 0 || tgt >= V;
+  float xt = 0.f;
+  if (tid == 0 && !ignored && RO_CHECK(tgt >= 0 && tgt < V, 4)) xt = to_f<T>(use_smem ? srow[tgt] : lr[tgt]);
   __syncthreads();
   const float lse = bcast;
-  const bool ignored = (tgt == ignore_index) || tgt < 0 || tgt >= V;
-  if (tid == 0 && RO_CHECK(ignored || (tgt >= 0 && tgt < V), 4)) {
-    const float xt = ignored ? 0.f : to_f<T>(use_smem ? srow[tgt] : lr[tgt]);
-    loss_row[row] = ignored ? 0.f : (lse - xt);
-  }
+  if (tid == 0) loss_row[row] = ignored ? 0.f : (lse - xt);
   const float scale = ignored ? 0.f : grad_scale;
   if (vec_ok) {
     for (int i = tid * 8; i < V; i += kCeThreads * 8) {

@@ -37,7 +37,9 @@ from torch.autograd.graph import increment_version
 from .. import _ext
 from . import param_ready
 
-PULL_CTAS = 24
+# CTAs per owner copy (RO_PULL_CTAS): enough to keep NVLink busy without
+# taking many SMs from the forward that the copies overlap
+PULL_CTAS = int(os.environ.get("RO_PULL_CTAS", "24"))
 
 
 def available() -> bool:

@@ -36,7 +36,8 @@ import torch.distributed as dist
 
 from .. import _ext
 
-SEND_CTAS = 16
+# CTAs per send (RO_SEND_CTAS): sends run beside the backward's kernels
+SEND_CTAS = int(os.environ.get("RO_SEND_CTAS", "16"))
 REDUCE_CTAS = 296
 MODES = {"f32": 0, "bf16": 1, "int8": 2}
 QBLOCK = 256  # int8: elements per fp32 scale
@@ -74,7 +75,7 @@ def counter_index(layer, owners):
 
 class OwnerReduce:
     def __init__(self, flat: torch.Tensor, segments, owners, *, group=None, transport="f32",
-                 timeout_s=None):
+                 timeout_s=None, send_ctas=None):
         if transport not in MODES:
             raise ValueError(f"owner transport must be one of {sorted(MODES)}, got {transport!r}")
         C = _ext.ext()
@@ -87,6 +88,9 @@ class OwnerReduce:
         self.owners = [int(r) for r in owners]
         self.transport = transport
         self.mode = MODES[transport]
+        # CTAs per send launch; the owner expects (world - 1) * send_ctas arrivals per layer,
+        # so every rank must use the same value
+        self.send_ctas = int(send_ctas or SEND_CTAS)
         for off, n in self.segments:
             if off % 8 or n % 8:
                 raise ValueError("owner-reduce segments must start and end on 32-byte boundaries")
@@ -157,15 +161,15 @@ class OwnerReduce:
         C = _ext.ext()
         with torch.cuda.stream(self.stream):
             if not delivered:
-                C.owner_send(self.flat[off:off + n], dst, self.mode, counter, SEND_CTAS)
+                C.owner_send(self.flat[off:off + n], dst, self.mode, counter, self.send_ctas)
                 return
             cursor = 0
             for start, length in sorted(delivered) + [(n, 0)]:
                 if start > cursor:  # a gap the GEMMs did not store: send it without an arrival
-                    C.owner_send(self.flat[off + cursor:off + start], dst + 4 * cursor, self.mode, 0, SEND_CTAS)
+                    C.owner_send(self.flat[off + cursor:off + start], dst + 4 * cursor, self.mode, 0, self.send_ctas)
                 cursor = max(cursor, start + length)
             # one arrival worth a full send, after everything this stream ordered before it
-            C.owner_signal(counter, SEND_CTAS)
+            C.owner_signal(counter, self.send_ctas)
 
     def reduce(self):
         """Send what backward did not report, then reduce the owned layers (current stream)."""
@@ -177,7 +181,7 @@ class OwnerReduce:
         if self.owned:
             _ext.ext().owner_reduce(self.flat, self.recv.data_ptr(), self.counters, self.dev_offsets,
                                     self.dev_sizes, self.dev_recv_offsets, self.sumsq, self.rank,
-                                    self.world, (self.world - 1) * SEND_CTAS, 1.0 / self.world, self.mode,
+                                    self.world, (self.world - 1) * self.send_ctas, 1.0 / self.world, self.mode,
                                     self.err, self.timeout_ns)
         else:
             self.sumsq.zero_()

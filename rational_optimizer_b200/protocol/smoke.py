@@ -70,8 +70,14 @@ def owner_checks(rank, world, device):
     seg = ELEMS // world // 256 * 256
     out = {}
     flat = torch.empty(seg * world, device=device)
-    for transport in ("f32", "bf16", "int8"):
-        red = OwnerReduce(flat, [(r * seg, seg) for r in range(world)], list(range(world)), transport=transport)
+    from ..parallel.owner_reduce import SEND_CTAS
+    # the training configuration (few send CTAs, beside the backward's kernels)
+    # and a wide one (about one CTA per SM), which bounds what the kernels reach
+    for transport, ctas in (("f32", SEND_CTAS), ("bf16", SEND_CTAS), ("int8", SEND_CTAS), ("f32", 128),
+                            ("bf16", 128), ("int8", 128)):
+        red = OwnerReduce(flat, [(r * seg, seg) for r in range(world)], list(range(world)), transport=transport,
+                          send_ctas=ctas)
+        name = transport if ctas == SEND_CTAS else f"{transport}_ctas{ctas}"
 
         def once():
             flat.fill_(float(rank + 1))
@@ -90,14 +96,15 @@ def owner_checks(rank, world, device):
         else:
             ok = torch.equal(mine, want)
         if not ok:
-            raise RuntimeError(f"reduce-to-owner ({transport}): rank {rank} holds {mine[0].item()}, "
+            raise RuntimeError(f"reduce-to-owner ({name}): rank {rank} holds {mine[0].item()}, "
                                f"expected {(world + 1) / 2}")
         ms = _time(once, device)
         red.close()
         moved = (world - 1) * slot_bytes(seg, transport)  # bytes each rank receives (and sends)
-        out[f"owner_reduce_{transport}_ms"] = ms
-        out[f"owner_reduce_{transport}_ingress_gbs"] = moved / ms / 1e6
-        out[f"owner_reduce_{transport}_frac_nvlink"] = moved / ms / 1e6 / NVLINK_GBS
+        out[f"owner_reduce_{name}_ms"] = ms
+        out[f"owner_reduce_{name}_ingress_gbs"] = moved / ms / 1e6
+        out[f"owner_reduce_{name}_frac_nvlink"] = moved / ms / 1e6 / NVLINK_GBS
+    out["send_ctas_training"] = SEND_CTAS
     raw, weights = owner_gather.shared_buffer(seg * world, device)
     gather = owner_gather.OwnerGather(raw, weights, [(r * seg, (r + 1) * seg) for r in range(world)],
                                       [[] for _ in range(world)])

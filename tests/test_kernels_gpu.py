@@ -237,3 +237,20 @@ def test_weight_gradient_accumulates_in_one_fp32_gemm():
     gemm.matmul_tn_accumulate_(out, dy, x)
     assert gemm.ACCUMULATE_PATH == "addmm_fp32_out"  # beta = 1 into the fp32 buffer, no extra pass
     torch.testing.assert_close(out, want, rtol=1e-3, atol=1e-2)
+
+
+@pytest.mark.parametrize("V", [50304, 1000])
+def test_cross_entropy_row_losses_match_oracle_every_row(V):
+    """Every row's loss (not only the mean): the target logit must be read
+    before the gradient overwrites the row."""
+    C = _ext.ext()
+    torch.manual_seed(3)
+    rows = 4096
+    logits = (torch.randn(rows, V, device=DEV) * 3).to(torch.bfloat16)
+    target = torch.randint(0, V, (rows,), device=DEV)
+    target[::97] = -100
+    ref = F.cross_entropy(logits.float(), target, ignore_index=-100, reduction="none")
+    for _ in range(3):
+        work = logits.clone()
+        loss = C.cross_entropy_fwd_bwd(work, target, 1.0 / rows, -100)
+        torch.testing.assert_close(loss, ref, rtol=1e-4, atol=2e-4)
