@@ -37,6 +37,7 @@ namespace ro {
 namespace owner {
 
 constexpr int kThreads = 512;
+constexpr int kUnroll = 4;  // 8-element vectors per thread per pass in the copy loops
 constexpr int kF32 = 0, kBF16 = 1, kI8 = 2;  // transport formats
 constexpr int kQBlock = 256;                   // int8: elements per fp32 scale
 
@@ -87,30 +88,52 @@ send_kernel(const float* __restrict__ src, void* __restrict__ dst, int64_t n, un
     const int lane = threadIdx.x & 31;
     const int64_t blocks = (n + kQBlock - 1) / kQBlock;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-    for (int64_t b = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); b < blocks;
-         b += warps) {
-      const int64_t e0 = b * kQBlock + lane * 8;
-      const bool valid = e0 < n;  // n is a multiple of 8: a lane's 8 elements are all in or all out
-      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (valid) load_vec<float, 8>(src + e0, x);
-      float amax = 0.f;
+    // kUnroll blocks per warp per pass, loads first (bytes in flight)
+    for (int64_t b0 = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); b0 < blocks;
+         b0 += warps * kUnroll) {
+      float x[kUnroll][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
-      amax = warp_max(amax);
-      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-      float q[8];
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t e0 = (b0 + u * warps) * kQBlock + lane * 8;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = fminf(fmaxf(rintf(x[i] * inv), -127.f), 127.f);
-      if (valid) *reinterpret_cast<uint2*>(q8 + e0) = make_uint2(pack_i8x4(q), pack_i8x4(q + 4));
-      if (lane == 0) scales[b] = amax / 127.0f;
+        for (int i = 0; i < 8; ++i) x[u][i] = 0.f;
+        // n is a multiple of 8: a lane's 8 elements are all in or all out
+        if (b0 + u * warps < blocks && e0 < n) load_vec<float, 8>(src + e0, x[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t b = b0 + u * warps;
+        if (b >= blocks) break;  // uniform across the warp
+        const int64_t e0 = b * kQBlock + lane * 8;
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[u][i]));
+        amax = warp_max(amax);
+        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+        float q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = fminf(fmaxf(rintf(x[u][i] * inv), -127.f), 127.f);
+        if (e0 < n) *reinterpret_cast<uint2*>(q8 + e0) = make_uint2(pack_i8x4(q), pack_i8x4(q + 4));
+        if (lane == 0) scales[b] = amax / 127.0f;
+      }
     }
   } else {
+    // kUnroll vectors per thread per pass: their loads are all issued before
+    // the first peer store, so a few CTAs keep enough bytes in flight
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-      float x[8];
-      load_vec<float, 8>(src + v * 8, x);
-      if constexpr (MODE == kBF16) store_vec<__nv_bfloat16, 8>(static_cast<__nv_bfloat16*>(dst) + v * 8, x);
-      else store_vec<float, 8>(static_cast<float*>(dst) + v * 8, x);
+    for (int64_t v0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v0 < nvec;
+         v0 += stride * kUnroll) {
+      float x[kUnroll][8];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (v0 + u * stride < nvec) load_vec<float, 8>(src + (v0 + u * stride) * 8, x[u]);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t v = v0 + u * stride;
+        if (v >= nvec) break;
+        if constexpr (MODE == kBF16) store_vec<__nv_bfloat16, 8>(static_cast<__nv_bfloat16*>(dst) + v * 8, x[u]);
+        else store_vec<float, 8>(static_cast<float*>(dst) + v * 8, x[u]);
+      }
     }
     if (blockIdx.x == 0 && threadIdx.x < n - nvec * 8) {
       const int64_t i = nvec * 8 + threadIdx.x;
@@ -321,12 +344,22 @@ copy_kernel(const float* __restrict__ src, float* __restrict__ dst, __nv_bfloat1
             const int* err) {
   if (*reinterpret_cast<const volatile int*>(err) != 0) return;
   const int64_t nvec = n / 8;
+  // kUnroll peer loads in flight per thread before the first store (remote
+  // latency is several times local latency)
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-    float x[8];
-    load_vec<float, 8>(src + v * 8, x);
-    store_vec<float, 8>(dst + v * 8, x);
-    if (dst16 != nullptr) store_vec<__nv_bfloat16, 8>(dst16 + v * 8, x);
+  for (int64_t v0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v0 < nvec;
+       v0 += stride * kUnroll) {
+    float x[kUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      if (v0 + u * stride < nvec) load_vec<float, 8>(src + (v0 + u * stride) * 8, x[u]);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v >= nvec) break;
+      store_vec<float, 8>(dst + v * 8, x[u]);
+      if (dst16 != nullptr) store_vec<__nv_bfloat16, 8>(dst16 + v * 8, x[u]);
+    }
   }
   if (blockIdx.x == 0 && threadIdx.x < n - nvec * 8) {
     const int64_t i = nvec * 8 + threadIdx.x;
