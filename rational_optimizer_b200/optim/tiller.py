@@ -1062,6 +1062,21 @@ class TILLERRouter(torch.optim.Optimizer):
             lo, hi, sharded = dirs["owned"]
             if sharded:
                 global_packet = self._sharded_scores(packets, adjoint, dirs["selected"], lo, hi, wd)
+            elif not self.strict and packets[0][0].is_cuda:
+                # every layer at once (batched GEMMs); the per-layer loop below is the
+                # CPU oracle's path
+                inputs = torch.stack([pk[0] for pk in packets])
+                features = torch.stack([pk[2] for pk in packets])
+                cot = torch.stack([pk[3] for pk in packets])
+                s = tm.group_scores_stacked(inputs, features, cot, dirs["selected"]["incoming"],
+                                            dirs["selected"]["outgoing"], adjoint, groups=self.groups,
+                                            width=self.width)
+                w_in = torch.stack([p["in_weight"] for p in self.pairs])
+                w_out_t = torch.stack([p["out_weight"].T for p in self.pairs])
+                decay = (tm.group_scores_stacked(inputs, features, cot, w_in, w_out_t, adjoint,
+                                                 groups=self.groups, width=self.width).sum(-1) * wd).sum(0)
+                lattice = s.transpose(0, 1).reshape(self.probe_layout.local_probe_count, L * self.groups)
+                global_packet = self._gather_rows(torch.cat((lattice, decay[:, None]), dim=1))
             else:
                 inc_b = dirs["selected"]["incoming"]
                 out_b = dirs["selected"]["outgoing"]

@@ -229,6 +229,19 @@ def group_scores(inputs, features, cotangents, incoming_direction, outgoing_dire
     return score
 
 
+def group_scores_stacked(inputs, features, cotangents, incoming_direction, outgoing_direction_t, adjoint, *,
+                         groups, width):
+    """:func:`group_scores` for every layer at once: ``[L, P, G]`` from
+    ``inputs`` / ``cotangents`` ``[L, P, d]``, ``features`` ``[L, P, H]``,
+    directions ``[L, H, d]`` and ``adjoint`` ``[L, P, G, w]`` (a few batched
+    launches instead of a few per layer)."""
+    layers, probes = int(inputs.shape[0]), int(inputs.shape[1])
+    shape = (layers, probes, int(groups), int(width))
+    perturbation = torch.bmm(inputs.float(), incoming_direction.float().transpose(1, 2)).view(shape)
+    projection = torch.bmm(cotangents.float(), outgoing_direction_t.float().transpose(1, 2)).view(shape)
+    return (perturbation * adjoint.float()).sum(-1) + (features.float().view(shape) * projection).sum(-1)
+
+
 # ---------------------------------------------------------------------------
 # Direction: factorized adaptive-tangent chord.
 
