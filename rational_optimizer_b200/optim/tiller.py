@@ -477,8 +477,11 @@ class TILLERRouter(torch.optim.Optimizer):
         self._clip_factor = None
 
     def _consume_probes(self):
-        packets = []
         mb = self.microbatches
+        first = self._functional_records[0][0][0] if self._functional_records[0] else None
+        if not self.strict and first is not None and first.is_cuda:
+            return self._consume_probes_stacked()
+        packets = []
         for layer in range(len(self.pairs)):
             if self._pending_inputs[layer] is not None:
                 raise RuntimeError("TILLER probe input remained unmatched")
@@ -501,6 +504,37 @@ class TILLERRouter(torch.optim.Optimizer):
             packets.append((inputs.index_select(0, sel).float(), pre.index_select(0, sel).float(),
                             feat.index_select(0, sel).float(), scaled.index_select(0, sel).float()))
         return packets
+
+    def _consume_probes_stacked(self):
+        """The per-layer packets of :meth:`_consume_probes` built for all layers at
+        once (a few launches instead of a dozen per layer); same values."""
+        mb = self.microbatches
+        L = len(self.pairs)
+        records, cots = self._functional_records, self._cotangent_records
+        if any(p is not None for p in self._pending_inputs):
+            raise RuntimeError("TILLER probe input remained unmatched")
+        if any(len(r) != mb for r in records) or any(len(c) != mb for c in cots):
+            raise RuntimeError("TILLER microbatch inventory changed")
+        self._functional_records = [[] for _ in range(L)]
+        self._cotangent_records = [[] for _ in range(L)]
+        factors = {rows * mb for layer in cots for _, rows in layer}
+        if len(factors) != 1:
+            raise RuntimeError("TILLER cotangent row counts differ across layers")
+
+        def stacked(parts):
+            return torch.stack([part[0] if mb == 1 else torch.cat(part) for part in parts])
+
+        inputs = stacked([[r[0] for r in rec] for rec in records])
+        pre = stacked([[r[1] for r in rec] for rec in records])
+        feat = stacked([[r[2] for r in rec] for rec in records])
+        clip = self._clip_factor if torch.is_tensor(self._clip_factor) else float(self._clip_factor)
+        scaled = stacked([[v.float() for v, _ in c] for c in cots]) * float(factors.pop()) * clip
+        captured = self.capture_rows * mb
+        if inputs.shape[1:] != (captured, self.external) or pre.shape[1:] != (captured, self.hidden):
+            raise RuntimeError("TILLER captured packet changed")
+        sel = tm.evenly_spaced_indices(captured, self.probe_layout.local_probe_count, device=inputs.device)
+        inputs, pre, feat, scaled = (t.index_select(1, sel).float() for t in (inputs, pre, feat, scaled))
+        return [(inputs[l], pre[l], feat[l], scaled[l]) for l in range(L)]
 
     # -- trainer contract --------------------------------------------------
     def record_realized_clipping(self, preclip_norm, max_norm):
