@@ -39,6 +39,51 @@ SEQ = 1024
 ZIPF_TOKENS = 8_000_000
 
 
+# where the reference's unmodified source tree is read from when baseline/_ref
+# has to be installed on this machine (RO_REFERENCE_SRC overrides it)
+REF_SRC = os.environ.get("RO_REFERENCE_SRC", "/root/reference")
+
+
+def ensure_reference() -> str | None:
+    """Install the unmodified reference into baseline/_ref when it is missing.
+
+    The install is the same one recorded for this arm: ``pip install --no-index
+    --no-build-isolation --find-links /opt/wheelhouse --target baseline/_ref``
+    of a copy of the reference tree (its build writes into the source tree),
+    with its CUDA extension compiled for sm_100; the reference's unpackaged
+    study directories are copied beside it unmodified.  Ranks of one node
+    serialise on a lock file, so one of them installs and the rest reuse it.
+    Returns None when the package is present afterwards, else the reason.
+    """
+    import fcntl
+    import shutil
+    import tempfile
+    if os.path.isdir(os.path.join(REF_DIR, "training")):
+        return None
+    if not os.path.isdir(REF_SRC):
+        return "reference package not installed in baseline/_ref and no reference source to build it from"
+    os.makedirs(os.path.dirname(REF_DIR), exist_ok=True)
+    with open(os.path.join(os.path.dirname(REF_DIR), ".install.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if os.path.isdir(os.path.join(REF_DIR, "training")):
+            return None
+        with tempfile.TemporaryDirectory() as tmp:
+            src = os.path.join(tmp, "reference")
+            shutil.copytree(REF_SRC, src, ignore=shutil.ignore_patterns(".git"))
+            env = dict(os.environ, TORCH_CUDA_ARCH_LIST="10.0")
+            done = subprocess.run([sys.executable, "-m", "pip", "install", "--no-index",
+                                   "--no-build-isolation", "--no-deps", "--find-links", "/opt/wheelhouse",
+                                   "--target", REF_DIR, src], env=env, capture_output=True, text=True)
+            if done.returncode != 0:
+                tail = (done.stderr or done.stdout).strip().splitlines()[-1:] or [""]
+                return f"reference install failed: {tail[0][:200]}"
+        for sub in ("mha_1b_tokens", "swiglu_tiller", "results"):
+            there = os.path.join(REF_SRC, "experiments", sub)
+            if os.path.isdir(there):
+                shutil.copytree(there, os.path.join(REF_DIR, "experiments", sub), dirs_exist_ok=True)
+    return None if os.path.isdir(os.path.join(REF_DIR, "training")) else "reference install left no package"
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -134,7 +179,8 @@ def timed(step_fn, steps, device, dist_on, flush=None, kind=None):
     An event is also recorded after every step (no synchronisation), so the
     per-step device times can be split by ``kind()`` (called before each
     step, e.g. ``"plain"`` / ``"refresh"``); returns (ms, {kind: [median ms,
-    count]}) with each median also reduced with MAX over ranks.
+    count, max ms]}) with each median and maximum also reduced with MAX over
+    ranks (the maximum shows a slow outlier step that the median hides).
     """
     import torch
     import torch.distributed as dist
@@ -161,20 +207,27 @@ def timed(step_fn, steps, device, dist_on, flush=None, kind=None):
         per.setdefault(k, []).append(marks[i].elapsed_time(marks[i + 1]))
     names = sorted(per)
     med = [sorted(per[k])[len(per[k]) // 2] for k in names]
-    global LAST_RANK_MS
+    top = [max(per[k]) for k in names]
+    global LAST_RANK_MS, LAST_STEP_MS
+    steps_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(steps)]
     LAST_RANK_MS = [round(ms, 3)]
     if dist_on:
         every = torch.zeros(dist.get_world_size(), device=device)
         dist.all_gather_into_tensor(every, torch.tensor([ms], device=device))
         LAST_RANK_MS = [round(v, 3) for v in every.tolist()]
-        t = torch.tensor([ms] + med, device=device)
+        t = torch.tensor([ms] + med + top + steps_ms, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, med = float(t[0].item()), t[1:].tolist()
-    return ms, {k: [round(m, 3), len(per[k])] for k, m in zip(names, med)}
+        n = len(names)
+        vals = t.tolist()
+        ms, med, top, steps_ms = vals[0], vals[1:1 + n], vals[1 + n:1 + 2 * n], vals[1 + 2 * n:]
+    LAST_STEP_MS = [round(v, 2) for v in steps_ms]
+    return ms, {k: [round(m, 3), len(per[k]), round(x, 3)] for k, m, x in zip(names, med, top)}
 
 
-# device ms per step of every rank in the last timed() window (which rank sets the MAX)
+# device ms per step of every rank in the last timed() window (which rank sets the MAX),
+# and each step's device ms in that window (MAX over ranks), in order
 LAST_RANK_MS = []
+LAST_STEP_MS = []
 
 
 def run_ours(a, info):
@@ -234,7 +287,7 @@ def run_ours(a, info):
     start_step = counter["i"]
     ms, split = timed(device_step, a.steps, device, info.is_distributed, flush=param_ready.wait_all,
                       kind=kind)
-    split = dict(split, ms_per_rank=list(LAST_RANK_MS))
+    split = dict(split, ms_per_rank=list(LAST_RANK_MS), steps_ms=list(LAST_STEP_MS))
     clocks = sampler.stop() if sampler else None
     e2e_ms = e2e_split = None
     if not a.no_e2e:
@@ -332,6 +385,7 @@ def run_reference(a, info):
 def main():
     a = parse()
     sys.path.insert(0, ROOT)
+    missing = ensure_reference() if a.impl == "reference" else None
     import torch
     from rational_optimizer_b200.parallel.dist import cleanup_distributed, setup_distributed
     info = setup_distributed()
@@ -351,7 +405,7 @@ def main():
             res = None
             reason = f"reference run failed: {type(exc).__name__}: {str(exc)[:200]}"
         else:
-            reason = "reference package not installed in baseline/_ref"
+            reason = missing or "reference package not installed in baseline/_ref"
         if res is None:
             if info.rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
@@ -383,7 +437,7 @@ def main():
         "config": cfg, "clocks": clocks, "final_loss": loss,
     }
     out["config"]["grad_transport"] = transport
-    # per-step device time by step kind: {kind: [median ms, steps]}; "refresh"
+    # per-step device time by step kind: {kind: [median ms, steps, max ms]}; "refresh"
     # steps run the optimizer's response-probe refresh (one in eight)
     out["step_ms_by_kind"] = split
     if e2e_ms is not None:
