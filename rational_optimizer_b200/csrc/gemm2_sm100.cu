@@ -386,6 +386,38 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// The same store without waiting for it: a later tcgen05.wait::st (before
+// any read of those columns) completes every store issued so far.
+__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Split load: issue without waiting, then wait with the destination
+// registers as operands, so no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16_wait(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 // UMMA shared-memory descriptor, 128B swizzle, K-major (8-row core groups
 // 1024 B apart).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -456,25 +488,6 @@ __device__ __forceinline__ void load_grain_coeffs(GrainCoeffs& c, int g, const f
   for (int j = 0; j < 4; ++j) c.b[j] = splat2(fabsf(den[g * 4 + j]));
 }
 
-// Derivative coefficients, formed once per tile: P'(t) = a1 + t (2 a2 + t (3 a3
-// + t (4 a4 + 5 a5 t))) and dQ/dt = sign0(t)|b0| + t (2|b1| + |t| (3|b2| + 4|b3||t|)).
-struct GrainDerivCoeffs {
-  float2 da5, da4, da3, da2;
-  float2 db3, db2, db1;
-};
-
-__device__ __forceinline__ GrainDerivCoeffs grain_deriv_coeffs(const GrainCoeffs& c) {
-  GrainDerivCoeffs d;
-  d.da5 = mul2(splat2(5.0f), c.a[5]);
-  d.da4 = mul2(splat2(4.0f), c.a[4]);
-  d.da3 = mul2(splat2(3.0f), c.a[3]);
-  d.da2 = mul2(splat2(2.0f), c.a[2]);
-  d.db3 = mul2(splat2(4.0f), c.b[3]);
-  d.db2 = mul2(splat2(3.0f), c.b[2]);
-  d.db1 = mul2(splat2(2.0f), c.b[1]);
-  return d;
-}
-
 // GRAIN backward behind the out-projection's input-gradient GEMM.  The
 // accumulator holds gy = dL/dy for one 128-row x 256-column tile (one group).
 // Sixteen epilogue warps: four per TMEM lane quarter (32 rows), each owning
@@ -536,22 +549,21 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
     }
   }
   const float rho = sqrtf(quarter_sum(ss) * (1.0f / 256.0f) + p.eps);
-  const float2 ir = splat2(__fdividef(1.0f, rho)), rh = splat2(rho);
+  const float2 ir = splat2(__fdividef(1.0f, rho));
   GrainCoeffs c;
   load_grain_coeffs(c, tn, p.num, p.den);
-  const GrainDerivCoeffs dc = grain_deriv_coeffs(c);
   const float2 one = splat2(1.0f);
   float2 acc[10];
 #pragma unroll
   for (int k = 0; k < 10; ++k) acc[k] = splat2(0.0f);
   float2 sacc = splat2(0.0f);
-  // pass 2
-#pragma unroll 1
-  for (int ch = 0; ch < kChunks; ++ch) {
+  // pass 2: chunk ch+1's TMEM load is in flight while chunk ch is processed
+  // (two register sets; the loop body covers two chunks so neither set is
+  // indexed dynamically)
+  static_assert(kChunks % 2 == 0, "pass 2 walks the chunks in pairs");
+  auto pass2_chunk = [&](int ch, uint32_t (&r)[16]) {
     uint32_t zc[8];
     load_z(ch, zc);
-    uint32_t r[16];
-    tmem_ld16(tbase + ch * 16, r);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       // gy rounded to bf16 as the unfused GEMM output is (one paired conversion)
@@ -561,27 +573,33 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
       const float2 t = mul2(z, ir);
       const float2 at = abs2(t);
       const float2 t2 = mul2(t, t);
+      // P(t) by Horner's rule with P'(t) carried along (synthetic division:
+      // each derivative step folds in the running value of P)
       float2 pp = fma2(c.a[5], t, c.a[4]);
+      float2 dp = fma2(c.a[5], t, pp);
       pp = fma2(pp, t, c.a[3]);
+      dp = fma2(dp, t, pp);
       pp = fma2(pp, t, c.a[2]);
+      dp = fma2(dp, t, pp);
       pp = fma2(pp, t, c.a[1]);
+      dp = fma2(dp, t, pp);
       pp = fma2(pp, t, c.a[0]);
-      float2 dp = fma2(dc.da5, t, dc.da4);
-      dp = fma2(dp, t, dc.da3);
-      dp = fma2(dp, t, dc.da2);
-      dp = fma2(dp, t, c.a[1]);
+      // Q(x) = 1 + |b0| x + |b1| x^2 + |b2| x^3 + |b3| x^4 at x = |t|, with
+      // dQ/dx the same way; dQ/dt = sign0(t) dQ/dx
       float2 q = fma2(c.b[3], at, c.b[2]);
+      float2 hq = fma2(c.b[3], at, q);
       q = fma2(q, at, c.b[1]);
+      hq = fma2(hq, at, q);
       q = fma2(q, at, c.b[0]);
+      const float2 dq = mul2(fma2(hq, at, q), sign02(t));
       q = fma2(q, at, one);
-      float2 hq = fma2(dc.db3, at, dc.db2);
-      hq = fma2(hq, at, dc.db1);
-      const float2 dq = fma2(t, hq, mul2(c.b[0], sign02(t)));
       const float2 iq = rcp2(q);
       const float2 f = mul2(pp, iq);
       const float2 df = mul2(fma2(neg2(f), dq, dp), iq);
       sacc = fma2(g2, fma2(neg2(t), df, f), sacc);
-      const float2 s1 = mul2(mul2(g2, rh), iq);
+      // the row's rho multiplies every coefficient partial of the row: it is
+      // applied once to the row's sums below instead of per element
+      const float2 s1 = mul2(g2, iq);
       const float2 t3 = mul2(t2, t), t4 = mul2(t2, t2);
       acc[0] = add2(acc[0], s1);
       acc[1] = fma2(s1, t, acc[1]);
@@ -598,16 +616,32 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
       r[2 * j] = __float_as_uint(gd.x);
       r[2 * j + 1] = __float_as_uint(gd.y);
     }
-    tmem_st16(tbase + ch * 16, r);
-  }
-  const float2 sw = splat2(quarter_sum(sacc.x + sacc.y) * (1.0f / 256.0f));
-  // pass 3: gx over z in the staging tile (each lane rewrites its own row) -> one bulk store
+    tmem_st16_async(tbase + ch * 16, r);
+  };
+  uint32_t ra[16], rb[16];
+  tmem_ld16_issue(tbase, ra);
 #pragma unroll 1
+  for (int ch = 0; ch < kChunks; ch += 2) {
+    tmem_ld16_wait(ra);
+    tmem_ld16_issue(tbase + (ch + 1) * 16, rb);
+    pass2_chunk(ch, ra);
+    tmem_ld16_wait(rb);
+    if (ch + 2 < kChunks) tmem_ld16_issue(tbase + (ch + 2) * 16, ra);
+    pass2_chunk(ch + 1, rb);
+  }
+  tmem_wait_st();  // pass 3 reads these columns back
+  const float2 sw = splat2(quarter_sum(sacc.x + sacc.y) * (1.0f / 256.0f));
+  // pass 3: gx over z in the staging tile (each lane rewrites its own row) ->
+  // one bulk store; chunk ch+1's TMEM load is in flight while chunk ch is formed
+  uint32_t rr[2][16];
+  tmem_ld16_issue(tbase, rr[0]);
+#pragma unroll
   for (int ch = 0; ch < kChunks; ++ch) {
+    uint32_t (&r)[16] = rr[ch & 1];
+    tmem_ld16_wait(r);
+    if (ch + 1 < kChunks) tmem_ld16_issue(tbase + (ch + 1) * 16, rr[(ch + 1) & 1]);
     uint32_t zc[8];
     load_z(ch, zc);
-    uint32_t r[16];
-    tmem_ld16(tbase + ch * 16, r);
     float out[16];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -628,7 +662,7 @@ __device__ __forceinline__ void grain_bwd_epilogue(const Params& p, uint32_t tba
   // coefficient partials of the CTA's rows (fixed-order reduction)
 #pragma unroll
   for (int k = 0; k < 10; ++k) {
-    float v = acc[k].x + acc[k].y;
+    float v = (acc[k].x + acc[k].y) * rho;
     if (k >= 6) {
       const float b = p.den[tn * 4 + (k - 6)];
       v *= b > 0.f ? -1.f : (b < 0.f ? 1.f : 0.f);
