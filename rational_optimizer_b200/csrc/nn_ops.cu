@@ -7,6 +7,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "packed.cuh"
 
 namespace ro {
 namespace nn {
@@ -243,8 +244,20 @@ add_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __rest
   if (r1 > rows) r1 = rows;
   for (int64_t row = r0 + warp; row < r1; row += kNormWarps) {
     const float r = rstd[row];
-    float xv[NCH][8], gv[NCH][8];
+    float xv[NCH][8], gv[NCH][8], ov[NCH][8];
     float dot = 0.f;
+    // the residual gradient is loaded with x and dy, so a row costs one
+    // round trip to memory instead of two
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t off = row * d + c * 256 + lane * 8;
+      if (dres != nullptr) {
+        load_vec<float, 8>(dres + off, ov[c]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ov[c][j] = 0.f;
+      }
+    }
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int64_t off = row * d + c * 256 + lane * 8;
@@ -266,13 +279,7 @@ add_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __rest
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int64_t off = row * d + c * 256 + lane * 8;
-      float o[8];
-      if (dres != nullptr) {
-        load_vec<float, 8>(dres + off, o);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = 0.f;
-      }
+      float (&o)[8] = ov[c];
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] += r * (gv[c][j] - xv[c][j] * dot);
       store_vec<float, 8>(dx + off, o);
@@ -347,6 +354,10 @@ __global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __re
   store_vec<T, 8>(out + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
 }
 
+// Tokens per CTA of the RoPE backward: each thread loads its 16-byte vector
+// of every token first, so kRopeTokens loads are in flight per thread.
+constexpr int kRopeTokens = 4;
+
 template <typename T>
 __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ dk,
                                     const T* __restrict__ dv, const float* __restrict__ cos_t,
@@ -355,25 +366,35 @@ __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restric
   const int vec = hd / 8;
   const int t = blockIdx.y * blockDim.x + threadIdx.x;
   if (t >= 3 * H * vec) return;
-  const int token = blockIdx.x;
-  const int b = token / S, s = token - b * S;
   const int which = t / (H * vec);
   const int rem = t - which * H * vec;
   const int h = rem / vec, jv = rem - h * vec;
   const int d = H * hd;
   const int64_t tokens = static_cast<int64_t>(B) * S;
-  if (!(span_ok(static_cast<int64_t>(token) * 3 + which, h * hd + jv * 8, h * hd + jv * 8 + 8, tokens * 3, d, 3) &&
-        span_ok(static_cast<int64_t>(token) * H + h, jv * 8, jv * 8 + 8, tokens * H, hd, 3) &&
-        span_ok(s, jv * 4, jv * 4 + 4, S, hd / 2, 3)))
-    return;
   const T* in = which == 0 ? dq : (which == 1 ? dk : dv);
-  float val[8];
-  load_vec<T, 8>(in + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
-  if (which < 2) {
-    const int half = hd / 2;
-    rope_rotate(val, cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, true);
+  float val[kRopeTokens][8];
+  bool live[kRopeTokens];
+#pragma unroll
+  for (int u = 0; u < kRopeTokens; ++u) {
+    const int64_t token = static_cast<int64_t>(blockIdx.x) * kRopeTokens + u;
+    const int s = static_cast<int>(token % S);
+    live[u] = token < tokens &&
+              span_ok(token * 3 + which, h * hd + jv * 8, h * hd + jv * 8 + 8, tokens * 3, d, 3) &&
+              span_ok(token * H + h, jv * 8, jv * 8 + 8, tokens * H, hd, 3) &&
+              span_ok(s, jv * 4, jv * 4 + 4, S, hd / 2, 3);
+    if (live[u]) load_vec<T, 8>(in + (token * H + h) * hd + jv * 8, val[u]);
   }
-  store_vec<T, 8>(dqkv + (static_cast<int64_t>(token) * 3 + which) * d + h * hd + jv * 8, val);
+#pragma unroll
+  for (int u = 0; u < kRopeTokens; ++u) {
+    if (!live[u]) continue;
+    const int64_t token = static_cast<int64_t>(blockIdx.x) * kRopeTokens + u;
+    if (which < 2) {
+      const int half = hd / 2;
+      const int s = static_cast<int>(token % S);
+      rope_rotate(val[u], cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, true);
+    }
+    store_vec<T, 8>(dqkv + (token * 3 + which) * d + h * hd + jv * 8, val[u]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -405,6 +426,11 @@ ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tgt = target[row];
   const bool vec_ok = (V % 8 == 0) && (reinterpret_cast<uintptr_t>(lr) % 16 == 0);
+  // The vector path works in base-2 units of the logits (u = v log2 e):
+  // m is the running max of v, s the sum of 2^(u - m log2 e), so each element
+  // costs one packed FMA and one ex2 per pass.
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float2 l2e = splat2(kLog2e);
   float m = -INFINITY, s = 0.f;
   auto absorb = [&](const float (&v)[8], int count) {
     float mx = v[0];
@@ -420,13 +446,27 @@ ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
       if (j < count) s += __expf(v[j] - m);
   };
   if (vec_ok) {
+    float2 s2 = splat2(0.f);
     for (int i = tid * 8; i < V; i += kCeThreads * 8) {
       const uint4 raw = *reinterpret_cast<const uint4*>(lr + i);
       if (use_smem) *reinterpret_cast<uint4*>(srow + i) = raw;
       float v8[8];
       load_vec<T, 8>(reinterpret_cast<const T*>(&raw), v8);
-      absorb(v8, 8);
+      const float mx = fmaxf(fmaxf(fmaxf(v8[0], v8[1]), fmaxf(v8[2], v8[3])),
+                             fmaxf(fmaxf(v8[4], v8[5]), fmaxf(v8[6], v8[7])));
+      if (mx > m) {
+        const float r = exp2f((m - mx) * kLog2e);  // 0 while m = -inf
+        s2 = mul2(s2, splat2(r));
+        m = mx;
+      }
+      const float2 nm = splat2(-m * kLog2e);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float2 u = fma2(make_float2(v8[j], v8[j + 1]), l2e, nm);
+        s2 = add2(s2, make_float2(ex2_approx(u.x), ex2_approx(u.y)));
+      }
     }
+    s = s2.x + s2.y;
   } else {
     for (int i = tid; i < V; i += kCeThreads) {
       const T raw = lr[i];
@@ -472,14 +512,27 @@ ce_fwd_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ target,
   if (tid == 0) loss_row[row] = ignored ? 0.f : (lse - xt);
   const float scale = ignored ? 0.f : grad_scale;
   if (vec_ok) {
+    const float2 nl = splat2(-lse * kLog2e), sc = splat2(scale);
     for (int i = tid * 8; i < V; i += kCeThreads * 8) {
       float v8[8];
       load_vec<T, 8>(use_smem ? srow + i : lr + i, v8);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float p = __expf(v8[j] - lse);
-        if (i + j == tgt) p -= 1.0f;
-        v8[j] = p * scale;
+      for (int j = 0; j < 8; j += 2) {
+        const float2 u = fma2(make_float2(v8[j], v8[j + 1]), l2e, nl);
+        v8[j] = ex2_approx(u.x);
+        v8[j + 1] = ex2_approx(u.y);
+      }
+      // the target's probability loses 1 (one vector of the row holds it)
+      if (static_cast<uint64_t>(tgt - i) < 8u) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i + j == tgt) v8[j] -= 1.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float2 g = mul2(make_float2(v8[j], v8[j + 1]), sc);
+        v8[j] = g.x;
+        v8[j + 1] = g.y;
       }
       store_vec<T, 8>(lr + i, v8);
     }
@@ -654,7 +707,8 @@ int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const floa
   if (static_cast<int64_t>(B) * S * H == 0) return 0;
   const int per_token = 3 * H * (hd / 8);
   const int threads = per_token < 512 ? ((per_token + 31) / 32) * 32 : 512;
-  const dim3 blocks(static_cast<unsigned>(B * S), static_cast<unsigned>((per_token + threads - 1) / threads));
+  const int64_t token_blocks = (static_cast<int64_t>(B) * S + nn::kRopeTokens - 1) / nn::kRopeTokens;
+  const dim3 blocks(static_cast<unsigned>(token_blocks), static_cast<unsigned>((per_token + threads - 1) / threads));
   if (dtype == 0)
     nn::rope_qkv_bwd_kernel<float><<<blocks, threads, 0, stream>>>(
         static_cast<const float*>(dq), static_cast<const float*>(dk), static_cast<const float*>(dv),

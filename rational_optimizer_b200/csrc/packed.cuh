@@ -21,6 +21,14 @@ __device__ __forceinline__ float2 rcp2(float2 a) {
   return make_float2(__fdividef(1.0f, a.x), __fdividef(1.0f, a.y));
 }
 
+// 2^x by the hardware approximation (ex2.approx.ftz.f32: about 2 ulp,
+// subnormal results flushed to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // P = E / 2 consecutive pairs from E contiguous elements (16-byte aligned for
 // the vector paths: E * sizeof(T) in {8, 16, 32}).
 template <typename T, int E>

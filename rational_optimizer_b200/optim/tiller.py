@@ -181,7 +181,7 @@ class OwnerPacking:
         from ..parallel import owner_gather
         self.gather = None
         use_gather = (device.type == "cuda" and self.world > 1 and owner_gather.available()
-                      and os.environ.get("RO_WEIGHT_TRANSPORT", "p2p") == "p2p")
+                      and os.environ.get("RO_WEIGHT_TRANSPORT", "nccl") == "p2p")
         if use_gather:
             raw, self.flat = owner_gather.shared_buffer(total, device)
         else:

@@ -19,9 +19,9 @@ training/train.py:2366-2371).  Two ways to average it across ranks:
   buckets.
 
 * reduce-to-owner (``transport="owner"`` / ``"owner-bf16"`` /
-  ``"owner-int8"`` (per-256 fp32 block scales; lossy, opt-in), the default
-  with several ranks when ``owner_layers`` names the matrices of layer-sharded
-  optimizers): those matrices are laid out first in the buffer, one
+  ``"owner-int8"`` (per-256 fp32 block scales; lossy); opt-in through
+  ``RO_GRAD_TRANSPORT``, and it needs ``owner_layers`` naming the matrices of
+  layer-sharded optimizers): those matrices are laid out first in the buffer, one
   contiguous segment per layer, and each segment goes only to the rank that
   owns the layer (:class:`~.owner_reduce.OwnerReduce`, own NVLink kernels,
   sent during backward); the remaining parameters (embeddings, norms, GRAIN
@@ -59,11 +59,13 @@ class GradientSynchronizer:
         device = params[0].device
         total = sum(p.numel() for p in params)
         if transport is None:
-            default = "nccl"
-            if (owner_layers is not None and self.world > 1 and device.type == "cuda" and _ext.available()
-                    and hasattr(_ext.ext(), "owner_send")):
-                default = "owner"
-            transport = os.environ.get("RO_GRAD_TRANSPORT", default)
+            # per-layer NCCL buckets overlapped with backward by default: on
+            # 2 and 8 B200s they measured faster than the reduce-to-owner
+            # transport with owner weight pulls (RO_GRAD_TRANSPORT=owner*)
+            transport = os.environ.get("RO_GRAD_TRANSPORT", "nccl")
+            if transport.startswith("owner") and not (
+                    _ext.available() and hasattr(_ext.ext(), "owner_send")):
+                transport = "nccl"
         self.owner = None
         owned_matrices = []
         if transport.startswith("owner"):
