@@ -354,10 +354,6 @@ __global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __re
   store_vec<T, 8>(out + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
 }
 
-// Tokens per CTA of the RoPE backward: each thread loads its 16-byte vector
-// of every token first, so kRopeTokens loads are in flight per thread.
-constexpr int kRopeTokens = 4;
-
 template <typename T>
 __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ dk,
                                     const T* __restrict__ dv, const float* __restrict__ cos_t,
@@ -366,35 +362,25 @@ __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restric
   const int vec = hd / 8;
   const int t = blockIdx.y * blockDim.x + threadIdx.x;
   if (t >= 3 * H * vec) return;
+  const int token = blockIdx.x;
+  const int b = token / S, s = token - b * S;
   const int which = t / (H * vec);
   const int rem = t - which * H * vec;
   const int h = rem / vec, jv = rem - h * vec;
   const int d = H * hd;
   const int64_t tokens = static_cast<int64_t>(B) * S;
+  if (!(span_ok(static_cast<int64_t>(token) * 3 + which, h * hd + jv * 8, h * hd + jv * 8 + 8, tokens * 3, d, 3) &&
+        span_ok(static_cast<int64_t>(token) * H + h, jv * 8, jv * 8 + 8, tokens * H, hd, 3) &&
+        span_ok(s, jv * 4, jv * 4 + 4, S, hd / 2, 3)))
+    return;
   const T* in = which == 0 ? dq : (which == 1 ? dk : dv);
-  float val[kRopeTokens][8];
-  bool live[kRopeTokens];
-#pragma unroll
-  for (int u = 0; u < kRopeTokens; ++u) {
-    const int64_t token = static_cast<int64_t>(blockIdx.x) * kRopeTokens + u;
-    const int s = static_cast<int>(token % S);
-    live[u] = token < tokens &&
-              span_ok(token * 3 + which, h * hd + jv * 8, h * hd + jv * 8 + 8, tokens * 3, d, 3) &&
-              span_ok(token * H + h, jv * 8, jv * 8 + 8, tokens * H, hd, 3) &&
-              span_ok(s, jv * 4, jv * 4 + 4, S, hd / 2, 3);
-    if (live[u]) load_vec<T, 8>(in + (token * H + h) * hd + jv * 8, val[u]);
+  float val[8];
+  load_vec<T, 8>(in + (static_cast<int64_t>(token) * H + h) * hd + jv * 8, val);
+  if (which < 2) {
+    const int half = hd / 2;
+    rope_rotate(val, cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, true);
   }
-#pragma unroll
-  for (int u = 0; u < kRopeTokens; ++u) {
-    if (!live[u]) continue;
-    const int64_t token = static_cast<int64_t>(blockIdx.x) * kRopeTokens + u;
-    if (which < 2) {
-      const int half = hd / 2;
-      const int s = static_cast<int>(token % S);
-      rope_rotate(val[u], cos_t + s * half + jv * 4, sin_t + s * half + jv * 4, true);
-    }
-    store_vec<T, 8>(dqkv + (token * 3 + which) * d + h * hd + jv * 8, val[u]);
-  }
+  store_vec<T, 8>(dqkv + (static_cast<int64_t>(token) * 3 + which) * d + h * hd + jv * 8, val);
 }
 
 // ---------------------------------------------------------------------------
@@ -707,8 +693,7 @@ int rope_qkv_backward(const void* dq, const void* dk, const void* dv, const floa
   if (static_cast<int64_t>(B) * S * H == 0) return 0;
   const int per_token = 3 * H * (hd / 8);
   const int threads = per_token < 512 ? ((per_token + 31) / 32) * 32 : 512;
-  const int64_t token_blocks = (static_cast<int64_t>(B) * S + nn::kRopeTokens - 1) / nn::kRopeTokens;
-  const dim3 blocks(static_cast<unsigned>(token_blocks), static_cast<unsigned>((per_token + threads - 1) / threads));
+  const dim3 blocks(static_cast<unsigned>(B * S), static_cast<unsigned>((per_token + threads - 1) / threads));
   if (dtype == 0)
     nn::rope_qkv_bwd_kernel<float><<<blocks, threads, 0, stream>>>(
         static_cast<const float*>(dq), static_cast<const float*>(dk), static_cast<const float*>(dv),
