@@ -77,10 +77,13 @@ def ensure_reference() -> str | None:
             if done.returncode != 0:
                 tail = (done.stderr or done.stdout).strip().splitlines()[-1:] or [""]
                 return f"reference install failed: {tail[0][:200]}"
-        for sub in ("mha_1b_tokens", "swiglu_tiller", "results"):
+        # the protocol's data files (manifest, matrix, source freeze) sit beside
+        # its installed modules; the studies and results are not packaged
+        for sub in ("protocol", "mha_1b_tokens", "swiglu_tiller", "results"):
             there = os.path.join(REF_SRC, "experiments", sub)
             if os.path.isdir(there):
-                shutil.copytree(there, os.path.join(REF_DIR, "experiments", sub), dirs_exist_ok=True)
+                shutil.copytree(there, os.path.join(REF_DIR, "experiments", sub), dirs_exist_ok=True,
+                                ignore=shutil.ignore_patterns("__pycache__"))
     return None if os.path.isdir(os.path.join(REF_DIR, "training")) else "reference install left no package"
 
 

@@ -652,6 +652,16 @@ void owner_signal(int64_t counter, int64_t count) {
            "owner_signal");
 }
 
+// fp32 payload copied into the owner's slot by a copy engine (no arrival).
+void owner_copy(torch::Tensor src, int64_t dst) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat32 && src.is_contiguous(),
+              "owner_copy expects a contiguous fp32 CUDA tensor");
+  const c10::cuda::CUDAGuard guard(src.device());
+  check_rc(ro::owner_copy(src.data_ptr<float>(), reinterpret_cast<void*>(dst), src.numel(),
+                          at::cuda::getCurrentCUDAStream()),
+           "owner_copy");
+}
+
 void owner_send(torch::Tensor src, int64_t dst, int64_t mode, int64_t counter, int64_t ctas) {
   TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat32 && src.is_contiguous(),
               "owner_send expects a contiguous fp32 CUDA tensor");
@@ -1097,6 +1107,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("owner_slot_bytes", &owner_slot_bytes);
   m.def("owner_send", &owner_send);
   m.def("owner_signal", &owner_signal);
+  m.def("owner_copy", &owner_copy);
   m.def("owner_reduce", &owner_reduce);
   m.def("owner_publish", &owner_publish);
   m.def("owner_pull", &owner_pull);

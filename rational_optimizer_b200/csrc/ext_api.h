@@ -73,6 +73,7 @@ int gemm2_grain_partial_rows(int M);
 // fp32 scale per 256 elements.  recv_offsets are byte offsets.
 int64_t owner_slot_bytes(int64_t n, int mode);
 int owner_signal(unsigned int* counter, unsigned int count, cudaStream_t stream);
+int owner_copy(const float* src, void* dst, int64_t n, cudaStream_t stream);
 int owner_send(const float* src, void* dst, int64_t n, int mode, unsigned int* counter, int ctas,
                cudaStream_t stream);
 int owner_reduce(float* grad, const void* recv, unsigned int* counters, const int64_t* offsets,

@@ -269,6 +269,17 @@ int owner_signal(unsigned int* counter, unsigned int count, cudaStream_t stream)
   return static_cast<int>(cudaGetLastError());
 }
 
+// fp32 send by a copy engine: one device-to-device copy into the owner's
+// slot (peer memory through the IPC mapping), so no SM works on the send.
+// The arrival is a separate owner_signal after it on the same stream: stream
+// order makes the copy complete before that kernel fences and increments.
+int owner_copy(const float* src, void* dst, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return -1;
+  if (!aligned16(src) || !aligned16(dst)) return -2;
+  return static_cast<int>(cudaMemcpyAsync(dst, src, static_cast<size_t>(n) * sizeof(float),
+                                          cudaMemcpyDeviceToDevice, stream));
+}
+
 int owner_send(const float* src, void* dst, int64_t n, int mode, unsigned int* counter, int ctas,
                cudaStream_t stream) {
   using namespace owner;

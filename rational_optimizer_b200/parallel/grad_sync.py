@@ -19,7 +19,8 @@ training/train.py:2366-2371).  Two ways to average it across ranks:
   buckets.
 
 * reduce-to-owner (``transport="owner"`` / ``"owner-bf16"`` /
-  ``"owner-int8"`` (per-256 fp32 block scales; lossy); opt-in through
+  ``"owner-int8"`` (per-256 fp32 block scales; lossy) / ``"owner-ce"``
+  (fp32 sent by copy engines, no SM taken from backward); opt-in through
   ``RO_GRAD_TRANSPORT``, and it needs ``owner_layers`` naming the matrices of
   layer-sharded optimizers): those matrices are laid out first in the buffer, one
   contiguous segment per layer, and each segment goes only to the rank that
@@ -88,7 +89,7 @@ class GradientSynchronizer:
         if communicator is not None:
             self.transport = "p2p"
         elif self.owner_mode:
-            self.transport = transport if transport in ("owner-bf16", "owner-int8") else "owner-f32"
+            self.transport = transport if transport in ("owner-bf16", "owner-int8", "owner-ce") else "owner-f32"
         elif self.world > 1:
             self.transport = "nccl-overlap" if self.overlap else "nccl"
         else:
@@ -139,8 +140,10 @@ class GradientSynchronizer:
         self._layer_size = list(self._layer_left)
         self._tail = segments[-1][0] + segments[-1][1] if segments else 0
         owners = [int(layer_owner(l)) for l in range(len(layers))]
+        copy_engine = self.transport == "owner-ce"  # fp32 payload, copy-engine sends
         self.owner = OwnerReduce(self.flat, segments, owners, group=self.group,
-                                 transport=self.transport.split("-", 1)[1])
+                                 transport="f32" if copy_engine else self.transport.split("-", 1)[1],
+                                 copy_engine=copy_engine)
         self._reported = set()
         self._delivered = {}   # layer -> [(start, length)] stored in the owner's slot by GEMMs
         self._dirty = False    # a backward ran since zero_grad (gradient accumulation)

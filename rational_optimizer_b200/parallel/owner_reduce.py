@@ -9,7 +9,8 @@ training/train.py:2366-2371) by
   other rank writes it (fp32; bf16 with ``transport="bf16"``; int8 with one
   fp32 scale per 256 elements with ``transport="int8"``) into its slot of the
   owner's receive buffer with peer stores, on a communication stream,
-  overlapped with the rest of backward;
+  overlapped with the rest of backward (fp32 with ``copy_engine=True``: one
+  copy-engine copy per layer, so the sends occupy no SM);
 * ``reduce()``: after backward the owner waits (bounded) for every sender,
   sums the slots in rank order together with its own gradient, scales by
   1/world, writes the result over its own gradient, and keeps the sum of
@@ -75,9 +76,15 @@ def counter_index(layer, owners):
 
 class OwnerReduce:
     def __init__(self, flat: torch.Tensor, segments, owners, *, group=None, transport="f32",
-                 timeout_s=None, send_ctas=None):
+                 timeout_s=None, send_ctas=None, copy_engine=False):
+        """``copy_engine`` (fp32 transport only): each send is one device-to-device
+        copy into the owner's slot, done by a copy engine instead of send CTAs,
+        followed by the same arrival; the backward's kernels keep every SM."""
         if transport not in MODES:
             raise ValueError(f"owner transport must be one of {sorted(MODES)}, got {transport!r}")
+        if copy_engine and transport != "f32":
+            raise ValueError("copy-engine sends carry the fp32 transport only")
+        self.copy_engine = bool(copy_engine)
         C = _ext.ext()
         self.flat = flat
         self.device = flat.device
@@ -161,12 +168,20 @@ class OwnerReduce:
         C = _ext.ext()
         with torch.cuda.stream(self.stream):
             if not delivered:
-                C.owner_send(self.flat[off:off + n], dst, self.mode, counter, self.send_ctas)
+                if self.copy_engine:
+                    C.owner_copy(self.flat[off:off + n], dst)
+                    C.owner_signal(counter, self.send_ctas)
+                else:
+                    C.owner_send(self.flat[off:off + n], dst, self.mode, counter, self.send_ctas)
                 return
             cursor = 0
             for start, length in sorted(delivered) + [(n, 0)]:
                 if start > cursor:  # a gap the GEMMs did not store: send it without an arrival
-                    C.owner_send(self.flat[off + cursor:off + start], dst + 4 * cursor, self.mode, 0, self.send_ctas)
+                    if self.copy_engine:
+                        C.owner_copy(self.flat[off + cursor:off + start], dst + 4 * cursor)
+                    else:
+                        C.owner_send(self.flat[off + cursor:off + start], dst + 4 * cursor, self.mode, 0,
+                                     self.send_ctas)
                 cursor = max(cursor, start + length)
             # one arrival worth a full send, after everything this stream ordered before it
             C.owner_signal(counter, self.send_ctas)

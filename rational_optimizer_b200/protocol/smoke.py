@@ -73,11 +73,13 @@ def owner_checks(rank, world, device):
     from ..parallel.owner_reduce import SEND_CTAS
     # the training configuration (few send CTAs, beside the backward's kernels)
     # and a wide one (about one CTA per SM), which bounds what the kernels reach
-    for transport, ctas in (("f32", SEND_CTAS), ("bf16", SEND_CTAS), ("int8", SEND_CTAS), ("f32", 128),
-                            ("bf16", 128), ("int8", 128)):
+    # and the copy-engine fp32 send (no send CTAs)
+    for transport, ctas, ce in (("f32", SEND_CTAS, False), ("bf16", SEND_CTAS, False),
+                                ("int8", SEND_CTAS, False), ("f32", 128, False), ("bf16", 128, False),
+                                ("int8", 128, False), ("f32", SEND_CTAS, True)):
         red = OwnerReduce(flat, [(r * seg, seg) for r in range(world)], list(range(world)), transport=transport,
-                          send_ctas=ctas)
-        name = transport if ctas == SEND_CTAS else f"{transport}_ctas{ctas}"
+                          send_ctas=ctas, copy_engine=ce)
+        name = "f32_ce" if ce else (transport if ctas == SEND_CTAS else f"{transport}_ctas{ctas}")
 
         def once():
             flat.fill_(float(rank + 1))

@@ -40,6 +40,7 @@ def test_overlapped_sharded_training_matches_replicated():
     assert "MUON_SHARD_OK" in res.stdout
     assert "INT8_OK" in res.stdout
     assert "FUSED_WGRAD_OK" in res.stdout
+    assert "COPY_ENGINE_OK" in res.stdout
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,

@@ -46,7 +46,8 @@ def run(info, *, overlap, shard, accum, graph=False, transport="nccl", weights="
         from rational_optimizer_b200.optim.composite import owner_layers
         layers, owner_of = owner_layers(opt)
         sync = GradientSynchronizer(model, transport=transport, owner_layers=layers, layer_owner=owner_of)
-        assert sync.transport == (transport if transport in ("owner-bf16", "owner-int8") else "owner-f32")
+        assert sync.transport == (transport if transport in ("owner-bf16", "owner-int8", "owner-ce")
+                                  else "owner-f32")
         assert sync.fused_wgrad == fused
     else:
         sync = GradientSynchronizer(model, transport="nccl", overlap=overlap)
@@ -84,7 +85,9 @@ def main():
                dict(overlap=False, shard=True, accum=1, transport="owner-int8", weights="p2p"),
                dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", fused=True),
                dict(overlap=False, shard=True, accum=1, transport="owner", weights="p2p", fused=True, graph=True),
-               dict(overlap=False, shard=True, accum=2, transport="owner", weights="p2p", fused=True)]
+               dict(overlap=False, shard=True, accum=2, transport="owner", weights="p2p", fused=True),
+               dict(overlap=False, shard=True, accum=1, transport="owner-ce"),
+               dict(overlap=False, shard=True, accum=1, transport="owner-ce", graph=True)]
     runs = [run(info, **c) for c in configs]
     digests = [None] * info.world_size
     dist.all_gather_object(digests, [r[1] for r in runs])
@@ -127,6 +130,10 @@ def main():
         rel_fused2 = max(abs(x - y) / abs(y) for x, y in zip(runs[17][0], runs[4][0]))
         assert rel_fused2 < 1e-2, (runs[17][0], runs[4][0])
         print("FUSED_WGRAD_OK max rel loss diff", rel_fused, rel_fused2, flush=True)
+        # fp32 sends by copy engines deliver the same bytes as the send kernels
+        assert runs[18][0] == runs[6][0] and digests[0][18] == digests[0][6], (runs[18][0], runs[6][0])
+        assert runs[19][0] == runs[6][0] and digests[0][19] == digests[0][6], (runs[19][0], runs[6][0])
+        print("COPY_ENGINE_OK", flush=True)
         print("TRAIN_OK", info.world_size, "max rel loss diff", rel, flush=True)
     dist.barrier()
     dist.destroy_process_group()
