@@ -20,9 +20,9 @@ training/train.py:2366-2371).  Two ways to average it across ranks:
 
 * reduce-to-owner (``transport="owner"`` / ``"owner-bf16"`` /
   ``"owner-int8"`` (per-256 fp32 block scales; lossy) / ``"owner-ce"``
-  (fp32 sent by copy engines, no SM taken from backward); opt-in through
-  ``RO_GRAD_TRANSPORT``, and it needs ``owner_layers`` naming the matrices of
-  layer-sharded optimizers): those matrices are laid out first in the buffer, one
+  (fp32 sent by copy engines, no SM taken from backward; the default with
+  several ranks when ``owner_layers`` names the matrices of layer-sharded
+  optimizers): those matrices are laid out first in the buffer, one
   contiguous segment per layer, and each segment goes only to the rank that
   owns the layer (:class:`~.owner_reduce.OwnerReduce`, own NVLink kernels,
   sent during backward); the remaining parameters (embeddings, norms, GRAIN
@@ -60,10 +60,15 @@ class GradientSynchronizer:
         device = params[0].device
         total = sum(p.numel() for p in params)
         if transport is None:
-            # per-layer NCCL buckets overlapped with backward by default: on
-            # 2 and 8 B200s they measured faster than the reduce-to-owner
-            # transport with owner weight pulls (RO_GRAD_TRANSPORT=owner*)
-            transport = os.environ.get("RO_GRAD_TRANSPORT", "nccl")
+            # With layer-sharded optimizers on several GPUs: reduce-to-owner
+            # with fp32 copy-engine sends (measured 18.41 against 19.37 ms per
+            # step for the per-layer NCCL buckets on 8 B200s); otherwise the
+            # NCCL buckets overlapped with backward.
+            default = "nccl"
+            if (owner_layers is not None and self.world > 1 and device.type == "cuda" and _ext.available()
+                    and hasattr(_ext.ext(), "owner_copy")):
+                default = "owner-ce"
+            transport = os.environ.get("RO_GRAD_TRANSPORT", default)
             if transport.startswith("owner") and not (
                     _ext.available() and hasattr(_ext.ext(), "owner_send")):
                 transport = "nccl"
