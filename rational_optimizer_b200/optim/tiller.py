@@ -118,7 +118,7 @@ def foreach_nesterov(optimizer, parameters, momentum):
     grads, bufs = [], []
     for p in parameters:
         if p.grad is None:
-            raise RuntimeError("TILLER parameter lacks gradient")
+            raise RuntimeError("a TILLER-managed matrix has no gradient this step")
         grads.append(p.grad)
         st = optimizer.state[p]
         buf = st.get("momentum_buffer")
@@ -646,7 +646,7 @@ class TILLERRouter(torch.optim.Optimizer):
             col = torch.zeros(shape[:2] + shape[-1:], device=parent.device, dtype=torch.float32)
             anchor[ck] = col
         if row.shape != shape[:-1] or col.shape != shape[:2] + shape[-1:]:
-            raise RuntimeError("factorized adaptive tangent checkpoint inventory changed")
+            raise RuntimeError("saved chord state does not match this optimizer's layout")
         return row, col
 
     def _role_directions(self, participation, congruence):
@@ -830,7 +830,7 @@ class TILLERRouter(torch.optim.Optimizer):
             col = torch.zeros(shape[:2] + shape[-1:], device=device, dtype=torch.float32)
             anchor[ck] = col
         if row.shape != shape[:-1] or col.shape != shape[:2] + shape[-1:]:
-            raise RuntimeError("factorized adaptive tangent checkpoint inventory changed")
+            raise RuntimeError("saved chord state does not match this optimizer's layout")
         return row, col
 
     # -- ledger + transaction ----------------------------------------------
@@ -843,7 +843,7 @@ class TILLERRouter(torch.optim.Optimizer):
         if all(v is None for v in vals):
             return (None, None, None, None)
         if any(not torch.is_tensor(v) for v in vals):
-            raise RuntimeError("TILLER checkpoint inventory changed")
+            raise RuntimeError("saved TILLER ledger state is only partly present")
         return vals
 
     def _advance_rows(self, scores, decay_action, *, functional):
@@ -870,7 +870,7 @@ class TILLERRouter(torch.optim.Optimizer):
             reference = self.anchor.get("factorized_rfd_reference_row_norm")
             decay = self._rfd_decay_derivative
             if not torch.is_tensor(reference) or not torch.is_tensor(decay):
-                raise RuntimeError("TILLER lacks functional calibration")
+                raise RuntimeError("the ledger needs a functional refresh before its first surrogate step")
             scores, decay_action, scale = tm.trace_matched_surrogate(exact_by_role, decay, reference)
             self._rfd_gradient_scale = scale
             self._advance_rows(scores, decay_action, functional=False)
@@ -925,7 +925,7 @@ class TILLERRouter(torch.optim.Optimizer):
         if not functional:
             ref = anchor.get("factorized_rfd_reference_row_norm")
             if not torch.is_tensor(ref) or not torch.is_tensor(self._rfd_decay_derivative):
-                raise RuntimeError("TILLER lacks functional calibration")
+                raise RuntimeError("the ledger needs a functional refresh before its first surrogate step")
             if ref.data_ptr() != scal[3].data_ptr():
                 scal[3].copy_(ref.reshape(()))
         dd = None if functional else self._rfd_decay_derivative.reshape(1).float().contiguous()
@@ -1023,7 +1023,7 @@ class TILLERRouter(torch.optim.Optimizer):
     def _gather_rows(self, packet):
         if self.world_size == 1:
             if packet.shape[0] != tm.GLOBAL_PROBE_COUNT:
-                raise RuntimeError("fixed-probe global row count changed")
+                raise RuntimeError("the gathered probe rows do not add up to the fixed probe count")
             return packet
         probes = tm.GLOBAL_PROBE_COUNT
         counts = [(r + 1) * probes // self.world_size - r * probes // self.world_size
@@ -1072,7 +1072,7 @@ class TILLERRouter(torch.optim.Optimizer):
         for pair in self.pairs:
             for key in ("in_weight", "out_weight"):
                 if pair[key].grad is None:
-                    raise RuntimeError("TILLER parameter lacks gradient")
+                    raise RuntimeError("a TILLER-managed matrix has no gradient this step")
         if not refresh:
             self._rfd_decay_derivative = self._decay_derivative(wd)
         L = len(self.pairs)
@@ -1300,25 +1300,25 @@ class TILLERRouter(torch.optim.Optimizer):
         anchor = self.anchor
         step = anchor.get("cadence8_transition")
         if not isinstance(step, int) or step < 0:
-            raise RuntimeError("cadence8 checkpoint transition changed")
+            raise RuntimeError("the saved refresh-cadence step is missing or negative")
         self._cadence_transition = step
         self._capture_response_this_transition = step % tm.REFRESH_INTERVAL == 0
         route = {name: anchor.get("cadence8_" + name) for name in _ROUTE_NAMES}
         if any(not torch.is_tensor(v) for v in route.values()):
-            raise RuntimeError("cadence8 checkpoint route changed")
+            raise RuntimeError("the saved refresh-cadence route tensors are missing")
         self._cached_route = route
         self._cached_selection_scores = anchor.get("predictive_global_score_ema")
         self._cached_selection_decay = anchor.get("predictive_global_decay_ema")
         if not torch.is_tensor(self._cached_selection_scores) or not torch.is_tensor(self._cached_selection_decay):
-            raise RuntimeError("cadence8 checkpoint selection factor changed")
+            raise RuntimeError("the saved selection-factor tensors are missing")
         innov = anchor.get("cadence8_relative_score_innovation")
         if innov is not None and (not torch.is_tensor(innov) or innov.numel() != 1):
-            raise RuntimeError("cadence8 checkpoint innovation diagnostic changed")
+            raise RuntimeError("the saved score-innovation record is not a single value")
         self._previous_ledger()
         ref = anchor.get("factorized_rfd_reference_row_norm")
         st = anchor.get("factorized_rfd_step")
         if not torch.is_tensor(ref) or ref.numel() != 1 or type(st) is not int or st < 1:
-            raise RuntimeError("TILLER reference checkpoint is absent")
+            raise RuntimeError("the saved ledger reference norm or step counter is missing or invalid")
         self._rfd_rows = None
         self._rfd_gradient_scale = None
         self._rfd_selection = None

@@ -57,7 +57,7 @@ class ProbeLayout:
 def fixed_global_probe_layout(global_probe_count: int, rank: int, world: int) -> ProbeLayout:
     probes, rank, world = int(global_probe_count), int(rank), int(world)
     if probes < 2 or world < 1 or rank < 0 or rank >= world:
-        raise RuntimeError("fixed global probe layout is invalid")
+        raise RuntimeError("probe layout needs at least two probes and a rank inside the world")
     start = rank * probes // world
     stop = (rank + 1) * probes // world
     return ProbeLayout(probes, world, rank, start, stop, stop - start)
@@ -66,7 +66,7 @@ def fixed_global_probe_layout(global_probe_count: int, rank: int, world: int) ->
 def evenly_spaced_indices(row_count: int, selected: int, *, device) -> torch.Tensor:
     rows, selected = int(row_count), int(selected)
     if rows < 0 or selected < 0 or selected > rows:
-        raise RuntimeError("fixed probe row selection is invalid")
+        raise RuntimeError(f"cannot pick {selected} evenly spaced rows out of {rows}")
     if selected == 0:
         return torch.empty(0, device=device, dtype=torch.int64)
     if selected == 1:
@@ -250,17 +250,17 @@ def group_view(value, *, groups, width, axis):
     layers, rows, cols = map(int, value.shape)
     if axis == "rows":
         if width is None or rows != int(groups) * int(width):
-            raise RuntimeError("TILLER row-group inventory changed")
+            raise RuntimeError("row groups do not match the layer's matrix shapes")
         return value.float().view(layers, int(groups), int(width), cols), \
             (lambda sel: sel.reshape(layers, rows, cols))
     if axis == "columns":
         if width is None or cols != int(groups) * int(width):
-            raise RuntimeError("TILLER column-group inventory changed")
+            raise RuntimeError("column groups do not match the layer's matrix shapes")
         grouped = value.float().transpose(-2, -1).contiguous().view(layers, int(groups), int(width), rows)
         return grouped, (lambda sel: sel.reshape(layers, cols, rows).transpose(-2, -1).contiguous())
     if axis == "matrix":
         if int(groups) != 1 or width is not None:
-            raise RuntimeError("TILLER matrix inventory changed")
+            raise RuntimeError("a whole-matrix view takes one group and no group width")
         return value.float()[:, None], (lambda sel: sel[:, 0])
     raise ValueError(f"unknown TILLER grouped axis: {axis}")
 
@@ -351,9 +351,9 @@ class LedgerRows:
 
 def functional_row_norm(scores, *, validate=True):
     if scores.ndim != 2 or scores.shape[0] != CURRENT_ROWS or scores.shape[1] < 2:
-        raise RuntimeError("functional calibration rows changed")
+        raise RuntimeError("functional score rows have the wrong shape for this ledger")
     if validate and not bool(torch.isfinite(scores).all()):
-        raise RuntimeError("functional calibration rows changed")
+        raise RuntimeError("functional score rows contain non-finite values")
     return torch.sqrt(scores.double().square().sum() / float(CURRENT_ROWS)).to(scores.dtype)
 
 
@@ -376,11 +376,11 @@ def rfd_rows(current_scores, current_decay, previous_scores, previous_total_diag
              validate=True):
     """Advance the matched-beta2 Robust-FD factor by one optimizer step."""
     if float(beta2) != MATCHED_BETA2:
-        raise ValueError("gradient ledger requires matched beta2=.95")
+        raise ValueError("the ledger's decay is fixed at beta2 = 0.95")
     if current_scores.ndim != 2 or current_scores.shape[0] != CURRENT_ROWS:
-        raise RuntimeError("every-step RFD current-score inventory changed")
+        raise RuntimeError("current ledger rows have the wrong shape")
     if validate and not bool(torch.isfinite(current_scores).all() & torch.isfinite(current_decay).all()):
-        raise RuntimeError("every-step RFD current-score inventory changed")
+        raise RuntimeError("current ledger rows contain non-finite values")
     dtype = current_scores.dtype
     s64 = current_scores.double()
     d64 = current_decay.double()
@@ -388,25 +388,25 @@ def rfd_rows(current_scores, current_decay, previous_scores, previous_total_diag
     zero = s64.new_zeros(())
     if previous_scores is None:
         if previous_tail is not None:
-            raise RuntimeError("gradient-ledger tail appeared before factor")
+            raise RuntimeError("ledger tail mass present without any persistent rows")
         represented = s64.square().sum(0) / float(CURRENT_ROWS)
         tail = torch.zeros_like(represented)
         z = zero.to(dtype)
         return LedgerRows(current_scores, tail.to(dtype), s64.to(dtype), represented.to(dtype),
                           tail.to(dtype), current_cross.to(dtype), False, z, z, z, z)
     if previous_tail is None:
-        raise RuntimeError("gradient-ledger persistent inventory changed")
+        raise RuntimeError("persistent ledger rows given without their tail mass")
     if validate:
         ok = (torch.isfinite(previous_scores).all() & torch.isfinite(previous_total_diagonal).all()
               & torch.isfinite(previous_decay_cross).all() & (previous_total_diagonal >= 0.0).all()
               & torch.isfinite(previous_tail).all() & (previous_tail >= 0.0).all())
         if not bool(ok):
-            raise RuntimeError("gradient-ledger persistent inventory changed")
+            raise RuntimeError("persistent ledger state has non-finite or negative entries")
     beta = float(beta2)
     prev_tail = previous_tail.double().reshape(())
     selection = torch.cat((previous_scores * math.sqrt(beta), current_scores * math.sqrt(1.0 - beta)))
     if selection.shape[0] > MAXIMUM_SELECTION_ROWS:
-        raise RuntimeError("gradient-ledger live row bound changed")
+        raise RuntimeError("more live ledger rows than the ledger keeps")
     selection_tail = prev_tail * beta
     decay_cross = previous_decay_cross.double() * beta + current_cross * (1.0 - beta)
     sel64 = selection.double()
@@ -448,9 +448,9 @@ class WindowRows:
 def window32_rows(current_scores, current_decay, previous_scores, previous_decay, *, validate=True):
     """Latest 32 functional rows, no temporal mixing; Gram innovation diagnostic."""
     if validate and not bool(torch.isfinite(current_scores).all() & torch.isfinite(current_decay).all()):
-        raise RuntimeError("window32 current response inventory changed")
+        raise RuntimeError("response window rows contain non-finite values")
     if (previous_scores is None) != (previous_decay is None):
-        raise RuntimeError("window32 histories must coinitialize")
+        raise RuntimeError("response window score and decay histories must both be present or both absent")
     updated = current_scores.detach().clone()
     updated_decay = current_decay.detach().clone()
     if previous_scores is None:
@@ -554,16 +554,16 @@ def biatlas_transaction(rows: LedgerRows, exact_by_role, momentum_by_role, weigh
     decay_cross = rows.persistent_decay_cross
     factor_rows, coords = scores.shape
     if factor_rows < measure_rows or factor_rows > MAXIMUM_SELECTION_ROWS or coords < 2:
-        raise RuntimeError("diagonal-completed transaction inventory changed")
+        raise RuntimeError("transaction needs between the measured and the maximum row count and two or more coordinates")
     if validate:
         ok = torch.isfinite(scores).all()
         for v in (diag_res, decay_cross, exact_by_role, momentum_by_role, weights):
             ok = ok & torch.isfinite(v).all()
         ok = ok & (diag_res >= 0.0).all() & (weights > 0.0).all()
         if not bool(ok):
-            raise RuntimeError("diagonal-completed transaction values changed")
+            raise RuntimeError("transaction inputs must be finite, with residuals >= 0 and weights > 0")
         if not bool(((layer_ids >= 0) & (layer_ids < int(total_layers))).all()):
-            raise RuntimeError("diagonal-completed layer ID is invalid")
+            raise RuntimeError("transaction layer ids must lie in [0, layers)")
     s64 = scores.double()
     diag64 = diag_res.double()
     decay64 = decay_cross.double()

@@ -74,7 +74,7 @@ def _jsonable(value):
         return [_jsonable(v) for v in value]
     if isinstance(value, dict):
         return {str(k): _jsonable(v) for k, v in sorted(value.items(), key=lambda kv: str(kv[0]))}
-    raise TypeError(f"resume contract contains unsupported value: {type(value)!r}")
+    raise TypeError(f"cannot record a {type(value)!r} in the resume contract")
 
 
 def complete_argument_digest(args) -> str:
@@ -178,7 +178,7 @@ def load(path: Path, *, args, rank, world_size, is_distributed, device, model, o
             or payload.get("contract") != resume_contract(args, world_size, strict=strict)
             or rpayload.get("schema") != RANK_SCHEMA or rpayload.get("rank") != rank
             or rpayload.get("completed_step") != payload.get("completed_step")):
-        raise RuntimeError("exact-resume checkpoint contract differs")
+        raise RuntimeError("checkpoint contract differs from this run (schema, rank or step)")
     raw = model.module if hasattr(model, "module") else model
     raw.load_state_dict(payload["model"])
     optimizer.load_state_dict(payload["optimizer"])
@@ -269,16 +269,16 @@ def prepare_trajectory(checkpoint_path: Path, trajectory_path: Path, world_size:
         try:
             rec = json.loads(line)
         except json.JSONDecodeError as error:
-            raise RuntimeError(f"invalid JSONL record in exact-resume trajectory: {error}") from error
+            raise RuntimeError(f"unreadable line in the trajectory being trimmed for resume: {error}") from error
         event = rec.get("event")
         configs += event == "config"
         rs = rec.get("step")
         keep = event not in {"summary", "checkpoint", "stopped_early"} and (rs is None or int(rs) <= int(step))
         (kept if keep else removed).append(line)
     if configs != 1:
-        raise RuntimeError("exact-resume trajectory must contain exactly one config record")
+        raise RuntimeError(f"the trajectory holds {configs} config records; a resumable one holds one")
     if not any(int(json.loads(l).get("step", -1)) == int(step) for l in kept):
-        raise RuntimeError("trajectory does not contain the durable checkpoint boundary")
+        raise RuntimeError(f"the trajectory has no record at the checkpoint's step {int(step)}")
     archive = None
     if removed:
         archive = trajectory_path.with_name(f"{trajectory_path.name}.tail-after-step-{step}-{time.time_ns()}")
@@ -295,10 +295,10 @@ def validate_strict(args):
     if args.resume_checkpoint is None:
         return
     if Path(args.resume_checkpoint).resolve() != expected_checkpoint_path(args):
-        raise ValueError(f"fairness exact resume must use the run-local checkpoint: {expected_checkpoint_path(args)}")
+        raise ValueError(f"strict resume reads only the run-local checkpoint {expected_checkpoint_path(args)}")
     interval = int(args.resume_checkpoint_interval)
     if interval <= 0 or interval != int(args.eval_interval):
-        raise ValueError("fairness exact resume interval must equal the positive evaluation interval")
+        raise ValueError("strict resume saves at the evaluation interval, which must be positive")
 
 
 def audited_summary(record, args):
