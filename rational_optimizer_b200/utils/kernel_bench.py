@@ -284,6 +284,53 @@ def cases(rows):
     return out
 
 
+def ledger_phases(layers=18, groups=18, steps=10, functional_every=3):
+    """Phase times of the ledger + transaction kernel from its ``%globaltimer``
+    stamps: one JSON line per call, a functional (refresh) call every
+    ``functional_every`` calls, the rest surrogate calls."""
+    C = _ext.ext()
+    dev = "cuda"
+    n = layers * groups
+    gen = torch.Generator(device=dev).manual_seed(7)
+    layer_ids = torch.arange(layers, device=dev).repeat_interleave(groups)
+    pers = torch.zeros(64, n, device=dev)
+    diag = torch.zeros(n, device=dev)
+    cross = torch.zeros(n, device=dev)
+    scal = torch.zeros(8, device=dev)
+    ws = torch.empty(int(C.tiller_ledger_workspace(n)), device=dev, dtype=torch.float64)
+    timing = torch.zeros(16, dtype=torch.int64, device=dev)
+    # stamp index -> the phase that ends there
+    names = {1: "gram", 2: "gram_eigensolve", 3: "persistent_rows", 4: "transaction_setup", 6: "lanczos",
+             7: "tridiagonal_eigensolve", 8: "projection", 9: "acceptance"}
+    prev = 0
+    for step in range(steps):
+        functional = step % functional_every == 0
+        exact = (torch.rand(2, n, device=dev, generator=gen) + 0.1) * 1e-3
+        mom = (torch.rand(2, n, device=dev, generator=gen) + 0.1) * 1e-3
+        w = torch.rand(n, device=dev, generator=gen) + 0.5
+        sc = torch.randn(32, n, device=dev, generator=gen) * 1e-3
+        dc = torch.randn(32, device=dev, generator=gen) * 1e-4
+        dd = torch.randn((), device=dev, generator=gen).abs().reshape(1) * 1e-4
+        timing.zero_()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        C.tiller_ledger_transaction(sc if functional else None, dc if functional else None, exact, mom, w,
+                                    layer_ids, None if functional else dd, pers, diag, cross, scal, ws, prev,
+                                    layers, 3e-4, timing=timing)
+        end.record()
+        torch.cuda.synchronize()
+        t = timing.tolist()
+        phases, last = {}, t[0]
+        for k in sorted(names):
+            if t[k]:
+                phases[names[k]] = round((t[k] - last) / 1e3, 1)
+                last = t[k]
+        print(json.dumps({"case": "ledger_phases", "call": step, "functional": functional, "prev_rows": prev,
+                          "ms": round(start.elapsed_time(end), 3), "gram_sweeps": t[12],
+                          "tridiagonal_sweeps": t[13], "phase_us": phases}), flush=True)
+        prev = 32 if prev == 0 else 64
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all")
@@ -292,6 +339,9 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
     hbm, tflops, kind = peaks()
+    if a.case == "ledger_phases":
+        ledger_phases()
+        return
     table = cases(a.rows)
     names = list(table) if a.case == "all" else a.case.split(",")
     for name in names:
