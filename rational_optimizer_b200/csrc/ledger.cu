@@ -119,6 +119,13 @@ __device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double
   }
   const int m = (n + 1) & ~1;  // even number of players (a dummy if n is odd)
   const int half = m / 2;
+  const int nblk = half * half;
+  // first item of this thread and the per-item step, as (pair k, pair l) of
+  // the A blocks and (pair k, row i) of the V updates
+  const int a_k0 = tid / half, a_l0 = tid - a_k0 * half;
+  const int a_dk = static_cast<int>(blockDim.x) / half, a_dl = static_cast<int>(blockDim.x) - a_dk * half;
+  const int v_k0 = tid / n, v_i0 = tid - v_k0 * n;
+  const int v_dk = static_cast<int>(blockDim.x) / n, v_di = static_cast<int>(blockDim.x) - v_dk * n;
   __syncthreads();
   double total = 0.0;
   for (int i = tid; i < n * n; i += blockDim.x) {
@@ -178,38 +185,55 @@ __device__ int jacobi_eigh(double* A, double* V, int n, int* rp, int* rq, double
         rs[k] = s;
       }
       __syncthreads();
-      // A <- R^T A R and V <- V R in one pass.  R is block diagonal over the
-      // round's disjoint pairs, so each 2 x 2 block (pair k rows, pair l
-      // columns) of A and each (row, pair) of V is updated independently.
-      const int nblk = half * half;
-      for (int idx = tid; idx < nblk + n * half; idx += blockDim.x) {
-        if (idx < nblk) {
-          const int k = idx / half, l = idx - k * half;
+      // A <- R^T A R and V <- V R.  R is block diagonal over the round's
+      // disjoint pairs, so each 2 x 2 block (pair k rows, pair l columns) of A
+      // and each (row, pair) of V is updated independently.  A thread's items
+      // are tid, tid + blockDim.x, ...; their (k, l) and (pair, row) indices
+      // advance by fixed steps instead of being divided out per item.
+      {
+        int k = a_k0, l = a_l0;
+        for (int idx = tid; idx < nblk; idx += blockDim.x) {
           const int p = rp[k], q = rq[k], u = rp[l], w = rq[l];
           const double c = rc[k], sk = rs[k], c2 = rc[l], s2 = rs[l];
-          if (sk == 0.0 && s2 == 0.0) continue;
-          const bool qk = q < n, wl = w < n;
-          const double apu = A[p * ld + u];
-          const double apw = wl ? A[p * ld + w] : 0.0;
-          const double aqu = qk ? A[q * ld + u] : 0.0;
-          const double aqw = (qk && wl) ? A[q * ld + w] : 0.0;
-          // rows (pair k)
-          const double bpu = c * apu - sk * aqu, bqu = sk * apu + c * aqu;
-          const double bpw = c * apw - sk * aqw, bqw = sk * apw + c * aqw;
-          // columns (pair l); the rotated pair's own off-diagonal is zero
-          A[p * ld + u] = c2 * bpu - s2 * bpw;
-          if (wl) A[p * ld + w] = (k == l) ? 0.0 : s2 * bpu + c2 * bpw;
-          if (qk) A[q * ld + u] = (k == l) ? 0.0 : c2 * bqu - s2 * bqw;
-          if (qk && wl) A[q * ld + w] = s2 * bqu + c2 * bqw;
-        } else {
-          const int j = idx - nblk;
-          const int k = j / n, i = j - k * n;
+          if (sk != 0.0 || s2 != 0.0) {
+            const bool qk = q < n, wl = w < n;
+            const double apu = A[p * ld + u];
+            const double apw = wl ? A[p * ld + w] : 0.0;
+            const double aqu = qk ? A[q * ld + u] : 0.0;
+            const double aqw = (qk && wl) ? A[q * ld + w] : 0.0;
+            // rows (pair k)
+            const double bpu = c * apu - sk * aqu, bqu = sk * apu + c * aqu;
+            const double bpw = c * apw - sk * aqw, bqw = sk * apw + c * aqw;
+            // columns (pair l); the rotated pair's own off-diagonal is zero
+            A[p * ld + u] = c2 * bpu - s2 * bpw;
+            if (wl) A[p * ld + w] = (k == l) ? 0.0 : s2 * bpu + c2 * bpw;
+            if (qk) A[q * ld + u] = (k == l) ? 0.0 : c2 * bqu - s2 * bqw;
+            if (qk && wl) A[q * ld + w] = s2 * bqu + c2 * bqw;
+          }
+          l += a_dl;
+          k += a_dk;
+          if (l >= half) {
+            l -= half;
+            ++k;
+          }
+        }
+      }
+      {
+        int k = v_k0, i = v_i0;
+        for (int j = tid; j < n * half; j += blockDim.x) {
           const int p = rp[k], q = rq[k];
-          if (q >= n || rs[k] == 0.0) continue;
-          const double c = rc[k], sk = rs[k];
-          const double vp = V[i * ld + p], vq = V[i * ld + q];
-          V[i * ld + p] = c * vp - sk * vq;
-          V[i * ld + q] = sk * vp + c * vq;
+          if (q < n && rs[k] != 0.0) {
+            const double c = rc[k], sk = rs[k];
+            const double vp = V[i * ld + p], vq = V[i * ld + q];
+            V[i * ld + p] = c * vp - sk * vq;
+            V[i * ld + q] = sk * vp + c * vq;
+          }
+          i += v_di;
+          k += v_dk;
+          if (i >= n) {
+            i -= n;
+            ++k;
+          }
         }
       }
       __syncthreads();
