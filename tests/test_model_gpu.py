@@ -65,3 +65,25 @@ def test_tiller_gpu_matches_cpu_fp32():
         assert abs(lc - lg) < 5e-3 * max(1.0, abs(lc)), (step, lc, lg)
     for (n, a), (_, b) in zip(cpu.named_parameters(), gpu.named_parameters()):
         torch.testing.assert_close(b.detach().cpu(), a.detach(), rtol=5e-2, atol=2e-3, msg=n)
+
+
+@pytest.mark.parametrize("hd", [96, 128])
+def test_seq2048_head_dims_match_cpu(hd):
+    """Causal attention at seq 2048 with head_dim 96 / 128 (cuDNN attention for
+    96, the fused projection where it applies): bf16 CUDA model against the
+    fp32 CPU model, loss and gradients."""
+    heads = 2
+    args = _args(layers=1, d_model=heads * hd, heads=heads, ffn_dim=256, seq_len=2048,
+                 rational_group_size=64)
+    torch.manual_seed(0)
+    cpu = CausalTransformer(args, 300)
+    gpu = copy.deepcopy(cpu).cuda()
+    t = torch.randint(0, 300, (1, 2049))
+    lc = cpu.forward_loss(t[:, :-1], t[:, 1:])
+    lc.backward()
+    lg = gpu.forward_loss(t[:, :-1].cuda(), t[:, 1:].cuda())
+    lg.backward()
+    assert abs(lc.detach().item() - lg.detach().item()) < 2e-2 * abs(lc.detach().item())
+    for (n, a), (_, b) in zip(cpu.named_parameters(), gpu.named_parameters()):
+        scale = a.grad.abs().amax().item() + 1e-6
+        assert (b.grad.cpu().float() - a.grad).abs().amax().item() <= 5e-2 * scale, n
